@@ -1,0 +1,125 @@
+/*
+ * spikegpt_wkv.h -- C ABI of the B200 (sm_100a) WKV recurrence library
+ * (libspikegpt_wkv.so).
+ *
+ * The library implements SpikeGPT's RWKV-4 WKV time-mix recurrence, forward and
+ * backward, as hand-written CUDA kernels. The entry points take plain device
+ * pointers, sizes and a cudaStream_t passed as void*; there are no torch types in
+ * any signature. Every entry point is asynchronous on the given stream, performs
+ * no host synchronisation and allocates no device memory: scratch ("workspace")
+ * is sized by the *_workspace_size query and owned by the caller.
+ *
+ * Layout: key, value, y, grad_y, grad_key, grad_value are contiguous row-major
+ * [B, T, C] (element (b, t, c) at b*T*C + t*C + c). time_decay, time_first, w, u,
+ * grad_time_decay, grad_time_first are contiguous float32 [C].
+ *
+ * Arithmetic: the recurrence runs in float32 whatever the I/O dtype; I/O values
+ * are widened in registers and results are rounded to the I/O dtype on store.
+ *
+ * Reference interfaces these entry points replace (paths relative to the
+ * reference project djsaunde/spikegpt-myelin):
+ *   wkv_forward   <- torch op myelin::wkv_forward, src/spikegpt/wkv_triton.py:147-158,
+ *                    and its bf16 twin myelin::wkv_forward_bf16io, src/spikegpt/wkv_bf16.py:143-154
+ *   wkv_backward  <- torch op myelin::wkv_backward, src/spikegpt/wkv_triton.py:164-194,
+ *                    and myelin::wkv_backward_bf16io, src/spikegpt/wkv_bf16.py:160-191
+ */
+#ifndef SPIKEGPT_WKV_H_
+#define SPIKEGPT_WKV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define WKV_API __attribute__((visibility("default")))
+#else
+#define WKV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* I/O element types of key, value, y, grad_y, grad_key, grad_value. */
+#define WKV_DTYPE_F32 0
+#define WKV_DTYPE_BF16 1
+#define WKV_DTYPE_F16 2
+
+/* Status codes returned by every int-valued entry point. */
+#define WKV_OK 0
+#define WKV_ERR_INVALID_ARGUMENT 1   /* bad dtype, negative size, null pointer, ...   */
+#define WKV_ERR_WORKSPACE_TOO_SMALL 2 /* workspace_bytes < the *_workspace_size query */
+#define WKV_ERR_CUDA 3               /* a CUDA runtime call or kernel launch failed   */
+#define WKV_ERR_DRIVER 4             /* TMA descriptor encoding failed                 */
+
+/* Sticky device-side error flags (see wkv_device_error_flags). */
+#define WKV_DEVERR_PIPELINE_TIMEOUT 1u /* a bounded wait on a copy barrier expired */
+
+/* ABI version of this header; bumped on incompatible changes. */
+#define WKV_ABI_VERSION 1
+WKV_API int wkv_abi_version(void);
+
+/* Human-readable text for a status code (static storage). */
+WKV_API const char* wkv_status_string(int status);
+
+/* Details of the last failure on the calling thread ("" if none). */
+WKV_API const char* wkv_last_error(void);
+
+/*
+ * Forward: y = WKV(key, value; w = -exp(time_decay), u = time_first).
+ * Replaces myelin::wkv_forward / myelin::wkv_forward_bf16io
+ * (reference src/spikegpt/wkv_triton.py:147-158, src/spikegpt/wkv_bf16.py:143-154):
+ * same arithmetic contract (float32 recurrence, y in the I/O dtype). Unlike the
+ * reference wrapper, the I/O tensors are read in their native dtype; no float32
+ * copies are made.
+ * Sizes: B, T, C >= 0 (any zero size is a no-op).
+ */
+WKV_API size_t wkv_forward_workspace_size(int dtype, int64_t B, int64_t T, int64_t C);
+WKV_API int wkv_forward(int dtype, const void* key, const void* value, const float* time_decay,
+                const float* time_first, void* y, int64_t B, int64_t T, int64_t C,
+                void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Backward of the forward above given grad_y = dL/dy.
+ * Replaces myelin::wkv_backward / myelin::wkv_backward_bf16io
+ * (reference src/spikegpt/wkv_triton.py:164-194, src/spikegpt/wkv_bf16.py:160-191):
+ * inputs w = -exp(time_decay) and u = time_first (float32 [C]); outputs
+ * grad_key, grad_value ([B,T,C], I/O dtype), grad_time_decay = dL/dw * w summed
+ * over the batch (the reference folds the chain rule of w = -exp(time_decay) in,
+ * wkv_triton.py:117,194) and grad_time_first = dL/du summed over the batch
+ * (float32 [C]). The per-channel sums are reduced in a fixed order (no atomics),
+ * so results are deterministic.
+ */
+WKV_API size_t wkv_backward_workspace_size(int dtype, int64_t B, int64_t T, int64_t C);
+WKV_API int wkv_backward(int dtype, const void* grad_y, const float* w, const float* u,
+                 const void* key, const void* value, void* grad_key, void* grad_value,
+                 float* grad_time_decay, float* grad_time_first, int64_t B, int64_t T,
+                 int64_t C, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Execution plan the library picks for a shape (no reference counterpart; it
+ * exposes the choice the reference never had to make). tma = 1 when tiles are
+ * staged with TMA (needs C*sizeof(dtype) % 16 == 0 and 16-byte aligned
+ * pointers), segments = number of time segments per (b, c) lane (1 = one
+ * sequential sweep; > 1 = chunked two-level scan for small B*C).
+ */
+WKV_API int wkv_plan(int dtype, int64_t B, int64_t T, int64_t C, int* tma, int* segments);
+
+/*
+ * Test and benchmark hooks (process-wide; no reference counterpart).
+ * force_segments > 0 fixes the segment count; force_generic != 0 disables the
+ * TMA path; force_slow != 0 makes every sub-chunk take the exact per-step
+ * rescaling path. Pass zeros to restore the defaults.
+ */
+WKV_API int wkv_set_debug_overrides(int force_segments, int force_generic, int force_slow);
+
+/*
+ * Reads (and with clear != 0 resets) the sticky device-side error flags of the
+ * current device; synchronises the device. Returns a status code.
+ */
+WKV_API int wkv_device_error_flags(unsigned* flags, int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPIKEGPT_WKV_H_ */

@@ -1,0 +1,510 @@
+// C ABI of libspikegpt_wkv.so (declared in include/spikegpt_wkv.h).
+//
+// Host side: argument validation, the execution plan (TMA vs generic tiles,
+// number of time segments), the caller-provided workspace carve-up, TMA
+// descriptor encoding, and the kernel launch sequence. Every entry point is
+// asynchronous on the caller's stream and allocates nothing.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+
+#include "spikegpt_wkv.h"
+#include "wkv_kernels.cuh"
+
+namespace {
+
+using namespace wkv;
+
+thread_local char g_last_error[512] = "";
+std::atomic<int> g_force_segments{0};
+std::atomic<int> g_force_generic{0};
+std::atomic<int> g_force_slow{0};
+
+__device__ unsigned g_device_error_flags = 0;
+
+int fail(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(WKV_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+size_t dtype_size(int dtype) {
+  switch (dtype) {
+    case WKV_DTYPE_F32: return 4;
+    case WKV_DTYPE_BF16: return 2;
+    case WKV_DTYPE_F16: return 2;
+    default: return 0;
+  }
+}
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+struct Plan {
+  bool tma;
+  int nseg;
+  int seg_len;
+};
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Segments: one sequential sweep per lane when B*C lanes give every SM enough
+// warps; otherwise split time so that lanes * segments reaches that count.
+Plan make_plan(int dtype, int64_t B, int64_t T, int64_t C, bool ptrs_aligned) {
+  Plan p;
+  const size_t es = dtype_size(dtype);
+  p.tma = g_force_generic.load() == 0 && ptrs_aligned && (C * (int64_t)es) % 16 == 0;
+  const int64_t lanes = B * ((C + kLanes - 1) / kLanes) * kLanes;
+  const int64_t want = (int64_t)sm_count() * 6 * kLanes;
+  int64_t nseg = 1;
+  if (lanes > 0 && lanes < want) nseg = (want + lanes - 1) / lanes;
+  const int64_t max_seg = T / (2 * kTile);  // keep >= 2 tiles per segment
+  if (nseg > max_seg) nseg = max_seg;
+  if (g_force_segments.load() > 0) nseg = g_force_segments.load();
+  if (nseg < 1) nseg = 1;
+  if (nseg == 1) {
+    p.nseg = 1;
+    p.seg_len = static_cast<int>(T);
+  } else {
+    int64_t len = (T + nseg - 1) / nseg;
+    len = (len + kTile - 1) / kTile * kTile;
+    p.seg_len = static_cast<int>(len);
+    p.nseg = static_cast<int>((T + len - 1) / len);
+    if (p.nseg == 1) p.seg_len = static_cast<int>(T);
+  }
+  return p;
+}
+
+constexpr size_t kAlign = 256;
+size_t round_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+struct FwdWs {
+  float* seg;
+  size_t bytes;
+};
+FwdWs fwd_workspace(const Plan& p, int64_t B, int64_t C, void* base) {
+  FwdWs w{nullptr, 0};
+  if (p.nseg > 1) {
+    w.bytes = round_up((size_t)B * p.nseg * 3 * C * sizeof(float));
+    w.seg = static_cast<float*>(base);
+  }
+  return w;
+}
+
+struct BwdWs {
+  float* ckpt;
+  float* seg;
+  float* adj;
+  float* partial;
+  size_t bytes;
+};
+BwdWs bwd_workspace(const Plan& p, int64_t B, int64_t T, int64_t C, void* base) {
+  BwdWs w{};
+  char* cur = static_cast<char*>(base);
+  auto take = [&](size_t n) {
+    char* r = cur;
+    const size_t sz = round_up(n);
+    if (cur) cur += sz;
+    w.bytes += sz;
+    return reinterpret_cast<float*>(r);
+  };
+  const int64_t nsub = (T + kSub - 1) / kSub;
+  w.ckpt = take((size_t)B * nsub * 3 * C * sizeof(float));
+  if (p.nseg > 1) {
+    w.seg = take((size_t)B * p.nseg * 3 * C * sizeof(float));
+    w.adj = take((size_t)B * p.nseg * 3 * C * sizeof(float));
+  }
+  w.partial = take((size_t)B * p.nseg * 2 * C * sizeof(float));
+  if (!base) w.ckpt = w.seg = w.adj = w.partial = nullptr;
+  return w;
+}
+
+// ------------------------------------------------------------ TMA descriptors
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// [B, T, C] tensor as a 3-D map with dims {C, T, B} and a [1][kTile][kLanes] box.
+int make_map(CUtensorMap* m, int dtype, const void* ptr, int64_t B, int64_t T, int64_t C) {
+  std::memset(m, 0, sizeof(*m));
+  if (ptr == nullptr) return WKV_OK;
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(WKV_ERR_DRIVER, "cuTensorMapEncodeTiled is not available");
+  const size_t es = dtype_size(dtype);
+  const CUtensorMapDataType dt = dtype == WKV_DTYPE_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == WKV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)T, (cuuint64_t)B};
+  const cuuint64_t strides[2] = {(cuuint64_t)(C * es), (cuuint64_t)(T * C * es)};
+  const cuuint32_t box[3] = {(cuuint32_t)kLanes, (cuuint32_t)kTile, 1u};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUresult r = fn(m, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(WKV_ERR_DRIVER, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return WKV_OK;
+}
+
+// Device address of g_device_error_flags for the current device (looked up once
+// per device; the host-side symbol itself is not a device address).
+unsigned* device_err_ptr() {
+  static std::atomic<unsigned*> cached[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  unsigned* p = cached[dev].load();
+  if (p == nullptr) {
+    void* q = nullptr;
+    if (cudaGetSymbolAddress(&q, g_device_error_flags) != cudaSuccess) return nullptr;
+    p = static_cast<unsigned*>(q);
+    cached[dev].store(p);
+  }
+  return p;
+}
+
+int check_dims(int dtype, int64_t B, int64_t T, int64_t C) {
+  if (dtype_size(dtype) == 0) return fail(WKV_ERR_INVALID_ARGUMENT, "unknown dtype code %d", dtype);
+  if (B < 0 || T < 0 || C < 0)
+    return fail(WKV_ERR_INVALID_ARGUMENT, "negative size B=%lld T=%lld C=%lld", (long long)B,
+                (long long)T, (long long)C);
+  if (T > (1ll << 30) || C > (1ll << 30) || B > (1ll << 30) || B * ((C + 31) / 32) > (1ll << 31) - 1)
+    return fail(WKV_ERR_INVALID_ARGUMENT, "size out of range B=%lld T=%lld C=%lld", (long long)B,
+                (long long)T, (long long)C);
+  return WKV_OK;
+}
+
+// ----------------------------------------------------------- launch helpers
+
+template <typename IO>
+int launch_forward(const void* k, const void* v, const float* decay, int decay_is_w,
+                   const float* u, void* y, int B, int T, int C, const Plan& p, float* seg,
+                   cudaStream_t st) {
+  CUtensorMap mk, mv, my;
+  const int dt = sizeof(IO) == 4 ? WKV_DTYPE_F32
+                 : std::is_same<IO, __nv_bfloat16>::value ? WKV_DTYPE_BF16
+                                                         : WKV_DTYPE_F16;
+  int rc;
+  if (p.tma) {
+    if ((rc = make_map(&mk, dt, k, B, T, C)) || (rc = make_map(&mv, dt, v, B, T, C)) ||
+        (rc = make_map(&my, dt, y, B, T, C)))
+      return rc;
+  } else {
+    std::memset(&mk, 0, sizeof(mk));
+    std::memset(&mv, 0, sizeof(mv));
+    std::memset(&my, 0, sizeof(my));
+  }
+  FwdArgs a{};
+  a.k = k;
+  a.v = v;
+  a.y = y;
+  a.decay = decay;
+  a.u = u;
+  a.decay_is_w = decay_is_w;
+  a.B = B;
+  a.T = T;
+  a.C = C;
+  a.ncblk = (C + kLanes - 1) / kLanes;
+  a.seg_len = p.seg_len;
+  a.nseg = p.nseg;
+  a.nsub = (T + kSub - 1) / kSub;
+  a.force_slow = g_force_slow.load();
+  a.err = device_err_ptr();
+  const unsigned gx = (unsigned)a.ncblk * (unsigned)B;
+  if (p.nseg > 1) {
+    // summaries of segments 0..nseg-2, then the carry
+    FwdArgs s = a;
+    s.seg_end = seg;
+    const size_t sm = fwd_smem_bytes<IO>(false);
+    if (p.tma)
+      wkv_fwd_kernel<IO, false, true><<<dim3(gx, p.nseg - 1), kLanes, sm, st>>>(s, mk, mv, my);
+    else
+      wkv_fwd_kernel<IO, false, false><<<dim3(gx, p.nseg - 1), kLanes, sm, st>>>(s, mk, mv, my);
+    const int64_t lanes = (int64_t)B * C;
+    wkv_carry_fwd_kernel<<<(unsigned)((lanes + 127) / 128), 128, 0, st>>>(seg, decay, decay_is_w, B,
+                                                                          T, C, p.nseg, p.seg_len);
+    a.seg_start = seg;
+  }
+  const size_t sm = fwd_smem_bytes<IO>(true);
+  if (p.tma)
+    wkv_fwd_kernel<IO, true, true><<<dim3(gx, p.nseg), kLanes, sm, st>>>(a, mk, mv, my);
+  else
+    wkv_fwd_kernel<IO, true, false><<<dim3(gx, p.nseg), kLanes, sm, st>>>(a, mk, mv, my);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "wkv forward launch");
+  return WKV_OK;
+}
+
+template <typename IO>
+int launch_backward(const void* gy, const float* w, const float* u, const void* k, const void* v,
+                    void* gk, void* gv, float* gtd, float* gtf, int B, int T, int C,
+                    const Plan& p, const BwdWs& ws, cudaStream_t st) {
+  const int dt = sizeof(IO) == 4 ? WKV_DTYPE_F32
+                 : std::is_same<IO, __nv_bfloat16>::value ? WKV_DTYPE_BF16
+                                                         : WKV_DTYPE_F16;
+  CUtensorMap mk, mv, mgy, mgk, mgv, none;
+  std::memset(&none, 0, sizeof(none));
+  int rc;
+  if (p.tma) {
+    if ((rc = make_map(&mk, dt, k, B, T, C)) || (rc = make_map(&mv, dt, v, B, T, C)) ||
+        (rc = make_map(&mgy, dt, gy, B, T, C)) || (rc = make_map(&mgk, dt, gk, B, T, C)) ||
+        (rc = make_map(&mgv, dt, gv, B, T, C)))
+      return rc;
+  } else {
+    mk = mv = mgy = mgk = mgv = none;
+  }
+  const int ncblk = (C + kLanes - 1) / kLanes;
+  const int nsub = (T + kSub - 1) / kSub;
+  const unsigned gx = (unsigned)ncblk * (unsigned)B;
+  unsigned* err = device_err_ptr();
+  const int force_slow = g_force_slow.load();
+
+  // 1. forward state sweep: checkpoints at every sub-chunk start (+ segment ends)
+  FwdArgs f{};
+  f.k = k;
+  f.v = v;
+  f.decay = w;
+  f.u = u;
+  f.decay_is_w = 1;
+  f.B = B;
+  f.T = T;
+  f.C = C;
+  f.ncblk = ncblk;
+  f.seg_len = p.seg_len;
+  f.nseg = p.nseg;
+  f.nsub = nsub;
+  f.ckpt = ws.ckpt;
+  f.seg_end = p.nseg > 1 ? ws.seg : nullptr;
+  f.force_slow = force_slow;
+  f.err = err;
+  const size_t fsm = fwd_smem_bytes<IO>(false);
+  if (p.tma)
+    wkv_fwd_kernel<IO, false, true><<<dim3(gx, p.nseg), kLanes, fsm, st>>>(f, mk, mv, none);
+  else
+    wkv_fwd_kernel<IO, false, false><<<dim3(gx, p.nseg), kLanes, fsm, st>>>(f, mk, mv, none);
+
+  BwdArgs a{};
+  a.k = k;
+  a.v = v;
+  a.gy = gy;
+  a.gk = gk;
+  a.gv = gv;
+  a.w = w;
+  a.u = u;
+  a.B = B;
+  a.T = T;
+  a.C = C;
+  a.ncblk = ncblk;
+  a.seg_len = p.seg_len;
+  a.nseg = p.nseg;
+  a.nsub = nsub;
+  a.ckpt = ws.ckpt;
+  a.force_slow = force_slow;
+  a.err = err;
+  const int64_t lanes = (int64_t)B * C;
+  const unsigned cgrid = (unsigned)((lanes + 127) / 128);
+  if (p.nseg > 1) {
+    // 2. segment start states; 3. adjoint summaries of segments 1..nseg-1;
+    // 4. adjoint at every segment end
+    wkv_carry_fwd_kernel<<<cgrid, 128, 0, st>>>(ws.seg, w, 1, B, T, C, p.nseg, p.seg_len);
+    BwdArgs s = a;
+    s.seg_start = ws.seg;
+    s.seg_base = 1;
+    s.adj_out = ws.adj;
+    const size_t ssm = bwd_smem_bytes<IO>(false);
+    if (p.tma)
+      wkv_bwd_kernel<IO, false, true>
+          <<<dim3(gx, p.nseg - 1), kLanes, ssm, st>>>(s, mk, mv, mgy, none, none);
+    else
+      wkv_bwd_kernel<IO, false, false>
+          <<<dim3(gx, p.nseg - 1), kLanes, ssm, st>>>(s, mk, mv, mgy, none, none);
+    wkv_carry_adj_kernel<<<cgrid, 128, 0, st>>>(ws.adj, w, B, T, C, p.nseg, p.seg_len);
+    a.seg_start = ws.seg;
+    a.adj_in = ws.adj;
+  }
+  // 5. reverse sweep writing grad_key / grad_value and per-lane partials
+  a.partial = ws.partial;
+  const size_t bsm = bwd_smem_bytes<IO>(true);
+  if (p.tma)
+    wkv_bwd_kernel<IO, true, true><<<dim3(gx, p.nseg), kLanes, bsm, st>>>(a, mk, mv, mgy, mgk, mgv);
+  else
+    wkv_bwd_kernel<IO, true, false><<<dim3(gx, p.nseg), kLanes, bsm, st>>>(a, mk, mv, mgy, mgk, mgv);
+  // 6. per-channel reduction of the partials
+  wkv_reduce_kernel<<<(unsigned)((C + 127) / 128), 128, 0, st>>>(ws.partial, B * p.nseg, C, w, gtd,
+                                                                  gtf);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "wkv backward launch");
+  return WKV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int wkv_abi_version(void) { return WKV_ABI_VERSION; }
+
+const char* wkv_status_string(int status) {
+  switch (status) {
+    case WKV_OK: return "ok";
+    case WKV_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case WKV_ERR_WORKSPACE_TOO_SMALL: return "workspace too small";
+    case WKV_ERR_CUDA: return "CUDA error";
+    case WKV_ERR_DRIVER: return "CUDA driver (TMA descriptor) error";
+    default: return "unknown status";
+  }
+}
+
+const char* wkv_last_error(void) { return g_last_error; }
+
+int wkv_set_debug_overrides(int force_segments, int force_generic, int force_slow) {
+  g_force_segments.store(force_segments > 0 ? force_segments : 0);
+  g_force_generic.store(force_generic != 0);
+  g_force_slow.store(force_slow != 0);
+  return WKV_OK;
+}
+
+int wkv_plan(int dtype, int64_t B, int64_t T, int64_t C, int* tma, int* segments) {
+  int rc = check_dims(dtype, B, T, C);
+  if (rc) return rc;
+  const Plan p = make_plan(dtype, B, T, C, true);
+  if (tma) *tma = p.tma ? 1 : 0;
+  if (segments) *segments = p.nseg;
+  return WKV_OK;
+}
+
+size_t wkv_forward_workspace_size(int dtype, int64_t B, int64_t T, int64_t C) {
+  if (check_dims(dtype, B, T, C)) return 0;
+  const Plan p = make_plan(dtype, B, T, C, true);
+  return fwd_workspace(p, B, C, nullptr).bytes;
+}
+
+size_t wkv_backward_workspace_size(int dtype, int64_t B, int64_t T, int64_t C) {
+  if (check_dims(dtype, B, T, C)) return 0;
+  const Plan p = make_plan(dtype, B, T, C, true);
+  return bwd_workspace(p, B, T, C, nullptr).bytes;
+}
+
+int wkv_forward(int dtype, const void* key, const void* value, const float* time_decay,
+                const float* time_first, void* y, int64_t B, int64_t T, int64_t C,
+                void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error[0] = '\0';
+  int rc = check_dims(dtype, B, T, C);
+  if (rc) return rc;
+  if (B == 0 || T == 0 || C == 0) return WKV_OK;
+  if (!key || !value || !time_decay || !time_first || !y)
+    return fail(WKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  const bool al = aligned16(key) && aligned16(value) && aligned16(y);
+  const Plan p = make_plan(dtype, B, T, C, al);
+  const FwdWs need = fwd_workspace(p, B, C, workspace);
+  if (need.bytes > 0 && (workspace == nullptr || workspace_bytes < need.bytes))
+    return fail(WKV_ERR_WORKSPACE_TOO_SMALL, "forward needs %zu workspace bytes, got %zu",
+                need.bytes, workspace_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int b = (int)B, t = (int)T, c = (int)C;
+  switch (dtype) {
+    case WKV_DTYPE_F32:
+      return launch_forward<float>(key, value, time_decay, 0, time_first, y, b, t, c, p, need.seg, st);
+    case WKV_DTYPE_BF16:
+      return launch_forward<__nv_bfloat16>(key, value, time_decay, 0, time_first, y, b, t, c, p,
+                                           need.seg, st);
+    default:
+      return launch_forward<__half>(key, value, time_decay, 0, time_first, y, b, t, c, p, need.seg, st);
+  }
+}
+
+int wkv_backward(int dtype, const void* grad_y, const float* w, const float* u, const void* key,
+                 const void* value, void* grad_key, void* grad_value, float* grad_time_decay,
+                 float* grad_time_first, int64_t B, int64_t T, int64_t C, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+  g_last_error[0] = '\0';
+  int rc = check_dims(dtype, B, T, C);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (C > 0 && (B == 0 || T == 0)) {
+    if (!grad_time_decay || !grad_time_first)
+      return fail(WKV_ERR_INVALID_ARGUMENT, "null gradient pointer");
+    cudaError_t e = cudaMemsetAsync(grad_time_decay, 0, C * sizeof(float), st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(grad_time_first, 0, C * sizeof(float), st);
+    return e == cudaSuccess ? WKV_OK : cuda_fail(e, "zeroing time gradients");
+  }
+  if (B == 0 || T == 0 || C == 0) return WKV_OK;
+  if (!grad_y || !w || !u || !key || !value || !grad_key || !grad_value || !grad_time_decay ||
+      !grad_time_first)
+    return fail(WKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  const bool al = aligned16(grad_y) && aligned16(key) && aligned16(value) && aligned16(grad_key) &&
+                  aligned16(grad_value);
+  const Plan p = make_plan(dtype, B, T, C, al);
+  const BwdWs need = bwd_workspace(p, B, T, C, nullptr);
+  if (workspace == nullptr || workspace_bytes < need.bytes)
+    return fail(WKV_ERR_WORKSPACE_TOO_SMALL, "backward needs %zu workspace bytes, got %zu",
+                need.bytes, workspace_bytes);
+  if (!aligned16(workspace))
+    return fail(WKV_ERR_INVALID_ARGUMENT, "workspace must be 16-byte aligned");
+  const BwdWs ws = bwd_workspace(p, B, T, C, workspace);
+  const int b = (int)B, t = (int)T, c = (int)C;
+  switch (dtype) {
+    case WKV_DTYPE_F32:
+      return launch_backward<float>(grad_y, w, u, key, value, grad_key, grad_value,
+                                    grad_time_decay, grad_time_first, b, t, c, p, ws, st);
+    case WKV_DTYPE_BF16:
+      return launch_backward<__nv_bfloat16>(grad_y, w, u, key, value, grad_key, grad_value,
+                                            grad_time_decay, grad_time_first, b, t, c, p, ws, st);
+    default:
+      return launch_backward<__half>(grad_y, w, u, key, value, grad_key, grad_value,
+                                     grad_time_decay, grad_time_first, b, t, c, p, ws, st);
+  }
+}
+
+int wkv_device_error_flags(unsigned* flags, int clear) {
+  g_last_error[0] = '\0';
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  unsigned v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_device_error_flags, sizeof(v));
+  if (e != cudaSuccess) return cuda_fail(e, "reading device error flags");
+  if (flags) *flags = v;
+  if (clear) {
+    const unsigned zero = 0;
+    e = cudaMemcpyToSymbol(g_device_error_flags, &zero, sizeof(zero));
+    if (e != cudaSuccess) return cuda_fail(e, "clearing device error flags");
+  }
+  return WKV_OK;
+}
+
+}  // extern "C"
