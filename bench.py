@@ -1,0 +1,458 @@
+"""WKV fwd+bwd benchmark on B200 (SpikeGPT RWKV-4 time-mix recurrence).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+
+One step = one forward and one backward pass of the WKV op over one batch of
+synthetic config-1 inputs (B=64, T=1024, C=512, bf16 I/O, k/v ~ 4*N(0,1),
+time_decay ~ U(-5,1), time_first ~ U(-1,1), grad_y ~ N(0,1)).
+
+* value: algorithmic bytes per step (16 B/element for bf16: fwd reads k,v and
+  writes y; bwd reads k,v,grad_y and writes grad_k,grad_v) times steps, divided
+  by the device time of the K timed steps, with inputs resident in HBM, through
+  the C ABI (libspikegpt_wkv.so). Inputs are larger than L2 (201 MB of inputs
+  per step, ~470 MB touched), so no L2 flush is inserted.
+* e2e: the same metric through the public torch ops (myelin::wkv_forward_bf16io
+  and myelin::wkv_backward_bf16io) with pinned host buffers: every step copies
+  k, v, grad_y, time_decay, time_first host->device and y, grad_k, grad_v and the
+  two per-channel grads device->host inside the timed region.
+* roofline: the kernel with the largest share of device time, timed per launch
+  with CUDA events on its stream during the timed region.
+* cpu_baseline: the CPU oracle port (oracle/wkv_oracle.c, float32, all host
+  threads) on a bounded sample of the same workload, rank 0 at N=1.
+
+Multi-GPU (torchrun): the batch shards across ranks with no data-path
+collective (every (b, c) lane is independent): each rank runs the config-1
+batch on its own GPU (weak scaling); timing is the max over ranks.
+
+--impl reference times the reference's CPU implementation of the path (the
+oracle port, since the reference is Python and cannot travel) on the same
+config, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "spikegpt-myelin_b200"))
+sys.path.insert(0, str(ROOT))
+
+BYTES_PER_ELEM = {"bf16": 16, "fp16": 16, "fp32": 32}  # fwd 3 tensors + bwd 5 tensors
+WORKLOADS = {
+    "cfg1": dict(B=64, T=1024, C=512, dtype="bf16", kscale=4.0, desc="config 1: B=64 T=1024 C=512 bf16, k/v x4"),
+    "cfg1-fp32": dict(B=64, T=1024, C=512, dtype="fp32", kscale=4.0, desc="config 1 with fp32 I/O"),
+    "cfg2": dict(B=24, T=3072, C=512, dtype="bf16", kscale=4.0, desc="config 2: B=24 T=3072 C=512 bf16, k/v x4"),
+    "cfg2b-1": dict(B=1, T=3072, C=512, dtype="bf16", kscale=4.0, desc="config 2b: B=1 T=3072 C=512 bf16"),
+    "cfg2b-8": dict(B=8, T=3072, C=512, dtype="bf16", kscale=4.0, desc="config 2b: B=8 T=3072 C=512 bf16"),
+}
+METRIC = "WKV fwd+bwd algorithmic HBM throughput"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=("native", "reference"), default="native")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg1")
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--profile", action="store_true", help="device loop only (for ncu): no CPU leg, e2e or clocks")
+    return ap.parse_args()
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        d["source"] = "measured"
+        return d
+    return dict(PEAKS_FALLBACK)
+
+
+def make_inputs(wl: dict, seed: int):
+    """Seeded synthetic inputs with the config's distributions (numpy PCG64)."""
+    rng = np.random.default_rng(seed)
+    b, t, c = wl["B"], wl["T"], wl["C"]
+    k = (rng.standard_normal((b, t, c), dtype=np.float32) * wl["kscale"]).astype(np.float32)
+    v = (rng.standard_normal((b, t, c), dtype=np.float32) * wl["kscale"]).astype(np.float32)
+    td = rng.uniform(-5.0, 1.0, c).astype(np.float32)
+    tf = rng.uniform(-1.0, 1.0, c).astype(np.float32)
+    gy = rng.standard_normal((b, t, c), dtype=np.float32)
+    return k, v, td, tf, gy
+
+
+# ------------------------------------------------------------------ clocks
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples for one GPU, with host timestamps."""
+
+    FIELDS = (
+        "clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, gpu_index: int, period_ms: int = 100):
+        self.samples: list[tuple[float, list[str]]] = []
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(gpu_index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", str(period_ms)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+        except OSError:
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), [x.strip() for x in line.split(",")]))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self, t0: float, t1: float) -> dict:
+        rows = [s for ts, s in self.samples if t0 <= ts <= t1 and len(s) >= 8]
+        if not rows:  # very short region: take the samples nearest to it
+            rows = [s for ts, s in self.samples if t0 - 0.3 <= ts <= t1 + 0.3 and len(s) >= 8]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        sm = [num(r[0]) for r in rows if num(r[0]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[4:8], strict=False) if v.lower().startswith("active")})
+        power = [num(r[2]) for r in rows if num(r[2]) is not None]
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": num(rows[0][1]),
+            "reasons": reasons,
+            "power_w_max": max(power) if power else None,
+            "samples": len(rows),
+        }
+
+
+# -------------------------------------------------------------- CPU legs
+
+
+def cpu_oracle_throughput(wl: dict, *, seconds: float = 10.0, steps: int | None = None, warmup: int = 0):
+    """Time the float32 CPU oracle (oracle/wkv_oracle.c) fwd+bwd on one batch
+    row of the workload per step with all host threads."""
+    from oracle import oracle
+
+    k, v, td, tf, gy = make_inputs(dict(wl, B=1), seed=0)
+    threads = os.cpu_count() or 1
+    w = -np.exp(td.astype(np.float64)).astype(np.float32)
+    run = lambda: (oracle.forward(k, v, td, tf, dtype=np.float32, threads=threads),  # noqa: E731
+                   oracle.backward(gy, w, tf, k, v, dtype=np.float32, threads=threads))
+    for _ in range(warmup):
+        run()
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        run()
+        n += 1
+        el = time.perf_counter() - t0
+        if (steps is not None and n >= steps) or (steps is None and el >= seconds):
+            break
+    elems = wl["T"] * wl["C"] * n
+    value = BYTES_PER_ELEM[wl["dtype"]] * elems / el / 1e9
+    return {
+        "value": value,
+        "unit": "GB/s",
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{n} x (1 of {wl['B']} batch rows: T={wl['T']} C={wl['C']}), float32, {el:.1f} s",
+        "host_cpus": os.cpu_count(),
+    }
+
+
+# ------------------------------------------------------------- native arm
+
+
+def run_native(args, wl):
+    import torch
+    import torch.distributed as dist
+
+    import spikegpt_b200
+    from spikegpt_b200 import _capi
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    tdt = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}[wl["dtype"]]
+    code = {"bf16": _capi.DTYPE_BF16, "fp16": _capi.DTYPE_F16, "fp32": _capi.DTYPE_F32}[wl["dtype"]]
+    b, t, c = wl["B"], wl["T"], wl["C"]
+    k_np, v_np, td_np, tf_np, gy_np = make_inputs(wl, seed=rank)
+    k = torch.as_tensor(k_np).to(dev, tdt)
+    v = torch.as_tensor(v_np).to(dev, tdt)
+    gy = torch.as_tensor(gy_np).to(dev, tdt)
+    td = torch.as_tensor(td_np).to(dev)
+    tf = torch.as_tensor(tf_np).to(dev)
+    w = -torch.exp(td)
+    y = torch.empty_like(k)
+    gk, gv = torch.empty_like(k), torch.empty_like(k)
+    gtd, gtf = torch.empty_like(td), torch.empty_like(td)
+    lib = _capi.lib()
+    fws_n = int(lib.wkv_forward_workspace_size(code, b, t, c))
+    bws_n = int(lib.wkv_backward_workspace_size(code, b, t, c))
+    fws = torch.empty(max(fws_n, 1), dtype=torch.uint8, device=dev)
+    bws = torch.empty(max(bws_n, 1), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+
+    def step():
+        _capi.check(lib.wkv_forward(code, k.data_ptr(), v.data_ptr(), td.data_ptr(), tf.data_ptr(), y.data_ptr(),
+                                    b, t, c, fws.data_ptr(), fws_n, sp), "wkv_forward")
+        _capi.check(lib.wkv_backward(code, gy.data_ptr(), w.data_ptr(), tf.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                     gk.data_ptr(), gv.data_ptr(), gtd.data_ptr(), gtf.data_ptr(),
+                                     b, t, c, bws.data_ptr(), bws_n, sp), "wkv_backward")
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    sampler = None if args.profile else ClockSampler(local)
+    time.sleep(0.3 if sampler else 0)
+    _capi.timing_collect()
+    _capi.timing_enable(True)
+    launches0 = sum(_capi.launch_counts().values())
+    barrier()
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    host0 = time.time()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    host1 = time.time()
+    barrier()
+    _capi.timing_enable(False)
+    launches = sum(_capi.launch_counts().values()) - launches0
+    per_kernel = _capi.timing_collect()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        tmax = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        ms = float(tmax.item())
+    if sampler:
+        time.sleep(0.25)
+        sampler.stop()
+    clocks = sampler.summary(host0, host1) if sampler else None
+
+    elems = b * t * c
+    step_bytes = BYTES_PER_ELEM[wl["dtype"]] * elems
+    value = step_bytes * args.steps * world / (ms * 1e-3) / 1e9
+
+    # roofline of the dominant kernel (largest share of device time)
+    io_bytes = BYTES_PER_ELEM[wl["dtype"]] // 8  # bytes of one element of one tensor
+    alg_per_launch = {
+        "wkv_fwd_kernel<y>": 3 * io_bytes * elems,       # read k, v; write y
+        "wkv_bwd_kernel<grad>": 5 * io_bytes * elems,    # read k, v, gy; write gk, gv
+        "wkv_fwd_kernel<state>": 0,                      # recompute: no algorithmic bytes
+    }
+    kernels = {n: {"ms_per_launch": tot / cnt, "launches": cnt, "share": None}
+               for n, (tot, cnt) in per_kernel.items() if cnt > 0}
+    total_kernel_ms = sum(tot for tot, cnt in per_kernel.values())
+    for n, (tot, cnt) in per_kernel.items():
+        if cnt:
+            kernels[n]["share"] = tot / total_kernel_ms
+    dom = max(kernels, key=lambda n: kernels[n]["ms_per_launch"] * kernels[n]["launches"])
+    pk = peaks()
+    hbm = float(pk.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+    achieved = alg_per_launch.get(dom, 0) / (kernels[dom]["ms_per_launch"] * 1e-3) / 1e9
+    roofline = {
+        "kernel": dom,
+        "bound": "hbm",
+        "achieved": achieved,
+        "peak": hbm,
+        "unit": "GB/s",
+        "frac": achieved / hbm,
+        "peak_source": f"{pk.get('source')} (MEASURED_PEAKS.json hbm_gbs)" if pk.get("source") == "measured" else "fallback 6.65 TB/s",
+        "alg_bytes_per_launch": alg_per_launch.get(dom, 0),
+        "traffic": ncu_traffic(dom, args.workload),
+    }
+
+    result = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": wl["dtype"],
+        "data": "synthetic (seeded numpy PCG64; config distributions)",
+        "config": {
+            "workload": wl["desc"],
+            "B_per_gpu": b,
+            "T": t,
+            "C": c,
+            "global_batch": b * world,
+            "parallelism": f"{world} batch-sharded replica(s), no data-path collective",
+            "l2": "inputs larger than L2 (201 MB of k,v,grad_y read per step); no flush",
+            "frac_of_hbm_peak": value / world / hbm,
+            "plan": dict(zip(("tma", "segments"), _capi.plan(code, b, t, c), strict=True)),
+        },
+        "roofline": roofline,
+        "kernels": kernels,
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+    }
+    if not args.profile:
+        result["e2e"] = run_e2e(args, wl, dev, k_np, v_np, td_np, tf_np, gy_np, tdt, world)
+        if world == 1 and rank == 0:
+            result["cpu_baseline"] = cpu_oracle_throughput(wl, seconds=10.0)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def ncu_traffic(kernel: str, workload: str):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary for the
+    workload (profiles/*.md line 'dram_bytes_per_launch[<kernel>] = N'), else None."""
+    pat = re.compile(r"dram_bytes_per_launch\[" + re.escape(kernel) + r"\]\[" + re.escape(workload) + r"\]\s*=\s*([0-9.eE+]+)")
+    for p in sorted((ROOT / "profiles").glob("*.md")):
+        m = pat.search(p.read_text())
+        if m:
+            return float(m.group(1))
+    return None
+
+
+def run_e2e(args, wl, dev, k_np, v_np, td_np, tf_np, gy_np, tdt, world):
+    """The metric through the public ops with host buffers (pinned)."""
+    import torch
+    import torch.distributed as dist
+
+    import spikegpt_b200  # noqa: F401
+
+    def pin(x, dt):
+        return torch.as_tensor(x).to(dt).pin_memory()
+
+    hk, hv, hgy = pin(k_np, tdt), pin(v_np, tdt), pin(gy_np, tdt)
+    htd, htf = pin(td_np, torch.float32), pin(tf_np, torch.float32)
+    hy, hgk, hgv = (torch.empty_like(hk).pin_memory() for _ in range(3))
+    hgtd, hgtf = torch.empty_like(htd).pin_memory(), torch.empty_like(htf).pin_memory()
+    h2d = sum(x.numel() * x.element_size() for x in (hk, hv, hgy, htd, htf))
+    d2h = sum(x.numel() * x.element_size() for x in (hy, hgk, hgv, hgtd, hgtf))
+
+    def step():
+        k = hk.to(dev, non_blocking=True)
+        v = hv.to(dev, non_blocking=True)
+        gy = hgy.to(dev, non_blocking=True)
+        td = htd.to(dev, non_blocking=True)
+        tf = htf.to(dev, non_blocking=True)
+        y = torch.ops.myelin.wkv_forward_bf16io(k, v, td, tf)
+        gk, gv, gtd, gtf = torch.ops.myelin.wkv_backward_bf16io(gy, -torch.exp(td), tf, k, v)
+        hy.copy_(y, non_blocking=True)
+        hgk.copy_(gk, non_blocking=True)
+        hgv.copy_(gv, non_blocking=True)
+        hgtd.copy_(gtd, non_blocking=True)
+        hgtf.copy_(gtf, non_blocking=True)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.e2e_steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    elems = wl["B"] * wl["T"] * wl["C"]
+    value = BYTES_PER_ELEM[wl["dtype"]] * elems * args.e2e_steps * world / (ms * 1e-3) / 1e9
+    return {"value": value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "steps": args.e2e_steps, "ms_per_step": ms / args.e2e_steps,
+            "path": "torch.ops.myelin.wkv_forward_bf16io / wkv_backward_bf16io, pinned host buffers"}
+
+
+# ----------------------------------------------------------- reference arm
+
+
+def run_reference(args, wl):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    base = cpu_oracle_throughput(wl, steps=args.steps, warmup=args.warmup)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    out = {
+        "metric": METRIC,
+        "value": base["value"],
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": wl["dtype"],
+        "data": "synthetic (seeded numpy PCG64; config distributions)",
+        "config": {"workload": wl["desc"], "B_per_gpu": wl["B"], "T": wl["T"], "C": wl["C"]},
+        "impl": "reference",
+        "cpu_baseline": base,
+        "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference is pure Python (its only GPU code is Triton); this arm times the C "
+                "restatement of its WKV arithmetic (oracle/wkv_oracle.c), float32, on the host cores",
+    }
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    args = parse_args()
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, wl)
+    else:
+        run_native(args, wl)
+
+
+if __name__ == "__main__":
+    main()

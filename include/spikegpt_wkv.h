@@ -113,6 +113,22 @@ WKV_API int wkv_plan(int dtype, int64_t B, int64_t T, int64_t C, int* tma, int* 
 WKV_API int wkv_set_debug_overrides(int force_segments, int force_generic, int force_slow);
 
 /*
+ * Launch accounting and per-kernel device timing (no reference counterpart; the
+ * benchmark uses them for its launch count and roofline figures).
+ * Kernel kinds 0 .. wkv_kernel_kinds()-1, named by wkv_kernel_name().
+ * wkv_launch_counts: cumulative launches per kind since the library loaded.
+ * wkv_timing_enable(1): bracket every later launch with CUDA events on its stream.
+ * wkv_timing_collect: waits for the recorded events and returns, per kind, the
+ * summed device milliseconds and the number of timed launches since the last
+ * collect.
+ */
+WKV_API int wkv_kernel_kinds(void);
+WKV_API const char* wkv_kernel_name(int kind);
+WKV_API int wkv_launch_counts(long long* counts, int n);
+WKV_API int wkv_timing_enable(int on);
+WKV_API int wkv_timing_collect(double* total_ms, long long* launches, int n);
+
+/*
  * Reads (and with clear != 0 resets) the sticky device-side error flags of the
  * current device; synchronises the device. Returns a status code.
  */

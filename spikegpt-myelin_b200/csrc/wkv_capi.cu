@@ -13,6 +13,7 @@
 #include <cstring>
 #include <mutex>
 #include <type_traits>
+#include <vector>
 
 #include "spikegpt_wkv.h"
 #include "wkv_kernels.cuh"
@@ -27,6 +28,56 @@ std::atomic<int> g_force_generic{0};
 std::atomic<int> g_force_slow{0};
 
 __device__ unsigned g_device_error_flags = 0;
+
+// ------------------------------------------------ launch accounting / timing
+//
+// Every kernel launch goes through launch(): it bumps a per-kind counter and,
+// while timing is enabled, brackets the launch with CUDA events recorded on the
+// launch stream, so per-kernel device time can be read back by the caller.
+
+enum Kind { K_FWD_Y, K_FWD_STATE, K_BWD_GRAD, K_BWD_ADJ, K_CARRY_FWD, K_CARRY_ADJ, K_COUNT };
+const char* const kKindNames[K_COUNT] = {
+    "wkv_fwd_kernel<y>",      "wkv_fwd_kernel<state>", "wkv_bwd_kernel<grad>",
+    "wkv_bwd_kernel<adjoint>", "wkv_carry_fwd_kernel",  "wkv_carry_adj_kernel"};
+
+std::atomic<long long> g_launches[K_COUNT];
+std::atomic<bool> g_timing{false};
+std::mutex g_timing_mu;
+struct TimedLaunch {
+  int kind;
+  cudaEvent_t start, stop;
+};
+std::vector<TimedLaunch> g_timed;
+std::vector<cudaEvent_t> g_event_pool;
+
+cudaEvent_t pooled_event() {
+  std::lock_guard<std::mutex> lk(g_timing_mu);
+  if (!g_event_pool.empty()) {
+    cudaEvent_t e = g_event_pool.back();
+    g_event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+  return e;
+}
+
+template <class F>
+void launch(int kind, cudaStream_t st, F&& f) {
+  g_launches[kind].fetch_add(1, std::memory_order_relaxed);
+  if (!g_timing.load(std::memory_order_relaxed)) {
+    f();
+    return;
+  }
+  cudaEvent_t a = pooled_event(), b = pooled_event();
+  if (a) cudaEventRecord(a, st);
+  f();
+  if (b) cudaEventRecord(b, st);
+  if (a && b) {
+    std::lock_guard<std::mutex> lk(g_timing_mu);
+    g_timed.push_back(TimedLaunch{kind, a, b});
+  }
+}
 
 int fail(int status, const char* fmt, ...) {
   va_list ap;
@@ -118,6 +169,7 @@ struct BwdWs {
   float* seg;
   float* adj;
   float* partial;
+  unsigned* tickets;
   size_t bytes;
 };
 BwdWs bwd_workspace(const Plan& p, int64_t B, int64_t T, int64_t C, void* base) {
@@ -137,7 +189,11 @@ BwdWs bwd_workspace(const Plan& p, int64_t B, int64_t T, int64_t C, void* base) 
     w.adj = take((size_t)B * p.nseg * 3 * C * sizeof(float));
   }
   w.partial = take((size_t)B * p.nseg * 2 * C * sizeof(float));
-  if (!base) w.ckpt = w.seg = w.adj = w.partial = nullptr;
+  w.tickets = reinterpret_cast<unsigned*>(take((size_t)((C + kLanes - 1) / kLanes) * sizeof(unsigned)));
+  if (!base) {
+    w.ckpt = w.seg = w.adj = w.partial = nullptr;
+    w.tickets = nullptr;
+  }
   return w;
 }
 
@@ -252,20 +308,26 @@ int launch_forward(const void* k, const void* v, const float* decay, int decay_i
     FwdArgs s = a;
     s.seg_end = seg;
     const size_t sm = fwd_smem_bytes<IO>(false);
-    if (p.tma)
-      wkv_fwd_kernel<IO, false, true><<<dim3(gx, p.nseg - 1), kLanes, sm, st>>>(s, mk, mv, my);
-    else
-      wkv_fwd_kernel<IO, false, false><<<dim3(gx, p.nseg - 1), kLanes, sm, st>>>(s, mk, mv, my);
+    launch(K_FWD_STATE, st, [&] {
+      if (p.tma)
+        wkv_fwd_kernel<IO, false, true><<<dim3(gx, p.nseg - 1), kLanes, sm, st>>>(s, mk, mv, my);
+      else
+        wkv_fwd_kernel<IO, false, false><<<dim3(gx, p.nseg - 1), kLanes, sm, st>>>(s, mk, mv, my);
+    });
     const int64_t lanes = (int64_t)B * C;
-    wkv_carry_fwd_kernel<<<(unsigned)((lanes + 127) / 128), 128, 0, st>>>(seg, decay, decay_is_w, B,
-                                                                          T, C, p.nseg, p.seg_len);
+    launch(K_CARRY_FWD, st, [&] {
+      wkv_carry_fwd_kernel<<<(unsigned)((lanes + 127) / 128), 128, 0, st>>>(
+          seg, decay, decay_is_w, B, T, C, p.nseg, p.seg_len);
+    });
     a.seg_start = seg;
   }
   const size_t sm = fwd_smem_bytes<IO>(true);
-  if (p.tma)
-    wkv_fwd_kernel<IO, true, true><<<dim3(gx, p.nseg), kLanes, sm, st>>>(a, mk, mv, my);
-  else
-    wkv_fwd_kernel<IO, true, false><<<dim3(gx, p.nseg), kLanes, sm, st>>>(a, mk, mv, my);
+  launch(K_FWD_Y, st, [&] {
+    if (p.tma)
+      wkv_fwd_kernel<IO, true, true><<<dim3(gx, p.nseg), kLanes, sm, st>>>(a, mk, mv, my);
+    else
+      wkv_fwd_kernel<IO, true, false><<<dim3(gx, p.nseg), kLanes, sm, st>>>(a, mk, mv, my);
+  });
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "wkv forward launch");
   return WKV_OK;
@@ -311,13 +373,17 @@ int launch_backward(const void* gy, const float* w, const float* u, const void* 
   f.nsub = nsub;
   f.ckpt = ws.ckpt;
   f.seg_end = p.nseg > 1 ? ws.seg : nullptr;
+  f.zero_tickets = ws.tickets;
+  f.nzero = ncblk;
   f.force_slow = force_slow;
   f.err = err;
   const size_t fsm = fwd_smem_bytes<IO>(false);
-  if (p.tma)
-    wkv_fwd_kernel<IO, false, true><<<dim3(gx, p.nseg), kLanes, fsm, st>>>(f, mk, mv, none);
-  else
-    wkv_fwd_kernel<IO, false, false><<<dim3(gx, p.nseg), kLanes, fsm, st>>>(f, mk, mv, none);
+  launch(K_FWD_STATE, st, [&] {
+    if (p.tma)
+      wkv_fwd_kernel<IO, false, true><<<dim3(gx, p.nseg), kLanes, fsm, st>>>(f, mk, mv, none);
+    else
+      wkv_fwd_kernel<IO, false, false><<<dim3(gx, p.nseg), kLanes, fsm, st>>>(f, mk, mv, none);
+  });
 
   BwdArgs a{};
   a.k = k;
@@ -342,32 +408,43 @@ int launch_backward(const void* gy, const float* w, const float* u, const void* 
   if (p.nseg > 1) {
     // 2. segment start states; 3. adjoint summaries of segments 1..nseg-1;
     // 4. adjoint at every segment end
-    wkv_carry_fwd_kernel<<<cgrid, 128, 0, st>>>(ws.seg, w, 1, B, T, C, p.nseg, p.seg_len);
+    launch(K_CARRY_FWD, st, [&] {
+      wkv_carry_fwd_kernel<<<cgrid, 128, 0, st>>>(ws.seg, w, 1, B, T, C, p.nseg, p.seg_len);
+    });
     BwdArgs s = a;
     s.seg_start = ws.seg;
     s.seg_base = 1;
     s.adj_out = ws.adj;
     const size_t ssm = bwd_smem_bytes<IO>(false);
-    if (p.tma)
-      wkv_bwd_kernel<IO, false, true>
-          <<<dim3(gx, p.nseg - 1), kLanes, ssm, st>>>(s, mk, mv, mgy, none, none);
-    else
-      wkv_bwd_kernel<IO, false, false>
-          <<<dim3(gx, p.nseg - 1), kLanes, ssm, st>>>(s, mk, mv, mgy, none, none);
-    wkv_carry_adj_kernel<<<cgrid, 128, 0, st>>>(ws.adj, w, B, T, C, p.nseg, p.seg_len);
+    launch(K_BWD_ADJ, st, [&] {
+      if (p.tma)
+        wkv_bwd_kernel<IO, false, true>
+            <<<dim3(gx, p.nseg - 1), kLanes, ssm, st>>>(s, mk, mv, mgy, none, none);
+      else
+        wkv_bwd_kernel<IO, false, false>
+            <<<dim3(gx, p.nseg - 1), kLanes, ssm, st>>>(s, mk, mv, mgy, none, none);
+    });
+    launch(K_CARRY_ADJ, st, [&] {
+      wkv_carry_adj_kernel<<<cgrid, 128, 0, st>>>(ws.adj, w, B, T, C, p.nseg, p.seg_len);
+    });
     a.seg_start = ws.seg;
     a.adj_in = ws.adj;
   }
-  // 5. reverse sweep writing grad_key / grad_value and per-lane partials
+  // 5. reverse sweep writing grad_key / grad_value and per-lane partials; the
+  // last CTA of each column block reduces the partials into the time gradients
   a.partial = ws.partial;
+  a.tickets = ws.tickets;
+  a.gtd = gtd;
+  a.gtf = gtf;
   const size_t bsm = bwd_smem_bytes<IO>(true);
-  if (p.tma)
-    wkv_bwd_kernel<IO, true, true><<<dim3(gx, p.nseg), kLanes, bsm, st>>>(a, mk, mv, mgy, mgk, mgv);
-  else
-    wkv_bwd_kernel<IO, true, false><<<dim3(gx, p.nseg), kLanes, bsm, st>>>(a, mk, mv, mgy, mgk, mgv);
-  // 6. per-channel reduction of the partials
-  wkv_reduce_kernel<<<(unsigned)((C + 127) / 128), 128, 0, st>>>(ws.partial, B * p.nseg, C, w, gtd,
-                                                                  gtf);
+  launch(K_BWD_GRAD, st, [&] {
+    if (p.tma)
+      wkv_bwd_kernel<IO, true, true>
+          <<<dim3(gx, p.nseg), kLanes, bsm, st>>>(a, mk, mv, mgy, mgk, mgv);
+    else
+      wkv_bwd_kernel<IO, true, false>
+          <<<dim3(gx, p.nseg), kLanes, bsm, st>>>(a, mk, mv, mgy, mgk, mgv);
+  });
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "wkv backward launch");
   return WKV_OK;
@@ -489,6 +566,53 @@ int wkv_backward(int dtype, const void* grad_y, const float* w, const float* u, 
       return launch_backward<__half>(grad_y, w, u, key, value, grad_key, grad_value,
                                      grad_time_decay, grad_time_first, b, t, c, p, ws, st);
   }
+}
+
+int wkv_kernel_kinds(void) { return K_COUNT; }
+
+const char* wkv_kernel_name(int kind) {
+  return (kind >= 0 && kind < K_COUNT) ? kKindNames[kind] : "";
+}
+
+int wkv_launch_counts(long long* counts, int n) {
+  if (!counts || n < 0) return fail(WKV_ERR_INVALID_ARGUMENT, "null counts");
+  for (int i = 0; i < n && i < K_COUNT; ++i) counts[i] = g_launches[i].load();
+  return WKV_OK;
+}
+
+int wkv_timing_enable(int on) {
+  g_timing.store(on != 0);
+  return WKV_OK;
+}
+
+int wkv_timing_collect(double* total_ms, long long* launches, int n) {
+  g_last_error[0] = '\0';
+  std::vector<TimedLaunch> recs;
+  {
+    std::lock_guard<std::mutex> lk(g_timing_mu);
+    recs.swap(g_timed);
+  }
+  for (int i = 0; i < n; ++i) {
+    if (total_ms) total_ms[i] = 0.0;
+    if (launches) launches[i] = 0;
+  }
+  int rc = WKV_OK;
+  for (const TimedLaunch& r : recs) {
+    float ms = 0.f;
+    cudaError_t e = cudaEventSynchronize(r.stop);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, r.start, r.stop);
+    if (e != cudaSuccess && rc == WKV_OK) rc = cuda_fail(e, "reading kernel timing events");
+    if (r.kind < n) {
+      if (total_ms) total_ms[r.kind] += ms;
+      if (launches) launches[r.kind] += 1;
+    }
+  }
+  std::lock_guard<std::mutex> lk(g_timing_mu);
+  for (const TimedLaunch& r : recs) {
+    g_event_pool.push_back(r.start);
+    g_event_pool.push_back(r.stop);
+  }
+  return rc;
 }
 
 int wkv_device_error_flags(unsigned* flags, int clear) {

@@ -236,38 +236,80 @@ __device__ __forceinline__ bool fast_ok(const Fwd& st, float kmax, float kmin, i
          (decayed >= 0x1p-60f || low >= -kMargin);
 }
 
+// Masked tree reductions over a sub-chunk held in registers.
+template <bool kTail>
+__device__ __forceinline__ void minmax16(const float (&x)[kSub], int L, float& mx, float& mn) {
+  float a[kSub / 2], b[kSub / 2];
+#pragma unroll
+  for (int i = 0; i < kSub / 2; ++i) {
+    const bool i0 = !kTail || i < L, i1 = !kTail || i + kSub / 2 < L;
+    const float x0 = x[i], x1 = x[i + kSub / 2];
+    a[i] = fmaxf(i0 ? x0 : -INFINITY, i1 ? x1 : -INFINITY);
+    b[i] = fminf(i0 ? x0 : INFINITY, i1 ? x1 : INFINITY);
+  }
+#pragma unroll
+  for (int w = kSub / 4; w > 0; w /= 2) {
+#pragma unroll
+    for (int i = 0; i < w; ++i) {
+      a[i] = fmaxf(a[i], a[i + w]);
+      b[i] = fminf(b[i], b[i + w]);
+    }
+  }
+  mx = a[0];
+  mn = b[0];
+}
+
+template <bool kTail>
+__device__ __forceinline__ float absmax16(const float (&x)[kSub], int L) {
+  float a[kSub / 2];
+#pragma unroll
+  for (int i = 0; i < kSub / 2; ++i) {
+    const bool i0 = !kTail || i < L, i1 = !kTail || i + kSub / 2 < L;
+    a[i] = fmaxf(i0 ? fabsf(x[i]) : 0.f, i1 ? fabsf(x[i + kSub / 2]) : 0.f);
+  }
+#pragma unroll
+  for (int w = kSub / 4; w > 0; w /= 2) {
+#pragma unroll
+    for (int i = 0; i < w; ++i) a[i] = fmaxf(a[i], a[i + w]);
+  }
+  return a[0];
+}
+
+// Loads a sub-chunk column (kSub rows, stride kLanes) into registers. Rows past
+// L inside the staged tile are zero-filled or stale; they are masked by callers.
+template <typename T>
+__device__ __forceinline__ void load16(float (&r)[kSub], const T* src) {
+#pragma unroll
+  for (int i = 0; i < kSub; ++i) r[i] = IOType<T>::ld(src[i * kLanes]);
+}
+
 // ------------------------------------------------------ forward sub-chunk
 //
 // Advances st over L (<= kSub) steps whose k/v sit in shared memory at
-// ks[i*kLanes], vs[i*kLanes]; with kY writes y to ys[i*kLanes].
+// ks[i*kLanes], vs[i*kLanes]; with kY writes y to ys[i*kLanes]. Inputs are
+// staged into registers first and outputs written last, so the 16 steps are
+// free to overlap (the only true dependency is the p/q recurrence).
 template <typename T, bool kTail, bool kY>
 __device__ __forceinline__ void fwd_sub(Fwd& st, const T* ks, const T* vs, T* ys, int L,
                                         const Lane& lc, bool force_slow) {
   using io = IOType<T>;
-  float kr[kSub];
-  float kmax = -INFINITY, kmin = INFINITY;
-#pragma unroll
-  for (int i = 0; i < kSub; ++i) {
-    if (!kTail || i < L) {
-      kr[i] = io::ld(ks[i * kLanes]);
-      kmax = fmaxf(kmax, kr[i]);
-      kmin = fminf(kmin, kr[i]);
-    }
-  }
+  float kr[kSub], vr[kSub], yr[kSub];
+  load16(kr, ks);
+  load16(vr, vs);
+  float kmax, kmin;
+  minmax16<kTail>(kr, L, kmax, kmin);
   float s, p, q;
   const bool ok = fast_ok(st, kmax, kmin, kTail ? L : kSub, lc, s, p, q) && !force_slow;
   if (__all_sync(kFull, ok)) {
 #pragma unroll
     for (int i = 0; i < kSub; ++i) {
       if (kTail && i >= L) break;
-      const float v = io::ld(vs[i * kLanes]);
       const float ek = ex2(fmaf(kr[i], kL2E, -s));
       if (kY) {
         const float eb = ek * lc.eu;
-        const float rd = rcp(q + eb);
-        ys[i * kLanes] = io::st(fmaf(eb, v, p) * rd);
+        yr[i] = fmaf(eb, vr[i], p) * rcp(q + eb);
       }
-      p = fmaf(lc.ew, p, ek * v);
+      p = fmaf(lc.ew, p, ek * vr[i]);
       q = fmaf(lc.ew, q, ek);
     }
     st = Fwd{s, p, q};
@@ -275,19 +317,23 @@ __device__ __forceinline__ void fwd_sub(Fwd& st, const T* ks, const T* vs, T* ys
     float o = st.S;
     p = st.p;
     q = st.q;
-#pragma unroll 1
-    for (int i = 0; i < L; ++i) {
-      const float k = io::ld(ks[i * kLanes]);
-      const float v = io::ld(vs[i * kLanes]);
+#pragma unroll
+    for (int i = 0; i < kSub; ++i) {
+      if (kTail && i >= L) break;
       if (kY) {  // reference wkv_triton.py:49-52
-        const float uk = lc.u2 + k * kL2E;
+        const float uk = lc.u2 + kr[i] * kL2E;
         const float no = fmaxf(o, uk);
         const float a = ex2(o - no), b = ex2(uk - no);
-        ys[i * kLanes] = io::st(fmaf(a, p, b * v) * rcp(fmaf(a, q, b)));
+        yr[i] = fmaf(a, p, b * vr[i]) * rcp(fmaf(a, q, b));
       }
-      slow_update(o, p, q, k, v, lc);
+      slow_update(o, p, q, kr[i], vr[i], lc);
     }
     st = Fwd{o, p, q};
+  }
+  if (kY) {
+#pragma unroll
+    for (int i = 0; i < kSub; ++i)
+      if (!kTail || i < L) ys[i * kLanes] = io::st(yr[i]);
   }
 }
 
@@ -302,18 +348,13 @@ __device__ __forceinline__ void bwd_sub(const Fwd& st0, Adj& adj, const T* ks, c
                                         const T* gys, T* gks, T* gvs, int L, const Lane& lc,
                                         float& gwacc, float& gu, bool force_slow) {
   using io = IOType<T>;
-  float kr[kSub], gyv[kSub];
-  float kmax = -INFINITY, kmin = INFINITY, gymax = 0.f;
-#pragma unroll
-  for (int i = 0; i < kSub; ++i) {
-    if (!kTail || i < L) {
-      kr[i] = io::ld(ks[i * kLanes]);
-      gyv[i] = io::ld(gys[i * kLanes]);
-      kmax = fmaxf(kmax, kr[i]);
-      kmin = fminf(kmin, kr[i]);
-      gymax = fmaxf(gymax, fabsf(gyv[i]));
-    }
-  }
+  float kr[kSub], vr[kSub], gr[kSub];
+  load16(kr, ks);
+  load16(vr, vs);
+  load16(gr, gys);
+  float kmax, kmin;
+  minmax16<kTail>(kr, L, kmax, kmin);
+  const float gymax = absmax16<kTail>(gr, L);
   float s, p, q;
   bool ok = fast_ok(st0, kmax, kmin, kTail ? L : kSub, lc, s, p, q) && !force_slow;
   // Adjoint rescaled to the sub-chunk scale: dL/dP = 2^{-s} gp.
@@ -326,23 +367,22 @@ __device__ __forceinline__ void bwd_sub(const Fwd& st0, Adj& adj, const T* ks, c
 #pragma unroll
     for (int i = 0; i < kSub; ++i) {
       if (kTail && i >= L) break;
-      const float v = io::ld(vs[i * kLanes]);
       const float ek = ex2(fmaf(kr[i], kL2E, -s));
       const float eb = ek * lc.eu;
       const float rd = rcp(q + eb);
-      ry[i] = fmaf(eb, v, p) * rd;
-      rg[i] = gyv[i] * rd;  // gy * 2^s / D_t
+      ry[i] = fmaf(eb, vr[i], p) * rd;
+      rg[i] = gr[i] * rd;  // gy * 2^s / D_t
       re[i] = ek;
       rp[i] = p;
       rq[i] = q;
-      p = fmaf(lc.ew, p, ek * v);
+      p = fmaf(lc.ew, p, ek * vr[i]);
       q = fmaf(lc.ew, q, ek);
     }
     // reverse sweep
 #pragma unroll
     for (int i = kSub - 1; i >= 0; --i) {
       if (kTail && i >= L) continue;
-      const float v = io::ld(vs[i * kLanes]);
+      const float v = vr[i];
       const float a = rg[i] * re[i] * lc.eu;  // gy e^{u+k} / D
       const float av = a * (v - ry[i]);
       gu += av;

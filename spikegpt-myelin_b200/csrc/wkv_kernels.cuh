@@ -19,11 +19,12 @@
 //                                the segment-end summary
 //   wkv_bwd_kernel<T, kOut>      reverse sweep over sub-chunks with forward
 //                                recompute from checkpoints (reference
-//                                wkv_triton.py:60-142); kOut=false only
-//                                produces the segment's adjoint summary
+//                                wkv_triton.py:60-142); its last CTA per
+//                                column block reduces grad_time_decay/first;
+//                                kOut=false only produces the segment's
+//                                adjoint summary
 //   wkv_carry_fwd_kernel         segment summaries -> segment start states
 //   wkv_carry_adj_kernel         adjoint summaries -> adjoint at segment ends
-//   wkv_reduce_kernel            per-lane partials -> grad_time_decay/first
 #pragma once
 
 #include "wkv_device.cuh"
@@ -63,6 +64,8 @@ struct FwdArgs {
   float* ckpt;             // [B][nsub][3][C] states at sub-chunk starts, or null
   const float* seg_start;  // [B][nseg][3][C] segment start states, or null (zero state)
   float* seg_end;          // [B][nseg][3][C] segment end states, or null
+  unsigned* zero_tickets;  // counters the first CTA resets for a later wkv_bwd_kernel, or null
+  int nzero;
   int force_slow;
   unsigned* err;
 };
@@ -82,6 +85,9 @@ struct BwdArgs {
   const float* adj_in;     // [B][nseg][3][C] adjoint at segment ends, or null (zero)
   float* adj_out;          // [B][nseg][3][C] adjoint at segment starts, or null
   float* partial;          // [B][nseg][2][C] (gwacc, gu) per lane-segment, or null
+  unsigned* tickets;       // [ncblk] arrival counters (zeroed beforehand), or null
+  float* gtd;              // [C] grad_time_decay, written by the last CTA of a column block
+  float* gtf;              // [C] grad_time_first
   int force_slow;
   unsigned* err;
 };
@@ -154,6 +160,9 @@ __global__ void __launch_bounds__(kLanes)
   const int t_end = min(a.T, t_begin + a.seg_len);
   const int ntiles = (t_end - t_begin + kTile - 1) / kTile;
   const bool force_slow = a.force_slow != 0;
+
+  if (a.zero_tickets != nullptr && blockIdx.x == 0 && blockIdx.y == 0)
+    for (int i = lane; i < a.nzero; i += kLanes) a.zero_tickets[i] = 0u;
 
   Fwd st = fwd_identity();
   if (a.seg_start != nullptr && cval) st = load_fwd(a.seg_start, (size_t)b * a.nseg + seg, a.C, c);
@@ -271,6 +280,11 @@ __global__ void __launch_bounds__(kLanes)
   Fwd segst = fwd_identity();
   if (a.seg_start != nullptr && cval) segst = load_fwd(a.seg_start, lseg, a.C, c);
   float gwacc = 0.f, gu = 0.f;
+  // Checkpoints are loaded one sub-chunk ahead of their use (sub-chunks are
+  // visited last to first, kSub steps apart).
+  const int t_last = t_begin + ((t_end - t_begin - 1) / kSub) * kSub;
+  Fwd pend = fwd_identity();
+  if (cval) pend = load_fwd(a.ckpt, (size_t)b * a.nsub + t_last / kSub, a.C, c);
 
   // Tiles are visited last to first; the jj-th visited tile is j = ntiles-1-jj.
   auto issue = [&](int jj) {
@@ -333,8 +347,8 @@ __global__ void __launch_bounds__(kLanes)
       if (r0 >= rows) continue;
       const int L = min(kSub, rows - r0);
       const int t = t0 + r0;
-      Fwd st = fwd_identity();
-      if (cval) st = load_fwd(a.ckpt, (size_t)b * a.nsub + t / kSub, a.C, c);
+      Fwd st = pend;
+      if (cval && t - kSub >= t_begin) pend = load_fwd(a.ckpt, (size_t)b * a.nsub + (t - kSub) / kSub, a.C, c);
       if (a.seg_start != nullptr) st = (t == t_begin) ? segst : fwd_combine(segst, t - t_begin, lc, st);
       const int off = r0 * kLanes + lane;
       if (L == kSub)
@@ -363,13 +377,44 @@ __global__ void __launch_bounds__(kLanes)
     if (kTma && lane == 0 && jj + S < ntiles) issue(jj + S);
   }
   if (kTma && kOut && lane == 0) bulk_wait_all();
-  if (!cval) return;
-  if (a.partial != nullptr) {
+  if (cval && a.adj_out != nullptr) store_adj(a.adj_out, lseg, a.C, c, adj);
+  if (a.partial == nullptr) return;
+  if (cval) {
     float* r = a.partial + lseg * 2 * (size_t)a.C + c;
     r[0] = gwacc;
     r[a.C] = gu;
   }
-  if (a.adj_out != nullptr) store_adj(a.adj_out, lseg, a.C, c, adj);
+  if (a.tickets == nullptr) return;
+  // The last CTA of this column block to finish sums every (b, segment) row in
+  // a fixed order: grad_time_decay = w e^w sum gwacc (dL/dw * w, reference
+  // wkv_triton.py:117,194), grad_time_first = sum gu. No CTA waits for another.
+  __threadfence();
+  __syncwarp();
+  unsigned ticket = 0;
+  if (lane == 0) ticket = atomicAdd(&a.tickets[cb], 1u);
+  ticket = __shfl_sync(kFull, ticket, 0);
+  const int rows = a.B * a.nseg;
+  if (ticket + 1 != static_cast<unsigned>(rows)) return;
+  __threadfence();
+  if (!cval) return;
+  double sw = 0.0, su = 0.0;
+  const float* base = a.partial + c;
+  for (int r0 = 0; r0 < rows; r0 += 16) {
+    float pw[16], pu[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const bool in = r0 + i < rows;
+      pw[i] = in ? __ldcg(base + (size_t)(r0 + i) * 2 * a.C) : 0.f;
+      pu[i] = in ? __ldcg(base + ((size_t)(r0 + i) * 2 + 1) * a.C) : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      sw += pw[i];
+      su += pu[i];
+    }
+  }
+  a.gtd[c] = static_cast<float>(static_cast<double>(lc.w) * static_cast<double>(lc.ew) * sw);
+  a.gtf[c] = static_cast<float>(su);
 }
 
 // ------------------------------------------------------------------- carries
@@ -410,22 +455,6 @@ __global__ void wkv_carry_adj_kernel(float* adj, const float* w, int B, int T, i
     store_adj(adj, row, C, c, a);
     if (s > 0) a = adj_combine(local, a, min(seg_len, T - s * seg_len), lc);
   }
-}
-
-// grad_time_decay[c] = w e^w sum_r gwacc[r][c]  (dL/dw * w, reference
-// wkv_triton.py:117,194), grad_time_first[c] = sum_r gu[r][c]; fixed order.
-__global__ void wkv_reduce_kernel(const float* partial, int rows, int C, const float* w,
-                                  float* gtd, float* gtf) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= C) return;
-  double sw = 0.0, su = 0.0;
-  for (int r = 0; r < rows; ++r) {
-    sw += partial[(size_t)r * 2 * C + c];
-    su += partial[((size_t)r * 2 + 1) * C + c];
-  }
-  const float wc = w[c];
-  gtd[c] = static_cast<float>(static_cast<double>(wc) * static_cast<double>(expf(wc)) * sw);
-  gtf[c] = static_cast<float>(su);
 }
 
 }  // namespace wkv

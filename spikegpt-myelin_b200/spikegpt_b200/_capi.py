@@ -75,6 +75,16 @@ def lib() -> ctypes.CDLL:
         handle.wkv_plan.restype = ci
         handle.wkv_set_debug_overrides.argtypes = [ci, ci, ci]
         handle.wkv_set_debug_overrides.restype = ci
+        handle.wkv_kernel_kinds.argtypes = []
+        handle.wkv_kernel_kinds.restype = ci
+        handle.wkv_kernel_name.argtypes = [ci]
+        handle.wkv_kernel_name.restype = ctypes.c_char_p
+        handle.wkv_launch_counts.argtypes = [ctypes.POINTER(ctypes.c_longlong), ci]
+        handle.wkv_launch_counts.restype = ci
+        handle.wkv_timing_enable.argtypes = [ci]
+        handle.wkv_timing_enable.restype = ci
+        handle.wkv_timing_collect.argtypes = [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong), ci]
+        handle.wkv_timing_collect.restype = ci
         handle.wkv_device_error_flags.argtypes = [ctypes.POINTER(ctypes.c_uint), ci]
         handle.wkv_device_error_flags.restype = ci
         _lib = handle
@@ -112,6 +122,31 @@ def device_error_flags(clear: bool = False) -> int:
     flags = ctypes.c_uint(0)
     check(lib().wkv_device_error_flags(ctypes.byref(flags), int(clear)), "wkv_device_error_flags")
     return int(flags.value)
+
+
+def kernel_names() -> list[str]:
+    n = lib().wkv_kernel_kinds()
+    return [lib().wkv_kernel_name(i).decode() for i in range(n)]
+
+
+def launch_counts() -> dict[str, int]:
+    names = kernel_names()
+    arr = (ctypes.c_longlong * len(names))()
+    check(lib().wkv_launch_counts(arr, len(names)), "wkv_launch_counts")
+    return dict(zip(names, (int(x) for x in arr), strict=True))
+
+
+def timing_enable(on: bool = True) -> None:
+    check(lib().wkv_timing_enable(int(on)), "wkv_timing_enable")
+
+
+def timing_collect() -> dict[str, tuple[float, int]]:
+    """{kernel: (summed device ms, timed launches)} since the last collect."""
+    names = kernel_names()
+    ms = (ctypes.c_double * len(names))()
+    n = (ctypes.c_longlong * len(names))()
+    check(lib().wkv_timing_collect(ms, n, len(names)), "wkv_timing_collect")
+    return {name: (float(ms[i]), int(n[i])) for i, name in enumerate(names)}
 
 
 def declared_symbols() -> list[str]:

@@ -63,6 +63,14 @@ def _assert_close(got, ref, tol, what=""):
 # ------------------------------------------------------------ golden vectors
 
 
+def _fp32_tol(k, v, td, tf, gy) -> float:
+    """1e-5, or, where the reference's own algorithm run in float32 cannot reach
+    it (keys of magnitude ~80 in kscale20), twice that algorithm's error."""
+    ref = oracle.forward_backward(k, v, td, tf, gy)
+    f32 = oracle.forward_backward(k, v, td, tf, gy, dtype=np.float32)
+    return max(TOL_FP32, 2.0 * max(scaled_err(a, b) for a, b in zip(f32, ref, strict=True)))
+
+
 @pytest.mark.parametrize("name", NAMES)
 def test_golden_cases_float32(cuda, name):
     """Every reference-generated golden case, float32 I/O through myelin::wkv_forward."""
@@ -71,7 +79,7 @@ def test_golden_cases_float32(cuda, name):
     g = CASES[name]
     if name == "cfg0":
         got[:3] = [a.reshape(-1)[::CFG0_STRIDE] for a in got[:3]]
-    _assert_close(got, [g[f] for f in FIELDS], TOL_FP32, name)
+    _assert_close(got, [g[f] for f in FIELDS], _fp32_tol(k, v, td, tf, gy), name)
 
 
 @pytest.mark.parametrize("name", ["triton_t7", "triton_t64", "channels70", "kscale4", "kscale20", "decay_extremes", "bf16_rounded"])
@@ -81,7 +89,7 @@ def test_golden_cases_on_every_execution_path(cuda, name, path):
     seg = {"seg2": 2, "seg3": 3, "slow_seg2": 2}.get(path, 0)
     _capi.set_debug_overrides(force_segments=seg, force_generic=path == "generic", force_slow=path.startswith("slow"))
     got = _run(weighted_key_value_cuda, k, v, td, tf, gy, dtype=torch.float32, device=cuda)
-    _assert_close(got, [CASES[name][f] for f in FIELDS], TOL_FP32, f"{name}/{path}")
+    _assert_close(got, [CASES[name][f] for f in FIELDS], _fp32_tol(k, v, td, tf, gy), f"{name}/{path}")
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
@@ -186,6 +194,7 @@ def test_shift_invariance_in_key_at_full_size(cuda, dtype):
     """Adding a constant to every key scales every weight by the same factor, so
     y is unchanged (checked at config-1 size, both execution regimes)."""
     k, v, td, tf, _ = config_inputs(64, 1024, 512, seed=9, kscale=4.0)
+    k = np.clip(np.round(k * 4.0) / 4.0, -48.0, 48.0)  # k and k + 8 exact in bf16
     kt = torch.as_tensor(k).to(cuda, dtype)
     vt = torch.as_tensor(v).to(cuda, dtype)
     tdt, tft = torch.as_tensor(td).to(cuda), torch.as_tensor(tf).to(cuda)
