@@ -69,6 +69,8 @@ def parse_args():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg1")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--profile", action="store_true", help="device loop only (for ncu): no CPU leg, e2e or clocks")
+    ap.add_argument("--no-state", action="store_true",
+                    help="time the self-contained op pair (backward re-runs the forward sweep)")
     return ap.parse_args()
 
 
@@ -228,17 +230,33 @@ def run_native(args, wl):
     lib = _capi.lib()
     fws_n = int(lib.wkv_forward_workspace_size(code, b, t, c))
     bws_n = int(lib.wkv_backward_workspace_size(code, b, t, c))
+    st_n = int(lib.wkv_state_size(code, b, t, c))
     fws = torch.empty(max(fws_n, 1), dtype=torch.uint8, device=dev)
     bws = torch.empty(max(bws_n, 1), dtype=torch.uint8, device=dev)
+    state = torch.empty(max(st_n, 16), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
 
-    def step():
+    # The training path: the forward keeps the recurrence state (every 16 steps)
+    # and the backward consumes it, as autograd does through the model-facing
+    # wrappers. --no-state times the self-contained op pair instead.
+    def step_state():
+        _capi.check(lib.wkv_forward_with_state(code, k.data_ptr(), v.data_ptr(), td.data_ptr(), tf.data_ptr(),
+                                               y.data_ptr(), state.data_ptr(), st_n, b, t, c,
+                                               fws.data_ptr(), fws_n, sp), "wkv_forward_with_state")
+        _capi.check(lib.wkv_backward_from_state(code, gy.data_ptr(), w.data_ptr(), tf.data_ptr(), k.data_ptr(),
+                                                v.data_ptr(), state.data_ptr(), st_n, gk.data_ptr(), gv.data_ptr(),
+                                                gtd.data_ptr(), gtf.data_ptr(), b, t, c, bws.data_ptr(), bws_n, sp),
+                    "wkv_backward_from_state")
+
+    def step_plain():
         _capi.check(lib.wkv_forward(code, k.data_ptr(), v.data_ptr(), td.data_ptr(), tf.data_ptr(), y.data_ptr(),
                                     b, t, c, fws.data_ptr(), fws_n, sp), "wkv_forward")
         _capi.check(lib.wkv_backward(code, gy.data_ptr(), w.data_ptr(), tf.data_ptr(), k.data_ptr(), v.data_ptr(),
                                      gk.data_ptr(), gv.data_ptr(), gtd.data_ptr(), gtf.data_ptr(),
                                      b, t, c, bws.data_ptr(), bws_n, sp), "wkv_backward")
+
+    step = step_plain if args.no_state else step_state
 
     def barrier():
         if world > 1:
@@ -332,6 +350,8 @@ def run_native(args, wl):
             "l2": "inputs larger than L2 (201 MB of k,v,grad_y read per step); no flush",
             "frac_of_hbm_peak": value / world / hbm,
             "plan": dict(zip(("tma", "segments"), _capi.plan(code, b, t, c), strict=True)),
+            "path": ("wkv_forward + wkv_backward (backward re-runs the forward sweep)" if args.no_state else
+                     "wkv_forward_with_state + wkv_backward_from_state (the autograd path)"),
         },
         "roofline": roofline,
         "kernels": kernels,
@@ -377,19 +397,21 @@ def run_e2e(args, wl, dev, k_np, v_np, td_np, tf_np, gy_np, tdt, world):
     h2d = sum(x.numel() * x.element_size() for x in (hk, hv, hgy, htd, htf))
     d2h = sum(x.numel() * x.element_size() for x in (hy, hgk, hgv, hgtd, hgtf))
 
+    from spikegpt_b200 import weighted_key_value_triton_bf16io
+
     def step():
-        k = hk.to(dev, non_blocking=True)
-        v = hv.to(dev, non_blocking=True)
+        k = hk.to(dev, non_blocking=True).requires_grad_()
+        v = hv.to(dev, non_blocking=True).requires_grad_()
         gy = hgy.to(dev, non_blocking=True)
-        td = htd.to(dev, non_blocking=True)
-        tf = htf.to(dev, non_blocking=True)
-        y = torch.ops.myelin.wkv_forward_bf16io(k, v, td, tf)
-        gk, gv, gtd, gtf = torch.ops.myelin.wkv_backward_bf16io(gy, -torch.exp(td), tf, k, v)
-        hy.copy_(y, non_blocking=True)
-        hgk.copy_(gk, non_blocking=True)
-        hgv.copy_(gv, non_blocking=True)
-        hgtd.copy_(gtd, non_blocking=True)
-        hgtf.copy_(gtf, non_blocking=True)
+        td = htd.to(dev, non_blocking=True).requires_grad_()
+        tf = htf.to(dev, non_blocking=True).requires_grad_()
+        y = weighted_key_value_triton_bf16io(k, v, td, tf)
+        y.backward(gy)
+        hy.copy_(y.detach(), non_blocking=True)
+        hgk.copy_(k.grad, non_blocking=True)
+        hgv.copy_(v.grad, non_blocking=True)
+        hgtd.copy_(td.grad, non_blocking=True)
+        hgtf.copy_(tf.grad, non_blocking=True)
 
     for _ in range(3):
         step()
@@ -411,7 +433,7 @@ def run_e2e(args, wl, dev, k_np, v_np, td_np, tf_np, gy_np, tdt, world):
     value = BYTES_PER_ELEM[wl["dtype"]] * elems * args.e2e_steps * world / (ms * 1e-3) / 1e9
     return {"value": value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "steps": args.e2e_steps, "ms_per_step": ms / args.e2e_steps,
-            "path": "torch.ops.myelin.wkv_forward_bf16io / wkv_backward_bf16io, pinned host buffers"}
+            "path": "autograd through spikegpt_b200.weighted_key_value_triton_bf16io (myelin::wkv_forward_bf16io), pinned host buffers"}
 
 
 # ----------------------------------------------------------- reference arm

@@ -96,6 +96,31 @@ WKV_API int wkv_backward(int dtype, const void* grad_y, const float* w, const fl
                  int64_t C, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Forward/backward with a saved forward state (no reference counterpart; an
+ * optimisation of the pair above). wkv_forward_with_state computes y exactly as
+ * wkv_forward and also stores the recurrence state at every 16th step into
+ * `state` (wkv_state_size bytes, 16-byte aligned, caller-owned).
+ * wkv_backward_from_state returns the same gradients as wkv_backward for the
+ * same inputs, reading that state instead of re-running the forward sweep, so it
+ * reads key/value once instead of twice. The state must come from
+ * wkv_forward_with_state on the same key, value and time_decay; it is reusable
+ * by later backward calls, but calls that use one state buffer concurrently on
+ * the GPU race.
+ */
+WKV_API size_t wkv_state_size(int dtype, int64_t B, int64_t T, int64_t C);
+WKV_API int wkv_forward_with_state(int dtype, const void* key, const void* value,
+                                   const float* time_decay, const float* time_first, void* y,
+                                   float* state, size_t state_bytes, int64_t B, int64_t T,
+                                   int64_t C, void* workspace, size_t workspace_bytes,
+                                   void* stream);
+WKV_API int wkv_backward_from_state(int dtype, const void* grad_y, const float* w, const float* u,
+                                    const void* key, const void* value, const float* state,
+                                    size_t state_bytes, void* grad_key, void* grad_value,
+                                    float* grad_time_decay, float* grad_time_first, int64_t B,
+                                    int64_t T, int64_t C, void* workspace,
+                                    size_t workspace_bytes, void* stream);
+
+/*
  * Execution plan the library picks for a shape (no reference counterpart; it
  * exposes the choice the reference never had to make). tma = 1 when tiles are
  * staged with TMA (needs C*sizeof(dtype) % 16 == 0 and 16-byte aligned

@@ -128,10 +128,10 @@ Plan make_plan(int dtype, int64_t B, int64_t T, int64_t C, bool ptrs_aligned) {
   const size_t es = dtype_size(dtype);
   p.tma = g_force_generic.load() == 0 && ptrs_aligned && (C * (int64_t)es) % 16 == 0;
   const int64_t lanes = B * ((C + kLanes - 1) / kLanes) * kLanes;
-  const int64_t want = (int64_t)sm_count() * 6 * kLanes;
+  const int64_t want = (int64_t)sm_count() * 3 * kLanes;  // ~3 single-warp CTAs per SM
   int64_t nseg = 1;
   if (lanes > 0 && lanes < want) nseg = (want + lanes - 1) / lanes;
-  const int64_t max_seg = T / (2 * kTile);  // keep >= 2 tiles per segment
+  const int64_t max_seg = T / (2 * kSegAlign);  // keep >= 2 alignment units per segment
   if (nseg > max_seg) nseg = max_seg;
   if (g_force_segments.load() > 0) nseg = g_force_segments.load();
   if (nseg < 1) nseg = 1;
@@ -140,7 +140,7 @@ Plan make_plan(int dtype, int64_t B, int64_t T, int64_t C, bool ptrs_aligned) {
     p.seg_len = static_cast<int>(T);
   } else {
     int64_t len = (T + nseg - 1) / nseg;
-    len = (len + kTile - 1) / kTile * kTile;
+    len = (len + kSegAlign - 1) / kSegAlign * kSegAlign;
     p.seg_len = static_cast<int>(len);
     p.nseg = static_cast<int>((T + len - 1) / len);
     if (p.nseg == 1) p.seg_len = static_cast<int>(T);
@@ -186,7 +186,7 @@ BwdWs bwd_workspace(const Plan& p, int64_t B, int64_t T, int64_t C, void* base) 
   w.ckpt = take((size_t)B * nsub * 3 * C * sizeof(float));
   if (p.nseg > 1) {
     w.seg = take((size_t)B * p.nseg * 3 * C * sizeof(float));
-    w.adj = take((size_t)B * p.nseg * 3 * C * sizeof(float));
+    w.adj = take((size_t)B * p.nseg * 5 * C * sizeof(float));
   }
   w.partial = take((size_t)B * p.nseg * 2 * C * sizeof(float));
   w.tickets = reinterpret_cast<unsigned*>(take((size_t)((C + kLanes - 1) / kLanes) * sizeof(unsigned)));
@@ -218,7 +218,8 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// [B, T, C] tensor as a 3-D map with dims {C, T, B} and a [1][kTile][kLanes] box.
+// [B, T, C] tensor as a 3-D map with dims {C, T, B} and a [1][rows][kLanes] box,
+// rows = the dtype's tile height (Pair<T>::kTileRows).
 int make_map(CUtensorMap* m, int dtype, const void* ptr, int64_t B, int64_t T, int64_t C) {
   std::memset(m, 0, sizeof(*m));
   if (ptr == nullptr) return WKV_OK;
@@ -230,7 +231,8 @@ int make_map(CUtensorMap* m, int dtype, const void* ptr, int64_t B, int64_t T, i
                                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)T, (cuuint64_t)B};
   const cuuint64_t strides[2] = {(cuuint64_t)(C * es), (cuuint64_t)(T * C * es)};
-  const cuuint32_t box[3] = {(cuuint32_t)kLanes, (cuuint32_t)kTile, 1u};
+  const cuuint32_t rows = dtype == WKV_DTYPE_F32 ? Pair<float>::kTileRows : Pair<__half>::kTileRows;
+  const cuuint32_t box[3] = {(cuuint32_t)kLanes, rows, 1u};
   const cuuint32_t estr[3] = {1u, 1u, 1u};
   const CUresult r = fn(m, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -266,12 +268,30 @@ int check_dims(int dtype, int64_t B, int64_t T, int64_t C) {
   return WKV_OK;
 }
 
+// Kernels whose dynamic shared memory exceeds the 48 KB default opt in once per
+// device.
+template <typename K>
+cudaError_t allow_smem(K* kernel, size_t bytes) {
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  static std::mutex mu;
+  static std::vector<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(mu);
+  for (auto& d : done)
+    if (d.first == reinterpret_cast<const void*>(kernel) && d.second == dev) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess) done.emplace_back(reinterpret_cast<const void*>(kernel), dev);
+  return e;
+}
+
 // ----------------------------------------------------------- launch helpers
 
 template <typename IO>
 int launch_forward(const void* k, const void* v, const float* decay, int decay_is_w,
                    const float* u, void* y, int B, int T, int C, const Plan& p, float* seg,
-                   cudaStream_t st) {
+                   float* state, unsigned* state_tickets, cudaStream_t st) {
   CUtensorMap mk, mv, my;
   const int dt = sizeof(IO) == 4 ? WKV_DTYPE_F32
                  : std::is_same<IO, __nv_bfloat16>::value ? WKV_DTYPE_BF16
@@ -310,9 +330,9 @@ int launch_forward(const void* k, const void* v, const float* decay, int decay_i
     const size_t sm = fwd_smem_bytes<IO>(false);
     launch(K_FWD_STATE, st, [&] {
       if (p.tma)
-        wkv_fwd_kernel<IO, false, true><<<dim3(gx, p.nseg - 1), kLanes, sm, st>>>(s, mk, mv, my);
+        wkv_fwd_kernel<IO, false, true><<<dim3(gx, p.nseg - 1), kThreads, sm, st>>>(s, mk, mv, my);
       else
-        wkv_fwd_kernel<IO, false, false><<<dim3(gx, p.nseg - 1), kLanes, sm, st>>>(s, mk, mv, my);
+        wkv_fwd_kernel<IO, false, false><<<dim3(gx, p.nseg - 1), kThreads, sm, st>>>(s, mk, mv, my);
     });
     const int64_t lanes = (int64_t)B * C;
     launch(K_CARRY_FWD, st, [&] {
@@ -321,12 +341,17 @@ int launch_forward(const void* k, const void* v, const float* decay, int decay_i
     });
     a.seg_start = seg;
   }
+  // The main pass starts every segment from its true state, so the checkpoints
+  // it writes are true states; it also zeroes the backward's arrival counters.
+  a.ckpt = state;
+  a.zero_tickets = state_tickets;
+  a.nzero = state_tickets ? a.ncblk : 0;
   const size_t sm = fwd_smem_bytes<IO>(true);
   launch(K_FWD_Y, st, [&] {
     if (p.tma)
-      wkv_fwd_kernel<IO, true, true><<<dim3(gx, p.nseg), kLanes, sm, st>>>(a, mk, mv, my);
+      wkv_fwd_kernel<IO, true, true><<<dim3(gx, p.nseg), kThreads, sm, st>>>(a, mk, mv, my);
     else
-      wkv_fwd_kernel<IO, true, false><<<dim3(gx, p.nseg), kLanes, sm, st>>>(a, mk, mv, my);
+      wkv_fwd_kernel<IO, true, false><<<dim3(gx, p.nseg), kThreads, sm, st>>>(a, mk, mv, my);
   });
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "wkv forward launch");
@@ -336,7 +361,8 @@ int launch_forward(const void* k, const void* v, const float* decay, int decay_i
 template <typename IO>
 int launch_backward(const void* gy, const float* w, const float* u, const void* k, const void* v,
                     void* gk, void* gv, float* gtd, float* gtf, int B, int T, int C,
-                    const Plan& p, const BwdWs& ws, cudaStream_t st) {
+                    const Plan& p, const BwdWs& ws, const float* state,
+                    unsigned* state_tickets, cudaStream_t st) {
   const int dt = sizeof(IO) == 4 ? WKV_DTYPE_F32
                  : std::is_same<IO, __nv_bfloat16>::value ? WKV_DTYPE_BF16
                                                          : WKV_DTYPE_F16;
@@ -378,11 +404,11 @@ int launch_backward(const void* gy, const float* w, const float* u, const void* 
   f.force_slow = force_slow;
   f.err = err;
   const size_t fsm = fwd_smem_bytes<IO>(false);
-  launch(K_FWD_STATE, st, [&] {
+  if (state == nullptr) launch(K_FWD_STATE, st, [&] {
     if (p.tma)
-      wkv_fwd_kernel<IO, false, true><<<dim3(gx, p.nseg), kLanes, fsm, st>>>(f, mk, mv, none);
+      wkv_fwd_kernel<IO, false, true><<<dim3(gx, p.nseg), kThreads, fsm, st>>>(f, mk, mv, none);
     else
-      wkv_fwd_kernel<IO, false, false><<<dim3(gx, p.nseg), kLanes, fsm, st>>>(f, mk, mv, none);
+      wkv_fwd_kernel<IO, false, false><<<dim3(gx, p.nseg), kThreads, fsm, st>>>(f, mk, mv, none);
   });
 
   BwdArgs a{};
@@ -400,50 +426,56 @@ int launch_backward(const void* gy, const float* w, const float* u, const void* 
   a.seg_len = p.seg_len;
   a.nseg = p.nseg;
   a.nsub = nsub;
-  a.ckpt = ws.ckpt;
+  a.ckpt = state ? state : ws.ckpt;
   a.force_slow = force_slow;
   a.err = err;
   const int64_t lanes = (int64_t)B * C;
   const unsigned cgrid = (unsigned)((lanes + 127) / 128);
   if (p.nseg > 1) {
-    // 2. segment start states; 3. adjoint summaries of segments 1..nseg-1;
-    // 4. adjoint at every segment end
-    launch(K_CARRY_FWD, st, [&] {
-      wkv_carry_fwd_kernel<<<cgrid, 128, 0, st>>>(ws.seg, w, 1, B, T, C, p.nseg, p.seg_len);
-    });
+    // 2. segment start states (only when the checkpoints are segment-local);
+    // 3. adjoint summaries of segments 1..nseg-1; 4. adjoint at every segment end
+    if (state == nullptr)
+      launch(K_CARRY_FWD, st, [&] {
+        wkv_carry_fwd_kernel<<<cgrid, 128, 0, st>>>(ws.seg, w, 1, B, T, C, p.nseg, p.seg_len);
+      });
     BwdArgs s = a;
-    s.seg_start = ws.seg;
+    s.seg_start = state ? nullptr : ws.seg;
     s.seg_base = 1;
     s.adj_out = ws.adj;
     const size_t ssm = bwd_smem_bytes<IO>(false);
     launch(K_BWD_ADJ, st, [&] {
       if (p.tma)
         wkv_bwd_kernel<IO, false, true>
-            <<<dim3(gx, p.nseg - 1), kLanes, ssm, st>>>(s, mk, mv, mgy, none, none);
+            <<<dim3(gx, p.nseg - 1), kThreads, ssm, st>>>(s, mk, mv, mgy, none, none);
       else
         wkv_bwd_kernel<IO, false, false>
-            <<<dim3(gx, p.nseg - 1), kLanes, ssm, st>>>(s, mk, mv, mgy, none, none);
+            <<<dim3(gx, p.nseg - 1), kThreads, ssm, st>>>(s, mk, mv, mgy, none, none);
     });
     launch(K_CARRY_ADJ, st, [&] {
       wkv_carry_adj_kernel<<<cgrid, 128, 0, st>>>(ws.adj, w, B, T, C, p.nseg, p.seg_len);
     });
-    a.seg_start = ws.seg;
+    a.seg_start = state ? nullptr : ws.seg;
     a.adj_in = ws.adj;
   }
   // 5. reverse sweep writing grad_key / grad_value and per-lane partials; the
   // last CTA of each column block reduces the partials into the time gradients
   a.partial = ws.partial;
-  a.tickets = ws.tickets;
+  a.tickets = state ? state_tickets : ws.tickets;
   a.gtd = gtd;
   a.gtf = gtf;
   const size_t bsm = bwd_smem_bytes<IO>(true);
+  {
+    const cudaError_t e = p.tma ? allow_smem(wkv_bwd_kernel<IO, true, true>, bsm)
+                                : allow_smem(wkv_bwd_kernel<IO, true, false>, bsm);
+    if (e != cudaSuccess) return cuda_fail(e, "setting the backward kernel's shared memory size");
+  }
   launch(K_BWD_GRAD, st, [&] {
     if (p.tma)
       wkv_bwd_kernel<IO, true, true>
-          <<<dim3(gx, p.nseg), kLanes, bsm, st>>>(a, mk, mv, mgy, mgk, mgv);
+          <<<dim3(gx, p.nseg), kThreads, bsm, st>>>(a, mk, mv, mgy, mgk, mgv);
     else
       wkv_bwd_kernel<IO, true, false>
-          <<<dim3(gx, p.nseg), kLanes, bsm, st>>>(a, mk, mv, mgy, mgk, mgv);
+          <<<dim3(gx, p.nseg), kThreads, bsm, st>>>(a, mk, mv, mgy, mgk, mgv);
   });
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "wkv backward launch");
@@ -497,9 +529,26 @@ size_t wkv_backward_workspace_size(int dtype, int64_t B, int64_t T, int64_t C) {
   return bwd_workspace(p, B, T, C, nullptr).bytes;
 }
 
-int wkv_forward(int dtype, const void* key, const void* value, const float* time_decay,
-                const float* time_first, void* y, int64_t B, int64_t T, int64_t C,
-                void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Saved forward state: checkpoint rows [B][ceil(T/kSub)][3][C] floats, then one
+// arrival counter per 64-channel block.
+struct StateLayout {
+  size_t ckpt_bytes, bytes;
+};
+StateLayout state_layout(int64_t B, int64_t T, int64_t C) {
+  StateLayout l;
+  const int64_t nsub = (T + kSub - 1) / kSub;
+  l.ckpt_bytes = round_up((size_t)B * nsub * 3 * C * sizeof(float));
+  l.bytes = l.ckpt_bytes + round_up((size_t)((C + kLanes - 1) / kLanes) * sizeof(unsigned));
+  return l;
+}
+
+int forward_impl(int dtype, const void* key, const void* value, const float* time_decay,
+                 const float* time_first, void* y, float* state, size_t state_bytes, int64_t B,
+                 int64_t T, int64_t C, void* workspace, size_t workspace_bytes, void* stream) {
   g_last_error[0] = '\0';
   int rc = check_dims(dtype, B, T, C);
   if (rc) return rc;
@@ -512,23 +561,33 @@ int wkv_forward(int dtype, const void* key, const void* value, const float* time
   if (need.bytes > 0 && (workspace == nullptr || workspace_bytes < need.bytes))
     return fail(WKV_ERR_WORKSPACE_TOO_SMALL, "forward needs %zu workspace bytes, got %zu",
                 need.bytes, workspace_bytes);
+  unsigned* state_tickets = nullptr;
+  if (state != nullptr) {
+    const StateLayout sl = state_layout(B, T, C);
+    if (state_bytes < sl.bytes)
+      return fail(WKV_ERR_WORKSPACE_TOO_SMALL, "state needs %zu bytes, got %zu", sl.bytes, state_bytes);
+    if (!aligned16(state)) return fail(WKV_ERR_INVALID_ARGUMENT, "state must be 16-byte aligned");
+    state_tickets = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(state) + sl.ckpt_bytes);
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int b = (int)B, t = (int)T, c = (int)C;
   switch (dtype) {
     case WKV_DTYPE_F32:
-      return launch_forward<float>(key, value, time_decay, 0, time_first, y, b, t, c, p, need.seg, st);
+      return launch_forward<float>(key, value, time_decay, 0, time_first, y, b, t, c, p, need.seg,
+                                   state, state_tickets, st);
     case WKV_DTYPE_BF16:
       return launch_forward<__nv_bfloat16>(key, value, time_decay, 0, time_first, y, b, t, c, p,
-                                           need.seg, st);
+                                           need.seg, state, state_tickets, st);
     default:
-      return launch_forward<__half>(key, value, time_decay, 0, time_first, y, b, t, c, p, need.seg, st);
+      return launch_forward<__half>(key, value, time_decay, 0, time_first, y, b, t, c, p, need.seg,
+                                    state, state_tickets, st);
   }
 }
 
-int wkv_backward(int dtype, const void* grad_y, const float* w, const float* u, const void* key,
-                 const void* value, void* grad_key, void* grad_value, float* grad_time_decay,
-                 float* grad_time_first, int64_t B, int64_t T, int64_t C, void* workspace,
-                 size_t workspace_bytes, void* stream) {
+int backward_impl(int dtype, const void* grad_y, const float* w, const float* u, const void* key,
+                  const void* value, const float* state, size_t state_bytes, void* grad_key,
+                  void* grad_value, float* grad_time_decay, float* grad_time_first, int64_t B,
+                  int64_t T, int64_t C, void* workspace, size_t workspace_bytes, void* stream) {
   g_last_error[0] = '\0';
   int rc = check_dims(dtype, B, T, C);
   if (rc) return rc;
@@ -554,18 +613,77 @@ int wkv_backward(int dtype, const void* grad_y, const float* w, const float* u, 
   if (!aligned16(workspace))
     return fail(WKV_ERR_INVALID_ARGUMENT, "workspace must be 16-byte aligned");
   const BwdWs ws = bwd_workspace(p, B, T, C, workspace);
+  unsigned* state_tickets = nullptr;
+  if (state != nullptr) {
+    const StateLayout sl = state_layout(B, T, C);
+    if (state_bytes < sl.bytes)
+      return fail(WKV_ERR_WORKSPACE_TOO_SMALL, "state needs %zu bytes, got %zu", sl.bytes, state_bytes);
+    if (!aligned16(state)) return fail(WKV_ERR_INVALID_ARGUMENT, "state must be 16-byte aligned");
+    state_tickets = reinterpret_cast<unsigned*>(
+        reinterpret_cast<char*>(const_cast<float*>(state)) + sl.ckpt_bytes);
+  }
   const int b = (int)B, t = (int)T, c = (int)C;
   switch (dtype) {
     case WKV_DTYPE_F32:
       return launch_backward<float>(grad_y, w, u, key, value, grad_key, grad_value,
-                                    grad_time_decay, grad_time_first, b, t, c, p, ws, st);
+                                    grad_time_decay, grad_time_first, b, t, c, p, ws, state,
+                                    state_tickets, st);
     case WKV_DTYPE_BF16:
       return launch_backward<__nv_bfloat16>(grad_y, w, u, key, value, grad_key, grad_value,
-                                            grad_time_decay, grad_time_first, b, t, c, p, ws, st);
+                                            grad_time_decay, grad_time_first, b, t, c, p, ws,
+                                            state, state_tickets, st);
     default:
       return launch_backward<__half>(grad_y, w, u, key, value, grad_key, grad_value,
-                                     grad_time_decay, grad_time_first, b, t, c, p, ws, st);
+                                     grad_time_decay, grad_time_first, b, t, c, p, ws, state,
+                                     state_tickets, st);
   }
+}
+
+}  // namespace
+
+extern "C" {
+
+int wkv_forward(int dtype, const void* key, const void* value, const float* time_decay,
+                const float* time_first, void* y, int64_t B, int64_t T, int64_t C,
+                void* workspace, size_t workspace_bytes, void* stream) {
+  return forward_impl(dtype, key, value, time_decay, time_first, y, nullptr, 0, B, T, C,
+                      workspace, workspace_bytes, stream);
+}
+
+int wkv_backward(int dtype, const void* grad_y, const float* w, const float* u, const void* key,
+                 const void* value, void* grad_key, void* grad_value, float* grad_time_decay,
+                 float* grad_time_first, int64_t B, int64_t T, int64_t C, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+  return backward_impl(dtype, grad_y, w, u, key, value, nullptr, 0, grad_key, grad_value,
+                       grad_time_decay, grad_time_first, B, T, C, workspace, workspace_bytes,
+                       stream);
+}
+
+size_t wkv_state_size(int dtype, int64_t B, int64_t T, int64_t C) {
+  if (check_dims(dtype, B, T, C)) return 0;
+  return state_layout(B, T, C).bytes;
+}
+
+int wkv_forward_with_state(int dtype, const void* key, const void* value, const float* time_decay,
+                           const float* time_first, void* y, float* state, size_t state_bytes,
+                           int64_t B, int64_t T, int64_t C, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  if (state == nullptr && B > 0 && T > 0 && C > 0)
+    return fail(WKV_ERR_INVALID_ARGUMENT, "null state pointer");
+  return forward_impl(dtype, key, value, time_decay, time_first, y, state, state_bytes, B, T, C,
+                      workspace, workspace_bytes, stream);
+}
+
+int wkv_backward_from_state(int dtype, const void* grad_y, const float* w, const float* u,
+                            const void* key, const void* value, const float* state,
+                            size_t state_bytes, void* grad_key, void* grad_value,
+                            float* grad_time_decay, float* grad_time_first, int64_t B, int64_t T,
+                            int64_t C, void* workspace, size_t workspace_bytes, void* stream) {
+  if (state == nullptr && B > 0 && T > 0 && C > 0)
+    return fail(WKV_ERR_INVALID_ARGUMENT, "null state pointer");
+  return backward_impl(dtype, grad_y, w, u, key, value, state, state_bytes, grad_key, grad_value,
+                       grad_time_decay, grad_time_first, B, T, C, workspace, workspace_bytes,
+                       stream);
 }
 
 int wkv_kernel_kinds(void) { return K_COUNT; }

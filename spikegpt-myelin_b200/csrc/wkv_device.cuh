@@ -1,7 +1,7 @@
 // Device-side building blocks of the WKV recurrence for sm_100a: PTX wrappers
-// (MUFU ex2/rcp, mbarrier, TMA bulk-tensor copies), I/O dtype traits, and the
-// per-sub-chunk arithmetic shared by the forward, checkpoint and backward
-// kernels in wkv_kernels.cuh.
+// (MUFU ex2/rcp, packed f32x2 FMA/MUL/ADD, mbarrier, TMA bulk-tensor copies),
+// I/O dtype traits, and the per-sub-chunk arithmetic shared by the forward,
+// checkpoint and backward kernels in wkv_kernels.cuh.
 //
 // The recurrence is the RWKV-4 WKV of the reference (src/spikegpt/language.py:
 // 399-449, src/spikegpt/wkv_triton.py:34-142). Per lane (b, c), with
@@ -16,6 +16,10 @@
 // cheap check proves every denominator stays >= 2^-kMargin (no underflow) and no
 // term can overflow; otherwise the warp runs the exact per-step-rescaling
 // arithmetic of the reference for that sub-chunk ("slow path").
+//
+// Each thread owns two adjacent channels ("a lane pair"): their recurrences
+// advance together with Blackwell's packed fma/mul/add.f32x2, and their I/O
+// moves as one 32-bit bf16x2/f16x2 (or 64-bit float2) word.
 #pragma once
 
 #include <cuda.h>
@@ -28,15 +32,13 @@ namespace wkv {
 
 constexpr float kL2E = 1.4426950408889634f;  // log2(e)
 constexpr float kNegBig = -1e38f;            // "log2 of zero" (reference wkv_triton.py:43)
-constexpr int kLanes = 32;                   // channels per CTA: one warp, one lane each
+constexpr int kThreads = 32;                 // one warp per CTA
+constexpr int kLanes = 2 * kThreads;         // channels per CTA (two per thread)
 constexpr int kSub = 16;                     // steps per sub-chunk = checkpoint interval
-constexpr int kTile = 32;                    // steps per staged tile
-constexpr int kSubPerTile = kTile / kSub;
+constexpr int kSegAlign = 32;                // segment lengths are multiples of this
 constexpr float kMargin = 60.f;              // log2 headroom kept above fp32's normal range
 constexpr unsigned kFull = 0xffffffffu;
 constexpr long long kWaitLimitCycles = 4000000000ll;  // ~2 s at 2 GHz
-
-static_assert(kTile % kSub == 0, "tile must hold whole sub-chunks");
 
 // ---------------------------------------------------------------- PTX helpers
 
@@ -51,6 +53,55 @@ __device__ __forceinline__ float rcp(float x) {
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+
+struct f2 {
+  float x, y;
+};
+
+// Packed two-wide fp32 arithmetic (sm_100: one FFMA2/FMUL2/FADD2 per pair).
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
+  f2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ f2 mul2(f2 a, f2 b) {
+  f2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ f2 add2(f2 a, f2 b) {
+  f2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ f2 sub2(f2 a, f2 b) {
+  f2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "sub.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ f2 ex2x2(f2 a) { return f2{ex2(a.x), ex2(a.y)}; }
+__device__ __forceinline__ f2 rcpx2(f2 a) { return f2{rcp(a.x), rcp(a.y)}; }
+__device__ __forceinline__ f2 splat(float a) { return f2{a, a}; }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -136,84 +187,157 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
 }
 
 // ------------------------------------------------------------ I/O dtype traits
+//
+// Pair<T>::raw is the in-memory form of two adjacent elements; unpack widens it
+// to f2 (element c in .x, c+1 in .y), pack rounds to nearest even. hi/lo give a
+// raw pair the packed max/min identity for the prescan.
 
 template <typename T>
-struct IOType;
+struct Pair;
+
 template <>
-struct IOType<float> {
-  static __device__ __forceinline__ float ld(float x) { return x; }
-  static __device__ __forceinline__ float st(float x) { return x; }
+struct Pair<float> {
+  using raw = float2;
+  static constexpr int kTileRows = 16;  // 16 rows x 64 channels x 4 B = 4 KB tiles
+  static __device__ __forceinline__ raw ld(const float* p) {
+    return *reinterpret_cast<const float2*>(p);
+  }
+  static __device__ __forceinline__ void st(float* p, raw r) { *reinterpret_cast<float2*>(p) = r; }
+  static __device__ __forceinline__ f2 unpack(raw r) { return f2{r.x, r.y}; }
+  static __device__ __forceinline__ raw pack(f2 v) { return make_float2(v.x, v.y); }
+  static __device__ __forceinline__ float scalar(float x) { return x; }
+  static __device__ __forceinline__ float from_float(float x) { return x; }
 };
+
 template <>
-struct IOType<__nv_bfloat16> {
-  static __device__ __forceinline__ float ld(__nv_bfloat16 x) { return __bfloat162float(x); }
-  static __device__ __forceinline__ __nv_bfloat16 st(float x) { return __float2bfloat16_rn(x); }
+struct Pair<__nv_bfloat16> {
+  using raw = uint32_t;
+  static constexpr int kTileRows = 32;  // 32 rows x 64 channels x 2 B = 4 KB tiles
+  static __device__ __forceinline__ raw ld(const __nv_bfloat16* p) {
+    return *reinterpret_cast<const uint32_t*>(p);
+  }
+  static __device__ __forceinline__ void st(__nv_bfloat16* p, raw r) {
+    *reinterpret_cast<uint32_t*>(p) = r;
+  }
+  static __device__ __forceinline__ f2 unpack(raw r) {
+    return f2{__uint_as_float(r << 16), __uint_as_float(r & 0xffff0000u)};
+  }
+  static __device__ __forceinline__ raw pack(f2 v) {
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(v.y), "f"(v.x));
+    return d;
+  }
+  static __device__ __forceinline__ float scalar(__nv_bfloat16 x) { return __bfloat162float(x); }
+  static __device__ __forceinline__ __nv_bfloat16 from_float(float x) { return __float2bfloat16_rn(x); }
 };
+
 template <>
-struct IOType<__half> {
-  static __device__ __forceinline__ float ld(__half x) { return __half2float(x); }
-  static __device__ __forceinline__ __half st(float x) { return __float2half_rn(x); }
+struct Pair<__half> {
+  using raw = uint32_t;
+  static constexpr int kTileRows = 32;
+  static __device__ __forceinline__ raw ld(const __half* p) {
+    return *reinterpret_cast<const uint32_t*>(p);
+  }
+  static __device__ __forceinline__ void st(__half* p, raw r) { *reinterpret_cast<uint32_t*>(p) = r; }
+  static __device__ __forceinline__ f2 unpack(raw r) {
+    __half2 h = *reinterpret_cast<__half2*>(&r);
+    const float2 f = __half22float2(h);
+    return f2{f.x, f.y};
+  }
+  static __device__ __forceinline__ raw pack(f2 v) {
+    uint32_t d;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(v.y), "f"(v.x));
+    return d;
+  }
+  static __device__ __forceinline__ float scalar(__half x) { return __half2float(x); }
+  static __device__ __forceinline__ __half from_float(float x) { return __float2half_rn(x); }
 };
 
 // ------------------------------------------------------------------- state
 
-// Per-channel constants. w = -exp(time_decay) <= 0 (reference wkv_triton.py:152).
-struct Lane {
-  float w;   // natural-log decay per step
-  float w2;  // w * log2(e)
-  float u2;  // time_first * log2(e)
-  float ew;  // e^w
-  float eu;  // e^u
+// Per-channel constants of a lane pair. w = -exp(time_decay) <= 0 (reference
+// wkv_triton.py:152).
+struct Lane2 {
+  f2 w;   // natural-log decay per step
+  f2 w2;  // w * log2(e)
+  f2 u2;  // time_first * log2(e)
+  f2 ew;  // e^w
+  f2 eu;  // e^u
 };
 
-__device__ __forceinline__ Lane make_lane(float w, float u) {
-  Lane l;
+__device__ __forceinline__ Lane2 make_lane2(f2 w, f2 u) {
+  Lane2 l;
   l.w = w;
-  l.w2 = w * kL2E;
-  l.u2 = u * kL2E;
-  l.ew = expf(w);
-  l.eu = expf(u);
+  l.w2 = f2{w.x * kL2E, w.y * kL2E};
+  l.u2 = f2{u.x * kL2E, u.y * kL2E};
+  l.ew = f2{expf(w.x), expf(w.y)};
+  l.eu = f2{expf(u.x), expf(u.y)};
   return l;
 }
 
-struct Fwd {  // P = 2^S p, Q = 2^S q
-  float S, p, q;
+struct Fwd2 {  // P = 2^S p, Q = 2^S q, per lane of the pair
+  f2 S, p, q;
 };
-struct Adj {  // dL/dP = 2^G gp, dL/dQ = 2^G gq
-  float G, gp, gq;
+// Adjoint at a step boundary t: dL/dP_t = 2^G gp, dL/dQ_t = 2^G gq, and their
+// derivatives with respect to w, d(dL/dP_t)/dw = 2^G hp, d(dL/dQ_t)/dw = 2^G hq.
+// With H_t = d(dL/dP_t)/dw = e^w (dL/dP_{t+1} + H_{t+1}), the decay gradient is
+// dL/dw = sum_s e^{k_s} (v_s H^P_{s+1} + H^Q_{s+1}).
+struct Adj2 {
+  f2 G, gp, gq, hp, hq;
 };
 
-__device__ __forceinline__ Fwd fwd_identity() { return Fwd{kNegBig, 0.f, 0.f}; }
-__device__ __forceinline__ Adj adj_zero() { return Adj{kNegBig, 0.f, 0.f}; }
+__device__ __forceinline__ Fwd2 fwd_identity2() {
+  return Fwd2{splat(kNegBig), splat(0.f), splat(0.f)};
+}
+__device__ __forceinline__ Adj2 adj_zero2() {
+  return Adj2{splat(kNegBig), splat(0.f), splat(0.f), splat(0.f), splat(0.f)};
+}
 
 // State after `delta` more steps of pure decay from g, plus a local state l
 // that was accumulated from zero over those same steps (P is linear in the
-// history, so the two parts add).
-__device__ __forceinline__ Fwd fwd_combine(const Fwd& g, int delta, const Lane& lc,
-                                           const Fwd& l) {
-  const float sg = g.S + lc.w2 * static_cast<float>(delta);
-  const float s = fmaxf(sg, l.S);
-  const float a = ex2(sg - s), b = ex2(l.S - s);
-  return Fwd{s, fmaf(g.p, a, l.p * b), fmaf(g.q, a, l.q * b)};
+// history, so the two parts add). One lane.
+__device__ __forceinline__ void fwd_combine1(float gS, float gp, float gq, int delta, float w2,
+                                             float& lS, float& lp, float& lq) {
+  const float sg = gS + w2 * static_cast<float>(delta);
+  const float s = fmaxf(sg, lS);
+  const float a = ex2(sg - s), b = ex2(lS - s);
+  lp = fmaf(gp, a, lp * b);
+  lq = fmaf(gq, a, lq * b);
+  lS = s;
+}
+
+__device__ __forceinline__ Fwd2 fwd_combine2(const Fwd2& g, int delta, const Lane2& lc,
+                                             Fwd2 l) {
+  fwd_combine1(g.S.x, g.p.x, g.q.x, delta, lc.w2.x, l.S.x, l.p.x, l.q.x);
+  fwd_combine1(g.S.y, g.p.y, g.q.y, delta, lc.w2.y, l.S.y, l.p.y, l.q.y);
+  return l;
 }
 
 // Adjoint at the start of a segment of `len` steps: its own contribution
 // `local` (accumulated from a zero adjoint) plus the adjoint at the segment end
-// decayed through the segment.
-__device__ __forceinline__ Adj adj_combine(const Adj& local, const Adj& end, int len,
-                                           const Lane& lc) {
-  const float ge = end.G + lc.w2 * static_cast<float>(len);
-  const float g = fmaxf(ge, local.G);
-  const float a = ex2(ge - g), b = ex2(local.G - g);
-  return Adj{g, fmaf(end.gp, a, local.gp * b), fmaf(end.gq, a, local.gq * b)};
+// decayed through the segment, e^{w len} dL/dP_end; the w-derivatives pick up
+// the product rule term len e^{w len} dL/dP_end. One lane; l = local,
+// e = end (overwritten with the result).
+__device__ __forceinline__ void adj_combine1(const float (&l)[5], float (&e)[5], int len,
+                                             float w2) {
+  const float fl = static_cast<float>(len);
+  const float ge = e[0] + w2 * fl;
+  const float g = fmaxf(ge, l[0]);
+  const float a = ex2(ge - g), b = ex2(l[0] - g);
+  const float hp = fmaf(fl, e[1], e[3]), hq = fmaf(fl, e[2], e[4]);
+  e[1] = fmaf(e[1], a, l[1] * b);
+  e[2] = fmaf(e[2], a, l[2] * b);
+  e[3] = fmaf(hp, a, l[3] * b);
+  e[4] = fmaf(hq, a, l[4] * b);
+  e[0] = g;
 }
 
 // One exact step of the state update with per-step rescaling (the second half
-// of the reference loop body, wkv_triton.py:53-58), in log2 units.
+// of the reference loop body, wkv_triton.py:53-58), in log2 units. One lane.
 __device__ __forceinline__ void slow_update(float& o, float& p, float& q, float k, float v,
-                                            const Lane& lc) {
+                                            float w2) {
   const float k2 = k * kL2E;
-  const float wo = lc.w2 + o;
+  const float wo = w2 + o;
   const float no = fmaxf(wo, k2);
   const float a = ex2(wo - no), b = ex2(k2 - no);
   p = fmaf(a, p, b * v);
@@ -221,220 +345,21 @@ __device__ __forceinline__ void slow_update(float& o, float& p, float& q, float 
   o = no;
 }
 
-// Fast-path admissibility for a sub-chunk of L steps starting from state st.
-// s: the sub-chunk scale; p, q: the carried state rescaled to s.
-__device__ __forceinline__ bool fast_ok(const Fwd& st, float kmax, float kmin, int L,
-                                        const Lane& lc, float& s, float& p, float& q) {
-  s = fmaxf(st.S, kmax * kL2E);
-  const float c = ex2(st.S - s);
-  p = st.p * c;
-  q = st.q * c;
+// Fast-path admissibility for one lane over a sub-chunk of L steps starting
+// from state (S, p, q). Outputs the sub-chunk scale s and the carried state
+// rescaled to it.
+__device__ __forceinline__ bool fast_ok1(float S, float p0, float q0, float kmax, float kmin,
+                                         int L, float w2, float u2, float& s, float& p,
+                                         float& q) {
+  s = fmaxf(S, kmax * kL2E);
+  const float c = ex2(S - s);
+  p = p0 * c;
+  q = q0 * c;
   // den_t >= max(q e^{w t}, e^{u + k_t}) / 2^s; e^{k_t}/2^s bounds the q update.
-  const float decayed = q * ex2(lc.w2 * static_cast<float>(L));
-  const float low = fmaf(kmin, kL2E, -s) + fminf(lc.u2, 0.f);
-  return (lc.w2 <= 0.f) && (fabsf(lc.u2) <= 64.f) && (s < 1e30f) &&
+  const float decayed = q * ex2(w2 * static_cast<float>(L));
+  const float low = fmaf(kmin, kL2E, -s) + fminf(u2, 0.f);
+  return (w2 <= 0.f) && (fabsf(u2) <= 64.f) && (s < 1e30f) &&
          (decayed >= 0x1p-60f || low >= -kMargin);
-}
-
-// Masked tree reductions over a sub-chunk held in registers.
-template <bool kTail>
-__device__ __forceinline__ void minmax16(const float (&x)[kSub], int L, float& mx, float& mn) {
-  float a[kSub / 2], b[kSub / 2];
-#pragma unroll
-  for (int i = 0; i < kSub / 2; ++i) {
-    const bool i0 = !kTail || i < L, i1 = !kTail || i + kSub / 2 < L;
-    const float x0 = x[i], x1 = x[i + kSub / 2];
-    a[i] = fmaxf(i0 ? x0 : -INFINITY, i1 ? x1 : -INFINITY);
-    b[i] = fminf(i0 ? x0 : INFINITY, i1 ? x1 : INFINITY);
-  }
-#pragma unroll
-  for (int w = kSub / 4; w > 0; w /= 2) {
-#pragma unroll
-    for (int i = 0; i < w; ++i) {
-      a[i] = fmaxf(a[i], a[i + w]);
-      b[i] = fminf(b[i], b[i + w]);
-    }
-  }
-  mx = a[0];
-  mn = b[0];
-}
-
-template <bool kTail>
-__device__ __forceinline__ float absmax16(const float (&x)[kSub], int L) {
-  float a[kSub / 2];
-#pragma unroll
-  for (int i = 0; i < kSub / 2; ++i) {
-    const bool i0 = !kTail || i < L, i1 = !kTail || i + kSub / 2 < L;
-    a[i] = fmaxf(i0 ? fabsf(x[i]) : 0.f, i1 ? fabsf(x[i + kSub / 2]) : 0.f);
-  }
-#pragma unroll
-  for (int w = kSub / 4; w > 0; w /= 2) {
-#pragma unroll
-    for (int i = 0; i < w; ++i) a[i] = fmaxf(a[i], a[i + w]);
-  }
-  return a[0];
-}
-
-// Loads a sub-chunk column (kSub rows, stride kLanes) into registers. Rows past
-// L inside the staged tile are zero-filled or stale; they are masked by callers.
-template <typename T>
-__device__ __forceinline__ void load16(float (&r)[kSub], const T* src) {
-#pragma unroll
-  for (int i = 0; i < kSub; ++i) r[i] = IOType<T>::ld(src[i * kLanes]);
-}
-
-// ------------------------------------------------------ forward sub-chunk
-//
-// Advances st over L (<= kSub) steps whose k/v sit in shared memory at
-// ks[i*kLanes], vs[i*kLanes]; with kY writes y to ys[i*kLanes]. Inputs are
-// staged into registers first and outputs written last, so the 16 steps are
-// free to overlap (the only true dependency is the p/q recurrence).
-template <typename T, bool kTail, bool kY>
-__device__ __forceinline__ void fwd_sub(Fwd& st, const T* ks, const T* vs, T* ys, int L,
-                                        const Lane& lc, bool force_slow) {
-  using io = IOType<T>;
-  float kr[kSub], vr[kSub], yr[kSub];
-  load16(kr, ks);
-  load16(vr, vs);
-  float kmax, kmin;
-  minmax16<kTail>(kr, L, kmax, kmin);
-  float s, p, q;
-  const bool ok = fast_ok(st, kmax, kmin, kTail ? L : kSub, lc, s, p, q) && !force_slow;
-  if (__all_sync(kFull, ok)) {
-#pragma unroll
-    for (int i = 0; i < kSub; ++i) {
-      if (kTail && i >= L) break;
-      const float ek = ex2(fmaf(kr[i], kL2E, -s));
-      if (kY) {
-        const float eb = ek * lc.eu;
-        yr[i] = fmaf(eb, vr[i], p) * rcp(q + eb);
-      }
-      p = fmaf(lc.ew, p, ek * vr[i]);
-      q = fmaf(lc.ew, q, ek);
-    }
-    st = Fwd{s, p, q};
-  } else {
-    float o = st.S;
-    p = st.p;
-    q = st.q;
-#pragma unroll
-    for (int i = 0; i < kSub; ++i) {
-      if (kTail && i >= L) break;
-      if (kY) {  // reference wkv_triton.py:49-52
-        const float uk = lc.u2 + kr[i] * kL2E;
-        const float no = fmaxf(o, uk);
-        const float a = ex2(o - no), b = ex2(uk - no);
-        yr[i] = fmaf(a, p, b * vr[i]) * rcp(fmaf(a, q, b));
-      }
-      slow_update(o, p, q, kr[i], vr[i], lc);
-    }
-    st = Fwd{o, p, q};
-  }
-  if (kY) {
-#pragma unroll
-    for (int i = 0; i < kSub; ++i)
-      if (!kTail || i < L) ys[i * kLanes] = io::st(yr[i]);
-  }
-}
-
-// ----------------------------------------------------- backward sub-chunk
-//
-// Given the forward state st0 at the sub-chunk start and the adjoint at its end,
-// produces grad_key / grad_value for its L steps (kOut), accumulates
-// gwacc += sum_t (dL/dP_{t+1} P_t + dL/dQ_{t+1} Q_t)  (dL/dw = e^w gwacc) and
-// gu += dL/du, and leaves the adjoint at the sub-chunk start in adj.
-template <typename T, bool kTail, bool kOut>
-__device__ __forceinline__ void bwd_sub(const Fwd& st0, Adj& adj, const T* ks, const T* vs,
-                                        const T* gys, T* gks, T* gvs, int L, const Lane& lc,
-                                        float& gwacc, float& gu, bool force_slow) {
-  using io = IOType<T>;
-  float kr[kSub], vr[kSub], gr[kSub];
-  load16(kr, ks);
-  load16(vr, vs);
-  load16(gr, gys);
-  float kmax, kmin;
-  minmax16<kTail>(kr, L, kmax, kmin);
-  const float gymax = absmax16<kTail>(gr, L);
-  float s, p, q;
-  bool ok = fast_ok(st0, kmax, kmin, kTail ? L : kSub, lc, s, p, q) && !force_slow;
-  // Adjoint rescaled to the sub-chunk scale: dL/dP = 2^{-s} gp.
-  const float f = ex2(adj.G + s);
-  float gp = adj.gp * f, gq = adj.gq * f;
-  ok = ok && (gymax <= 0x1p40f) && (fabsf(gp) <= 0x1p80f) && (fabsf(gq) <= 0x1p80f);
-  if (__all_sync(kFull, ok)) {
-    float ry[kSub], rg[kSub], re[kSub], rp[kSub], rq[kSub];
-    // forward recompute of the sub-chunk
-#pragma unroll
-    for (int i = 0; i < kSub; ++i) {
-      if (kTail && i >= L) break;
-      const float ek = ex2(fmaf(kr[i], kL2E, -s));
-      const float eb = ek * lc.eu;
-      const float rd = rcp(q + eb);
-      ry[i] = fmaf(eb, vr[i], p) * rd;
-      rg[i] = gr[i] * rd;  // gy * 2^s / D_t
-      re[i] = ek;
-      rp[i] = p;
-      rq[i] = q;
-      p = fmaf(lc.ew, p, ek * vr[i]);
-      q = fmaf(lc.ew, q, ek);
-    }
-    // reverse sweep
-#pragma unroll
-    for (int i = kSub - 1; i >= 0; --i) {
-      if (kTail && i >= L) continue;
-      const float v = vr[i];
-      const float a = rg[i] * re[i] * lc.eu;  // gy e^{u+k} / D
-      const float av = a * (v - ry[i]);
-      gu += av;
-      gwacc = fmaf(gp, rp[i], fmaf(gq, rq[i], gwacc));
-      if (kOut) {
-        gvs[i * kLanes] = io::st(fmaf(re[i], gp, a));
-        gks[i * kLanes] = io::st(fmaf(re[i], fmaf(gp, v, gq), av));
-      }
-      gq = fmaf(lc.ew, gq, -rg[i] * ry[i]);
-      gp = fmaf(lc.ew, gp, rg[i]);
-    }
-    adj = Adj{-s, gp, gq};
-  } else {
-    // Exact path: for each step (last to first) replay the forward from st0 with
-    // per-step rescaling (reference wkv_triton.py:93-115), then take the reverse
-    // step of wkv_triton.py:124-142 with its own adjoint log-scale G.
-    float G = adj.G;
-    gp = adj.gp;
-    gq = adj.gq;
-#pragma unroll 1
-    for (int i = L - 1; i >= 0; --i) {
-      float o = st0.S, pp = st0.p, qq = st0.q;
-#pragma unroll 1
-      for (int j = 0; j < i; ++j)
-        slow_update(o, pp, qq, io::ld(ks[j * kLanes]), io::ld(vs[j * kLanes]), lc);
-      const float k = io::ld(ks[i * kLanes]), v = io::ld(vs[i * kLanes]);
-      const float gy = io::ld(gys[i * kLanes]);
-      const float k2 = k * kL2E, uk = lc.u2 + k2;
-      const float no = fmaxf(o, uk);
-      const float a = ex2(o - no), b = ex2(uk - no);
-      const float iden = rcp(fmaf(a, qq, b));
-      const float y = fmaf(a, pp, b * v) * iden;
-      const float A = gy * iden * b;
-      const float av = A * (v - y);
-      gu += av;
-      const float t = fmaf(gp, pp, gq * qq);
-      if (t != 0.f) gwacc = fmaf(ex2(o + G), t, gwacc);
-      if (kOut) {
-        const float ekg = (gp != 0.f || gq != 0.f) ? ex2(k2 + G) : 0.f;
-        gvs[i * kLanes] = io::st(fmaf(ekg, gp, A));
-        gks[i * kLanes] = io::st(fmaf(ekg, fmaf(gp, v, gq), av));
-      }
-      // dL/dP_t = gy / D_t + e^w dL/dP_{t+1}, with 1/D_t = iden 2^{-no}
-      const float ng = fmaxf(lc.w2 + G, -no);
-      const float aa = ex2(lc.w2 + G - ng);
-      const float bb = ex2(-no - ng) * gy * iden;
-      gp = fmaf(aa, gp, bb);
-      gq = fmaf(aa, gq, -bb * y);
-      G = ng;
-    }
-    adj = Adj{G, gp, gq};
-  }
 }
 
 }  // namespace wkv

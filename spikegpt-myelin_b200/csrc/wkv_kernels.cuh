@@ -1,12 +1,13 @@
 // WKV kernels for sm_100a.
 //
-// One CTA = one warp = 32 consecutive channels of one batch row; one thread per
-// (b, c) lane. Each CTA walks its time range in tiles of kTile steps. On the TMA
-// path a single elected lane streams [kTile x 32] tiles of every input through a
-// multi-stage ring of shared-memory buffers (cp.async.bulk.tensor + mbarrier
-// complete_tx) and writes output tiles back with bulk tensor stores; on the
-// generic path (C*sizeof(dtype) not a multiple of 16, or unaligned pointers) the
-// lanes fill the same tiles with plain loads.
+// One CTA = one warp = 64 consecutive channels of one batch row; each thread
+// owns two adjacent channels (a lane pair). A CTA walks its time range in tiles
+// of Pair<T>::kTileRows steps. On the TMA path a single elected lane streams
+// [rows x 64] tiles of every input through a multi-stage ring of shared-memory
+// buffers (cp.async.bulk.tensor + mbarrier complete_tx) and writes output tiles
+// back with bulk tensor stores; on the generic path (C*sizeof(dtype) not a
+// multiple of 16, or unaligned pointers) the lanes fill the same tiles with
+// plain loads.
 //
 // Time can be split into segments (blockIdx.y) so that small B*C still fills
 // the GPU: a segment is processed from a start state produced by a carry pass
@@ -27,25 +28,30 @@
 //   wkv_carry_adj_kernel         adjoint summaries -> adjoint at segment ends
 #pragma once
 
-#include "wkv_device.cuh"
+#include "wkv_sub.cuh"
 
 namespace wkv {
 
 template <typename T>
-struct Stages {
-  static constexpr int fwd = sizeof(T) == 4 ? 3 : 4;
-  static constexpr int bwd = sizeof(T) == 4 ? 2 : 3;
+struct Cfg {
+  static constexpr int kRows = Pair<T>::kTileRows;  // steps per staged tile
+  static constexpr int kTileElems = kRows * kLanes;
+  static constexpr uint32_t kTileBytes = kTileElems * sizeof(T);
+  static constexpr int kSubPerTile = kRows / kSub;
+  static constexpr int kFwdStages = 4;
+  static constexpr int kBwdStages = 3;
+  static_assert(kRows % kSub == 0 && kSegAlign % kRows == 0, "tile/segment alignment");
 };
 
 template <typename T>
 constexpr size_t fwd_smem_bytes(bool y) {
-  return (size_t)(2 * Stages<T>::fwd + (y ? 2 : 0)) * kTile * kLanes * sizeof(T) +
-         8 * Stages<T>::fwd;
+  return (size_t)(2 * Cfg<T>::kFwdStages + (y ? 2 : 0)) * Cfg<T>::kTileBytes +
+         8 * Cfg<T>::kFwdStages;
 }
 template <typename T>
 constexpr size_t bwd_smem_bytes(bool out) {
-  return (size_t)(3 * Stages<T>::bwd + (out ? 4 : 0)) * kTile * kLanes * sizeof(T) +
-         8 * Stages<T>::bwd;
+  return (size_t)(3 * Cfg<T>::kBwdStages + (out ? 4 : 0)) * Cfg<T>::kTileBytes +
+         8 * Cfg<T>::kBwdStages;
 }
 
 struct FwdArgs {
@@ -57,7 +63,7 @@ struct FwdArgs {
   int decay_is_w;
   int B, T, C;
   int ncblk;     // ceil(C / kLanes)
-  int seg_len;   // steps per segment (a multiple of kTile unless nseg == 1)
+  int seg_len;   // steps per segment (a multiple of kSegAlign unless nseg == 1)
   int nseg;      // segments per lane
   int seg_base;  // segment of blockIdx.y == 0
   int nsub;      // checkpoint rows per batch row: ceil(T / kSub)
@@ -82,8 +88,8 @@ struct BwdArgs {
   int ncblk, seg_len, nseg, seg_base, nsub;
   const float* ckpt;       // [B][nsub][3][C]: true states, or states local to the segment
   const float* seg_start;  // [B][nseg][3][C] (ckpt is segment-local when non-null)
-  const float* adj_in;     // [B][nseg][3][C] adjoint at segment ends, or null (zero)
-  float* adj_out;          // [B][nseg][3][C] adjoint at segment starts, or null
+  const float* adj_in;     // [B][nseg][5][C] adjoint at segment ends, or null (zero)
+  float* adj_out;          // [B][nseg][5][C] adjoint at segment starts, or null
   float* partial;          // [B][nseg][2][C] (gwacc, gu) per lane-segment, or null
   unsigned* tickets;       // [ncblk] arrival counters (zeroed beforehand), or null
   float* gtd;              // [C] grad_time_decay, written by the last CTA of a column block
@@ -92,42 +98,79 @@ struct BwdArgs {
   unsigned* err;
 };
 
-__device__ __forceinline__ Fwd load_fwd(const float* base, size_t row, int C, int c) {
+// Rows of 3 [C] planes ([row][3][C] floats) for the two channels c, c+1.
+__device__ __forceinline__ void load3(const float* base, size_t row, int C, int c, bool v0,
+                                      bool v1, f2& a, f2& b, f2& d) {
   const float* r = base + row * 3 * (size_t)C + c;
-  return Fwd{r[0], r[C], r[2 * (size_t)C]};
+  if (v0) {
+    a.x = r[0];
+    b.x = r[C];
+    d.x = r[2 * (size_t)C];
+  }
+  if (v1) {
+    a.y = r[1];
+    b.y = r[C + 1];
+    d.y = r[2 * (size_t)C + 1];
+  }
 }
-__device__ __forceinline__ void store_fwd(float* base, size_t row, int C, int c, const Fwd& s) {
+__device__ __forceinline__ void store3(float* base, size_t row, int C, int c, bool v0, bool v1,
+                                       f2 a, f2 b, f2 d) {
   float* r = base + row * 3 * (size_t)C + c;
-  r[0] = s.S;
-  r[C] = s.p;
-  r[2 * (size_t)C] = s.q;
-}
-__device__ __forceinline__ Adj load_adj(const float* base, size_t row, int C, int c) {
-  const float* r = base + row * 3 * (size_t)C + c;
-  return Adj{r[0], r[C], r[2 * (size_t)C]};
-}
-__device__ __forceinline__ void store_adj(float* base, size_t row, int C, int c, const Adj& s) {
-  float* r = base + row * 3 * (size_t)C + c;
-  r[0] = s.G;
-  r[C] = s.gp;
-  r[2 * (size_t)C] = s.gq;
+  if (v0) {
+    r[0] = a.x;
+    r[C] = b.x;
+    r[2 * (size_t)C] = d.x;
+  }
+  if (v1) {
+    r[1] = a.y;
+    r[C + 1] = b.y;
+    r[2 * (size_t)C + 1] = d.y;
+  }
 }
 
-// Generic path: the warp fills rows [0, rows) of a [kTile][kLanes] tile.
+// Rows of 5 [C] planes (an Adj2) for the two channels c, c+1.
+__device__ __forceinline__ void load_adj(const float* base, size_t row, int C, int c, bool v0,
+                                         bool v1, Adj2& a) {
+  f2* f[5] = {&a.G, &a.gp, &a.gq, &a.hp, &a.hq};
+  const float* r = base + row * 5 * (size_t)C + c;
+#pragma unroll
+  for (int i = 0; i < 5; ++i) {
+    if (v0) f[i]->x = r[i * (size_t)C];
+    if (v1) f[i]->y = r[i * (size_t)C + 1];
+  }
+}
+__device__ __forceinline__ void store_adj(float* base, size_t row, int C, int c, bool v0, bool v1,
+                                          const Adj2& a) {
+  const f2 f[5] = {a.G, a.gp, a.gq, a.hp, a.hq};
+  float* r = base + row * 5 * (size_t)C + c;
+#pragma unroll
+  for (int i = 0; i < 5; ++i) {
+    if (v0) r[i * (size_t)C] = f[i].x;
+    if (v1) r[i * (size_t)C + 1] = f[i].y;
+  }
+}
+
+// Generic path: the warp fills rows [0, rows) of a [rows][kLanes] tile.
 template <typename T>
 __device__ __forceinline__ void fill_tile(T* tile, const T* src, int b, int t0, int rows, int T_,
-                                          int C, int c, bool cval, int lane) {
+                                          int C, int c, bool v0, bool v1, int lane) {
   const size_t base = ((size_t)b * T_ + t0) * C + c;
+  const T zero = Pair<T>::from_float(0.f);
 #pragma unroll 4
-  for (int r = 0; r < rows; ++r) tile[r * kLanes + lane] = cval ? src[base + (size_t)r * C] : T(0.f);
+  for (int r = 0; r < rows; ++r) {
+    tile[r * kLanes + 2 * lane] = v0 ? src[base + (size_t)r * C] : zero;
+    tile[r * kLanes + 2 * lane + 1] = v1 ? src[base + (size_t)r * C + 1] : zero;
+  }
 }
 template <typename T>
 __device__ __forceinline__ void drain_tile(const T* tile, T* dst, int b, int t0, int rows, int T_,
-                                           int C, int c, bool cval, int lane) {
-  if (!cval) return;
+                                           int C, int c, bool v0, bool v1, int lane) {
   const size_t base = ((size_t)b * T_ + t0) * C + c;
 #pragma unroll 4
-  for (int r = 0; r < rows; ++r) dst[base + (size_t)r * C] = tile[r * kLanes + lane];
+  for (int r = 0; r < rows; ++r) {
+    if (v0) dst[base + (size_t)r * C] = tile[r * kLanes + 2 * lane];
+    if (v1) dst[base + (size_t)r * C + 1] = tile[r * kLanes + 2 * lane + 1];
+  }
 }
 
 __device__ __forceinline__ void report_timeout(unsigned* err) {
@@ -137,42 +180,73 @@ __device__ __forceinline__ void report_timeout(unsigned* err) {
 // ------------------------------------------------------------------ forward
 
 template <typename T, bool kY, bool kTma>
-__global__ void __launch_bounds__(kLanes)
+__global__ void __launch_bounds__(kThreads)
     wkv_fwd_kernel(const FwdArgs a, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap ty) {
-  constexpr int S = Stages<T>::fwd;
-  constexpr int kTileElems = kTile * kLanes;
-  constexpr uint32_t kTileBytes = kTileElems * sizeof(T);
+  using G = Cfg<T>;
+  constexpr int S = G::kFwdStages;
   extern __shared__ __align__(128) unsigned char smem[];
   T* kbuf = reinterpret_cast<T*>(smem);
-  T* vbuf = kbuf + S * kTileElems;
-  T* ybuf = vbuf + S * kTileElems;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ybuf + (kY ? 2 : 0) * kTileElems);
+  T* vbuf = kbuf + S * G::kTileElems;
+  T* ybuf = vbuf + S * G::kTileElems;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ybuf + (kY ? 2 : 0) * G::kTileElems);
 
   const int lane = threadIdx.x;
   const int cb = blockIdx.x % a.ncblk, b = blockIdx.x / a.ncblk;
-  const int c = cb * kLanes + lane;
+  const int c = cb * kLanes + 2 * lane;
   const int seg = blockIdx.y + a.seg_base;
-  const bool cval = c < a.C;
-  const float dec = cval ? a.decay[c] : 0.f;
-  const Lane lc = make_lane(a.decay_is_w ? dec : -expf(dec), cval ? a.u[c] : 0.f);
+  const bool v0 = c < a.C, v1 = c + 1 < a.C;
+  f2 dec = splat(0.f), uu = splat(0.f);
+  if (v0) {
+    dec.x = a.decay[c];
+    uu.x = a.u[c];
+  }
+  if (v1) {
+    dec.y = a.decay[c + 1];
+    uu.y = a.u[c + 1];
+  }
+  if (!a.decay_is_w) dec = f2{-expf(dec.x), -expf(dec.y)};
+  const Lane2 lc = make_lane2(dec, uu);
   const int t_begin = seg * a.seg_len;
   const int t_end = min(a.T, t_begin + a.seg_len);
-  const int ntiles = (t_end - t_begin + kTile - 1) / kTile;
+  const int ntiles = (t_end - t_begin + G::kRows - 1) / G::kRows;
   const bool force_slow = a.force_slow != 0;
 
   if (a.zero_tickets != nullptr && blockIdx.x == 0 && blockIdx.y == 0)
-    for (int i = lane; i < a.nzero; i += kLanes) a.zero_tickets[i] = 0u;
+    for (int i = lane; i < a.nzero; i += kThreads) a.zero_tickets[i] = 0u;
 
-  Fwd st = fwd_identity();
-  if (a.seg_start != nullptr && cval) st = load_fwd(a.seg_start, (size_t)b * a.nseg + seg, a.C, c);
+  Fwd2 st = fwd_identity2();
+  if (a.seg_start != nullptr)
+    load3(a.seg_start, (size_t)b * a.nseg + seg, a.C, c, v0, v1, st.S, st.p, st.q);
 
   auto issue = [&](int j) {
     const int s = j % S;
-    mbar_arrive_expect_tx(&bars[s], 2 * kTileBytes);
-    const int t0 = t_begin + j * kTile;
-    tma_load_3d(kbuf + s * kTileElems, &tk, &bars[s], cb * kLanes, t0, b);
-    tma_load_3d(vbuf + s * kTileElems, &tv, &bars[s], cb * kLanes, t0, b);
+    mbar_arrive_expect_tx(&bars[s], 2 * G::kTileBytes);
+    const int t0 = t_begin + j * G::kRows;
+    tma_load_3d(kbuf + s * G::kTileElems, &tk, &bars[s], cb * kLanes, t0, b);
+    tma_load_3d(vbuf + s * G::kTileElems, &tv, &bars[s], cb * kLanes, t0, b);
+  };
+  // Makes tile j resident (waits for its copy, or fills it on the generic path).
+  // On a copy timeout it records the error, drains the copies it issued and
+  // returns false; the caller then exits.
+  auto acquire = [&](int j) -> bool {
+    const int s = j % S;
+    if (kTma) {
+      const bool ok = mbar_wait_bounded(&bars[s], (j / S) & 1);
+      if (!__all_sync(kFull, ok)) {
+        if (lane == 0) report_timeout(a.err);
+        for (int r = j + 1; r < min(j + S, ntiles); ++r) mbar_wait_bounded(&bars[r % S], (r / S) & 1);
+        if (kY && lane == 0) bulk_wait_all();
+        return false;
+      }
+    } else {
+      const int t0 = t_begin + j * G::kRows;
+      const int rows = min(G::kRows, t_end - t0);
+      fill_tile(kbuf + s * G::kTileElems, static_cast<const T*>(a.k), b, t0, rows, a.T, a.C, c, v0, v1, lane);
+      fill_tile(vbuf + s * G::kTileElems, static_cast<const T*>(a.v), b, t0, rows, a.T, a.C, c, v0, v1, lane);
+      __syncwarp();
+    }
+    return true;
   };
   if (kTma) {
     if (lane == 0) {
@@ -187,43 +261,25 @@ __global__ void __launch_bounds__(kLanes)
       for (int j = 0; j < min(S, ntiles); ++j) issue(j);
   }
 
+#pragma unroll 1
   for (int j = 0; j < ntiles; ++j) {
-    const int s = j % S;
-    const int t0 = t_begin + j * kTile;
-    const int rows = min(kTile, t_end - t0);
-    T* ks = kbuf + s * kTileElems;
-    T* vs = vbuf + s * kTileElems;
-    T* ys = ybuf + (j & 1) * kTileElems;
-    if (kTma) {
-      const bool ok = mbar_wait_bounded(&bars[s], (j / S) & 1);
-      if (!__all_sync(kFull, ok)) {
-        if (lane == 0) report_timeout(a.err);
-        for (int r = j + 1; r < min(j + S, ntiles); ++r) mbar_wait_bounded(&bars[r % S], (r / S) & 1);
-        if (kY && lane == 0) bulk_wait_all();
-        return;
-      }
-      if (kY && j >= 2) {  // ys was last read by the store of tile j-2
-        if (lane == 0) bulk_wait_read<1>();
-        __syncwarp();
-      }
-    } else {
-      fill_tile(ks, static_cast<const T*>(a.k), b, t0, rows, a.T, a.C, c, cval, lane);
-      fill_tile(vs, static_cast<const T*>(a.v), b, t0, rows, a.T, a.C, c, cval, lane);
+    const int sidx = j % S;
+    const int t0 = t_begin + j * G::kRows;
+    const int rows = min(G::kRows, t_end - t0);
+    if (!acquire(j)) return;
+    T* ys = ybuf + (j & 1) * G::kTileElems;
+    if (kY && kTma && j >= 2) {  // ys was last read by the store of tile j-2
+      if (lane == 0) bulk_wait_read<1>();
       __syncwarp();
     }
-#pragma unroll 1
-    for (int sb = 0; sb < kSubPerTile; ++sb) {
-      const int r0 = sb * kSub;
-      if (r0 >= rows) break;
-      const int L = min(kSub, rows - r0);
-      if (!kY && a.ckpt != nullptr && cval)
-        store_fwd(a.ckpt, (size_t)b * a.nsub + (t0 + r0) / kSub, a.C, c, st);
-      const int off = r0 * kLanes + lane;
-      if (L == kSub)
-        fwd_sub<T, false, kY>(st, ks + off, vs + off, ys + off, L, lc, force_slow);
-      else
-        fwd_sub<T, true, kY>(st, ks + off, vs + off, ys + off, L, lc, force_slow);
-    }
+    const int off = 2 * lane;
+    const size_t ck_row0 = (size_t)b * a.nsub + t0 / kSub;
+    if (rows == G::kRows)
+      fwd_tile2<T, false, kY>(st, kbuf + sidx * G::kTileElems + off, vbuf + sidx * G::kTileElems + off,
+                              ys + off, rows, lc, force_slow, a.ckpt, ck_row0, a.C, c, v0, v1);
+    else
+      fwd_tile2<T, true, kY>(st, kbuf + sidx * G::kTileElems + off, vbuf + sidx * G::kTileElems + off,
+                             ys + off, rows, lc, force_slow, a.ckpt, ck_row0, a.C, c, v0, v1);
     if (kY) {
       if (kTma) {
         fence_proxy_async_smem();
@@ -234,66 +290,96 @@ __global__ void __launch_bounds__(kLanes)
         }
       } else {
         __syncwarp();
-        drain_tile(ys, static_cast<T*>(a.y), b, t0, rows, a.T, a.C, c, cval, lane);
+        drain_tile(ys, static_cast<T*>(a.y), b, t0, rows, a.T, a.C, c, v0, v1, lane);
       }
     }
     __syncwarp();
     if (kTma && lane == 0 && j + S < ntiles) issue(j + S);
   }
   if (kTma && kY && lane == 0) bulk_wait_all();
-  if (a.seg_end != nullptr && cval) store_fwd(a.seg_end, (size_t)b * a.nseg + seg, a.C, c, st);
+  if (a.seg_end != nullptr)
+    store3(a.seg_end, (size_t)b * a.nseg + seg, a.C, c, v0, v1, st.S, st.p, st.q);
 }
 
 // ----------------------------------------------------------------- backward
 
 template <typename T, bool kOut, bool kTma>
-__global__ void __launch_bounds__(kLanes)
+__global__ void __launch_bounds__(kThreads)
     wkv_bwd_kernel(const BwdArgs a, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tgy,
                    const __grid_constant__ CUtensorMap tgk,
                    const __grid_constant__ CUtensorMap tgv) {
-  constexpr int S = Stages<T>::bwd;
-  constexpr int kTileElems = kTile * kLanes;
-  constexpr uint32_t kTileBytes = kTileElems * sizeof(T);
+  using G = Cfg<T>;
+  constexpr int S = G::kBwdStages;
   extern __shared__ __align__(128) unsigned char smem[];
   T* kbuf = reinterpret_cast<T*>(smem);
-  T* vbuf = kbuf + S * kTileElems;
-  T* gybuf = vbuf + S * kTileElems;
-  T* gkbuf = gybuf + S * kTileElems;  // [2][tile] when kOut
-  T* gvbuf = gkbuf + (kOut ? 2 : 0) * kTileElems;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(gvbuf + (kOut ? 2 : 0) * kTileElems);
+  T* vbuf = kbuf + S * G::kTileElems;
+  T* gybuf = vbuf + S * G::kTileElems;
+  T* gkbuf = gybuf + S * G::kTileElems;  // [2][tile] when kOut
+  T* gvbuf = gkbuf + (kOut ? 2 : 0) * G::kTileElems;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(gvbuf + (kOut ? 2 : 0) * G::kTileElems);
 
   const int lane = threadIdx.x;
   const int cb = blockIdx.x % a.ncblk, b = blockIdx.x / a.ncblk;
-  const int c = cb * kLanes + lane;
+  const int c = cb * kLanes + 2 * lane;
   const int seg = blockIdx.y + a.seg_base;
-  const bool cval = c < a.C;
-  const Lane lc = make_lane(cval ? a.w[c] : 0.f, cval ? a.u[c] : 0.f);
+  const bool v0 = c < a.C, v1 = c + 1 < a.C;
+  f2 ww = splat(0.f), uu = splat(0.f);
+  if (v0) {
+    ww.x = a.w[c];
+    uu.x = a.u[c];
+  }
+  if (v1) {
+    ww.y = a.w[c + 1];
+    uu.y = a.u[c + 1];
+  }
+  const Lane2 lc = make_lane2(ww, uu);
   const int t_begin = seg * a.seg_len;
   const int t_end = min(a.T, t_begin + a.seg_len);
-  const int ntiles = (t_end - t_begin + kTile - 1) / kTile;
+  const int ntiles = (t_end - t_begin + G::kRows - 1) / G::kRows;
   const bool force_slow = a.force_slow != 0;
   const size_t lseg = (size_t)b * a.nseg + seg;
 
-  Adj adj = adj_zero();
-  if (a.adj_in != nullptr && cval) adj = load_adj(a.adj_in, lseg, a.C, c);
-  Fwd segst = fwd_identity();
-  if (a.seg_start != nullptr && cval) segst = load_fwd(a.seg_start, lseg, a.C, c);
-  float gwacc = 0.f, gu = 0.f;
+  Adj2 adj = adj_zero2();
+  if (a.adj_in != nullptr) load_adj(a.adj_in, lseg, a.C, c, v0, v1, adj);
+  Fwd2 segst = fwd_identity2();
+  if (a.seg_start != nullptr) load3(a.seg_start, lseg, a.C, c, v0, v1, segst.S, segst.p, segst.q);
+  f2 gwacc = splat(0.f), gu = splat(0.f);
   // Checkpoints are loaded one sub-chunk ahead of their use (sub-chunks are
   // visited last to first, kSub steps apart).
   const int t_last = t_begin + ((t_end - t_begin - 1) / kSub) * kSub;
-  Fwd pend = fwd_identity();
-  if (cval) pend = load_fwd(a.ckpt, (size_t)b * a.nsub + t_last / kSub, a.C, c);
+  Fwd2 pend = fwd_identity2();
+  load3(a.ckpt, (size_t)b * a.nsub + t_last / kSub, a.C, c, v0, v1, pend.S, pend.p, pend.q);
 
   // Tiles are visited last to first; the jj-th visited tile is j = ntiles-1-jj.
   auto issue = [&](int jj) {
     const int s = jj % S;
-    const int t0 = t_begin + (ntiles - 1 - jj) * kTile;
-    mbar_arrive_expect_tx(&bars[s], 3 * kTileBytes);
-    tma_load_3d(kbuf + s * kTileElems, &tk, &bars[s], cb * kLanes, t0, b);
-    tma_load_3d(vbuf + s * kTileElems, &tv, &bars[s], cb * kLanes, t0, b);
-    tma_load_3d(gybuf + s * kTileElems, &tgy, &bars[s], cb * kLanes, t0, b);
+    const int t0 = t_begin + (ntiles - 1 - jj) * G::kRows;
+    mbar_arrive_expect_tx(&bars[s], 3 * G::kTileBytes);
+    tma_load_3d(kbuf + s * G::kTileElems, &tk, &bars[s], cb * kLanes, t0, b);
+    tma_load_3d(vbuf + s * G::kTileElems, &tv, &bars[s], cb * kLanes, t0, b);
+    tma_load_3d(gybuf + s * G::kTileElems, &tgy, &bars[s], cb * kLanes, t0, b);
+  };
+  auto acquire = [&](int jj) -> bool {
+    const int s = jj % S;
+    if (kTma) {
+      const bool ok = mbar_wait_bounded(&bars[s], (jj / S) & 1);
+      if (!__all_sync(kFull, ok)) {
+        if (lane == 0) report_timeout(a.err);
+        for (int r = jj + 1; r < min(jj + S, ntiles); ++r)
+          mbar_wait_bounded(&bars[r % S], (r / S) & 1);
+        if (kOut && lane == 0) bulk_wait_all();
+        return false;
+      }
+    } else {
+      const int t0 = t_begin + (ntiles - 1 - jj) * G::kRows;
+      const int rows = min(G::kRows, t_end - t0);
+      fill_tile(kbuf + s * G::kTileElems, static_cast<const T*>(a.k), b, t0, rows, a.T, a.C, c, v0, v1, lane);
+      fill_tile(vbuf + s * G::kTileElems, static_cast<const T*>(a.v), b, t0, rows, a.T, a.C, c, v0, v1, lane);
+      fill_tile(gybuf + s * G::kTileElems, static_cast<const T*>(a.gy), b, t0, rows, a.T, a.C, c, v0, v1, lane);
+      __syncwarp();
+    }
+    return true;
   };
   if (kTma) {
     if (lane == 0) {
@@ -312,51 +398,42 @@ __global__ void __launch_bounds__(kLanes)
       for (int jj = 0; jj < min(S, ntiles); ++jj) issue(jj);
   }
 
+#pragma unroll 1
   for (int jj = 0; jj < ntiles; ++jj) {
     const int j = ntiles - 1 - jj;
-    const int s = jj % S;
-    const int t0 = t_begin + j * kTile;
-    const int rows = min(kTile, t_end - t0);
-    T* ks = kbuf + s * kTileElems;
-    T* vs = vbuf + s * kTileElems;
-    T* gys = gybuf + s * kTileElems;
-    T* gks = gkbuf + (jj & 1) * kTileElems;
-    T* gvs = gvbuf + (jj & 1) * kTileElems;
-    if (kTma) {
-      const bool ok = mbar_wait_bounded(&bars[s], (jj / S) & 1);
-      if (!__all_sync(kFull, ok)) {
-        if (lane == 0) report_timeout(a.err);
-        for (int r = jj + 1; r < min(jj + S, ntiles); ++r)
-          mbar_wait_bounded(&bars[r % S], (r / S) & 1);
-        if (kOut && lane == 0) bulk_wait_all();
-        return;
-      }
-      if (kOut && jj >= 2) {
-        if (lane == 0) bulk_wait_read<1>();
-        __syncwarp();
-      }
-    } else {
-      fill_tile(ks, static_cast<const T*>(a.k), b, t0, rows, a.T, a.C, c, cval, lane);
-      fill_tile(vs, static_cast<const T*>(a.v), b, t0, rows, a.T, a.C, c, cval, lane);
-      fill_tile(gys, static_cast<const T*>(a.gy), b, t0, rows, a.T, a.C, c, cval, lane);
+    const int sidx = jj % S;
+    const int t0 = t_begin + j * G::kRows;
+    const int rows = min(G::kRows, t_end - t0);
+    if (!acquire(jj)) return;
+    T* gks = gkbuf + (jj & 1) * G::kTileElems;
+    T* gvs = gvbuf + (jj & 1) * G::kTileElems;
+    if (kOut && kTma && jj >= 2) {
+      if (lane == 0) bulk_wait_read<1>();  // gks/gvs were last read by tile jj-2's store
       __syncwarp();
     }
 #pragma unroll 1
-    for (int sb = kSubPerTile - 1; sb >= 0; --sb) {
+    for (int sb = G::kSubPerTile - 1; sb >= 0; --sb) {
       const int r0 = sb * kSub;
       if (r0 >= rows) continue;
       const int L = min(kSub, rows - r0);
       const int t = t0 + r0;
-      Fwd st = pend;
-      if (cval && t - kSub >= t_begin) pend = load_fwd(a.ckpt, (size_t)b * a.nsub + (t - kSub) / kSub, a.C, c);
-      if (a.seg_start != nullptr) st = (t == t_begin) ? segst : fwd_combine(segst, t - t_begin, lc, st);
-      const int off = r0 * kLanes + lane;
-      if (L == kSub)
-        bwd_sub<T, false, kOut>(st, adj, ks + off, vs + off, gys + off, gks + off, gvs + off, L,
-                                lc, gwacc, gu, force_slow);
-      else
-        bwd_sub<T, true, kOut>(st, adj, ks + off, vs + off, gys + off, gks + off, gvs + off, L,
-                               lc, gwacc, gu, force_slow);
+      Fwd2 st = pend;
+      if (t - kSub >= t_begin)
+        load3(a.ckpt, (size_t)b * a.nsub + (t - kSub) / kSub, a.C, c, v0, v1, pend.S, pend.p, pend.q);
+      if (a.seg_start != nullptr) st = (t == t_begin) ? segst : fwd_combine2(segst, t - t_begin, lc, st);
+      const int off = r0 * kLanes + 2 * lane;
+      const T* ks = kbuf + sidx * G::kTileElems + off;
+      const T* vs = vbuf + sidx * G::kTileElems + off;
+      const T* gys = gybuf + sidx * G::kTileElems + off;
+      if (L == kSub) {
+        const Pre pre = prescan<T, false, true>(ks, gys, L);
+        bwd_sub2<T, false, kOut>(st, pre, adj, ks, vs, gys, gks + off, gvs + off, L, lc, gwacc, gu,
+                                 force_slow);
+      } else {
+        const Pre pre = prescan<T, true, true>(ks, gys, L);
+        bwd_sub2<T, true, kOut>(st, pre, adj, ks, vs, gys, gks + off, gvs + off, L, lc, gwacc, gu,
+                                force_slow);
+      }
     }
     if (kOut) {
       if (kTma) {
@@ -369,24 +446,30 @@ __global__ void __launch_bounds__(kLanes)
         }
       } else {
         __syncwarp();
-        drain_tile(gks, static_cast<T*>(a.gk), b, t0, rows, a.T, a.C, c, cval, lane);
-        drain_tile(gvs, static_cast<T*>(a.gv), b, t0, rows, a.T, a.C, c, cval, lane);
+        drain_tile(gks, static_cast<T*>(a.gk), b, t0, rows, a.T, a.C, c, v0, v1, lane);
+        drain_tile(gvs, static_cast<T*>(a.gv), b, t0, rows, a.T, a.C, c, v0, v1, lane);
       }
     }
     __syncwarp();
     if (kTma && lane == 0 && jj + S < ntiles) issue(jj + S);
   }
   if (kTma && kOut && lane == 0) bulk_wait_all();
-  if (cval && a.adj_out != nullptr) store_adj(a.adj_out, lseg, a.C, c, adj);
+  if (a.adj_out != nullptr) store_adj(a.adj_out, lseg, a.C, c, v0, v1, adj);
   if (a.partial == nullptr) return;
-  if (cval) {
+  {
     float* r = a.partial + lseg * 2 * (size_t)a.C + c;
-    r[0] = gwacc;
-    r[a.C] = gu;
+    if (v0) {
+      r[0] = gwacc.x;
+      r[a.C] = gu.x;
+    }
+    if (v1) {
+      r[1] = gwacc.y;
+      r[a.C + 1] = gu.y;
+    }
   }
   if (a.tickets == nullptr) return;
   // The last CTA of this column block to finish sums every (b, segment) row in
-  // a fixed order: grad_time_decay = w e^w sum gwacc (dL/dw * w, reference
+  // a fixed order: grad_time_decay = w sum gwacc (dL/dw * w, reference
   // wkv_triton.py:117,194), grad_time_first = sum gu. No CTA waits for another.
   __threadfence();
   __syncwarp();
@@ -396,28 +479,54 @@ __global__ void __launch_bounds__(kLanes)
   const int rows = a.B * a.nseg;
   if (ticket + 1 != static_cast<unsigned>(rows)) return;
   __threadfence();
-  if (!cval) return;
-  double sw = 0.0, su = 0.0;
+  if (lane == 0) a.tickets[cb] = 0u;  // ready for a later call that reuses the counters
+  double sw0 = 0.0, su0 = 0.0, sw1 = 0.0, su1 = 0.0;
   const float* base = a.partial + c;
-  for (int r0 = 0; r0 < rows; r0 += 16) {
-    float pw[16], pu[16];
+  for (int r0 = 0; r0 < rows; r0 += 8) {
+    float pw0[8], pu0[8], pw1[8], pu1[8];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < 8; ++i) {
       const bool in = r0 + i < rows;
-      pw[i] = in ? __ldcg(base + (size_t)(r0 + i) * 2 * a.C) : 0.f;
-      pu[i] = in ? __ldcg(base + ((size_t)(r0 + i) * 2 + 1) * a.C) : 0.f;
+      const size_t o = (size_t)(r0 + i) * 2 * a.C;
+      pw0[i] = (in && v0) ? __ldcg(base + o) : 0.f;
+      pu0[i] = (in && v0) ? __ldcg(base + o + a.C) : 0.f;
+      pw1[i] = (in && v1) ? __ldcg(base + o + 1) : 0.f;
+      pu1[i] = (in && v1) ? __ldcg(base + o + a.C + 1) : 0.f;
     }
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      sw += pw[i];
-      su += pu[i];
+    for (int i = 0; i < 8; ++i) {
+      sw0 += pw0[i];
+      su0 += pu0[i];
+      sw1 += pw1[i];
+      su1 += pu1[i];
     }
   }
-  a.gtd[c] = static_cast<float>(static_cast<double>(lc.w) * static_cast<double>(lc.ew) * sw);
-  a.gtf[c] = static_cast<float>(su);
+  if (v0) {
+    a.gtd[c] = static_cast<float>(static_cast<double>(lc.w.x) * sw0);
+    a.gtf[c] = static_cast<float>(su0);
+  }
+  if (v1) {
+    a.gtd[c + 1] = static_cast<float>(static_cast<double>(lc.w.y) * sw1);
+    a.gtf[c + 1] = static_cast<float>(su1);
+  }
 }
 
 // ------------------------------------------------------------------- carries
+
+__device__ __forceinline__ void load3s(const float* base, size_t row, int C, int c, float& a,
+                                       float& b, float& d) {
+  const float* r = base + row * 3 * (size_t)C + c;
+  a = r[0];
+  b = r[C];
+  d = r[2 * (size_t)C];
+}
+__device__ __forceinline__ void store3s(float* base, size_t row, int C, int c, float a, float b,
+                                        float d) {
+  float* r = base + row * 3 * (size_t)C + c;
+  r[0] = a;
+  r[C] = b;
+  r[2 * (size_t)C] = d;
+}
 
 // In place over seg[B][nseg][3][C]: entry s holds the state a segment reaches
 // from zero (its summary); on exit it holds the true state at the segment start.
@@ -427,18 +536,23 @@ __global__ void wkv_carry_fwd_kernel(float* seg, const float* decay, int decay_i
   if (i >= (int64_t)B * C) return;
   const int b = static_cast<int>(i / C), c = static_cast<int>(i % C);
   const float d = decay[c];
-  const Lane lc = make_lane(decay_is_w ? d : -expf(d), 0.f);
-  Fwd st = fwd_identity();
+  const float w2 = (decay_is_w ? d : -expf(d)) * kL2E;
+  float S = kNegBig, p = 0.f, q = 0.f;
   for (int s = 0; s < nseg; ++s) {
     const size_t row = (size_t)b * nseg + s;
-    Fwd sum = fwd_identity();
-    if (s + 1 < nseg) sum = load_fwd(seg, row, C, c);
-    store_fwd(seg, row, C, c, st);
-    if (s + 1 < nseg) st = fwd_combine(st, min(seg_len, T - s * seg_len), lc, sum);
+    float lS = kNegBig, lp = 0.f, lq = 0.f;
+    if (s + 1 < nseg) load3s(seg, row, C, c, lS, lp, lq);
+    store3s(seg, row, C, c, S, p, q);
+    if (s + 1 < nseg) {
+      fwd_combine1(S, p, q, min(seg_len, T - s * seg_len), w2, lS, lp, lq);
+      S = lS;
+      p = lp;
+      q = lq;
+    }
   }
 }
 
-// In place over adj[B][nseg][3][C]: entry s (s >= 1) holds the adjoint at the
+// In place over adj[B][nseg][5][C]: entry s (s >= 1) holds the adjoint at the
 // start of segment s accumulated from a zero adjoint at its end; on exit entry s
 // holds the true adjoint at the end of segment s.
 __global__ void wkv_carry_adj_kernel(float* adj, const float* w, int B, int T, int C, int nseg,
@@ -446,14 +560,15 @@ __global__ void wkv_carry_adj_kernel(float* adj, const float* w, int B, int T, i
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)B * C) return;
   const int b = static_cast<int>(i / C), c = static_cast<int>(i % C);
-  const Lane lc = make_lane(w[c], 0.f);
-  Adj a = adj_zero();
+  const float w2 = w[c] * kL2E;
+  float e[5] = {kNegBig, 0.f, 0.f, 0.f, 0.f};
   for (int s = nseg - 1; s >= 0; --s) {
-    const size_t row = (size_t)b * nseg + s;
-    Adj local = adj_zero();
-    if (s > 0) local = load_adj(adj, row, C, c);
-    store_adj(adj, row, C, c, a);
-    if (s > 0) a = adj_combine(local, a, min(seg_len, T - s * seg_len), lc);
+    float* r = adj + ((size_t)b * nseg + s) * 5 * (size_t)C + c;
+    float l[5] = {kNegBig, 0.f, 0.f, 0.f, 0.f};
+    if (s > 0)
+      for (int f = 0; f < 5; ++f) l[f] = r[f * (size_t)C];
+    for (int f = 0; f < 5; ++f) r[f * (size_t)C] = e[f];
+    if (s > 0) adj_combine1(l, e, min(seg_len, T - s * seg_len), w2);
   }
 }
 

@@ -11,11 +11,13 @@ The kernels live in ``libspikegpt_wkv.so`` behind the C ABI of
 from __future__ import annotations
 
 from . import _capi
-from ._ops import validate_wkv_inputs
+from ._ops import set_state_saving, state_saving_enabled, validate_wkv_inputs
 from .wkv import weighted_key_value_cuda, weighted_key_value_triton
 from .wkv_bf16 import weighted_key_value_cuda_bf16io, weighted_key_value_triton_bf16io
 
 __all__ = [
+    "set_state_saving",
+    "state_saving_enabled",
     "validate_wkv_inputs",
     "weighted_key_value_cuda",
     "weighted_key_value_cuda_bf16io",

@@ -71,6 +71,14 @@ def lib() -> ctypes.CDLL:
         handle.wkv_forward.restype = ci
         handle.wkv_backward.argtypes = [ci, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, vp, sz, vp]
         handle.wkv_backward.restype = ci
+        handle.wkv_state_size.argtypes = [ci, i64, i64, i64]
+        handle.wkv_state_size.restype = sz
+        handle.wkv_forward_with_state.argtypes = [ci, vp, vp, vp, vp, vp, vp, sz, i64, i64, i64, vp, sz, vp]
+        handle.wkv_forward_with_state.restype = ci
+        handle.wkv_backward_from_state.argtypes = [
+            ci, vp, vp, vp, vp, vp, vp, sz, vp, vp, vp, vp, i64, i64, i64, vp, sz, vp
+        ]
+        handle.wkv_backward_from_state.restype = ci
         handle.wkv_plan.argtypes = [ci, i64, i64, i64, ctypes.POINTER(ci), ctypes.POINTER(ci)]
         handle.wkv_plan.restype = ci
         handle.wkv_set_debug_overrides.argtypes = [ci, ci, ci]

@@ -8,6 +8,9 @@ and float16 I/O natively and always computes in float32.
 
 from __future__ import annotations
 
+import os
+import threading
+
 import torch
 from torch import Tensor
 
@@ -63,8 +66,65 @@ def _workspace(nbytes: int, device: torch.device) -> tuple[Tensor | None, int]:
     return buf, buf.data_ptr()
 
 
-def forward(key: Tensor, value: Tensor, time_decay: Tensor, time_first: Tensor) -> Tensor:
-    """y = WKV(key, value; -exp(time_decay), time_first), y in key.dtype."""
+# ---------------------------------------------------------------------------
+# Saved forward state (the autograd hand-off)
+#
+# The reference's backward op takes only (grad_y, w, u, k, v), so on its own it
+# must re-run the forward recurrence to recover the state. When the forward is
+# called through this package's model-facing wrappers in eager mode with
+# gradients required, the forward also stores the recurrence state every 16
+# steps (float32, 0.75 bytes per element of key) and hands it to the backward
+# through the autograd context; the backward then reads key/value once instead
+# of twice. Calls of the ops themselves, and everything traced by
+# torch.compile, use the self-contained schema path.
+# ---------------------------------------------------------------------------
+
+_TLS = threading.local()
+_SAVE_STATE = os.environ.get("SPIKEGPT_WKV_SAVE_STATE", "1") != "0"
+
+
+def set_state_saving(enabled: bool) -> None:
+    """Enable or disable the saved-state hand-off (default: enabled)."""
+    global _SAVE_STATE
+    _SAVE_STATE = bool(enabled)
+
+
+def state_saving_enabled() -> bool:
+    return _SAVE_STATE
+
+
+def call_saving_state(op, key: Tensor, value: Tensor, time_decay: Tensor, time_first: Tensor) -> Tensor:
+    """Call a forward custom op, asking it to keep the state for the backward
+    when autograd will record this call (eager, grad mode on, an input that
+    requires grad)."""
+    if not (_SAVE_STATE and torch.is_grad_enabled() and any(
+        t.requires_grad for t in (key, value, time_decay, time_first)
+    )):
+        return op(key, value, time_decay, time_first)
+    _TLS.want = True
+    try:
+        return op(key, value, time_decay, time_first)
+    finally:
+        _TLS.want = False
+        _TLS.pending = None
+
+
+def _take_pending(output: Tensor) -> Tensor | None:
+    pending = getattr(_TLS, "pending", None)
+    _TLS.pending = None
+    if pending is None or torch.compiler.is_compiling():
+        return None
+    ptr, shape, state = pending
+    if output.data_ptr() != ptr or tuple(output.shape) != shape:
+        return None
+    return state
+
+
+def forward(
+    key: Tensor, value: Tensor, time_decay: Tensor, time_first: Tensor, *, save_state: bool = False
+) -> Tensor | tuple[Tensor, Tensor]:
+    """y = WKV(key, value; -exp(time_decay), time_first), y in key.dtype. With
+    save_state, also returns the saved state for backward_from_state."""
     validate_wkv_inputs(key, value, time_decay, time_first)
     io = _io_dtype(key.dtype)
     k = key.to(io).contiguous()
@@ -75,23 +135,38 @@ def forward(key: Tensor, value: Tensor, time_decay: Tensor, time_first: Tensor) 
     y = torch.empty_like(k, memory_format=torch.contiguous_format)
     code = _CODES[io]
     lib = _capi.lib()
+    state = None
     with torch.cuda.device(k.device):
         stream = torch.cuda.current_stream(k.device).cuda_stream
         nbytes = int(lib.wkv_forward_workspace_size(code, b, t, c))
         ws, ws_ptr = _workspace(nbytes, k.device)
-        rc = lib.wkv_forward(
-            code, k.data_ptr(), v.data_ptr(), td.data_ptr(), tf.data_ptr(), y.data_ptr(),
-            b, t, c, ws_ptr, nbytes, stream,
-        )
-        _capi.check(rc, "wkv_forward")
-    return y if y.dtype == key.dtype else y.to(key.dtype)
+        if save_state:
+            sbytes = int(lib.wkv_state_size(code, b, t, c))
+            state = torch.empty(max(sbytes, 16), dtype=torch.uint8, device=k.device)
+            rc = lib.wkv_forward_with_state(
+                code, k.data_ptr(), v.data_ptr(), td.data_ptr(), tf.data_ptr(), y.data_ptr(),
+                state.data_ptr(), state.numel(), b, t, c, ws_ptr, nbytes, stream,
+            )
+            _capi.check(rc, "wkv_forward_with_state")
+        else:
+            rc = lib.wkv_forward(
+                code, k.data_ptr(), v.data_ptr(), td.data_ptr(), tf.data_ptr(), y.data_ptr(),
+                b, t, c, ws_ptr, nbytes, stream,
+            )
+            _capi.check(rc, "wkv_forward")
+    y = y if y.dtype == key.dtype else y.to(key.dtype)
+    return (y, state) if save_state else y
 
 
-def backward(grad_y: Tensor, w: Tensor, u: Tensor, k: Tensor, v: Tensor) -> list[Tensor]:
+def backward(
+    grad_y: Tensor, w: Tensor, u: Tensor, k: Tensor, v: Tensor, state: Tensor | None = None
+) -> list[Tensor]:
     """[grad_key, grad_value, grad_time_decay (already x w), grad_time_first].
 
     Mirrors the output contract of the reference op (wkv_triton.py:164-198):
     grad_key/grad_value like ``k``, the per-channel grads like ``w``/``u``.
+    With ``state`` (from forward(save_state=True) on the same inputs) the
+    forward sweep is skipped.
     """
     if k.ndim != 3 or grad_y.shape != k.shape or v.shape != k.shape:
         raise ValueError(
@@ -118,12 +193,22 @@ def backward(grad_y: Tensor, w: Tensor, u: Tensor, k: Tensor, v: Tensor) -> list
         stream = torch.cuda.current_stream(kk.device).cuda_stream
         nbytes = int(lib.wkv_backward_workspace_size(code, b, t, c))
         ws, ws_ptr = _workspace(nbytes, kk.device)
-        rc = lib.wkv_backward(
-            code, gy.data_ptr(), w32.data_ptr(), u32.data_ptr(), kk.data_ptr(), vv.data_ptr(),
-            gk.data_ptr(), gv.data_ptr(), gtd.data_ptr(), gtf.data_ptr(),
-            b, t, c, ws_ptr, nbytes, stream,
-        )
-        _capi.check(rc, "wkv_backward")
+        if state is not None:
+            if state.device != kk.device or state.dtype != torch.uint8 or not state.is_contiguous():
+                raise ValueError("state must be the contiguous uint8 buffer from forward(save_state=True)")
+            rc = lib.wkv_backward_from_state(
+                code, gy.data_ptr(), w32.data_ptr(), u32.data_ptr(), kk.data_ptr(), vv.data_ptr(),
+                state.data_ptr(), state.numel(), gk.data_ptr(), gv.data_ptr(), gtd.data_ptr(),
+                gtf.data_ptr(), b, t, c, ws_ptr, nbytes, stream,
+            )
+            _capi.check(rc, "wkv_backward_from_state")
+        else:
+            rc = lib.wkv_backward(
+                code, gy.data_ptr(), w32.data_ptr(), u32.data_ptr(), kk.data_ptr(), vv.data_ptr(),
+                gk.data_ptr(), gv.data_ptr(), gtd.data_ptr(), gtf.data_ptr(),
+                b, t, c, ws_ptr, nbytes, stream,
+            )
+            _capi.check(rc, "wkv_backward")
     out_dtype = k.dtype
     return [gk.to(out_dtype), gv.to(out_dtype), gtd.to(w.dtype), gtf.to(u.dtype)]
 
@@ -135,6 +220,11 @@ def register(namespace_op_fwd: str, namespace_op_bwd: str):
 
     @torch.library.custom_op(namespace_op_fwd, mutates_args=(), device_types="cuda")
     def wkv_forward_op(key: Tensor, value: Tensor, time_decay: Tensor, time_first: Tensor) -> Tensor:
+        if getattr(_TLS, "want", False):
+            _TLS.want = False
+            y, state = forward(key, value, time_decay, time_first, save_state=True)
+            _TLS.pending = (y.data_ptr(), tuple(y.shape), state)
+            return y
         return forward(key, value, time_decay, time_first)
 
     @wkv_forward_op.register_fake
@@ -153,16 +243,26 @@ def register(namespace_op_fwd: str, namespace_op_bwd: str):
 
     def setup_context(ctx, inputs, output):
         key, value, time_decay, time_first = inputs
-        ctx.save_for_backward(key, value, time_decay, time_first)
+        state = _take_pending(output)
+        if state is None:
+            ctx.save_for_backward(key, value, time_decay, time_first)
+        else:
+            ctx.save_for_backward(key, value, time_decay, time_first, state)
 
     def backward_fn(ctx, grad_y):
-        key, value, time_decay, time_first = ctx.saved_tensors
+        saved = ctx.saved_tensors
+        key, value, time_decay, time_first = saved[:4]
         w = -torch.exp(time_decay.float())
         u = time_first.float()
         # The kernels read key/value/grad_y in their own dtype, so the fp32
         # copies the reference glue makes (wkv_triton.py:206-210) are not needed;
         # the float32 results are identical.
-        gk, gv, gtd, gtf = getattr(torch.ops.myelin, bwd_name)(grad_y, w, u, key, value)
+        if len(saved) == 5:
+            gk, gv, gtd, gtf = torch.ops.spikegpt_b200.wkv_backward_from_state(
+                grad_y, w, u, key, value, saved[4]
+            )
+        else:
+            gk, gv, gtd, gtf = getattr(torch.ops.myelin, bwd_name)(grad_y, w, u, key, value)
         return (
             gk.to(key.dtype),
             gv.to(value.dtype),
@@ -172,3 +272,16 @@ def register(namespace_op_fwd: str, namespace_op_bwd: str):
 
     wkv_forward_op.register_autograd(backward_fn, setup_context=setup_context)
     return wkv_forward_op
+
+
+@torch.library.custom_op("spikegpt_b200::wkv_backward_from_state", mutates_args=(), device_types="cuda")
+def wkv_backward_from_state_op(
+    grad_y: Tensor, w: Tensor, u: Tensor, k: Tensor, v: Tensor, state: Tensor
+) -> list[Tensor]:
+    """The backward op's contract (wkv_triton.py:164-198) plus the saved state."""
+    return backward(grad_y, w, u, k, v, state)
+
+
+@wkv_backward_from_state_op.register_fake
+def _(grad_y, w, u, k, v, state):
+    return [torch.empty_like(k), torch.empty_like(k), torch.empty_like(w), torch.empty_like(u)]

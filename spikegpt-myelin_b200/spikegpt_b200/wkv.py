@@ -26,7 +26,10 @@ def weighted_key_value_cuda(
     time_first: Tensor,
 ) -> Tensor:
     """RWKV WKV recurrence via the sm_100a custom op (CUDA only)."""
-    return torch.ops.myelin.wkv_forward(key, value, time_decay, time_first)
+    if torch.compiler.is_compiling():
+        return torch.ops.myelin.wkv_forward(key, value, time_decay, time_first)
+    # eager: keep the forward state for the backward when autograd records
+    return _ops.call_saving_state(torch.ops.myelin.wkv_forward, key, value, time_decay, time_first)
 
 
 # Drop-in name used by the reference's model code (language.py:37-38, 1032).

@@ -25,7 +25,10 @@ def weighted_key_value_cuda_bf16io(
     time_first: Tensor,
 ) -> Tensor:
     """RWKV WKV via the native-dtype-I/O sm_100a custom op (CUDA only)."""
-    return torch.ops.myelin.wkv_forward_bf16io(key, value, time_decay, time_first)
+    if torch.compiler.is_compiling():
+        return torch.ops.myelin.wkv_forward_bf16io(key, value, time_decay, time_first)
+    # eager: keep the forward state for the backward when autograd records
+    return _ops.call_saving_state(torch.ops.myelin.wkv_forward_bf16io, key, value, time_decay, time_first)
 
 
 # Drop-in name used by the reference's model code (language.py:37, 1030).

@@ -30,6 +30,7 @@ FIELDS = ("y", "gk", "gv", "gtd", "gtf")
 def _reset_overrides():
     yield
     _capi.set_debug_overrides()
+    spikegpt_b200.set_state_saving(True)
 
 
 def _run(fn, k, v, td, tf, gy, *, dtype, device):
@@ -83,11 +84,14 @@ def test_golden_cases_float32(cuda, name):
 
 
 @pytest.mark.parametrize("name", ["triton_t7", "triton_t64", "channels70", "kscale4", "kscale20", "decay_extremes", "bf16_rounded"])
-@pytest.mark.parametrize("path", ["generic", "seg2", "seg3", "slow", "slow_seg2"])
+@pytest.mark.parametrize("path", ["generic", "seg2", "seg3", "slow", "slow_seg2", "nostate", "nostate_seg2", "nostate_slow"])
 def test_golden_cases_on_every_execution_path(cuda, name, path):
+    """Every execution path: TMA or generic tiles, one sequential sweep or time
+    segments, fast or exact arithmetic, with and without the saved-state hand-off."""
     k, v, td, tf, gy = golden_inputs(name, CASES)
-    seg = {"seg2": 2, "seg3": 3, "slow_seg2": 2}.get(path, 0)
-    _capi.set_debug_overrides(force_segments=seg, force_generic=path == "generic", force_slow=path.startswith("slow"))
+    seg = {"seg2": 2, "seg3": 3, "slow_seg2": 2, "nostate_seg2": 2}.get(path, 0)
+    _capi.set_debug_overrides(force_segments=seg, force_generic=path == "generic", force_slow="slow" in path)
+    spikegpt_b200.set_state_saving(not path.startswith("nostate"))
     got = _run(weighted_key_value_cuda, k, v, td, tf, gy, dtype=torch.float32, device=cuda)
     _assert_close(got, [CASES[name][f] for f in FIELDS], _fp32_tol(k, v, td, tf, gy), f"{name}/{path}")
 
@@ -223,6 +227,35 @@ def test_gradient_of_sum_over_batch_is_sum_of_shards(cuda):
     for idx in (3, 4):
         summed = sum(p[idx] for p in parts)
         assert scaled_err(summed, full[idx]) < 1e-5
+
+
+@pytest.mark.parametrize("segments", [1, 3])
+def test_state_handoff_matches_self_contained_backward_bitwise(cuda, segments):
+    """The saved-state backward and the self-contained one compute the same
+    checkpoints, so their gradients agree bit for bit."""
+    _capi.set_debug_overrides(force_segments=segments)
+    k, v, td, tf, gy = config_inputs(8, 512, 256, seed=31, kscale=4.0)
+    spikegpt_b200.set_state_saving(True)
+    before = _capi.launch_counts()["wkv_fwd_kernel<state>"]
+    a = _run(weighted_key_value_cuda_bf16io, k, v, td, tf, gy, dtype=torch.bfloat16, device=cuda)
+    # with the hand-off the only state-only launch is the forward's segment summary
+    assert _capi.launch_counts()["wkv_fwd_kernel<state>"] == before + (1 if segments > 1 else 0)
+    spikegpt_b200.set_state_saving(False)
+    b = _run(weighted_key_value_cuda_bf16io, k, v, td, tf, gy, dtype=torch.bfloat16, device=cuda)
+    for x, y in zip(a, b, strict=True):
+        np.testing.assert_array_equal(x, y)
+
+
+def test_no_state_is_saved_without_grad(cuda):
+    k, v, td, tf, _ = config_inputs(2, 64, 64, seed=32)
+    kt, vt = torch.as_tensor(k).cuda().requires_grad_(), torch.as_tensor(v).cuda()
+    before = _capi.launch_counts()
+    with torch.no_grad():
+        weighted_key_value_cuda_bf16io(kt, vt, torch.as_tensor(td).cuda(), torch.as_tensor(tf).cuda())
+    from spikegpt_b200 import _ops
+
+    assert getattr(_ops._TLS, "pending", None) is None
+    assert _capi.launch_counts()["wkv_fwd_kernel<y>"] == before["wkv_fwd_kernel<y>"] + 1
 
 
 def test_results_are_deterministic(cuda):
