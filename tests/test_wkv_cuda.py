@@ -230,9 +230,11 @@ def test_gradient_of_sum_over_batch_is_sum_of_shards(cuda):
 
 
 @pytest.mark.parametrize("segments", [1, 3])
-def test_state_handoff_matches_self_contained_backward_bitwise(cuda, segments):
-    """The saved-state backward and the self-contained one compute the same
-    checkpoints, so their gradients agree bit for bit."""
+def test_state_handoff_matches_self_contained_backward(cuda, segments):
+    """The saved-state backward agrees with the self-contained one: bit for bit
+    on the sequential plan (both sweep the same checkpoints from t=0), within
+    tolerance when time is split into segments (the self-contained backward then
+    builds segment-local checkpoints, rounded differently)."""
     _capi.set_debug_overrides(force_segments=segments)
     k, v, td, tf, gy = config_inputs(8, 512, 256, seed=31, kscale=4.0)
     spikegpt_b200.set_state_saving(True)
@@ -243,7 +245,10 @@ def test_state_handoff_matches_self_contained_backward_bitwise(cuda, segments):
     spikegpt_b200.set_state_saving(False)
     b = _run(weighted_key_value_cuda_bf16io, k, v, td, tf, gy, dtype=torch.bfloat16, device=cuda)
     for x, y in zip(a, b, strict=True):
-        np.testing.assert_array_equal(x, y)
+        if segments == 1:
+            np.testing.assert_array_equal(x, y)
+        else:
+            assert scaled_err(x, y) <= TOL_16BIT
 
 
 def test_no_state_is_saved_without_grad(cuda):
@@ -345,8 +350,11 @@ def test_torch_compile_fullgraph_matches_eager(cuda):
         leaves = [torch.as_tensor(x).cuda().requires_grad_() for x in (k, v, td, tf)]
         fn(*leaves).sum().backward()
         outs.append([leaves[0].grad, leaves[2].grad])
+    # eager takes the saved-state backward, the compiled graph the self-contained
+    # one (segment-local checkpoints for this small B*C), so agreement is to
+    # float32 rounding of the per-channel sums
     for a, b in zip(*outs, strict=True):
-        assert torch.allclose(a, b, atol=1e-5, rtol=1e-5)
+        assert scaled_err(a.cpu().numpy(), b.cpu().numpy()) <= TOL_FP32
 
 
 def test_no_device_side_errors_were_raised(cuda):
