@@ -203,6 +203,7 @@ def run_native(args, wl):
 
     import spikegpt_b200
     from spikegpt_b200 import _capi
+    from spikegpt_b200.sharding import max_over_ranks
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -285,10 +286,7 @@ def run_native(args, wl):
     launches = sum(_capi.launch_counts().values()) - launches0
     per_kernel = _capi.timing_collect()
     ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        tmax = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
-        ms = float(tmax.item())
+    ms = max_over_ranks(ms, dev)
     if sampler:
         time.sleep(0.25)
         sampler.stop()
