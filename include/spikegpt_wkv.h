@@ -96,8 +96,43 @@ WKV_API int wkv_backward(int dtype, const void* grad_y, const float* w, const fl
                  int64_t C, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Allocation-free backward (no counterpart in the reference: it is an extra
+ * entry point for callers of this library that must not allocate device
+ * memory). Same arguments and results as wkv_backward, minus the workspace:
+ * the scratch it needs (checkpoints, per-lane partial sums, reduction
+ * counters) lives in one static device array of WKV_NOALLOC_SCRATCH_BYTES
+ * inside this library. The CUDA runtime reserves that array on every device
+ * that loads the library and keeps it until the process exits.
+ *
+ * Who needs it: a host whose device memory is owned by another allocator (a
+ * framework's caching allocator or a serving engine's arena that has already
+ * reserved the HBM, where a raw cudaMalloc can fail or cudaFree would stall
+ * every stream), and thin FFI bindings that have no allocator to hand and
+ * cannot manage a workspace's lifetime.
+ *
+ * - Shapes whose scratch exceeds WKV_NOALLOC_SCRATCH_BYTES (roughly
+ *   B*T*C above 44 million elements: the checkpoints take 0.75 bytes per
+ *   element) fail with WKV_ERR_INVALID_ARGUMENT and a message naming the
+ *   bytes needed; use wkv_backward for those.
+ * - The first call on a device looks up the array's device address (once per
+ *   device, with that device current); make that first call before any stream
+ *   capture begins on the device.
+ * - Every call shares the one array and it keeps the previous call's
+ *   contents; the call clears what must start at zero itself. Calls that
+ *   overlap on the GPU (different streams, or different host threads on one
+ *   device) race on the array and give wrong gradients: serialise them.
+ * - Allocates nothing: no cudaMalloc, cudaFree or allocating library call.
+ */
+#define WKV_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
+WKV_API int wkv_backward_noalloc(int dtype, const void* grad_y, const float* w, const float* u,
+                                 const void* key, const void* value, void* grad_key,
+                                 void* grad_value, float* grad_time_decay,
+                                 float* grad_time_first, int64_t B, int64_t T, int64_t C,
+                                 void* stream);
+
+/*
  * Forward/backward with a saved forward state (no reference counterpart; an
- * optimisation of the pair above). wkv_forward_with_state computes y exactly as
+ * optimisation of wkv_forward/wkv_backward). wkv_forward_with_state computes y exactly as
  * wkv_forward and also stores the recurrence state at every 16th step into
  * `state` (wkv_state_size bytes, 16-byte aligned, caller-owned).
  * wkv_backward_from_state returns the same gradients as wkv_backward for the

@@ -639,9 +639,65 @@ int backward_impl(int dtype, const void* grad_y, const float* w, const float* u,
   }
 }
 
+// ------------------------------------------------- allocation-free backward
+//
+// Scratch of wkv_backward_noalloc. The runtime reserves it on each device that
+// loads this module and zero-fills it once; after that every call reuses it as
+// left by the previous call, so the launch sequence must clear whatever has to
+// start at zero (it does: the state sweep zeroes the reduction counters before
+// the gradient kernel reads them; checkpoints and partial sums are overwritten).
+__device__ __align__(256) unsigned char g_noalloc_scratch[WKV_NOALLOC_SCRATCH_BYTES];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_base[64] = {};
+
+// In host code `g_noalloc_scratch` names a host-side shadow of the symbol, not
+// device memory: the device address comes from cudaGetSymbolAddress, asked once
+// per device with that device current, and is cached.
+int noalloc_scratch(void** base) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(WKV_ERR_INVALID_ARGUMENT, "device ordinal %d unsupported", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_base[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    g_noalloc_base[dev] = p;
+  }
+  *base = g_noalloc_base[dev];
+  return WKV_OK;
+}
+
 }  // namespace
 
 extern "C" {
+
+int wkv_backward_noalloc(int dtype, const void* grad_y, const float* w, const float* u,
+                         const void* key, const void* value, void* grad_key, void* grad_value,
+                         float* grad_time_decay, float* grad_time_first, int64_t B, int64_t T,
+                         int64_t C, void* stream) {
+  g_last_error[0] = '\0';
+  const int rc = check_dims(dtype, B, T, C);
+  if (rc) return rc;
+  const bool al = aligned16(grad_y) && aligned16(key) && aligned16(value) && aligned16(grad_key) &&
+                  aligned16(grad_value);
+  const size_t need = bwd_workspace(make_plan(dtype, B, T, C, al), B, T, C, nullptr).bytes;
+  if (need > WKV_NOALLOC_SCRATCH_BYTES)
+    return fail(WKV_ERR_INVALID_ARGUMENT,
+                "wkv_backward_noalloc: B=%lld T=%lld C=%lld needs %zu scratch bytes but the "
+                "static scratch holds %zu; call wkv_backward with a workspace instead",
+                (long long)B, (long long)T, (long long)C, need, (size_t)WKV_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  if (B > 0 && T > 0 && C > 0) {
+    const int src = noalloc_scratch(&scratch);
+    if (src) return src;
+  }
+  return backward_impl(dtype, grad_y, w, u, key, value, nullptr, 0, grad_key, grad_value,
+                       grad_time_decay, grad_time_first, B, T, C, scratch,
+                       WKV_NOALLOC_SCRATCH_BYTES, stream);
+}
 
 int wkv_forward(int dtype, const void* key, const void* value, const float* time_decay,
                 const float* time_first, void* y, int64_t B, int64_t T, int64_t C,
