@@ -20,7 +20,7 @@ CSRC = PKG_ROOT / "csrc"
 LIB_DIR = PKG_ROOT / "lib"
 LIB = LIB_DIR / "libspikegpt_wkv.so"
 SOURCES = [CSRC / "wkv_capi.cu"]
-DEPS = SOURCES + [CSRC / "wkv_kernels.cuh", CSRC / "wkv_device.cuh", REPO_ROOT / "include" / "spikegpt_wkv.h"]
+DEPS = SOURCES + sorted(CSRC.glob("*.cuh")) + [REPO_ROOT / "include" / "spikegpt_wkv.h"]
 
 NVCC_FLAGS = [
     "-gencode",

@@ -16,7 +16,7 @@
 #include <vector>
 
 #include "spikegpt_wkv.h"
-#include "wkv_kernels.cuh"
+#include "wkv_tp.cuh"
 
 namespace {
 
@@ -219,8 +219,9 @@ EncodeTiledFn encode_fn() {
 }
 
 // [B, T, C] tensor as a 3-D map with dims {C, T, B} and a [1][rows][kLanes] box,
-// rows = the dtype's tile height (Pair<T>::kTileRows).
-int make_map(CUtensorMap* m, int dtype, const void* ptr, int64_t B, int64_t T, int64_t C) {
+// rows = box_rows, or the dtype's tile height (Pair<T>::kTileRows) when 0.
+int make_map(CUtensorMap* m, int dtype, const void* ptr, int64_t B, int64_t T, int64_t C,
+             int box_rows = 0) {
   std::memset(m, 0, sizeof(*m));
   if (ptr == nullptr) return WKV_OK;
   EncodeTiledFn fn = encode_fn();
@@ -231,7 +232,9 @@ int make_map(CUtensorMap* m, int dtype, const void* ptr, int64_t B, int64_t T, i
                                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)T, (cuuint64_t)B};
   const cuuint64_t strides[2] = {(cuuint64_t)(C * es), (cuuint64_t)(T * C * es)};
-  const cuuint32_t rows = dtype == WKV_DTYPE_F32 ? Pair<float>::kTileRows : Pair<__half>::kTileRows;
+  const cuuint32_t rows = box_rows > 0                 ? (cuuint32_t)box_rows
+                          : dtype == WKV_DTYPE_F32 ? Pair<float>::kTileRows
+                                                   : Pair<__half>::kTileRows;
   const cuuint32_t box[3] = {(cuuint32_t)kLanes, rows, 1u};
   const cuuint32_t estr[3] = {1u, 1u, 1u};
   const CUresult r = fn(m, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr,
@@ -296,11 +299,13 @@ int launch_forward(const void* k, const void* v, const float* decay, int decay_i
   const int dt = sizeof(IO) == 4 ? WKV_DTYPE_F32
                  : std::is_same<IO, __nv_bfloat16>::value ? WKV_DTYPE_BF16
                                                          : WKV_DTYPE_F16;
+  constexpr int TW = tp_warps<IO>();
   int rc;
   if (p.tma) {
-    if ((rc = make_map(&mk, dt, k, B, T, C)) || (rc = make_map(&mv, dt, v, B, T, C)) ||
-        (rc = make_map(&my, dt, y, B, T, C)))
+    if ((rc = make_map(&mk, dt, k, B, T, C, Tp<IO, TW>::kRoundRows)) ||
+        (rc = make_map(&mv, dt, v, B, T, C, Tp<IO, TW>::kRoundRows)))
       return rc;
+    std::memset(&my, 0, sizeof(my));
   } else {
     std::memset(&mk, 0, sizeof(mk));
     std::memset(&mv, 0, sizeof(mv));
@@ -327,13 +332,19 @@ int launch_forward(const void* k, const void* v, const float* decay, int decay_i
     // summaries of segments 0..nseg-2, then the carry
     FwdArgs s = a;
     s.seg_end = seg;
-    const size_t sm = fwd_smem_bytes<IO>(false);
-    launch(K_FWD_STATE, st, [&] {
-      if (p.tma)
-        wkv_fwd_kernel<IO, false, true><<<dim3(gx, p.nseg - 1), kThreads, sm, st>>>(s, mk, mv, my);
-      else
+    if (p.tma) {
+      const size_t sm = fwd_tp_smem_bytes<IO, TW>();
+      const cudaError_t e = allow_smem(wkv_fwd_tp_kernel<IO, TW, false>, sm);
+      if (e != cudaSuccess) return cuda_fail(e, "setting the forward kernel's shared memory size");
+      launch(K_FWD_STATE, st, [&] {
+        wkv_fwd_tp_kernel<IO, TW, false><<<dim3(gx, p.nseg - 1), 32 * TW, sm, st>>>(s, mk, mv);
+      });
+    } else {
+      const size_t sm = fwd_smem_bytes<IO>(false);
+      launch(K_FWD_STATE, st, [&] {
         wkv_fwd_kernel<IO, false, false><<<dim3(gx, p.nseg - 1), kThreads, sm, st>>>(s, mk, mv, my);
-    });
+      });
+    }
     const int64_t lanes = (int64_t)B * C;
     launch(K_CARRY_FWD, st, [&] {
       wkv_carry_fwd_kernel<<<(unsigned)((lanes + 127) / 128), 128, 0, st>>>(
@@ -346,13 +357,19 @@ int launch_forward(const void* k, const void* v, const float* decay, int decay_i
   a.ckpt = state;
   a.zero_tickets = state_tickets;
   a.nzero = state_tickets ? a.ncblk : 0;
-  const size_t sm = fwd_smem_bytes<IO>(true);
-  launch(K_FWD_Y, st, [&] {
-    if (p.tma)
-      wkv_fwd_kernel<IO, true, true><<<dim3(gx, p.nseg), kThreads, sm, st>>>(a, mk, mv, my);
-    else
+  if (p.tma) {
+    const size_t sm = fwd_tp_smem_bytes<IO, TW>();
+    const cudaError_t e = allow_smem(wkv_fwd_tp_kernel<IO, TW, true>, sm);
+    if (e != cudaSuccess) return cuda_fail(e, "setting the forward kernel's shared memory size");
+    launch(K_FWD_Y, st, [&] {
+      wkv_fwd_tp_kernel<IO, TW, true><<<dim3(gx, p.nseg), 32 * TW, sm, st>>>(a, mk, mv);
+    });
+  } else {
+    const size_t sm = fwd_smem_bytes<IO>(true);
+    launch(K_FWD_Y, st, [&] {
       wkv_fwd_kernel<IO, true, false><<<dim3(gx, p.nseg), kThreads, sm, st>>>(a, mk, mv, my);
-  });
+    });
+  }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "wkv forward launch");
   return WKV_OK;
@@ -403,13 +420,26 @@ int launch_backward(const void* gy, const float* w, const float* u, const void* 
   f.nzero = ncblk;
   f.force_slow = force_slow;
   f.err = err;
-  const size_t fsm = fwd_smem_bytes<IO>(false);
-  if (state == nullptr) launch(K_FWD_STATE, st, [&] {
-    if (p.tma)
-      wkv_fwd_kernel<IO, false, true><<<dim3(gx, p.nseg), kThreads, fsm, st>>>(f, mk, mv, none);
-    else
-      wkv_fwd_kernel<IO, false, false><<<dim3(gx, p.nseg), kThreads, fsm, st>>>(f, mk, mv, none);
-  });
+  if (state == nullptr) {
+    if (p.tma) {
+      constexpr int TW = tp_warps<IO>();
+      CUtensorMap rk, rv;
+      if ((rc = make_map(&rk, dt, k, B, T, C, Tp<IO, TW>::kRoundRows)) ||
+          (rc = make_map(&rv, dt, v, B, T, C, Tp<IO, TW>::kRoundRows)))
+        return rc;
+      const size_t fsm = fwd_tp_smem_bytes<IO, TW>();
+      const cudaError_t e = allow_smem(wkv_fwd_tp_kernel<IO, TW, false>, fsm);
+      if (e != cudaSuccess) return cuda_fail(e, "setting the forward kernel's shared memory size");
+      launch(K_FWD_STATE, st, [&] {
+        wkv_fwd_tp_kernel<IO, TW, false><<<dim3(gx, p.nseg), 32 * TW, fsm, st>>>(f, rk, rv);
+      });
+    } else {
+      const size_t fsm = fwd_smem_bytes<IO>(false);
+      launch(K_FWD_STATE, st, [&] {
+        wkv_fwd_kernel<IO, false, false><<<dim3(gx, p.nseg), kThreads, fsm, st>>>(f, mk, mv, none);
+      });
+    }
+  }
 
   BwdArgs a{};
   a.k = k;

@@ -255,14 +255,39 @@ struct Pair<__half> {
 
 // ------------------------------------------------------------------- state
 
+// Decay over n steps, ew^n = m 2^e (m in [0.5, 1), e an integer; m = 0 and
+// e = kNegBig once it underflows), where ew is the float32 per-step factor the recurrences
+// multiply by. The power is formed in double from that same float, so a state
+// decayed by a combine and a state decayed step by step carry the same
+// systematic rounding of ew. The backward's adjoint decays step by step with
+// ew; states whose decay differs from ew^n by even a few ulps (e.g. 2^{w n
+// log2 e} through ex2) make the gradients near dominant keys several times less
+// accurate, because the adjoint sums cancel.
+struct Decay1 {
+  float m, e;
+};
+__device__ __forceinline__ Decay1 ew_decay(float ew, int n) {
+  double x = static_cast<double>(ew), r = 1.0;
+  for (int k = n; k > 0; k >>= 1) {
+    if (k & 1) r *= x;
+    x *= x;
+  }
+  if (!(r > 0.0)) return Decay1{0.f, kNegBig};
+  int ex = 0;
+  const double m = frexp(r, &ex);
+  return Decay1{static_cast<float>(m), static_cast<float>(ex)};
+}
+
 // Per-channel constants of a lane pair. w = -exp(time_decay) <= 0 (reference
 // wkv_triton.py:152).
 struct Lane2 {
-  f2 w;   // natural-log decay per step
-  f2 w2;  // w * log2(e)
-  f2 u2;  // time_first * log2(e)
-  f2 ew;  // e^w
-  f2 eu;  // e^u
+  f2 w;     // natural-log decay per step
+  f2 w2;    // w * log2(e)
+  f2 u2;    // time_first * log2(e)
+  f2 ew;    // e^w
+  f2 eu;    // e^u
+  f2 dm16;  // ew^kSub = dm16 2^de16 (see ew_decay)
+  f2 de16;
 };
 
 __device__ __forceinline__ Lane2 make_lane2(f2 w, f2 u) {
@@ -272,6 +297,9 @@ __device__ __forceinline__ Lane2 make_lane2(f2 w, f2 u) {
   l.u2 = f2{u.x * kL2E, u.y * kL2E};
   l.ew = f2{expf(w.x), expf(w.y)};
   l.eu = f2{expf(u.x), expf(u.y)};
+  const Decay1 dx = ew_decay(l.ew.x, kSub), dy = ew_decay(l.ew.y, kSub);
+  l.dm16 = f2{dx.m, dy.m};
+  l.de16 = f2{dx.e, dy.e};
   return l;
 }
 
@@ -295,12 +323,14 @@ __device__ __forceinline__ Adj2 adj_zero2() {
 
 // State after `delta` more steps of pure decay from g, plus a local state l
 // that was accumulated from zero over those same steps (P is linear in the
-// history, so the two parts add). One lane.
-__device__ __forceinline__ void fwd_combine1(float gS, float gp, float gq, int delta, float w2,
-                                             float& lS, float& lp, float& lq) {
-  const float sg = gS + w2 * static_cast<float>(delta);
-  const float s = fmaxf(sg, lS);
-  const float a = ex2(sg - s), b = ex2(lS - s);
+// history, so the two parts add); d = ew^delta (ew_decay). One lane.
+// All scales are integers (see fast_ok1), so the new scale s is exact and each
+// part is rescaled by one rounding: g by d.m 2^{gS + d.e - s}, l by 2^{lS - s}.
+__device__ __forceinline__ void fwd_combine1(float gS, float gp, float gq, Decay1 d, float& lS,
+                                             float& lp, float& lq) {
+  const float ge = gS + d.e;
+  const float s = fmaxf(ge, lS);
+  const float a = d.m * ex2(ge - s), b = ex2(lS - s);
   lp = fmaf(gp, a, lp * b);
   lq = fmaf(gq, a, lq * b);
   lS = s;
@@ -308,22 +338,30 @@ __device__ __forceinline__ void fwd_combine1(float gS, float gp, float gq, int d
 
 __device__ __forceinline__ Fwd2 fwd_combine2(const Fwd2& g, int delta, const Lane2& lc,
                                              Fwd2 l) {
-  fwd_combine1(g.S.x, g.p.x, g.q.x, delta, lc.w2.x, l.S.x, l.p.x, l.q.x);
-  fwd_combine1(g.S.y, g.p.y, g.q.y, delta, lc.w2.y, l.S.y, l.p.y, l.q.y);
+  Decay1 dx, dy;
+  if (delta == kSub) {
+    dx = Decay1{lc.dm16.x, lc.de16.x};
+    dy = Decay1{lc.dm16.y, lc.de16.y};
+  } else {
+    dx = ew_decay(lc.ew.x, delta);
+    dy = ew_decay(lc.ew.y, delta);
+  }
+  fwd_combine1(g.S.x, g.p.x, g.q.x, dx, l.S.x, l.p.x, l.q.x);
+  fwd_combine1(g.S.y, g.p.y, g.q.y, dy, l.S.y, l.p.y, l.q.y);
   return l;
 }
 
 // Adjoint at the start of a segment of `len` steps: its own contribution
 // `local` (accumulated from a zero adjoint) plus the adjoint at the segment end
 // decayed through the segment, e^{w len} dL/dP_end; the w-derivatives pick up
-// the product rule term len e^{w len} dL/dP_end. One lane; l = local,
-// e = end (overwritten with the result).
+// the product rule term len e^{w len} dL/dP_end. d = ew^len (ew_decay). One
+// lane; l = local, e = end (overwritten with the result).
 __device__ __forceinline__ void adj_combine1(const float (&l)[5], float (&e)[5], int len,
-                                             float w2) {
+                                             Decay1 d) {
   const float fl = static_cast<float>(len);
-  const float ge = e[0] + w2 * fl;
+  const float ge = e[0] + d.e;
   const float g = fmaxf(ge, l[0]);
-  const float a = ex2(ge - g), b = ex2(l[0] - g);
+  const float a = d.m * ex2(ge - g), b = ex2(l[0] - g);
   const float hp = fmaf(fl, e[1], e[3]), hq = fmaf(fl, e[2], e[4]);
   e[1] = fmaf(e[1], a, l[1] * b);
   e[2] = fmaf(e[2], a, l[2] * b);
@@ -348,10 +386,16 @@ __device__ __forceinline__ void slow_update(float& o, float& p, float& q, float 
 // Fast-path admissibility for one lane over a sub-chunk of L steps starting
 // from state (S, p, q). Outputs the sub-chunk scale s and the carried state
 // rescaled to it.
+//
+// Scales are integers (log2 units) throughout: a change of scale then
+// multiplies by an exact power of two (ex2 of an integer argument is exact on
+// sm_100a), so state and adjoint pick up no rounding when consecutive
+// sub-chunks use different scales. Non-integer scales cost ~2^-22 relative per
+// change, which accumulates along T in the adjoint chain.
 __device__ __forceinline__ bool fast_ok1(float S, float p0, float q0, float kmax, float kmin,
                                          int L, float w2, float u2, float& s, float& p,
                                          float& q) {
-  s = fmaxf(S, kmax * kL2E);
+  s = fmaxf(S, ceilf(kmax * kL2E));
   const float c = ex2(S - s);
   p = p0 * c;
   q = q0 * c;

@@ -536,7 +536,7 @@ __global__ void wkv_carry_fwd_kernel(float* seg, const float* decay, int decay_i
   if (i >= (int64_t)B * C) return;
   const int b = static_cast<int>(i / C), c = static_cast<int>(i % C);
   const float d = decay[c];
-  const float w2 = (decay_is_w ? d : -expf(d)) * kL2E;
+  const float ew = expf(decay_is_w ? d : -expf(d));  // as make_lane2
   float S = kNegBig, p = 0.f, q = 0.f;
   for (int s = 0; s < nseg; ++s) {
     const size_t row = (size_t)b * nseg + s;
@@ -544,7 +544,7 @@ __global__ void wkv_carry_fwd_kernel(float* seg, const float* decay, int decay_i
     if (s + 1 < nseg) load3s(seg, row, C, c, lS, lp, lq);
     store3s(seg, row, C, c, S, p, q);
     if (s + 1 < nseg) {
-      fwd_combine1(S, p, q, min(seg_len, T - s * seg_len), w2, lS, lp, lq);
+      fwd_combine1(S, p, q, ew_decay(ew, min(seg_len, T - s * seg_len)), lS, lp, lq);
       S = lS;
       p = lp;
       q = lq;
@@ -560,7 +560,7 @@ __global__ void wkv_carry_adj_kernel(float* adj, const float* w, int B, int T, i
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)B * C) return;
   const int b = static_cast<int>(i / C), c = static_cast<int>(i % C);
-  const float w2 = w[c] * kL2E;
+  const float ew = expf(w[c]);  // as make_lane2
   float e[5] = {kNegBig, 0.f, 0.f, 0.f, 0.f};
   for (int s = nseg - 1; s >= 0; --s) {
     float* r = adj + ((size_t)b * nseg + s) * 5 * (size_t)C + c;
@@ -568,7 +568,10 @@ __global__ void wkv_carry_adj_kernel(float* adj, const float* w, int B, int T, i
     if (s > 0)
       for (int f = 0; f < 5; ++f) l[f] = r[f * (size_t)C];
     for (int f = 0; f < 5; ++f) r[f * (size_t)C] = e[f];
-    if (s > 0) adj_combine1(l, e, min(seg_len, T - s * seg_len), w2);
+    if (s > 0) {
+      const int len = min(seg_len, T - s * seg_len);
+      adj_combine1(l, e, len, ew_decay(ew, len));
+    }
   }
 }
 

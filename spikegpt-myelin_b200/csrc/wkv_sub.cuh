@@ -133,23 +133,29 @@ __device__ __forceinline__ Pre prescan(const T* ks, const T* gys, int L) {
 // ---------------------------------------------------------- exact (slow) path
 
 // Forward over L steps of one lane with per-step rescaling (reference
-// wkv_triton.py:45-58). ks/vs/ys point at this lane's element of row 0.
+// wkv_triton.py:45-58). ks/vs/ys point at this lane's element of row 0; rows
+// are `stride` elements apart (kLanes in a staged tile, C in global memory).
 template <typename T, bool kY>
 __device__ __noinline__ void fwd_slow1(float& S, float& p, float& q, const T* ks, const T* vs,
-                                       T* ys, int L, float w2, float u2) {
+                                       T* ys, int L, float w2, float u2, int stride = kLanes) {
   using P = Pair<T>;
   float o = S;
   for (int i = 0; i < L; ++i) {
-    const float k = P::scalar(ks[i * kLanes]), v = P::scalar(vs[i * kLanes]);
+    const size_t r = (size_t)i * stride;
+    const float k = P::scalar(ks[r]), v = P::scalar(vs[r]);
     if (kY) {
       const float uk = u2 + k * kL2E;
       const float no = fmaxf(o, uk);
       const float a = ex2(o - no), b = ex2(uk - no);
-      ys[i * kLanes] = P::from_float(fmaf(a, p, b * v) * rcp(fmaf(a, q, b)));
+      ys[r] = P::from_float(fmaf(a, p, b * v) * rcp(fmaf(a, q, b)));
     }
     slow_update(o, p, q, k, v, w2);
   }
-  S = o;
+  // back to an integer scale (see fast_ok1)
+  S = ceilf(o);
+  const float f = ex2(o - S);
+  p *= f;
+  q *= f;
 }
 
 // Backward over L steps of one lane: for each step (last to first) replay the
@@ -195,11 +201,14 @@ __device__ __noinline__ void bwd_slow1(float S0, float p0, float q0, float (&adj
     gq = fmaf(aa, gq, -bb * y);
     G = ng;
   }
-  adj[0] = G;
-  adj[1] = gp;
-  adj[2] = gq;
-  adj[3] = hp;
-  adj[4] = hq;
+  // back to an integer scale (see fast_ok1)
+  const float Gi = ceilf(G);
+  const float f = ex2(G - Gi);
+  adj[0] = Gi;
+  adj[1] = gp * f;
+  adj[2] = gq * f;
+  adj[3] = hp * f;
+  adj[4] = hq * f;
 }
 
 // ------------------------------------------------------------- forward tile
