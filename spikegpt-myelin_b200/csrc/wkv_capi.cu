@@ -244,6 +244,26 @@ int make_map(CUtensorMap* m, int dtype, const void* ptr, int64_t B, int64_t T, i
   return WKV_OK;
 }
 
+// Checkpoint rows [rows][3][C] float32 as a 3-D map with dims {C, 3, rows} and a
+// [tiles][3][kLanes] box (the checkpoints of `tiles` consecutive tiles).
+int make_ckpt_map(CUtensorMap* m, const float* ptr, int64_t rows, int64_t C, int tiles) {
+  std::memset(m, 0, sizeof(*m));
+  if (ptr == nullptr) return WKV_OK;
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(WKV_ERR_DRIVER, "cuTensorMapEncodeTiled is not available");
+  const cuuint64_t dims[3] = {(cuuint64_t)C, 3u, (cuuint64_t)rows};
+  const cuuint64_t strides[2] = {(cuuint64_t)(C * 4), (cuuint64_t)(3 * C * 4)};
+  const cuuint32_t box[3] = {(cuuint32_t)kLanes, 3u, (cuuint32_t)tiles};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(ptr), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(WKV_ERR_DRIVER, "cuTensorMapEncodeTiled (checkpoints) failed (%d)", (int)r);
+  return WKV_OK;
+}
+
 // Device address of g_device_error_flags for the current device (looked up once
 // per device; the host-side symbol itself is not a device address).
 unsigned* device_err_ptr() {
@@ -303,9 +323,9 @@ int launch_forward(const void* k, const void* v, const float* decay, int decay_i
   int rc;
   if (p.tma) {
     if ((rc = make_map(&mk, dt, k, B, T, C, Tp<IO, TW>::kRoundRows)) ||
-        (rc = make_map(&mv, dt, v, B, T, C, Tp<IO, TW>::kRoundRows)))
+        (rc = make_map(&mv, dt, v, B, T, C, Tp<IO, TW>::kRoundRows)) ||
+        (rc = make_map(&my, dt, y, B, T, C, kSub)))
       return rc;
-    std::memset(&my, 0, sizeof(my));
   } else {
     std::memset(&mk, 0, sizeof(mk));
     std::memset(&mv, 0, sizeof(mv));
@@ -337,7 +357,7 @@ int launch_forward(const void* k, const void* v, const float* decay, int decay_i
       const cudaError_t e = allow_smem(wkv_fwd_tp_kernel<IO, TW, false>, sm);
       if (e != cudaSuccess) return cuda_fail(e, "setting the forward kernel's shared memory size");
       launch(K_FWD_STATE, st, [&] {
-        wkv_fwd_tp_kernel<IO, TW, false><<<dim3(gx, p.nseg - 1), 32 * TW, sm, st>>>(s, mk, mv);
+        wkv_fwd_tp_kernel<IO, TW, false><<<dim3(gx, p.nseg - 1), 32 * TW, sm, st>>>(s, mk, mv, my);
       });
     } else {
       const size_t sm = fwd_smem_bytes<IO>(false);
@@ -362,7 +382,7 @@ int launch_forward(const void* k, const void* v, const float* decay, int decay_i
     const cudaError_t e = allow_smem(wkv_fwd_tp_kernel<IO, TW, true>, sm);
     if (e != cudaSuccess) return cuda_fail(e, "setting the forward kernel's shared memory size");
     launch(K_FWD_Y, st, [&] {
-      wkv_fwd_tp_kernel<IO, TW, true><<<dim3(gx, p.nseg), 32 * TW, sm, st>>>(a, mk, mv);
+      wkv_fwd_tp_kernel<IO, TW, true><<<dim3(gx, p.nseg), 32 * TW, sm, st>>>(a, mk, mv, my);
     });
   } else {
     const size_t sm = fwd_smem_bytes<IO>(true);
@@ -383,19 +403,23 @@ int launch_backward(const void* gy, const float* w, const float* u, const void* 
   const int dt = sizeof(IO) == 4 ? WKV_DTYPE_F32
                  : std::is_same<IO, __nv_bfloat16>::value ? WKV_DTYPE_BF16
                                                          : WKV_DTYPE_F16;
-  CUtensorMap mk, mv, mgy, mgk, mgv, none;
+  constexpr int BW = tp_bwd_warps<IO>();
+  CUtensorMap mk, mv, mgy, mck, mgk, mgv, none;
   std::memset(&none, 0, sizeof(none));
-  int rc;
-  if (p.tma) {
-    if ((rc = make_map(&mk, dt, k, B, T, C)) || (rc = make_map(&mv, dt, v, B, T, C)) ||
-        (rc = make_map(&mgy, dt, gy, B, T, C)) || (rc = make_map(&mgk, dt, gk, B, T, C)) ||
-        (rc = make_map(&mgv, dt, gv, B, T, C)))
-      return rc;
-  } else {
-    mk = mv = mgy = mgk = mgv = none;
-  }
   const int ncblk = (C + kLanes - 1) / kLanes;
   const int nsub = (T + kSub - 1) / kSub;
+  const float* ckpt = state ? state : ws.ckpt;
+  int rc;
+  if (p.tma) {
+    constexpr int rows = TpB<IO, BW>::kRoundRows;
+    if ((rc = make_map(&mk, dt, k, B, T, C, rows)) || (rc = make_map(&mv, dt, v, B, T, C, rows)) ||
+        (rc = make_map(&mgy, dt, gy, B, T, C, rows)) ||
+        (rc = make_ckpt_map(&mck, ckpt, (int64_t)B * nsub, C, BW)) ||
+        (rc = make_map(&mgk, dt, gk, B, T, C, kSub)) || (rc = make_map(&mgv, dt, gv, B, T, C, kSub)))
+      return rc;
+  } else {
+    mk = mv = mgy = mck = mgk = mgv = none;
+  }
   const unsigned gx = (unsigned)ncblk * (unsigned)B;
   unsigned* err = device_err_ptr();
   const int force_slow = g_force_slow.load();
@@ -431,7 +455,7 @@ int launch_backward(const void* gy, const float* w, const float* u, const void* 
       const cudaError_t e = allow_smem(wkv_fwd_tp_kernel<IO, TW, false>, fsm);
       if (e != cudaSuccess) return cuda_fail(e, "setting the forward kernel's shared memory size");
       launch(K_FWD_STATE, st, [&] {
-        wkv_fwd_tp_kernel<IO, TW, false><<<dim3(gx, p.nseg), 32 * TW, fsm, st>>>(f, rk, rv);
+        wkv_fwd_tp_kernel<IO, TW, false><<<dim3(gx, p.nseg), 32 * TW, fsm, st>>>(f, rk, rv, none);
       });
     } else {
       const size_t fsm = fwd_smem_bytes<IO>(false);
@@ -456,7 +480,7 @@ int launch_backward(const void* gy, const float* w, const float* u, const void* 
   a.seg_len = p.seg_len;
   a.nseg = p.nseg;
   a.nsub = nsub;
-  a.ckpt = state ? state : ws.ckpt;
+  a.ckpt = ckpt;
   a.force_slow = force_slow;
   a.err = err;
   const int64_t lanes = (int64_t)B * C;
@@ -472,15 +496,21 @@ int launch_backward(const void* gy, const float* w, const float* u, const void* 
     s.seg_start = state ? nullptr : ws.seg;
     s.seg_base = 1;
     s.adj_out = ws.adj;
-    const size_t ssm = bwd_smem_bytes<IO>(false);
-    launch(K_BWD_ADJ, st, [&] {
-      if (p.tma)
-        wkv_bwd_kernel<IO, false, true>
-            <<<dim3(gx, p.nseg - 1), kThreads, ssm, st>>>(s, mk, mv, mgy, none, none);
-      else
+    if (p.tma) {
+      const size_t ssm = bwd_tp_smem_bytes<IO, BW>();
+      const cudaError_t e = allow_smem(wkv_bwd_tp_kernel<IO, BW, false>, ssm);
+      if (e != cudaSuccess) return cuda_fail(e, "setting the backward kernel's shared memory size");
+      launch(K_BWD_ADJ, st, [&] {
+        wkv_bwd_tp_kernel<IO, BW, false>
+            <<<dim3(gx, p.nseg - 1), 32 * BW, ssm, st>>>(s, mk, mv, mgy, mck, none, none);
+      });
+    } else {
+      const size_t ssm = bwd_smem_bytes<IO>(false);
+      launch(K_BWD_ADJ, st, [&] {
         wkv_bwd_kernel<IO, false, false>
             <<<dim3(gx, p.nseg - 1), kThreads, ssm, st>>>(s, mk, mv, mgy, none, none);
-    });
+      });
+    }
     launch(K_CARRY_ADJ, st, [&] {
       wkv_carry_adj_kernel<<<cgrid, 128, 0, st>>>(ws.adj, w, B, T, C, p.nseg, p.seg_len);
     });
@@ -493,20 +523,23 @@ int launch_backward(const void* gy, const float* w, const float* u, const void* 
   a.tickets = state ? state_tickets : ws.tickets;
   a.gtd = gtd;
   a.gtf = gtf;
-  const size_t bsm = bwd_smem_bytes<IO>(true);
-  {
-    const cudaError_t e = p.tma ? allow_smem(wkv_bwd_kernel<IO, true, true>, bsm)
-                                : allow_smem(wkv_bwd_kernel<IO, true, false>, bsm);
+  if (p.tma) {
+    const size_t bsm = bwd_tp_smem_bytes<IO, BW>();
+    const cudaError_t e = allow_smem(wkv_bwd_tp_kernel<IO, BW, true>, bsm);
     if (e != cudaSuccess) return cuda_fail(e, "setting the backward kernel's shared memory size");
-  }
-  launch(K_BWD_GRAD, st, [&] {
-    if (p.tma)
-      wkv_bwd_kernel<IO, true, true>
-          <<<dim3(gx, p.nseg), kThreads, bsm, st>>>(a, mk, mv, mgy, mgk, mgv);
-    else
+    launch(K_BWD_GRAD, st, [&] {
+      wkv_bwd_tp_kernel<IO, BW, true>
+          <<<dim3(gx, p.nseg), 32 * BW, bsm, st>>>(a, mk, mv, mgy, mck, mgk, mgv);
+    });
+  } else {
+    const size_t bsm = bwd_smem_bytes<IO>(true);
+    const cudaError_t e = allow_smem(wkv_bwd_kernel<IO, true, false>, bsm);
+    if (e != cudaSuccess) return cuda_fail(e, "setting the backward kernel's shared memory size");
+    launch(K_BWD_GRAD, st, [&] {
       wkv_bwd_kernel<IO, true, false>
-          <<<dim3(gx, p.nseg), kThreads, bsm, st>>>(a, mk, mv, mgy, mgk, mgv);
-  });
+          <<<dim3(gx, p.nseg), kThreads, bsm, st>>>(a, mk, mv, mgy, none, none);
+    });
+  }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "wkv backward launch");
   return WKV_OK;

@@ -177,6 +177,42 @@ __device__ __forceinline__ void report_timeout(unsigned* err) {
   if (err) atomicOr(err, 1u);
 }
 
+// The last CTA of a column block: sum the per-lane partials of all rows (batch
+// row x segment) in a fixed order, in double, and write grad_time_decay =
+// w * sum dL/dw and grad_time_first = sum dL/du for the lane's two channels.
+__device__ __forceinline__ void reduce_time_grads(const BwdArgs& a, int c, bool v0, bool v1, f2 w,
+                                                  int rows) {
+  double sw0 = 0.0, su0 = 0.0, sw1 = 0.0, su1 = 0.0;
+  const float* base = a.partial + c;
+  for (int r0 = 0; r0 < rows; r0 += 8) {
+    float pw0[8], pu0[8], pw1[8], pu1[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const bool in = r0 + i < rows;
+      const size_t o = (size_t)(r0 + i) * 2 * a.C;
+      pw0[i] = (in && v0) ? __ldcg(base + o) : 0.f;
+      pu0[i] = (in && v0) ? __ldcg(base + o + a.C) : 0.f;
+      pw1[i] = (in && v1) ? __ldcg(base + o + 1) : 0.f;
+      pu1[i] = (in && v1) ? __ldcg(base + o + a.C + 1) : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      sw0 += pw0[i];
+      su0 += pu0[i];
+      sw1 += pw1[i];
+      su1 += pu1[i];
+    }
+  }
+  if (v0) {
+    a.gtd[c] = static_cast<float>(static_cast<double>(w.x) * sw0);
+    a.gtf[c] = static_cast<float>(su0);
+  }
+  if (v1) {
+    a.gtd[c + 1] = static_cast<float>(static_cast<double>(w.y) * sw1);
+    a.gtf[c + 1] = static_cast<float>(su1);
+  }
+}
+
 // ------------------------------------------------------------------ forward
 
 template <typename T, bool kY, bool kTma>
@@ -480,35 +516,7 @@ __global__ void __launch_bounds__(kThreads)
   if (ticket + 1 != static_cast<unsigned>(rows)) return;
   __threadfence();
   if (lane == 0) a.tickets[cb] = 0u;  // ready for a later call that reuses the counters
-  double sw0 = 0.0, su0 = 0.0, sw1 = 0.0, su1 = 0.0;
-  const float* base = a.partial + c;
-  for (int r0 = 0; r0 < rows; r0 += 8) {
-    float pw0[8], pu0[8], pw1[8], pu1[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const bool in = r0 + i < rows;
-      const size_t o = (size_t)(r0 + i) * 2 * a.C;
-      pw0[i] = (in && v0) ? __ldcg(base + o) : 0.f;
-      pu0[i] = (in && v0) ? __ldcg(base + o + a.C) : 0.f;
-      pw1[i] = (in && v1) ? __ldcg(base + o + 1) : 0.f;
-      pu1[i] = (in && v1) ? __ldcg(base + o + a.C + 1) : 0.f;
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      sw0 += pw0[i];
-      su0 += pu0[i];
-      sw1 += pw1[i];
-      su1 += pu1[i];
-    }
-  }
-  if (v0) {
-    a.gtd[c] = static_cast<float>(static_cast<double>(lc.w.x) * sw0);
-    a.gtf[c] = static_cast<float>(su0);
-  }
-  if (v1) {
-    a.gtd[c + 1] = static_cast<float>(static_cast<double>(lc.w.y) * sw1);
-    a.gtf[c + 1] = static_cast<float>(su1);
-  }
+  reduce_time_grads(a, c, v0, v1, lc.w, rows);
 }
 
 // ------------------------------------------------------------------- carries

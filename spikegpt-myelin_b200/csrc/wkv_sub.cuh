@@ -133,11 +133,13 @@ __device__ __forceinline__ Pre prescan(const T* ks, const T* gys, int L) {
 // ---------------------------------------------------------- exact (slow) path
 
 // Forward over L steps of one lane with per-step rescaling (reference
-// wkv_triton.py:45-58). ks/vs/ys point at this lane's element of row 0; rows
-// are `stride` elements apart (kLanes in a staged tile, C in global memory).
+// wkv_triton.py:45-58). ks/vs/ys point at this lane's element of row 0; input
+// rows are `stride` elements apart, output rows `ystride` (kLanes in a staged
+// tile, C in global memory).
 template <typename T, bool kY>
 __device__ __noinline__ void fwd_slow1(float& S, float& p, float& q, const T* ks, const T* vs,
-                                       T* ys, int L, float w2, float u2, int stride = kLanes) {
+                                       T* ys, int L, float w2, float u2, int stride = kLanes,
+                                       int ystride = kLanes) {
   using P = Pair<T>;
   float o = S;
   for (int i = 0; i < L; ++i) {
@@ -147,7 +149,7 @@ __device__ __noinline__ void fwd_slow1(float& S, float& p, float& q, const T* ks
       const float uk = u2 + k * kL2E;
       const float no = fmaxf(o, uk);
       const float a = ex2(o - no), b = ex2(uk - no);
-      ys[r] = P::from_float(fmaf(a, p, b * v) * rcp(fmaf(a, q, b)));
+      ys[(size_t)i * ystride] = P::from_float(fmaf(a, p, b * v) * rcp(fmaf(a, q, b)));
     }
     slow_update(o, p, q, k, v, w2);
   }
@@ -163,18 +165,22 @@ __device__ __noinline__ void fwd_slow1(float& S, float& p, float& q, const T* ks
 // wkv_triton.py:93-115), then take the reverse step of wkv_triton.py:124-142
 // with its own adjoint log-scale G (adj = {G, gp, gq, hp, hq}, see Adj2).
 // O(L^2) work; only taken when the fast path's range checks fail.
+// Inputs are read at rows `istride` elements apart, outputs written `ostride`
+// apart (kLanes in a staged tile, C in global memory).
 template <typename T, bool kOut>
 __device__ __noinline__ void bwd_slow1(float S0, float p0, float q0, float (&adj)[5], const T* ks,
                                        const T* vs, const T* gys, T* gks, T* gvs, int L, float w2,
-                                       float u2, float& gwacc, float& gu) {
+                                       float u2, float& gwacc, float& gu, int istride = kLanes,
+                                       int ostride = kLanes) {
   using P = Pair<T>;
   float G = adj[0], gp = adj[1], gq = adj[2], hp = adj[3], hq = adj[4];
   for (int i = L - 1; i >= 0; --i) {
     float o = S0, pp = p0, qq = q0;
     for (int j = 0; j < i; ++j)
-      slow_update(o, pp, qq, P::scalar(ks[j * kLanes]), P::scalar(vs[j * kLanes]), w2);
-    const float k = P::scalar(ks[i * kLanes]), v = P::scalar(vs[i * kLanes]);
-    const float gy = P::scalar(gys[i * kLanes]);
+      slow_update(o, pp, qq, P::scalar(ks[(size_t)j * istride]), P::scalar(vs[(size_t)j * istride]), w2);
+    const size_t ri = (size_t)i * istride;
+    const float k = P::scalar(ks[ri]), v = P::scalar(vs[ri]);
+    const float gy = P::scalar(gys[ri]);
     const float k2 = k * kL2E, uk = u2 + k2;
     const float no = fmaxf(o, uk);
     const float a = ex2(o - no), b = ex2(uk - no);
@@ -187,8 +193,8 @@ __device__ __noinline__ void bwd_slow1(float S0, float p0, float q0, float (&adj
     const float ekg = live ? ex2(k2 + G) : 0.f;  // e^k 2^G
     gwacc = fmaf(ekg, fmaf(v, hp, hq), gwacc);
     if (kOut) {
-      gvs[i * kLanes] = P::from_float(fmaf(ekg, gp, A));
-      gks[i * kLanes] = P::from_float(fmaf(ekg, fmaf(gp, v, gq), av));
+      gvs[(size_t)i * ostride] = P::from_float(fmaf(ekg, gp, A));
+      gks[(size_t)i * ostride] = P::from_float(fmaf(ekg, fmaf(gp, v, gq), av));
     }
     // dL/dP_t = gy / D_t + e^w dL/dP_{t+1} with 1/D_t = iden 2^{-no};
     // H_t = e^w (dL/dP_{t+1} + H_{t+1})

@@ -36,16 +36,21 @@ struct Tp {
   static constexpr int kRoundRows = W * kSub;  // steps per round = rows of one TMA box
   static constexpr int kBoxElems = kRoundRows * kLanes;
   static constexpr uint32_t kBoxBytes = kBoxElems * sizeof(T);
-  static constexpr int kFwdStages = 3;
-  static constexpr int kSumFloats = 2 * W * 3 * kLanes;  // [2 rounds][W tiles][S,p,q][lanes]
+  // Two stages: a stage is read only in phase A, so the box of round r+2 is
+  // requested a whole round before it is needed.
+  static constexpr int kFwdStages = 2;
+  // [2 rounds][W tile summaries + the state after the round][S, p, q][lanes]
+  static constexpr int kSumFloats = 2 * (W + 1) * 3 * kLanes;
+  static constexpr uint32_t kYTileBytes = kSub * kLanes * sizeof(T);  // one warp's staged y tile
   static_assert(kSegAlign % kSub == 0, "segments start on tile boundaries");
 };
 
+// Shared memory: k stages | v stages | summaries | y tiles | barriers.
 template <typename T, int W>
 constexpr size_t fwd_tp_smem_bytes() {
   using G = Tp<T, W>;
   return (size_t)2 * G::kFwdStages * G::kBoxBytes + G::kSumFloats * sizeof(float) +
-         8 * G::kFwdStages;
+         W * G::kYTileBytes + 8 * G::kFwdStages;
 }
 
 // Packed max/min of k over rows [0, n) of a register tile (all kSub rows
@@ -103,11 +108,11 @@ __device__ __forceinline__ void fwd_tp_summary(const typename Pair<T>::raw (&kr)
 }
 
 // Phase C of the forward: y for the n rows of the tile from the carry-in
-// (sc, p, q), with e^{k_i - sc} = ek[i] * c2.
+// (sc, p, q), with e^{k_i - sc} = ek[i] * c2, into a staged tile.
 template <typename T, bool kTail>
 __device__ __forceinline__ void fwd_tp_y(const typename Pair<T>::raw (&vr)[kSub],
                                          const f2 (&ek)[kSub], int n, const Lane2& lc, f2 c2, f2 p,
-                                         f2 q, T* yrow, size_t ystride, bool v0, bool v1) {
+                                         f2 q, T* ys) {
   using P = Pair<T>;
 #pragma unroll
   for (int i = 0; i < kSub; ++i) {
@@ -116,10 +121,7 @@ __device__ __forceinline__ void fwd_tp_y(const typename Pair<T>::raw (&vr)[kSub]
     const f2 e = mul2(ek[i], c2);
     const f2 eb = mul2(e, lc.eu);
     const f2 y = mul2(fma2(eb, v, p), rcpx2(add2(q, eb)));
-    if (v1)
-      P::st(yrow + i * ystride, P::pack(y));
-    else if (v0)
-      yrow[i * ystride] = P::from_float(y.x);
+    P::st(ys + i * kLanes, P::pack(y));  // staged [kSub][kLanes] tile
     p = fma2(lc.ew, p, mul2(e, v));
     q = fma2(lc.ew, q, e);
   }
@@ -140,13 +142,28 @@ __device__ __forceinline__ void store_state2(float* base, size_t row, int C, int
   }
 }
 
+// Exact (per-step rescaling) y of a tile from its carry-in, reading k, v from
+// global memory and writing the staged y tile. Rare: only when the fast path's
+// range checks fail.
+template <typename T>
+__device__ __noinline__ void fwd_tp_exact(const FwdArgs& a, int b, int t0, int c, bool v0, bool v1,
+                                          int n, Fwd2 sin, Lane2 lc, T* ys) {
+  const size_t base = ((size_t)b * a.T + t0) * a.C + c;
+  const T* kg = static_cast<const T*>(a.k) + base;
+  const T* vg = static_cast<const T*>(a.v) + base;
+  if (v0) fwd_slow1<T, true>(sin.S.x, sin.p.x, sin.q.x, kg, vg, ys, n, lc.w2.x, lc.u2.x, a.C, kLanes);
+  if (v1)
+    fwd_slow1<T, true>(sin.S.y, sin.p.y, sin.q.y, kg + 1, vg + 1, ys + 1, n, lc.w2.y, lc.u2.y, a.C,
+                       kLanes);
+}
+
 // Forward. kY: write y (and checkpoints when a.ckpt != null); !kY: the state
 // sweep (checkpoints and/or segment-end states only). Grid (B * ncblk, nseg),
 // W warps per CTA; reference wkv_triton.py:34-58.
 template <typename T, int W, bool kY>
 __global__ void __launch_bounds__(32 * W, 4)
     wkv_fwd_tp_kernel(const FwdArgs a, const __grid_constant__ CUtensorMap tk,
-                      const __grid_constant__ CUtensorMap tv) {
+                      const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap ty) {
   using G = Tp<T, W>;
   using P = Pair<T>;
   using raw = typename P::raw;
@@ -156,9 +173,11 @@ __global__ void __launch_bounds__(32 * W, 4)
   T* kbuf = reinterpret_cast<T*>(smem);
   T* vbuf = kbuf + NS * G::kBoxElems;
   float* sum = reinterpret_cast<float*>(vbuf + NS * G::kBoxElems);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sum + G::kSumFloats);
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  T* ys = reinterpret_cast<T*>(sum + G::kSumFloats) + warp * kSub * kLanes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(sum + G::kSumFloats) +
+                                               W * G::kYTileBytes);
+
   const int cb = blockIdx.x % a.ncblk, b = blockIdx.x / a.ncblk;
   const int c = cb * kLanes + 2 * lane;
   const int seg = blockIdx.y + a.seg_base;
@@ -182,9 +201,9 @@ __global__ void __launch_bounds__(32 * W, 4)
   if (a.zero_tickets != nullptr && blockIdx.x == 0 && blockIdx.y == 0)
     for (int i = threadIdx.x; i < a.nzero; i += blockDim.x) a.zero_tickets[i] = 0u;
 
-  Fwd2 st = fwd_identity2();
+  Fwd2 start = fwd_identity2();  // state at the segment start
   if (a.seg_start != nullptr)
-    load3(a.seg_start, (size_t)b * a.nseg + seg, a.C, c, v0, v1, st.S, st.p, st.q);
+    load3(a.seg_start, (size_t)b * a.nseg + seg, a.C, c, v0, v1, start.S, start.p, start.q);
 
   auto issue = [&](int r) {
     const int s = r % NS;
@@ -198,16 +217,20 @@ __global__ void __launch_bounds__(32 * W, 4)
     fence_barrier_init();
     prefetch_tensormap(&tk);
     prefetch_tensormap(&tv);
+    if (kY) prefetch_tensormap(&ty);
   }
   __syncthreads();
   if (threadIdx.x == 0)
     for (int r = 0; r < min(NS, nrounds); ++r) issue(r);
 
+  Fwd2 cur = start;  // warp W-1: the state after the latest round
 #pragma unroll 1
   for (int r = 0; r < nrounds; ++r) {
     const int s = r % NS;
-    const int t0 = t_begin + r * G::kRoundRows + warp * R;  // this warp's tile
+    const int rt0 = t_begin + r * G::kRoundRows;
+    const int t0 = rt0 + warp * R;  // this warp's tile
     const int n = max(0, min(R, t_end - t0));
+    float* sr = sum + (r & 1) * (W + 1) * 3 * kLanes;  // this round's summaries
     const bool arrived = mbar_wait_bounded(&bars[s], (r / NS) & 1);
 
     // A. summary of the tile from a zero state, scaled by 2^-sj, sj = ceil(max k log2 e)
@@ -228,7 +251,7 @@ __global__ void __launch_bounds__(32 * W, 4)
       if (n == 0) sj = splat(kNegBig);
     }
     {
-      f2* sw = reinterpret_cast<f2*>(sum + ((r & 1) * W + warp) * 3 * kLanes) + lane;
+      f2* sw = reinterpret_cast<f2*>(sr + warp * 3 * kLanes) + lane;
       sw[0] = sj;
       sw[kLanes / 2] = lp;
       sw[kLanes] = lq;
@@ -239,56 +262,510 @@ __global__ void __launch_bounds__(32 * W, 4)
         report_timeout(a.err);
         for (int q = r; q < min(r + NS, nrounds); ++q) mbar_wait_bounded(&bars[q % NS], (q / NS) & 1);
       }
+      if (kY && lane == 0) bulk_wait_all();
       return;
     }
     if (threadIdx.x == 0 && r + NS < nrounds) issue(r + NS);
 
-    // B. carry-in of this warp's tile; st becomes the state after the round
-    Fwd2 sin = st;
+    // B. carry-in of this warp's tile: the round's start state (left in shared
+    // memory by warp W-1 during the previous round) folded with the summaries
+    // of the earlier tiles of the round; warp W-1 also folds its own tile and
+    // leaves the result for the next round.
+    Fwd2 sin = start;
+    if (r > 0) {
+      const f2* ps = reinterpret_cast<const f2*>(sum + ((r - 1) & 1) * (W + 1) * 3 * kLanes +
+                                                 W * 3 * kLanes) + lane;
+      sin = Fwd2{ps[0], ps[kLanes / 2], ps[kLanes]};
+    }
 #pragma unroll
-    for (int m = 0; m < W; ++m) {
-      const f2* sm = reinterpret_cast<const f2*>(sum + ((r & 1) * W + m) * 3 * kLanes) + lane;
-      const Fwd2 l{sm[0], sm[kLanes / 2], sm[kLanes]};
-      const int nm = max(0, min(R, t_end - (t_begin + r * G::kRoundRows + m * R)));
-      if (m == warp) sin = st;
-      st = fwd_combine2(st, nm, lc, l);
+    for (int m = 0; m < W - 1; ++m) {
+      if (m < warp) {
+        const f2* sm = reinterpret_cast<const f2*>(sr + m * 3 * kLanes) + lane;
+        sin = fwd_combine2(sin, min(R, max(0, t_end - (rt0 + m * R))), lc,
+                           Fwd2{sm[0], sm[kLanes / 2], sm[kLanes]});
+      }
+    }
+    if (warp == W - 1) {
+      cur = fwd_combine2(sin, n, lc, Fwd2{sj, lp, lq});
+      f2* pw = reinterpret_cast<f2*>(sr + W * 3 * kLanes) + lane;
+      pw[0] = cur.S;
+      pw[kLanes / 2] = cur.p;
+      pw[kLanes] = cur.q;
     }
 
     // C. outputs of the tile from its carry-in
     if (n > 0) {
       if (a.ckpt != nullptr) store_state2(a.ckpt, (size_t)b * a.nsub + t0 / kSub, a.C, c, v0, v1, sin);
       if (kY) {
+        if (lane == 0) bulk_wait_read<0>();  // the previous tile's store has read ys
+        __syncwarp();
         f2 sc, p, q;
         const bool ok = fast_ok1(sin.S.x, sin.p.x, sin.q.x, kmax.x, kmin.x, n, lc.w2.x, lc.u2.x,
                                  sc.x, p.x, q.x) &&
                         fast_ok1(sin.S.y, sin.p.y, sin.q.y, kmax.y, kmin.y, n, lc.w2.y, lc.u2.y,
                                  sc.y, p.y, q.y) &&
                         !force_slow;
-        const f2 c2 = ex2x2(sub2(sj, sc));  // e^{k - sj} -> e^{k - sc}
-        T* yrow = static_cast<T*>(a.y) + ((size_t)b * a.T + t0) * a.C + c;
-        if (n == R)
-          fwd_tp_y<T, false>(vr, ek, n, lc, c2, p, q, yrow, (size_t)a.C, v0, v1);
-        else
-          fwd_tp_y<T, true>(vr, ek, n, lc, c2, p, q, yrow, (size_t)a.C, v0, v1);
-        if (!__all_sync(kFull, ok)) {
-          // exact per-step rescaling from the carry-in, reading k, v from memory
-          const size_t base = ((size_t)b * a.T + t0) * a.C + c;
-          const T* kg = static_cast<const T*>(a.k) + base;
-          const T* vg = static_cast<const T*>(a.v) + base;
-          if (v0) {
-            float S0 = sin.S.x, p0 = sin.p.x, q0 = sin.q.x;
-            fwd_slow1<T, true>(S0, p0, q0, kg, vg, yrow, n, lc.w2.x, lc.u2.x, a.C);
-          }
-          if (v1) {
-            float S1 = sin.S.y, p1 = sin.p.y, q1 = sin.q.y;
-            fwd_slow1<T, true>(S1, p1, q1, kg + 1, vg + 1, yrow + 1, n, lc.w2.y, lc.u2.y, a.C);
-          }
+        const f2 c2 = ex2x2(sub2(sj, sc));  // e^{k - sj} -> e^{k - sc}; integer exponents
+        if (__all_sync(kFull, ok)) {
+          if (n == R)
+            fwd_tp_y<T, false>(vr, ek, n, lc, c2, p, q, ys + 2 * lane);
+          else
+            fwd_tp_y<T, true>(vr, ek, n, lc, c2, p, q, ys + 2 * lane);
+        } else {
+          fwd_tp_exact<T>(a, b, t0, c, v0, v1, n, sin, lc, ys + 2 * lane);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(&ty, ys, cb * kLanes, t0, b);
+          bulk_commit();
         }
       }
     }
   }
-  if (a.seg_end != nullptr && warp == 0)
-    store3(a.seg_end, (size_t)b * a.nseg + seg, a.C, c, v0, v1, st.S, st.p, st.q);
+  if (kY && lane == 0) bulk_wait_all();
+  if (a.seg_end != nullptr && warp == W - 1)
+    store3(a.seg_end, (size_t)b * a.nseg + seg, a.C, c, v0, v1, cur.S, cur.p, cur.q);
+}
+
+// ----------------------------------------------------------------- backward
+//
+// Rounds go backwards in time; warp w of a round takes the w-th of its W tiles
+// (in time order), so warp W-1 holds the latest tile.
+//   A. from the tile's checkpoint (its forward state, saved by the forward or the
+//      state sweep) recompute y_t and gy_t/D_t over the tile, then run the
+//      adjoint recurrence backwards over the tile from a zero adjoint: the
+//      tile's local adjoint summary (the adjoint recurrence is linear in the
+//      adjoint, so summaries compose with adj_combine1);
+//   B. fold the summaries, latest tile first, into the adjoint entering the
+//      round: the fold down to a warp's tile end is its incoming adjoint, the
+//      full fold enters the next round;
+//   C. rerun the reverse recurrence from the incoming adjoint, writing
+//      grad_key / grad_value and accumulating dL/dw, dL/du.
+
+// Warps per backward CTA (the backward keeps y and gy/D of a tile in registers
+// across the round barrier, ~150 registers a thread; 4 CTAs of 2 warps fit an
+// SM, so B*C = 32768 runs in one wave).
+template <typename T>
+constexpr int tp_bwd_warps() {
+  return 2;
+}
+
+template <typename T, int W>
+struct TpB {
+  static constexpr int kRoundRows = W * kSub;
+  static constexpr int kBoxElems = kRoundRows * kLanes;
+  static constexpr uint32_t kBoxBytes = kBoxElems * sizeof(T);
+  static constexpr uint32_t kCkBytes = W * 3 * kLanes * sizeof(float);  // W checkpoint rows
+  static constexpr uint32_t kStageBytes = 3 * kBoxBytes + kCkBytes;     // k, v, gy, ckpt
+  static constexpr int kStages = sizeof(T) == 4 ? 2 : 3;
+  static constexpr int kSumFloats = 2 * W * 5 * kLanes;  // [2 rounds][W][G,gp,gq,hp,hq][lanes]
+  static constexpr uint32_t kOutTileBytes = kSub * kLanes * sizeof(T);  // one warp's gk (or gv) tile
+  static constexpr uint32_t kOutBytes = W * 2 * kOutTileBytes;          // [W][gk, gv] tiles
+  static_assert(kBoxBytes % 128 == 0 && kCkBytes % 128 == 0, "128-byte aligned boxes");
+};
+
+// Shared memory: stages | summaries | per-warp partial sums | output tiles | barriers.
+template <typename T, int W>
+constexpr size_t bwd_tp_smem_bytes() {
+  using G = TpB<T, W>;
+  return (size_t)G::kStages * G::kStageBytes + G::kSumFloats * sizeof(float) +
+         W * 2 * kLanes * sizeof(float) + G::kOutBytes + 8 * G::kStages;
+}
+
+// Packed max |grad_y| over rows [0, n) of a register tile.
+template <typename T, bool kTail>
+__device__ __forceinline__ f2 tile_absmax(const typename Pair<T>::raw (&gr)[kSub], int n) {
+  using Sc = Scan<T>;
+  using raw = typename Pair<T>::raw;
+  raw g[kSub / 2];
+#pragma unroll
+  for (int i = 0; i < kSub / 2; ++i) {
+    const bool i0 = !kTail || i < n, i1 = !kTail || i + kSub / 2 < n;
+    g[i] = Sc::vmax(Sc::vabs(i0 ? gr[i] : scan_lo<T>()), Sc::vabs(i1 ? gr[i + kSub / 2] : scan_lo<T>()));
+  }
+#pragma unroll
+  for (int w = kSub / 4; w > 0; w /= 2) {
+#pragma unroll
+    for (int i = 0; i < w; ++i) g[i] = Sc::vmax(g[i], g[i + w]);
+  }
+  return Pair<T>::unpack(g[0]);
+}
+
+// Forward recompute of a tile from its start state rescaled to the tile scale
+// s: ry = y_t, rg = gy_t 2^s / D_t.
+template <typename T, bool kTail>
+__device__ __forceinline__ void bwd_tp_recompute(const typename Pair<T>::raw (&kr)[kSub],
+                                                 const typename Pair<T>::raw (&vr)[kSub],
+                                                 const typename Pair<T>::raw (&gr)[kSub], int n,
+                                                 const Lane2& lc, f2 s, f2 p, f2 q,
+                                                 f2 (&ry)[kSub], f2 (&rg)[kSub]) {
+  using P = Pair<T>;
+  const f2 l2e = splat(kL2E), ns = f2{-s.x, -s.y};
+#pragma unroll
+  for (int i = 0; i < kSub; ++i) {
+    if (kTail && i >= n) {
+      ry[i] = splat(0.f);
+      rg[i] = splat(0.f);
+      continue;
+    }
+    const f2 v = P::unpack(vr[i]);
+    const f2 ek = ex2x2(fma2(P::unpack(kr[i]), l2e, ns));
+    const f2 eb = mul2(ek, lc.eu);
+    const f2 rd = rcpx2(add2(q, eb));
+    ry[i] = mul2(fma2(eb, v, p), rd);
+    rg[i] = mul2(P::unpack(gr[i]), rd);
+    p = fma2(lc.ew, p, mul2(ek, v));
+    q = fma2(lc.ew, q, ek);
+  }
+}
+
+// The tile's adjoint summary: the reverse recurrence over its rows from a zero
+// adjoint at the tile end (scaled by 2^s, like rg).
+template <bool kTail>
+__device__ __forceinline__ void bwd_tp_summary(const f2 (&ry)[kSub], const f2 (&rg)[kSub], int n,
+                                               const Lane2& lc, f2& gp, f2& gq, f2& hp, f2& hq) {
+  gp = gq = hp = hq = splat(0.f);
+#pragma unroll
+  for (int i = kSub - 1; i >= 0; --i) {
+    if (kTail && i >= n) continue;
+    hp = mul2(lc.ew, add2(gp, hp));
+    hq = mul2(lc.ew, add2(gq, hq));
+    gq = sub2(mul2(lc.ew, gq), mul2(rg[i], ry[i]));
+    gp = fma2(lc.ew, gp, rg[i]);
+  }
+}
+
+// Reverse pass of a tile from the adjoint at its end (scaled by 2^s): grad_key /
+// grad_value of its rows (kOut) and dL/dw, dL/du accumulated into gw, gu.
+template <typename T, bool kTail, bool kOut>
+__device__ __forceinline__ void bwd_tp_outputs(const typename Pair<T>::raw (&kr)[kSub],
+                                               const typename Pair<T>::raw (&vr)[kSub],
+                                               const f2 (&ry)[kSub], const f2 (&rg)[kSub], int n,
+                                               const Lane2& lc, f2 s, f2 gp, f2 gq, f2 hp, f2 hq,
+                                               T* gks, T* gvs, f2& gw, f2& gu) {
+  using P = Pair<T>;
+  const f2 l2e = splat(kL2E), ns = f2{-s.x, -s.y};
+#pragma unroll
+  for (int i = kSub - 1; i >= 0; --i) {
+    if (kTail && i >= n) continue;
+    const f2 v = P::unpack(vr[i]);
+    const f2 ek = ex2x2(fma2(P::unpack(kr[i]), l2e, ns));
+    const f2 a = mul2(mul2(rg[i], ek), lc.eu);  // gy e^{u+k} / D
+    const f2 av = mul2(a, sub2(v, ry[i]));
+    gu = add2(gu, av);
+    gw = fma2(ek, fma2(v, hp, hq), gw);
+    if (kOut) {  // staged [kSub][kLanes] tiles
+      P::st(gvs + i * kLanes, P::pack(fma2(ek, gp, a)));
+      P::st(gks + i * kLanes, P::pack(fma2(ek, fma2(gp, v, gq), av)));
+    }
+    hp = mul2(lc.ew, add2(gp, hp));
+    hq = mul2(lc.ew, add2(gq, hq));
+    gq = sub2(mul2(lc.ew, gq), mul2(rg[i], ry[i]));
+    gp = fma2(lc.ew, gp, rg[i]);
+  }
+}
+
+__device__ __forceinline__ Adj2 adj_combine2(const Adj2& l, Adj2 e, int len, const Lane2& lc) {
+  Decay1 dx, dy;
+  if (len == kSub) {
+    dx = Decay1{lc.dm16.x, lc.de16.x};
+    dy = Decay1{lc.dm16.y, lc.de16.y};
+  } else {
+    dx = ew_decay(lc.ew.x, len);
+    dy = ew_decay(lc.ew.y, len);
+  }
+  float lx[5] = {l.G.x, l.gp.x, l.gq.x, l.hp.x, l.hq.x};
+  float ly[5] = {l.G.y, l.gp.y, l.gq.y, l.hp.y, l.hq.y};
+  float ex[5] = {e.G.x, e.gp.x, e.gq.x, e.hp.x, e.hq.x};
+  float ey[5] = {e.G.y, e.gp.y, e.gq.y, e.hp.y, e.hq.y};
+  adj_combine1(lx, ex, len, dx);
+  adj_combine1(ly, ey, len, dy);
+  return Adj2{f2{ex[0], ey[0]}, f2{ex[1], ey[1]}, f2{ex[2], ey[2]}, f2{ex[3], ey[3]}, f2{ex[4], ey[4]}};
+}
+
+// Exact (per-step rescaling) adjoint summary of a staged tile from a zero
+// adjoint, both channels of the lane pair. Rare: only when the fast path's
+// range checks fail.
+template <typename T>
+__device__ __noinline__ Adj2 bwd_tp_exact_summary(const T* ks, const T* vs, const T* gys, int n,
+                                                  Fwd2 st0, Lane2 lc) {
+  float lx[5] = {kNegBig, 0.f, 0.f, 0.f, 0.f}, ly[5] = {kNegBig, 0.f, 0.f, 0.f, 0.f};
+  float d0 = 0.f, d1 = 0.f;
+  bwd_slow1<T, false>(st0.S.x, st0.p.x, st0.q.x, lx, ks, vs, gys, nullptr, nullptr, n, lc.w2.x,
+                      lc.u2.x, d0, d1);
+  bwd_slow1<T, false>(st0.S.y, st0.p.y, st0.q.y, ly, ks + 1, vs + 1, gys + 1, nullptr, nullptr, n,
+                      lc.w2.y, lc.u2.y, d0, d1);
+  return Adj2{f2{lx[0], ly[0]}, f2{lx[1], ly[1]}, f2{lx[2], ly[2]}, f2{lx[3], ly[3]}, f2{lx[4], ly[4]}};
+}
+
+// Exact reverse pass of a tile from its incoming adjoint, reading k, v, gy from
+// global memory and writing grad_key / grad_value into the staged tiles. Rare.
+template <typename T>
+__device__ __noinline__ void bwd_tp_exact(const BwdArgs& a, int b, int t0, int c, bool v0, bool v1,
+                                          int n, Fwd2 st0, Adj2 ein, Lane2 lc, T* gks, T* gvs,
+                                          f2& gw, f2& gu) {
+  const size_t row = ((size_t)b * a.T + t0) * a.C + c;
+  const T* kg = static_cast<const T*>(a.k) + row;
+  const T* vg = static_cast<const T*>(a.v) + row;
+  const T* gg = static_cast<const T*>(a.gy) + row;
+  if (v0) {
+    float ax[5] = {ein.G.x, ein.gp.x, ein.gq.x, ein.hp.x, ein.hq.x};
+    bwd_slow1<T, true>(st0.S.x, st0.p.x, st0.q.x, ax, kg, vg, gg, gks, gvs, n, lc.w2.x, lc.u2.x,
+                       gw.x, gu.x, a.C, kLanes);
+  }
+  if (v1) {
+    float ay[5] = {ein.G.y, ein.gp.y, ein.gq.y, ein.hp.y, ein.hq.y};
+    bwd_slow1<T, true>(st0.S.y, st0.p.y, st0.q.y, ay, kg + 1, vg + 1, gg + 1, gks + 1, gvs + 1, n,
+                       lc.w2.y, lc.u2.y, gw.y, gu.y, a.C, kLanes);
+  }
+}
+
+// Backward. kOut: grad_key/grad_value, per-lane partial sums and (last CTA per
+// column block) the time gradients; !kOut: only the adjoint at the segment
+// start (a.adj_out), for the segmented plan. Grid (B * ncblk, nseg), W warps
+// per CTA; reference wkv_triton.py:60-142.
+template <typename T, int W, bool kOut>
+__global__ void __launch_bounds__(32 * W, 4)
+    wkv_bwd_tp_kernel(const BwdArgs a, const __grid_constant__ CUtensorMap tk,
+                      const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tgy,
+                      const __grid_constant__ CUtensorMap tck, const __grid_constant__ CUtensorMap tgk,
+                      const __grid_constant__ CUtensorMap tgv) {
+  using G = TpB<T, W>;
+  using P = Pair<T>;
+  using raw = typename P::raw;
+  constexpr int NS = G::kStages;
+  constexpr int R = kSub;
+  extern __shared__ __align__(128) unsigned char smem[];
+  float* sum = reinterpret_cast<float*>(smem + NS * G::kStageBytes);
+  float* red = sum + G::kSumFloats;  // [W][2][kLanes]
+  T* gks = reinterpret_cast<T*>(red + W * 2 * kLanes) + (threadIdx.x >> 5) * 2 * kSub * kLanes;
+  T* gvs = gks + kSub * kLanes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(red + W * 2 * kLanes) +
+                                               G::kOutBytes);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cb = blockIdx.x % a.ncblk, b = blockIdx.x / a.ncblk;
+  const int c = cb * kLanes + 2 * lane;
+  const int seg = blockIdx.y + a.seg_base;
+  const bool v0 = c < a.C, v1 = c + 1 < a.C;
+  f2 ww = splat(0.f), uu = splat(0.f);
+  if (v0) {
+    ww.x = a.w[c];
+    uu.x = a.u[c];
+  }
+  if (v1) {
+    ww.y = a.w[c + 1];
+    uu.y = a.u[c + 1];
+  }
+  const Lane2 lc = make_lane2(ww, uu);
+  const int t_begin = seg * a.seg_len;
+  const int t_end = min(a.T, t_begin + a.seg_len);
+  const int ntiles = (t_end - t_begin + R - 1) / R;
+  const int nrounds = (ntiles + W - 1) / W;
+  const bool force_slow = a.force_slow != 0;
+  const size_t lseg = (size_t)b * a.nseg + seg;
+
+  Adj2 adj = adj_zero2();  // adjoint entering the current round (at its last tile's end)
+  if (a.adj_in != nullptr) load_adj(a.adj_in, lseg, a.C, c, v0, v1, adj);
+  Fwd2 segst = fwd_identity2();
+  if (a.seg_start != nullptr) load3(a.seg_start, lseg, a.C, c, v0, v1, segst.S, segst.p, segst.q);
+  f2 gwacc = splat(0.f), gu = splat(0.f);
+
+  auto issue = [&](int r) {
+    const int st = r % NS;
+    unsigned char* base = smem + st * G::kStageBytes;
+    const int jb = ntiles - (r + 1) * W;  // first tile of the round (may be < 0)
+    const int t0 = t_begin + jb * R;
+    mbar_arrive_expect_tx(&bars[st], 3 * G::kBoxBytes + G::kCkBytes);
+    tma_load_3d(base, &tk, &bars[st], cb * kLanes, t0, b);
+    tma_load_3d(base + G::kBoxBytes, &tv, &bars[st], cb * kLanes, t0, b);
+    tma_load_3d(base + 2 * G::kBoxBytes, &tgy, &bars[st], cb * kLanes, t0, b);
+    tma_load_3d(base + 3 * G::kBoxBytes, &tck, &bars[st], cb * kLanes, 0,
+                b * a.nsub + t_begin / kSub + jb);
+  };
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < NS; ++st) mbar_init(&bars[st], 1);
+    fence_barrier_init();
+    prefetch_tensormap(&tk);
+    prefetch_tensormap(&tv);
+    prefetch_tensormap(&tgy);
+    prefetch_tensormap(&tck);
+    if (kOut) {
+      prefetch_tensormap(&tgk);
+      prefetch_tensormap(&tgv);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int r = 0; r < min(NS, nrounds); ++r) issue(r);
+
+#pragma unroll 1
+  for (int r = 0; r < nrounds; ++r) {
+    const int st = r % NS;
+    const unsigned char* base = smem + st * G::kStageBytes;
+    const int jb = ntiles - (r + 1) * W;
+    const int j = jb + warp;
+    const int t0 = t_begin + j * R;
+    const int n = j < 0 ? 0 : min(R, t_end - t0);
+    const bool arrived = mbar_wait_bounded(&bars[st], (r / NS) & 1);
+
+    // A. recompute and local adjoint summary
+    raw kr[R], vr[R], gr[R];
+    {
+      const T* kt = reinterpret_cast<const T*>(base) + warp * R * kLanes + 2 * lane;
+      const T* vt = reinterpret_cast<const T*>(base + G::kBoxBytes) + warp * R * kLanes + 2 * lane;
+      const T* gt = reinterpret_cast<const T*>(base + 2 * G::kBoxBytes) + warp * R * kLanes + 2 * lane;
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        kr[i] = P::ld(kt + i * kLanes);
+        vr[i] = P::ld(vt + i * kLanes);
+        gr[i] = P::ld(gt + i * kLanes);
+      }
+    }
+    Fwd2 st0;  // forward state at the tile start
+    {
+      const f2* ck = reinterpret_cast<const f2*>(base + 3 * G::kBoxBytes) + warp * 3 * (kLanes / 2) + lane;
+      st0 = Fwd2{ck[0], ck[kLanes / 2], ck[kLanes]};
+    }
+    if (a.seg_start != nullptr && n > 0)
+      st0 = (t0 == t_begin) ? segst : fwd_combine2(segst, t0 - t_begin, lc, st0);
+    f2 kmax, kmin, gymax, s, p, q;
+    if (n == R) {
+      tile_kminmax<T, false>(kr, n, kmax, kmin);
+      gymax = tile_absmax<T, false>(gr, n);
+    } else {
+      tile_kminmax<T, true>(kr, n, kmax, kmin);
+      gymax = tile_absmax<T, true>(gr, n);
+    }
+    bool ok = n == 0 || (fast_ok1(st0.S.x, st0.p.x, st0.q.x, kmax.x, kmin.x, n, lc.w2.x, lc.u2.x,
+                                  s.x, p.x, q.x) &&
+                         fast_ok1(st0.S.y, st0.p.y, st0.q.y, kmax.y, kmin.y, n, lc.w2.y, lc.u2.y,
+                                  s.y, p.y, q.y) &&
+                         fmaxf(gymax.x, gymax.y) <= 0x1p40f && !force_slow);
+    if (n == 0) s = p = q = splat(0.f);
+    f2 ry[R], rg[R];
+    Adj2 loc;
+    if (n == R) {
+      bwd_tp_recompute<T, false>(kr, vr, gr, n, lc, s, p, q, ry, rg);
+      bwd_tp_summary<false>(ry, rg, n, lc, loc.gp, loc.gq, loc.hp, loc.hq);
+    } else {
+      bwd_tp_recompute<T, true>(kr, vr, gr, n, lc, s, p, q, ry, rg);
+      bwd_tp_summary<true>(ry, rg, n, lc, loc.gp, loc.gq, loc.hp, loc.hq);
+    }
+    loc.G = f2{-s.x, -s.y};
+    const bool fast = __all_sync(kFull, ok);
+    if (!fast && n > 0)
+      loc = bwd_tp_exact_summary<T>(
+          reinterpret_cast<const T*>(base) + warp * R * kLanes + 2 * lane,
+          reinterpret_cast<const T*>(base + G::kBoxBytes) + warp * R * kLanes + 2 * lane,
+          reinterpret_cast<const T*>(base + 2 * G::kBoxBytes) + warp * R * kLanes + 2 * lane, n, st0,
+          lc);
+    {
+      f2* sw = reinterpret_cast<f2*>(sum + ((r & 1) * W + warp) * 5 * kLanes) + lane;
+      sw[0] = loc.G;
+      sw[kLanes / 2] = loc.gp;
+      sw[kLanes] = loc.gq;
+      sw[3 * kLanes / 2] = loc.hp;
+      sw[2 * kLanes] = loc.hq;
+    }
+    if (!__syncthreads_and(arrived)) {
+      if (threadIdx.x == 0) {
+        report_timeout(a.err);
+        for (int q2 = r; q2 < min(r + NS, nrounds); ++q2)
+          mbar_wait_bounded(&bars[q2 % NS], (q2 / NS) & 1);
+      }
+      if (kOut && lane == 0) bulk_wait_all();
+      return;
+    }
+    if (threadIdx.x == 0 && r + NS < nrounds) issue(r + NS);
+
+    // B. adjoint at this warp's tile end; adj becomes the adjoint at the round start
+    Adj2 ein = adj;
+#pragma unroll
+    for (int m = W - 1; m >= 0; --m) {
+      const int nm = (jb + m) < 0 ? 0 : min(R, t_end - (t_begin + (jb + m) * R));
+      if (m == warp) ein = adj;
+      if (nm > 0) {
+        const f2* sm = reinterpret_cast<const f2*>(sum + ((r & 1) * W + m) * 5 * kLanes) + lane;
+        const Adj2 l{sm[0], sm[kLanes / 2], sm[kLanes], sm[3 * kLanes / 2], sm[2 * kLanes]};
+        adj = adj_combine2(l, adj, nm, lc);
+      }
+    }
+
+    // C. outputs from the incoming adjoint, staged in this warp's tiles and
+    // written with one bulk tensor store per tensor
+    if (kOut && n > 0) {
+      if (lane == 0) bulk_wait_read<0>();  // the previous tile's store has read gks/gvs
+      __syncwarp();
+      const f2 f = ex2x2(add2(ein.G, s));  // integer exponents: exact
+      const f2 gp = mul2(ein.gp, f), gq = mul2(ein.gq, f), hp = mul2(ein.hp, f), hq = mul2(ein.hq, f);
+      const float amax = fmaxf(fmaxf(fmaxf(fabsf(gp.x), fabsf(gp.y)), fmaxf(fabsf(gq.x), fabsf(gq.y))),
+                               fmaxf(fmaxf(fabsf(hp.x), fabsf(hp.y)), fmaxf(fabsf(hq.x), fabsf(hq.y))));
+      if (fast && __all_sync(kFull, amax <= 0x1p80f)) {
+        if (n == R)
+          bwd_tp_outputs<T, false, kOut>(kr, vr, ry, rg, n, lc, s, gp, gq, hp, hq, gks + 2 * lane,
+                                         gvs + 2 * lane, gwacc, gu);
+        else
+          bwd_tp_outputs<T, true, kOut>(kr, vr, ry, rg, n, lc, s, gp, gq, hp, hq, gks + 2 * lane,
+                                        gvs + 2 * lane, gwacc, gu);
+      } else {
+        bwd_tp_exact<T>(a, b, t0, c, v0, v1, n, st0, ein, lc, gks + 2 * lane, gvs + 2 * lane,
+                        gwacc, gu);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_3d(&tgk, gks, cb * kLanes, t0, b);
+        tma_store_3d(&tgv, gvs, cb * kLanes, t0, b);
+        bulk_commit();
+      }
+    }
+  }
+  if (kOut && lane == 0) bulk_wait_all();
+  if (a.adj_out != nullptr && warp == 0) store_adj(a.adj_out, lseg, a.C, c, v0, v1, adj);
+  if (!kOut || a.partial == nullptr) return;
+
+  // per-lane partial sums of the CTA, summed over its warps in a fixed order
+  {
+    f2* rw = reinterpret_cast<f2*>(red + warp * 2 * kLanes) + lane;
+    rw[0] = gwacc;
+    rw[kLanes / 2] = gu;
+  }
+  __syncthreads();
+  if (warp != 0) return;
+  f2 sw = splat(0.f), su = splat(0.f);
+#pragma unroll
+  for (int m = 0; m < W; ++m) {
+    const f2* rw = reinterpret_cast<const f2*>(red + m * 2 * kLanes) + lane;
+    sw = add2(sw, rw[0]);
+    su = add2(su, rw[kLanes / 2]);
+  }
+  {
+    float* rp = a.partial + lseg * 2 * (size_t)a.C + c;
+    if (v0) {
+      rp[0] = sw.x;
+      rp[a.C] = su.x;
+    }
+    if (v1) {
+      rp[1] = sw.y;
+      rp[a.C + 1] = su.y;
+    }
+  }
+  if (a.tickets == nullptr) return;
+  // The last CTA of this column block to finish sums every (b, segment) row in
+  // a fixed order: grad_time_decay = w sum dL/dw (reference wkv_triton.py:117,
+  // 194), grad_time_first = sum dL/du. No CTA waits for another.
+  __threadfence();
+  __syncwarp();
+  unsigned ticket = 0;
+  if (lane == 0) ticket = atomicAdd(&a.tickets[cb], 1u);
+  ticket = __shfl_sync(kFull, ticket, 0);
+  const int rows = a.B * a.nseg;
+  if (ticket + 1 != static_cast<unsigned>(rows)) return;
+  __threadfence();
+  if (lane == 0) a.tickets[cb] = 0u;  // ready for a later call that reuses the counters
+  reduce_time_grads(a, c, v0, v1, lc.w, rows);
 }
 
 }  // namespace wkv
