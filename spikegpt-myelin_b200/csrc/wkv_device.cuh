@@ -168,6 +168,38 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
       : "memory");
 }
 
+// Predicated forms: only the threads with `on` set issue the copy, with no
+// branch (the elected-lane `if` of a warp otherwise costs a convergence region).
+__device__ __forceinline__ void mbar_arrive_expect_tx_if(bool on, uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t"
+      "@p mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;\n\t}" ::"r"(
+          smem_u32(bar)),
+      "r"(bytes), "r"((uint32_t)on)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_if(bool on, void* dst, const CUtensorMap* map,
+                                               uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %6, 0;\n\t"
+      "@p cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];\n\t}" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)),
+      "r"((uint32_t)on)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_3d_if(bool on, const CUtensorMap* map, const void* src,
+                                                int x, int y, int z) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %5, 0;\n\t"
+      "@p cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];\n\t}" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(x), "r"(y), "r"(z), "r"(smem_u32(src)), "r"((uint32_t)on)
+      : "memory");
+}
+
+// Bulk groups are per thread: committing or waiting on a thread that issued no
+// bulk copy is a no-op, so whole warps may execute these.
 __device__ __forceinline__ void bulk_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }

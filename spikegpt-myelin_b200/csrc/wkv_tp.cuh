@@ -205,12 +205,12 @@ __global__ void __launch_bounds__(32 * W, 4)
   if (a.seg_start != nullptr)
     load3(a.seg_start, (size_t)b * a.nseg + seg, a.C, c, v0, v1, start.S, start.p, start.q);
 
-  auto issue = [&](int r) {
+  auto issue = [&](bool on, int r) {  // by the threads with `on` (one per CTA)
     const int s = r % NS;
-    mbar_arrive_expect_tx(&bars[s], 2 * G::kBoxBytes);
+    mbar_arrive_expect_tx_if(on, &bars[s], 2 * G::kBoxBytes);
     const int t0 = t_begin + r * G::kRoundRows;
-    tma_load_3d(kbuf + s * G::kBoxElems, &tk, &bars[s], cb * kLanes, t0, b);
-    tma_load_3d(vbuf + s * G::kBoxElems, &tv, &bars[s], cb * kLanes, t0, b);
+    tma_load_3d_if(on, kbuf + s * G::kBoxElems, &tk, &bars[s], cb * kLanes, t0, b);
+    tma_load_3d_if(on, vbuf + s * G::kBoxElems, &tv, &bars[s], cb * kLanes, t0, b);
   };
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) mbar_init(&bars[s], 1);
@@ -220,8 +220,7 @@ __global__ void __launch_bounds__(32 * W, 4)
     if (kY) prefetch_tensormap(&ty);
   }
   __syncthreads();
-  if (threadIdx.x == 0)
-    for (int r = 0; r < min(NS, nrounds); ++r) issue(r);
+  for (int r = 0; r < min(NS, nrounds); ++r) issue(threadIdx.x == 0, r);
 
   Fwd2 cur = start;  // warp W-1: the state after the latest round
 #pragma unroll 1
@@ -262,10 +261,10 @@ __global__ void __launch_bounds__(32 * W, 4)
         report_timeout(a.err);
         for (int q = r; q < min(r + NS, nrounds); ++q) mbar_wait_bounded(&bars[q % NS], (q / NS) & 1);
       }
-      if (kY && lane == 0) bulk_wait_all();
+      if (kY) bulk_wait_all();
       return;
     }
-    if (threadIdx.x == 0 && r + NS < nrounds) issue(r + NS);
+    if (r + NS < nrounds) issue(threadIdx.x == 0, r + NS);
 
     // B. carry-in of this warp's tile: the round's start state (left in shared
     // memory by warp W-1 during the previous round) folded with the summaries
@@ -297,7 +296,7 @@ __global__ void __launch_bounds__(32 * W, 4)
     if (n > 0) {
       if (a.ckpt != nullptr) store_state2(a.ckpt, (size_t)b * a.nsub + t0 / kSub, a.C, c, v0, v1, sin);
       if (kY) {
-        if (lane == 0) bulk_wait_read<0>();  // the previous tile's store has read ys
+        bulk_wait_read<0>();  // the previous tile's store (lane 0's group) has read ys
         __syncwarp();
         f2 sc, p, q;
         const bool ok = fast_ok1(sin.S.x, sin.p.x, sin.q.x, kmax.x, kmin.x, n, lc.w2.x, lc.u2.x,
@@ -316,14 +315,12 @@ __global__ void __launch_bounds__(32 * W, 4)
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) {
-          tma_store_3d(&ty, ys, cb * kLanes, t0, b);
-          bulk_commit();
-        }
+        tma_store_3d_if(lane == 0, &ty, ys, cb * kLanes, t0, b);
+        bulk_commit();
       }
     }
   }
-  if (kY && lane == 0) bulk_wait_all();
+  if (kY) bulk_wait_all();
   if (a.seg_end != nullptr && warp == W - 1)
     store3(a.seg_end, (size_t)b * a.nseg + seg, a.C, c, v0, v1, cur.S, cur.p, cur.q);
 }
@@ -572,17 +569,17 @@ __global__ void __launch_bounds__(32 * W, 4)
   if (a.seg_start != nullptr) load3(a.seg_start, lseg, a.C, c, v0, v1, segst.S, segst.p, segst.q);
   f2 gwacc = splat(0.f), gu = splat(0.f);
 
-  auto issue = [&](int r) {
+  auto issue = [&](bool on, int r) {  // by the threads with `on` (one per CTA)
     const int st = r % NS;
     unsigned char* base = smem + st * G::kStageBytes;
     const int jb = ntiles - (r + 1) * W;  // first tile of the round (may be < 0)
     const int t0 = t_begin + jb * R;
-    mbar_arrive_expect_tx(&bars[st], 3 * G::kBoxBytes + G::kCkBytes);
-    tma_load_3d(base, &tk, &bars[st], cb * kLanes, t0, b);
-    tma_load_3d(base + G::kBoxBytes, &tv, &bars[st], cb * kLanes, t0, b);
-    tma_load_3d(base + 2 * G::kBoxBytes, &tgy, &bars[st], cb * kLanes, t0, b);
-    tma_load_3d(base + 3 * G::kBoxBytes, &tck, &bars[st], cb * kLanes, 0,
-                b * a.nsub + t_begin / kSub + jb);
+    mbar_arrive_expect_tx_if(on, &bars[st], 3 * G::kBoxBytes + G::kCkBytes);
+    tma_load_3d_if(on, base, &tk, &bars[st], cb * kLanes, t0, b);
+    tma_load_3d_if(on, base + G::kBoxBytes, &tv, &bars[st], cb * kLanes, t0, b);
+    tma_load_3d_if(on, base + 2 * G::kBoxBytes, &tgy, &bars[st], cb * kLanes, t0, b);
+    tma_load_3d_if(on, base + 3 * G::kBoxBytes, &tck, &bars[st], cb * kLanes, 0,
+                   b * a.nsub + t_begin / kSub + jb);
   };
   if (threadIdx.x == 0) {
     for (int st = 0; st < NS; ++st) mbar_init(&bars[st], 1);
@@ -597,8 +594,7 @@ __global__ void __launch_bounds__(32 * W, 4)
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0)
-    for (int r = 0; r < min(NS, nrounds); ++r) issue(r);
+  for (int r = 0; r < min(NS, nrounds); ++r) issue(threadIdx.x == 0, r);
 
 #pragma unroll 1
   for (int r = 0; r < nrounds; ++r) {
@@ -675,10 +671,10 @@ __global__ void __launch_bounds__(32 * W, 4)
         for (int q2 = r; q2 < min(r + NS, nrounds); ++q2)
           mbar_wait_bounded(&bars[q2 % NS], (q2 / NS) & 1);
       }
-      if (kOut && lane == 0) bulk_wait_all();
+      if (kOut) bulk_wait_all();
       return;
     }
-    if (threadIdx.x == 0 && r + NS < nrounds) issue(r + NS);
+    if (r + NS < nrounds) issue(threadIdx.x == 0, r + NS);
 
     // B. adjoint at this warp's tile end; adj becomes the adjoint at the round start
     Adj2 ein = adj;
@@ -696,7 +692,7 @@ __global__ void __launch_bounds__(32 * W, 4)
     // C. outputs from the incoming adjoint, staged in this warp's tiles and
     // written with one bulk tensor store per tensor
     if (kOut && n > 0) {
-      if (lane == 0) bulk_wait_read<0>();  // the previous tile's store has read gks/gvs
+      bulk_wait_read<0>();  // the previous tile's stores (lane 0's group) have read gks/gvs
       __syncwarp();
       const f2 f = ex2x2(add2(ein.G, s));  // integer exponents: exact
       const f2 gp = mul2(ein.gp, f), gq = mul2(ein.gq, f), hp = mul2(ein.hp, f), hq = mul2(ein.hq, f);
@@ -715,14 +711,12 @@ __global__ void __launch_bounds__(32 * W, 4)
       }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        tma_store_3d(&tgk, gks, cb * kLanes, t0, b);
-        tma_store_3d(&tgv, gvs, cb * kLanes, t0, b);
-        bulk_commit();
-      }
+      tma_store_3d_if(lane == 0, &tgk, gks, cb * kLanes, t0, b);
+      tma_store_3d_if(lane == 0, &tgv, gvs, cb * kLanes, t0, b);
+      bulk_commit();
     }
   }
-  if (kOut && lane == 0) bulk_wait_all();
+  if (kOut) bulk_wait_all();
   if (a.adj_out != nullptr && warp == 0) store_adj(a.adj_out, lseg, a.C, c, v0, v1, adj);
   if (!kOut || a.partial == nullptr) return;
 
