@@ -43,6 +43,8 @@ struct Tp {
   static constexpr int kSumFloats = 2 * (W + 1) * 3 * kLanes;
   static constexpr uint32_t kYTileBytes = kSub * kLanes * sizeof(T);  // one warp's staged y tile
   static_assert(kSegAlign % kSub == 0, "segments start on tile boundaries");
+  static_assert(kBoxBytes % 128 == 0 && (kSumFloats * 4) % 128 == 0 && kYTileBytes % 128 == 0,
+                "bulk-copy buffers start on 128-byte boundaries");
 };
 
 // Shared memory: k stages | v stages | summaries | y tiles | barriers.
@@ -359,7 +361,10 @@ struct TpB {
   static constexpr int kSumFloats = 2 * W * 5 * kLanes;  // [2 rounds][W][G,gp,gq,hp,hq][lanes]
   static constexpr uint32_t kOutTileBytes = kSub * kLanes * sizeof(T);  // one warp's gk (or gv) tile
   static constexpr uint32_t kOutBytes = W * 2 * kOutTileBytes;          // [W][gk, gv] tiles
-  static_assert(kBoxBytes % 128 == 0 && kCkBytes % 128 == 0, "128-byte aligned boxes");
+  static_assert(kBoxBytes % 128 == 0 && kCkBytes % 128 == 0 && kStageBytes % 128 == 0 &&
+                    (kSumFloats * 4) % 128 == 0 && (W * 2 * kLanes * 4) % 128 == 0 &&
+                    kOutTileBytes % 128 == 0,
+                "bulk-copy buffers start on 128-byte boundaries");
 };
 
 // Shared memory: stages | summaries | per-warp partial sums | output tiles | barriers.
