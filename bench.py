@@ -68,6 +68,7 @@ def parse_args():
     ap.add_argument("--impl", choices=("native", "reference"), default="native")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg1")
     ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--e2e-chunks", type=int, default=1, help="batch chunks streamed per e2e step")
     ap.add_argument("--profile", action="store_true", help="device loop only (for ncu): no CPU leg, e2e or clocks")
     ap.add_argument("--no-state", action="store_true",
                     help="time the self-contained op pair (backward re-runs the forward sweep)")
@@ -379,11 +380,22 @@ def ncu_traffic(kernel: str, workload: str):
 
 
 def run_e2e(args, wl, dev, k_np, v_np, td_np, tf_np, gy_np, tdt, world):
-    """The metric through the public ops with host buffers (pinned)."""
+    """The metric through the public autograd op with host buffers (pinned).
+
+    Each step moves that step's k, v, grad_y host->device and y, grad_key,
+    grad_value, grad_time_decay, grad_time_first device->host, as a user with
+    host-resident data does. Copies in, compute and copies out run on three
+    CUDA streams ordered by events, so one step's results travel to the host
+    while the next step's inputs travel to the device (the two PCIe directions
+    overlap). --e2e-chunks > 1 also splits each step's batch into chunks
+    (batch rows are independent; the per-channel gradients accumulate across
+    chunks in the leaves' .grad, as autograd does for any split batch).
+    """
     import torch
     import torch.distributed as dist
 
     import spikegpt_b200  # noqa: F401
+    from spikegpt_b200 import weighted_key_value_triton_bf16io
 
     def pin(x, dt):
         return torch.as_tensor(x).to(dt).pin_memory()
@@ -395,21 +407,59 @@ def run_e2e(args, wl, dev, k_np, v_np, td_np, tf_np, gy_np, tdt, world):
     h2d = sum(x.numel() * x.element_size() for x in (hk, hv, hgy, htd, htf))
     d2h = sum(x.numel() * x.element_size() for x in (hy, hgk, hgv, hgtd, hgtf))
 
-    from spikegpt_b200 import weighted_key_value_triton_bf16io
+    b = wl["B"]
+    nch = max(1, min(args.e2e_chunks, b))
+    bounds = [(i * b // nch, (i + 1) * b // nch) for i in range(nch)]
+    s_in, s_comp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    # device input slots, one per chunk
+    dk = [torch.empty((hi - lo,) + tuple(hk.shape[1:]), dtype=tdt, device=dev) for lo, hi in bounds]
+    dv = [torch.empty_like(x) for x in dk]
+    dgy = [torch.empty_like(x) for x in dk]
+    dtd = torch.empty(htd.shape, dtype=torch.float32, device=dev)
+    dtf = torch.empty_like(dtd)
+    slot_free = [torch.cuda.Event() for _ in bounds]  # compute of the slot's last use is done
+    for e in slot_free:
+        e.record(s_comp)
 
     def step():
-        k = hk.to(dev, non_blocking=True).requires_grad_()
-        v = hv.to(dev, non_blocking=True).requires_grad_()
-        gy = hgy.to(dev, non_blocking=True)
-        td = htd.to(dev, non_blocking=True).requires_grad_()
-        tf = htf.to(dev, non_blocking=True).requires_grad_()
-        y = weighted_key_value_triton_bf16io(k, v, td, tf)
-        y.backward(gy)
-        hy.copy_(y.detach(), non_blocking=True)
-        hgk.copy_(k.grad, non_blocking=True)
-        hgv.copy_(v.grad, non_blocking=True)
-        hgtd.copy_(td.grad, non_blocking=True)
-        hgtf.copy_(tf.grad, non_blocking=True)
+        ev_par = torch.cuda.Event()
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(slot_free[-1])  # the previous step's compute no longer reads dtd, dtf
+            dtd.copy_(htd, non_blocking=True)
+            dtf.copy_(htf, non_blocking=True)
+            ev_par.record(s_in)
+        with torch.cuda.stream(s_comp):
+            s_comp.wait_event(ev_par)
+            td = dtd.detach().requires_grad_()
+            tf = dtf.detach().requires_grad_()
+        for i, (lo, hi) in enumerate(bounds):
+            ev_in = torch.cuda.Event()
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(slot_free[i])
+                dk[i].copy_(hk[lo:hi], non_blocking=True)
+                dv[i].copy_(hv[lo:hi], non_blocking=True)
+                dgy[i].copy_(hgy[lo:hi], non_blocking=True)
+                ev_in.record(s_in)
+            with torch.cuda.stream(s_comp):
+                s_comp.wait_event(ev_in)
+                k = dk[i].detach().requires_grad_()
+                v = dv[i].detach().requires_grad_()
+                y = weighted_key_value_triton_bf16io(k, v, td, tf)
+                y.backward(dgy[i])
+                ev_done = torch.cuda.Event()
+                ev_done.record(s_comp)
+                slot_free[i] = ev_done
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_done)
+                for src, dst in ((y.detach(), hy[lo:hi]), (k.grad, hgk[lo:hi]), (v.grad, hgv[lo:hi])):
+                    dst.copy_(src, non_blocking=True)
+                    src.record_stream(s_out)  # not reused by the allocator before the copy ends
+        with torch.cuda.stream(s_out):
+            s_out.wait_stream(s_comp)
+            for src, dst in ((td.grad, hgtd), (tf.grad, hgtf)):
+                dst.copy_(src, non_blocking=True)
+                src.record_stream(s_out)
+        torch.cuda.current_stream(dev).wait_stream(s_out)
 
     for _ in range(3):
         step()
@@ -430,8 +480,9 @@ def run_e2e(args, wl, dev, k_np, v_np, td_np, tf_np, gy_np, tdt, world):
     elems = wl["B"] * wl["T"] * wl["C"]
     value = BYTES_PER_ELEM[wl["dtype"]] * elems * args.e2e_steps * world / (ms * 1e-3) / 1e9
     return {"value": value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "steps": args.e2e_steps, "ms_per_step": ms / args.e2e_steps,
-            "path": "autograd through spikegpt_b200.weighted_key_value_triton_bf16io (myelin::wkv_forward_bf16io), pinned host buffers"}
+            "steps": args.e2e_steps, "ms_per_step": ms / args.e2e_steps, "chunks": nch,
+            "path": "autograd through spikegpt_b200.weighted_key_value_triton_bf16io (myelin::wkv_forward_bf16io) "
+                    "on batch chunks; pinned host buffers; copy-in, compute and copy-out streams overlapped"}
 
 
 # ----------------------------------------------------------- reference arm
