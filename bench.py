@@ -55,7 +55,13 @@ WORKLOADS = {
     "cfg2": dict(B=24, T=3072, C=512, dtype="bf16", kscale=4.0, desc="config 2: B=24 T=3072 C=512 bf16, k/v x4"),
     "cfg2b-1": dict(B=1, T=3072, C=512, dtype="bf16", kscale=4.0, desc="config 2b: B=1 T=3072 C=512 bf16"),
     "cfg2b-8": dict(B=8, T=3072, C=512, dtype="bf16", kscale=4.0, desc="config 2b: B=8 T=3072 C=512 bf16"),
+    # recurrent (generation) step: B decode streams, one token each per step,
+    # bf16 keys/values with a float32 state (the autocast case)
+    "decode": dict(kind="step", B=16384, T=1, C=512, dtype="bf16", state="fp32", kscale=4.0,
+                   desc="recurrent step: B=16384 streams x C=512, bf16 k/v, float32 state"),
 }
+STEP_METRIC = "WKV recurrent step algorithmic HBM throughput"
+STEP_BYTES = {"bf16": 2, "fp16": 2, "fp32": 4}
 METRIC = "WKV fwd+bwd algorithmic HBM throughput"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "source": "fallback"}
 
@@ -368,6 +374,173 @@ def run_native(args, wl):
         dist.destroy_process_group()
 
 
+def run_step(args, wl):
+    """The recurrent step (generation): one wkv_step launch per step over B
+    streams, state resident on the device and updated in place, new k, v each
+    step (the same buffers, as a decode loop refills them). Algorithmic bytes
+    per element: read k, v and the three state planes, write y and the state."""
+    import torch
+    import torch.distributed as dist
+
+    from spikegpt_b200 import _capi
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    from spikegpt_b200.sharding import max_over_ranks
+
+    tk = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}[wl["dtype"]]
+    ts = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}[wl["state"]]
+    ck = {"bf16": _capi.DTYPE_BF16, "fp16": _capi.DTYPE_F16, "fp32": _capi.DTYPE_F32}[wl["dtype"]]
+    cs = {"bf16": _capi.DTYPE_BF16, "fp16": _capi.DTYPE_F16, "fp32": _capi.DTYPE_F32}[wl["state"]]
+    b, c = wl["B"], wl["C"]
+    rng = np.random.default_rng(rank)
+    k = torch.as_tensor((rng.standard_normal((b, c)) * wl["kscale"]).astype(np.float32)).to(dev, tk)
+    v = torch.as_tensor(rng.standard_normal((b, c)).astype(np.float32)).to(dev, tk)
+    td = torch.as_tensor(rng.uniform(-5, 1, c).astype(np.float32)).to(dev)
+    tf = torch.as_tensor(rng.uniform(-1, 1, c).astype(np.float32)).to(dev)
+    num = torch.zeros((b, c), device=dev, dtype=ts)
+    den = torch.zeros_like(num)
+    ls = torch.full((b, c), torch.finfo(ts).min, device=dev, dtype=ts)
+    y = torch.empty_like(num)
+    lib = _capi.lib()
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+
+    def step(kk=k, vv=v):
+        _capi.check(lib.wkv_step(ck, cs, kk.data_ptr(), vv.data_ptr(), td.data_ptr(), tf.data_ptr(), num.data_ptr(),
+                                 den.data_ptr(), ls.data_ptr(), y.data_ptr(), b, c, sp), "wkv_step")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    sampler = None if args.profile else ClockSampler(local)
+    time.sleep(0.3 if sampler else 0)
+    _capi.timing_collect()
+    _capi.timing_enable(True)
+    launches0 = sum(_capi.launch_counts().values())
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    host0 = time.time()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    host1 = time.time()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    _capi.timing_enable(False)
+    launches = sum(_capi.launch_counts().values()) - launches0
+    per_kernel = _capi.timing_collect()
+    ms = max_over_ranks(ev0.elapsed_time(ev1), dev)
+    if sampler:
+        time.sleep(0.25)
+        sampler.stop()
+    clocks = sampler.summary(host0, host1) if sampler else None
+
+    per_elem = 2 * STEP_BYTES[wl["dtype"]] + 7 * STEP_BYTES[wl["state"]]
+    step_bytes = per_elem * b * c
+    value = step_bytes * args.steps * world / (ms * 1e-3) / 1e9
+    tot, cnt = per_kernel["wkv_step_kernel"]
+    pk = peaks()
+    hbm = float(pk.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+    achieved = step_bytes / (tot / cnt * 1e-3) / 1e9
+    result = {
+        "metric": STEP_METRIC,
+        "value": value,
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": wl["dtype"],
+        "data": "synthetic (seeded numpy PCG64)",
+        "config": {
+            "workload": wl["desc"], "B_per_gpu": b, "C": c, "state_dtype": wl["state"],
+            "tokens_per_s": b * args.steps * world / (ms * 1e-3),
+            "parallelism": f"{world} stream-sharded replica(s), no collective",
+            "l2": f"{step_bytes / 1e6:.0f} MB moved per step (> L2); no flush",
+        },
+        "roofline": {"kernel": "wkv_step_kernel", "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "alg_bytes_per_launch": step_bytes,
+                     "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if pk.get("source") == "measured"
+                     else "fallback 6.65 TB/s",
+                     "traffic": ncu_traffic("wkv_step_kernel", args.workload)},
+        "kernels": {"wkv_step_kernel": {"ms_per_launch": tot / cnt, "launches": cnt, "share": 1.0}},
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+    }
+    if not args.profile:
+        # e2e: each step's k, v from pinned host memory, y back to the host;
+        # the state stays on the device (a decode loop keeps it there)
+        hk, hv = k.cpu().pin_memory(), v.cpu().pin_memory()
+        hy = torch.empty(y.shape, dtype=y.dtype).pin_memory()
+        dk, dv = torch.empty_like(k), torch.empty_like(v)
+
+        def e2e_step():
+            dk.copy_(hk, non_blocking=True)
+            dv.copy_(hv, non_blocking=True)
+            step(dk, dv)
+            hy.copy_(y, non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ems = max_over_ranks(e0.elapsed_time(e1), dev)
+        result["e2e"] = {"value": step_bytes * args.e2e_steps * world / (ems * 1e-3) / 1e9, "unit": "GB/s",
+                         "h2d_bytes_per_step": 2 * hk.numel() * hk.element_size(),
+                         "d2h_bytes_per_step": hy.numel() * hy.element_size(),
+                         "steps": args.e2e_steps, "ms_per_step": ems / args.e2e_steps,
+                         "path": "wkv_step through the C ABI; k, v copied in and y copied out every step"}
+        if world == 1 and rank == 0:
+            result["cpu_baseline"] = cpu_step_throughput(wl)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def cpu_step_throughput(wl: dict, seconds: float = 5.0):
+    """The float32 oracle step (a single-threaded C loop) on 64 of the
+    workload's streams, repeated for about `seconds`."""
+    from oracle import oracle
+
+    b, c = 64, wl["C"]
+    rng = np.random.default_rng(0)
+    k = (rng.standard_normal((b, c)) * wl["kscale"]).astype(np.float32)
+    v = rng.standard_normal((b, c)).astype(np.float32)
+    td = rng.uniform(-5, 1, c).astype(np.float32)
+    tf = rng.uniform(-1, 1, c).astype(np.float32)
+    state = oracle.initial_step_state(b, c, np.float32)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        _, *state = oracle.step(k, v, td, tf, *state, dtype=np.float32)
+        n += 1
+    el = time.perf_counter() - t0
+    per_elem = 2 * STEP_BYTES[wl["dtype"]] + 7 * STEP_BYTES[wl["state"]]
+    return {"value": per_elem * b * c * n / el / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{n} steps of 64 streams x C={c}, float32, {el:.1f} s", "host_cpus": os.cpu_count()}
+
+
 def ncu_traffic(kernel: str, workload: str):
     """DRAM bytes per launch of `kernel` from the committed ncu summary for the
     workload (profiles/*.md line 'dram_bytes_per_launch[<kernel>] = N'), else None."""
@@ -516,10 +689,31 @@ def run_reference(args, wl):
     print(json.dumps(out), flush=True)
 
 
+def run_step_reference(args, wl):
+    """Reference arm of the step workload: the oracle step on the host, rank 0."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    base = cpu_step_throughput(wl, seconds=2.0)
+    out = {"metric": STEP_METRIC, "value": base["value"], "unit": "GB/s",
+           "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl["dtype"],
+           "data": "synthetic (seeded numpy PCG64)", "config": {"workload": wl["desc"], "C": wl["C"]},
+           "impl": "reference", "cpu_baseline": base,
+           "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+           "note": "the reference's step is PyTorch code inside SpikeTimeMix.step; this arm times the C "
+                   "restatement of its arithmetic (oracle/wkv_oracle.c) on the host"}
+    print(json.dumps(out), flush=True)
+
+
 def main():
     args = parse_args()
     wl = WORKLOADS[args.workload]
-    if args.impl == "reference":
+    if wl.get("kind") == "step":
+        if args.impl == "reference":
+            run_step_reference(args, wl)
+        else:
+            run_step(args, wl)
+    elif args.impl == "reference":
         run_reference(args, wl)
     else:
         run_native(args, wl)

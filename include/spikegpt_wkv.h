@@ -131,6 +131,26 @@ WKV_API int wkv_backward_noalloc(int dtype, const void* grad_y, const float* w, 
                                  void* stream);
 
 /*
+ * One recurrent (single-token) WKV step for generation. Replaces the WKV
+ * arithmetic of SpikeTimeMix.step (reference src/spikegpt/language.py:977-1013,
+ * the lines 993-1010 between the key/value projections and the receptance
+ * gate), on the reference's state: numerator, denominator and log_scale
+ * (natural-log scale), all [B, C]. key, value: [B, C] in `dtype`; the state
+ * and y: [B, C] in `state_dtype`, which is either `dtype` (a module run
+ * entirely in one dtype) or WKV_DTYPE_F32 (mixed precision: under autocast the
+ * reference's state is float32 while the projections give bf16/fp16 keys, and
+ * torch promotes the step's result to float32). The state is updated in
+ * place; y receives the WKV output of the step. time_decay, time_first:
+ * float32 [C] (w = -exp(time_decay) is formed inside). Arithmetic is float32.
+ * The initial state is zeros with log_scale = the state dtype's most negative
+ * finite value, as the reference's initial_state (language.py:957-975).
+ */
+WKV_API int wkv_step(int dtype, int state_dtype, const void* key, const void* value,
+                     const float* time_decay, const float* time_first, void* numerator,
+                     void* denominator, void* log_scale, void* y, int64_t B, int64_t C,
+                     void* stream);
+
+/*
  * Forward/backward with a saved forward state (no reference counterpart; an
  * optimisation of wkv_forward/wkv_backward). wkv_forward_with_state computes y exactly as
  * wkv_forward and also stores the recurrence state at every 16th step into

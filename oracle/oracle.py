@@ -75,6 +75,9 @@ def _load() -> ctypes.CDLL:
         bwd = getattr(lib, f"wkv_oracle_backward_{suf}")
         bwd.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, ci]
         bwd.restype = ci
+        stp = getattr(lib, f"wkv_oracle_step_{suf}")
+        stp.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i64, i64]
+        stp.restype = None
     lib.wkv_oracle_max_threads.restype = ci
     _lib = lib
     return lib
@@ -149,6 +152,31 @@ def forward_backward(k, v, time_decay, time_first, gy, *, dtype=np.float64, thre
 # ---------------------------------------------------------------------------
 # numpy restatement (float64), vectorised over lanes
 # ---------------------------------------------------------------------------
+
+
+def step(k, v, time_decay, time_first, numerator, denominator, log_scale, *, dtype=np.float64):
+    """One recurrent step, reference src/spikegpt/language.py:993-1010.
+
+    k, v and the state (numerator, denominator, log_scale; natural-log scale)
+    are [B, C]; time_decay, time_first are [C]. Returns (y, numerator,
+    denominator, log_scale) as new arrays in ``dtype``.
+    """
+    suf = "f64" if np.dtype(dtype) == np.float64 else "f32"
+    k, v = _prep(k, dtype), _prep(v, dtype)
+    td, tf = _prep(time_decay, dtype), _prep(time_first, dtype)
+    num, den, ls = (np.array(x, dtype=dtype, copy=True, order="C") for x in (numerator, denominator, log_scale))
+    b, c = k.shape
+    y = np.empty_like(k)
+    getattr(_load(), f"wkv_oracle_step_{suf}")(
+        _ptr(k), _ptr(v), _ptr(td), _ptr(tf), _ptr(num), _ptr(den), _ptr(ls), _ptr(y), b, c
+    )
+    return y, num, den, ls
+
+
+def initial_step_state(b: int, c: int, dtype=np.float64):
+    """The reference's initial state (language.py:964-974): zeros and the
+    dtype's most negative finite log_scale."""
+    return (np.zeros((b, c), dtype), np.zeros((b, c), dtype), np.full((b, c), np.finfo(dtype).min, dtype))
 
 
 def forward_numpy(k, v, time_decay, time_first) -> np.ndarray:

@@ -154,6 +154,41 @@
 WKV_ORACLE_DEFINE(double, f64, exp, -1.7976931348623157e308)
 WKV_ORACLE_DEFINE(float, f32, expf, -3.4028234663852886e38f)
 
+/*
+ * One recurrent step (generation): the WKV part of SpikeTimeMix.step, reference
+ * src/spikegpt/language.py:993-1010, in REAL arithmetic, with the reference's
+ * state (numerator, denominator, log_scale; natural-log scale). key, value,
+ * numerator, denominator, log_scale, y: [B, C]; time_decay, time_first: [C].
+ * The state is updated in place; y receives the step's output before the
+ * receptance gate.
+ */
+#define WKV_ORACLE_STEP_DEFINE(REAL, SUF, EXP)                                               \
+  void wkv_oracle_step_##SUF(const REAL* key, const REAL* value, const REAL* time_decay,     \
+                             const REAL* time_first, REAL* num, REAL* den, REAL* log_scale,  \
+                             REAL* y, int64_t B, int64_t C) {                                \
+    for (int64_t b = 0; b < B; ++b) {                                                        \
+      for (int64_t c = 0; c < C; ++c) {                                                      \
+        const int64_t i = b * C + c;                                                         \
+        const REAL k = key[i], v = value[i], s = log_scale[i];                               \
+        const REAL w = -EXP(time_decay[c]), u = time_first[c];                               \
+        const REAL uk = u + k;                                                               \
+        const REAL ns = s > uk ? s : uk;                                                     \
+        REAL a = EXP(s - ns), e = EXP(uk - ns);                                              \
+        y[i] = (a * num[i] + e * v) / (a * den[i] + e);                                      \
+        const REAL ds = s + w;                                                               \
+        const REAL rs = ds > k ? ds : k;                                                     \
+        a = EXP(ds - rs);                                                                    \
+        e = EXP(k - rs);                                                                     \
+        num[i] = a * num[i] + e * v;                                                         \
+        den[i] = a * den[i] + e;                                                             \
+        log_scale[i] = rs;                                                                   \
+      }                                                                                      \
+    }                                                                                        \
+  }
+
+WKV_ORACLE_STEP_DEFINE(double, f64, exp)
+WKV_ORACLE_STEP_DEFINE(float, f32, expf)
+
 /* Number of OpenMP threads the runtime would use by default (1 without OpenMP). */
 int wkv_oracle_max_threads(void) {
 #ifdef _OPENMP

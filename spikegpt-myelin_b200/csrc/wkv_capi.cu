@@ -7,6 +7,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -16,6 +17,7 @@
 #include <vector>
 
 #include "spikegpt_wkv.h"
+#include "wkv_step.cuh"
 #include "wkv_tp.cuh"
 
 namespace {
@@ -35,10 +37,11 @@ __device__ unsigned g_device_error_flags = 0;
 // while timing is enabled, brackets the launch with CUDA events recorded on the
 // launch stream, so per-kernel device time can be read back by the caller.
 
-enum Kind { K_FWD_Y, K_FWD_STATE, K_BWD_GRAD, K_BWD_ADJ, K_CARRY_FWD, K_CARRY_ADJ, K_COUNT };
+enum Kind { K_FWD_Y, K_FWD_STATE, K_BWD_GRAD, K_BWD_ADJ, K_CARRY_FWD, K_CARRY_ADJ, K_STEP, K_COUNT };
 const char* const kKindNames[K_COUNT] = {
     "wkv_fwd_kernel<y>",      "wkv_fwd_kernel<state>", "wkv_bwd_kernel<grad>",
-    "wkv_bwd_kernel<adjoint>", "wkv_carry_fwd_kernel",  "wkv_carry_adj_kernel"};
+    "wkv_bwd_kernel<adjoint>", "wkv_carry_fwd_kernel",  "wkv_carry_adj_kernel",
+    "wkv_step_kernel"};
 
 std::atomic<long long> g_launches[K_COUNT];
 std::atomic<bool> g_timing{false};
@@ -803,6 +806,60 @@ int wkv_backward_from_state(int dtype, const void* grad_y, const float* w, const
   return backward_impl(dtype, grad_y, w, u, key, value, state, state_bytes, grad_key, grad_value,
                        grad_time_decay, grad_time_first, B, T, C, workspace, workspace_bytes,
                        stream);
+}
+
+int wkv_step(int dtype, int state_dtype, const void* key, const void* value,
+             const float* time_decay, const float* time_first, void* numerator, void* denominator,
+             void* log_scale, void* y, int64_t B, int64_t C, void* stream) {
+  g_last_error[0] = '\0';
+  int rc = check_dims(dtype, B, 1, C);
+  if (rc) return rc;
+  if (state_dtype != dtype && state_dtype != WKV_DTYPE_F32)
+    return fail(WKV_ERR_INVALID_ARGUMENT,
+                "state dtype code %d: the state must be float32 or the key/value dtype (%d)",
+                state_dtype, dtype);
+  if (B == 0 || C == 0) return WKV_OK;
+  if (!key || !value || !time_decay || !time_first || !numerator || !denominator || !log_scale || !y)
+    return fail(WKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  const int V = static_cast<int>(16 / dtype_size(dtype));
+  const bool vec = (C % V) == 0 && aligned16(key) && aligned16(value) && aligned16(numerator) &&
+                   aligned16(denominator) && aligned16(log_scale) && aligned16(y) &&
+                   aligned16(time_decay) && aligned16(time_first);
+  StepArgs a{key, value, time_decay, time_first, numerator, denominator, log_scale, y, B * C, (int)C};
+  const int64_t work = vec ? a.n / V : a.n;
+  const unsigned grid =
+      (unsigned)std::min<int64_t>((work + 255) / 256, (int64_t)sm_count() * 8);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool s32 = state_dtype == WKV_DTYPE_F32;
+  launch(K_STEP, st, [&] {
+    switch (dtype) {
+      case WKV_DTYPE_F32:
+        if (vec) wkv_step_kernel<float, float, 4><<<grid, 256, 0, st>>>(a);
+        else wkv_step_kernel<float, float, 1><<<grid, 256, 0, st>>>(a);
+        break;
+      case WKV_DTYPE_BF16:
+        if (s32) {
+          if (vec) wkv_step_kernel<__nv_bfloat16, float, 8><<<grid, 256, 0, st>>>(a);
+          else wkv_step_kernel<__nv_bfloat16, float, 1><<<grid, 256, 0, st>>>(a);
+        } else {
+          if (vec) wkv_step_kernel<__nv_bfloat16, __nv_bfloat16, 8><<<grid, 256, 0, st>>>(a);
+          else wkv_step_kernel<__nv_bfloat16, __nv_bfloat16, 1><<<grid, 256, 0, st>>>(a);
+        }
+        break;
+      default:
+        if (s32) {
+          if (vec) wkv_step_kernel<__half, float, 8><<<grid, 256, 0, st>>>(a);
+          else wkv_step_kernel<__half, float, 1><<<grid, 256, 0, st>>>(a);
+        } else {
+          if (vec) wkv_step_kernel<__half, __half, 8><<<grid, 256, 0, st>>>(a);
+          else wkv_step_kernel<__half, __half, 1><<<grid, 256, 0, st>>>(a);
+        }
+        break;
+    }
+  });
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "wkv step launch");
+  return WKV_OK;
 }
 
 int wkv_kernel_kinds(void) { return K_COUNT; }

@@ -73,6 +73,8 @@ def lib() -> ctypes.CDLL:
         handle.wkv_backward.restype = ci
         handle.wkv_backward_noalloc.argtypes = [ci, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, vp]
         handle.wkv_backward_noalloc.restype = ci
+        handle.wkv_step.argtypes = [ci, ci, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
+        handle.wkv_step.restype = ci
         handle.wkv_state_size.argtypes = [ci, i64, i64, i64]
         handle.wkv_state_size.restype = sz
         handle.wkv_forward_with_state.argtypes = [ci, vp, vp, vp, vp, vp, vp, sz, i64, i64, i64, vp, sz, vp]
