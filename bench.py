@@ -60,6 +60,9 @@ WORKLOADS = {
     "decode": dict(kind="step", B=16384, T=1, C=512, dtype="bf16", state="fp32", kscale=4.0,
                    desc="recurrent step: B=16384 streams x C=512, bf16 k/v, float32 state"),
 }
+WORKLOADS["lif"] = dict(kind="lif", B=64, T=1024, C=512, dtype="bf16", kscale=1.5,
+                        desc="LIF fwd+bwd: B=64 T=1024 C=512 bf16 (a SpikeGPT-41M block activation)")
+LIF_METRIC = "LIF fwd+bwd algorithmic HBM throughput"
 STEP_METRIC = "WKV recurrent step algorithmic HBM throughput"
 STEP_BYTES = {"bf16": 2, "fp16": 2, "fp32": 4}
 METRIC = "WKV fwd+bwd algorithmic HBM throughput"
@@ -519,6 +522,156 @@ def run_step(args, wl):
         dist.destroy_process_group()
 
 
+def run_lif(args, wl):
+    """LIF sequence op: one lif_forward (keeping its membrane state) plus one
+    lif_backward per step through the C ABI on device-resident inputs.
+    Algorithmic bytes per element: forward x in, spikes out; backward grad,
+    x in, grad x out (5 x the element size)."""
+    import torch
+    import torch.distributed as dist
+
+    from spikegpt_b200 import _capi, surrogate_lif
+    from spikegpt_b200.sharding import max_over_ranks
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    tdt = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}[wl["dtype"]]
+    code = {"bf16": _capi.DTYPE_BF16, "fp16": _capi.DTYPE_F16, "fp32": _capi.DTYPE_F32}[wl["dtype"]]
+    b, t, c = wl["B"], wl["T"], wl["C"]
+    rng = np.random.default_rng(rank)
+    x_np = (rng.standard_normal((b, t, c)) * wl["kscale"] + 0.3).astype(np.float32)
+    gs_np = rng.standard_normal((b, t, c)).astype(np.float32)
+    x = torch.as_tensor(x_np).to(dev, tdt)
+    gs = torch.as_tensor(gs_np).to(dev, tdt)
+    spikes, gx = torch.empty_like(x), torch.empty_like(x)
+    lib = _capi.lib()
+    nst = int(lib.lif_state_size(code, b, t, c))
+    state = torch.empty(nst // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    prm = (2.0, 1.0, 0.0, 2.0)  # tau, threshold, reset, surrogate_slope (the reference's defaults)
+
+    def step():
+        _capi.check(lib.lif_forward(code, x.data_ptr(), spikes.data_ptr(), state.data_ptr(), nst, b, t, c, *prm, sp),
+                    "lif_forward")
+        _capi.check(lib.lif_backward(code, gs.data_ptr(), x.data_ptr(), state.data_ptr(), nst, gx.data_ptr(),
+                                     b, t, c, *prm, sp), "lif_backward")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    sampler = None if args.profile else ClockSampler(local)
+    time.sleep(0.3 if sampler else 0)
+    _capi.timing_collect()
+    _capi.timing_enable(True)
+    launches0 = sum(_capi.launch_counts().values())
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    host0 = time.time()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    host1 = time.time()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    _capi.timing_enable(False)
+    launches = sum(_capi.launch_counts().values()) - launches0
+    per_kernel = _capi.timing_collect()
+    ms = max_over_ranks(ev0.elapsed_time(ev1), dev)
+    if sampler:
+        time.sleep(0.25)
+        sampler.stop()
+    clocks = sampler.summary(host0, host1) if sampler else None
+    es = STEP_BYTES[wl["dtype"]]
+    elems = b * t * c
+    value = 5 * es * elems * args.steps * world / (ms * 1e-3) / 1e9
+    alg = {"lif_fwd_kernel": 2 * es * elems, "lif_bwd_kernel": 3 * es * elems}
+    kernels = {n: {"ms_per_launch": tot / cnt, "launches": cnt} for n, (tot, cnt) in per_kernel.items() if cnt}
+    total = sum(k["ms_per_launch"] * k["launches"] for k in kernels.values())
+    for k in kernels.values():
+        k["share"] = k["ms_per_launch"] * k["launches"] / total
+    dom = max(kernels, key=lambda n: kernels[n]["share"])
+    pk = peaks()
+    hbm = float(pk.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+    achieved = alg[dom] / (kernels[dom]["ms_per_launch"] * 1e-3) / 1e9
+    result = {
+        "metric": LIF_METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": wl["dtype"], "data": "synthetic (seeded numpy PCG64)",
+        "config": {"workload": wl["desc"], "B_per_gpu": b, "T": t, "C": c,
+                   "parallelism": f"{world} batch-sharded replica(s), no collective",
+                   "l2": f"{4 * es * elems / 1e6:.0f} MB of inputs read per step (> L2); no flush"},
+        "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "alg_bytes_per_launch": alg[dom],
+                     "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if pk.get("source") == "measured"
+                     else "fallback 6.65 TB/s",
+                     "traffic": ncu_traffic(dom, args.workload)},
+        "kernels": kernels, "gpu_launches": int(launches), "clocks": clocks,
+    }
+    if not args.profile:
+        hx = torch.as_tensor(x_np).to(tdt).pin_memory()
+        hgs = torch.as_tensor(gs_np).to(tdt).pin_memory()
+        hs, hgx = torch.empty_like(hx).pin_memory(), torch.empty_like(hx).pin_memory()
+
+        def e2e_step():
+            xd = hx.to(dev, non_blocking=True).requires_grad_()
+            out = surrogate_lif(xd)
+            out.backward(hgs.to(dev, non_blocking=True))
+            hs.copy_(out.detach(), non_blocking=True)
+            hgx.copy_(xd.grad, non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ems = max_over_ranks(e0.elapsed_time(e1), dev)
+        result["e2e"] = {"value": 5 * es * elems * args.e2e_steps * world / (ems * 1e-3) / 1e9, "unit": "GB/s",
+                         "h2d_bytes_per_step": 2 * es * elems, "d2h_bytes_per_step": 2 * es * elems,
+                         "steps": args.e2e_steps, "ms_per_step": ems / args.e2e_steps,
+                         "path": "autograd through spikegpt_b200.surrogate_lif, pinned host buffers"}
+        if world == 1 and rank == 0:
+            result["cpu_baseline"] = cpu_lif_throughput(wl)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def cpu_lif_throughput(wl: dict, seconds: float = 5.0):
+    """The float32 LIF oracle fwd+bwd (a single-threaded C loop) on one batch row."""
+    from oracle import oracle
+
+    rng = np.random.default_rng(0)
+    x = (rng.standard_normal((1, wl["T"], wl["C"])) * wl["kscale"] + 0.3).astype(np.float32)
+    gs = rng.standard_normal(x.shape).astype(np.float32)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        oracle.lif_forward(x, dtype=np.float32)
+        oracle.lif_backward(gs, x, dtype=np.float32)
+        n += 1
+    el = time.perf_counter() - t0
+    return {"value": 5 * STEP_BYTES[wl["dtype"]] * x.size * n / el / 1e9, "unit": "GB/s", "cores": 1,
+            "kind": "port", "sample": f"{n} x (1 of {wl['B']} batch rows), float32, {el:.1f} s",
+            "host_cpus": os.cpu_count()}
+
+
 def cpu_step_throughput(wl: dict, seconds: float = 5.0):
     """The float32 oracle step (a single-threaded C loop) on 64 of the
     workload's streams, repeated for about `seconds`."""
@@ -705,6 +858,22 @@ def run_step_reference(args, wl):
     print(json.dumps(out), flush=True)
 
 
+def run_lif_reference(args, wl):
+    """Reference arm of the LIF workload: the oracle on the host, rank 0."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    base = cpu_lif_throughput(wl, seconds=2.0)
+    out = {"metric": LIF_METRIC, "value": base["value"], "unit": "GB/s",
+           "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl["dtype"],
+           "data": "synthetic (seeded numpy PCG64)", "config": {"workload": wl["desc"]},
+           "impl": "reference", "cpu_baseline": base,
+           "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+           "note": "the reference's CPU path is its per-step PyTorch loop; this arm times the C restatement "
+                   "of that loop (oracle/wkv_oracle.c) on the host"}
+    print(json.dumps(out), flush=True)
+
+
 def main():
     args = parse_args()
     wl = WORKLOADS[args.workload]
@@ -713,6 +882,11 @@ def main():
             run_step_reference(args, wl)
         else:
             run_step(args, wl)
+    elif wl.get("kind") == "lif":
+        if args.impl == "reference":
+            run_lif_reference(args, wl)
+        else:
+            run_lif(args, wl)
     elif args.impl == "reference":
         run_reference(args, wl)
     else:

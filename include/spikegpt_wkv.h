@@ -151,6 +151,30 @@ WKV_API int wkv_step(int dtype, int state_dtype, const void* key, const void* va
                      void* stream);
 
 /*
+ * LIF sequence op: the spiking activation of SpikeGPT blocks. Replaces the
+ * fused LIF kernels the reference calls from SpikingSequenceLIF.forward
+ * (src/spikegpt/language.py:849-906: myelin's surrogate_lif_bf16io and
+ * triton_surrogate_lif_function) with the semantics of its per-step loop
+ * (language.py:816-843, 907-918): per (b, c) over t,
+ *   v = v * decay + x_t (decay = 1 - 1/tau);  s_t = slope * (v - threshold) >= 0;
+ *   v = v * (1 - s_t) + reset * s_t,
+ * membrane in float32, x and spikes [B, T, C] in `dtype`. lif_forward writes
+ * the spikes and, when `state` is non-null (lif_state_size bytes, 16-byte
+ * aligned), the membrane entering every 16-step tile, which lif_backward
+ * needs. lif_backward gives grad_x from grad_spikes through the loop with the
+ * spike's surrogate derivative slope * 1 / (2 (1 + (pi/2 * centered)^2)) (the
+ * published arc-tangent surrogate; the reference's own surrogate lives in
+ * myelin@68b8ebb and is not available to pin against). tau > 0.
+ */
+WKV_API size_t lif_state_size(int dtype, int64_t B, int64_t T, int64_t C);
+WKV_API int lif_forward(int dtype, const void* x, void* spikes, float* state, size_t state_bytes,
+                        int64_t B, int64_t T, int64_t C, float tau, float threshold, float reset,
+                        float slope, void* stream);
+WKV_API int lif_backward(int dtype, const void* grad_spikes, const void* x, const float* state,
+                         size_t state_bytes, void* grad_x, int64_t B, int64_t T, int64_t C,
+                         float tau, float threshold, float reset, float slope, void* stream);
+
+/*
  * Forward/backward with a saved forward state (no reference counterpart; an
  * optimisation of wkv_forward/wkv_backward). wkv_forward_with_state computes y exactly as
  * wkv_forward and also stores the recurrence state at every 16th step into

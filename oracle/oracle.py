@@ -78,6 +78,13 @@ def _load() -> ctypes.CDLL:
         stp = getattr(lib, f"wkv_oracle_step_{suf}")
         stp.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i64, i64]
         stp.restype = None
+        real = ctypes.c_double if suf == "f64" else ctypes.c_float
+        lf = getattr(lib, f"lif_oracle_forward_{suf}")
+        lf.argtypes = [vp, vp, i64, i64, i64, real, real, real, real]
+        lf.restype = None
+        lb = getattr(lib, f"lif_oracle_backward_{suf}")
+        lb.argtypes = [vp, vp, vp, i64, i64, i64, real, real, real, real]
+        lb.restype = ci
     lib.wkv_oracle_max_threads.restype = ci
     _lib = lib
     return lib
@@ -177,6 +184,29 @@ def initial_step_state(b: int, c: int, dtype=np.float64):
     """The reference's initial state (language.py:964-974): zeros and the
     dtype's most negative finite log_scale."""
     return (np.zeros((b, c), dtype), np.zeros((b, c), dtype), np.full((b, c), np.finfo(dtype).min, dtype))
+
+
+def lif_forward(x, *, tau=2.0, threshold=1.0, reset=0.0, slope=2.0, dtype=np.float64) -> np.ndarray:
+    """Spikes of the LIF sequence op (reference SpikingSequenceLIF,
+    src/spikegpt/language.py:766-918) for currents x [B, T, C]."""
+    suf = "f64" if np.dtype(dtype) == np.float64 else "f32"
+    x = _prep(x, dtype)
+    s = np.empty_like(x)
+    getattr(_load(), f"lif_oracle_forward_{suf}")(_ptr(x), _ptr(s), *x.shape, tau, threshold, reset, slope)
+    return s
+
+
+def lif_backward(gs, x, *, tau=2.0, threshold=1.0, reset=0.0, slope=2.0, dtype=np.float64) -> np.ndarray:
+    """d loss / d x given d loss / d spikes (arc-tangent surrogate; see
+    wkv_oracle.c for the formula and why the surrogate is unpinned)."""
+    suf = "f64" if np.dtype(dtype) == np.float64 else "f32"
+    gs, x = _prep(gs, dtype), _prep(x, dtype)
+    gx = np.empty_like(x)
+    rc = getattr(_load(), f"lif_oracle_backward_{suf}")(_ptr(gs), _ptr(x), _ptr(gx), *x.shape, tau, threshold,
+                                                        reset, slope)
+    if rc != 0:
+        raise RuntimeError("lif oracle backward failed")
+    return gx
 
 
 def forward_numpy(k, v, time_decay, time_first) -> np.ndarray:

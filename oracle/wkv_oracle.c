@@ -189,6 +189,71 @@ WKV_ORACLE_DEFINE(float, f32, expf, -3.4028234663852886e38f)
 WKV_ORACLE_STEP_DEFINE(double, f64, exp)
 WKV_ORACLE_STEP_DEFINE(float, f32, expf)
 
+/*
+ * LIF sequence op (reference SpikingSequenceLIF, src/spikegpt/language.py:766-918),
+ * per (b, c) over t, in the operation order of the reference's step
+ * (language.py:831-841):
+ *   v = v * decay + x_t;  centered = slope * (v - threshold);
+ *   s_t = centered >= 0;  v = v * (1 - s_t) + reset * s_t
+ * with decay = 1 - 1/tau and v = 0 at t = 0. x, s: [B, T, C].
+ * The backward is the gradient of that loop under autograd with the spike's
+ * surrogate derivative slope * surrogate'(centered), surrogate'(x) =
+ * 1 / (2 (1 + (pi/2 x)^2)) (the published arc-tangent surrogate; the
+ * reference's own definition lives in myelin@68b8ebb, not available here):
+ *   dL/dv_t = ds/dv (gs_t + g (reset - v_t)) + g (1 - s_t),  dL/dx_t = dL/dv_t,
+ *   g <- decay * dL/dv_t  (g = dL/d(membrane after step t), 0 after the last step)
+ */
+#define LIF_ORACLE_DEFINE(REAL, SUF)                                                          \
+  void lif_oracle_forward_##SUF(const REAL* x, REAL* spikes, int64_t B, int64_t T, int64_t C, \
+                                REAL tau, REAL threshold, REAL reset, REAL slope) {           \
+    const REAL decay = (REAL)(1.0 - 1.0 / (double)tau);                                     \
+    for (int64_t b = 0; b < B; ++b)                                                           \
+      for (int64_t c = 0; c < C; ++c) {                                                       \
+        REAL v = 0;                                                                           \
+        for (int64_t t = 0; t < T; ++t) {                                                     \
+          const int64_t i = (b * T + t) * C + c;                                              \
+          v = v * decay + x[i];                                                               \
+          const REAL centered = slope * (v - threshold);                                      \
+          const REAL s = centered >= 0 ? (REAL)1 : (REAL)0;                                   \
+          spikes[i] = s;                                                                      \
+          v = v * ((REAL)1 - s) + reset * s;                                                  \
+        }                                                                                     \
+      }                                                                                       \
+  }                                                                                           \
+  int lif_oracle_backward_##SUF(const REAL* gs, const REAL* x, REAL* gx, int64_t B, int64_t T, \
+                                int64_t C, REAL tau, REAL threshold, REAL reset, REAL slope) { \
+    const REAL decay = (REAL)(1.0 - 1.0 / (double)tau);                                     \
+    REAL* vs = (REAL*)malloc(sizeof(REAL) * (size_t)(T > 0 ? T : 1));                         \
+    if (!vs) return 1;                                                                        \
+    for (int64_t b = 0; b < B; ++b)                                                           \
+      for (int64_t c = 0; c < C; ++c) {                                                       \
+        REAL v = 0;                                                                           \
+        for (int64_t t = 0; t < T; ++t) {                                                     \
+          const int64_t i = (b * T + t) * C + c;                                              \
+          v = v * decay + x[i];                                                               \
+          vs[t] = v;                                                                          \
+          const REAL s = slope * (v - threshold) >= 0 ? (REAL)1 : (REAL)0;                    \
+          v = v * ((REAL)1 - s) + reset * s;                                                  \
+        }                                                                                     \
+        REAL g = 0;                                                                           \
+        for (int64_t t = T - 1; t >= 0; --t) {                                                \
+          const int64_t i = (b * T + t) * C + c;                                              \
+          const REAL centered = slope * (vs[t] - threshold);                                  \
+          const REAL s = centered >= 0 ? (REAL)1 : (REAL)0;                                   \
+          const REAL h = (REAL)1.5707963267948966 * centered;                                 \
+          const REAL dsdv = slope * ((REAL)0.5 / ((REAL)1 + h * h));                          \
+          const REAL gv = dsdv * (gs[i] + g * (reset - vs[t])) + g * ((REAL)1 - s);           \
+          gx[i] = gv;                                                                         \
+          g = decay * gv;                                                                     \
+        }                                                                                     \
+      }                                                                                       \
+    free(vs);                                                                                 \
+    return 0;                                                                                 \
+  }
+
+LIF_ORACLE_DEFINE(double, f64)
+LIF_ORACLE_DEFINE(float, f32)
+
 /* Number of OpenMP threads the runtime would use by default (1 without OpenMP). */
 int wkv_oracle_max_threads(void) {
 #ifdef _OPENMP

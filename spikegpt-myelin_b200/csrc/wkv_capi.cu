@@ -17,6 +17,7 @@
 #include <vector>
 
 #include "spikegpt_wkv.h"
+#include "lif.cuh"
 #include "wkv_step.cuh"
 #include "wkv_tp.cuh"
 
@@ -37,11 +38,14 @@ __device__ unsigned g_device_error_flags = 0;
 // while timing is enabled, brackets the launch with CUDA events recorded on the
 // launch stream, so per-kernel device time can be read back by the caller.
 
-enum Kind { K_FWD_Y, K_FWD_STATE, K_BWD_GRAD, K_BWD_ADJ, K_CARRY_FWD, K_CARRY_ADJ, K_STEP, K_COUNT };
+enum Kind {
+  K_FWD_Y, K_FWD_STATE, K_BWD_GRAD, K_BWD_ADJ, K_CARRY_FWD, K_CARRY_ADJ, K_STEP, K_LIF_FWD, K_LIF_BWD,
+  K_COUNT
+};
 const char* const kKindNames[K_COUNT] = {
     "wkv_fwd_kernel<y>",      "wkv_fwd_kernel<state>", "wkv_bwd_kernel<grad>",
     "wkv_bwd_kernel<adjoint>", "wkv_carry_fwd_kernel",  "wkv_carry_adj_kernel",
-    "wkv_step_kernel"};
+    "wkv_step_kernel",        "lif_fwd_kernel",        "lif_bwd_kernel"};
 
 std::atomic<long long> g_launches[K_COUNT];
 std::atomic<bool> g_timing{false};
@@ -860,6 +864,144 @@ int wkv_step(int dtype, int state_dtype, const void* key, const void* value,
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "wkv step launch");
   return WKV_OK;
+}
+
+size_t lif_state_size(int dtype, int64_t B, int64_t T, int64_t C) {
+  if (check_dims(dtype, B, T, C)) return 0;
+  return round_up((size_t)B * ((T + kSub - 1) / kSub) * C * sizeof(float));
+}
+
+}  // extern "C"
+
+namespace {
+
+int lif_prepare(int dtype, int64_t B, int64_t T, int64_t C, float tau, float threshold,
+                float reset, float slope, LifArgs& a) {
+  int rc = check_dims(dtype, B, T, C);
+  if (rc) return rc;
+  if (!(tau > 0.f)) return fail(WKV_ERR_INVALID_ARGUMENT, "tau must be positive");
+  a = LifArgs{};
+  a.decay = static_cast<float>(1.0 - 1.0 / static_cast<double>(tau));  // as the reference's decay
+  a.threshold = threshold;
+  a.reset = reset;
+  a.slope = slope;
+  a.B = (int)B;
+  a.T = (int)T;
+  a.C = (int)C;
+  a.ncblk = (int)((C + kLanes - 1) / kLanes);
+  a.ntiles = (int)((T + kSub - 1) / kSub);
+  a.err = device_err_ptr();
+  return WKV_OK;
+}
+
+template <typename IO>
+int lif_launch_forward(LifArgs& a, bool tma, cudaStream_t st) {
+  const int dt = sizeof(IO) == 4 ? WKV_DTYPE_F32
+                 : std::is_same<IO, __nv_bfloat16>::value ? WKV_DTYPE_BF16
+                                                         : WKV_DTYPE_F16;
+  CUtensorMap mx, ms;
+  std::memset(&mx, 0, sizeof(mx));
+  std::memset(&ms, 0, sizeof(ms));
+  int rc;
+  if (tma && ((rc = make_map(&mx, dt, a.x, a.B, a.T, a.C, kSub)) ||
+              (rc = make_map(&ms, dt, a.s, a.B, a.T, a.C, kSub))))
+    return rc;
+  const size_t sm = lif_fwd_smem_bytes<IO>();
+  const cudaError_t e = tma ? allow_smem(lif_fwd_kernel<IO, true>, sm) : allow_smem(lif_fwd_kernel<IO, false>, sm);
+  if (e != cudaSuccess) return cuda_fail(e, "setting the LIF kernel's shared memory size");
+  const unsigned grid = (unsigned)a.ncblk * (unsigned)a.B;
+  launch(K_LIF_FWD, st, [&] {
+    if (tma) lif_fwd_kernel<IO, true><<<grid, 32, sm, st>>>(a, mx, ms);
+    else lif_fwd_kernel<IO, false><<<grid, 32, sm, st>>>(a, mx, ms);
+  });
+  const cudaError_t le = cudaGetLastError();
+  return le == cudaSuccess ? WKV_OK : cuda_fail(le, "LIF forward launch");
+}
+
+template <typename IO>
+int lif_launch_backward(LifArgs& a, bool tma, cudaStream_t st) {
+  const int dt = sizeof(IO) == 4 ? WKV_DTYPE_F32
+                 : std::is_same<IO, __nv_bfloat16>::value ? WKV_DTYPE_BF16
+                                                         : WKV_DTYPE_F16;
+  CUtensorMap mx, mg, mo;
+  std::memset(&mx, 0, sizeof(mx));
+  std::memset(&mg, 0, sizeof(mg));
+  std::memset(&mo, 0, sizeof(mo));
+  int rc;
+  if (tma && ((rc = make_map(&mx, dt, a.x, a.B, a.T, a.C, kSub)) ||
+              (rc = make_map(&mg, dt, a.gs, a.B, a.T, a.C, kSub)) ||
+              (rc = make_map(&mo, dt, a.gx, a.B, a.T, a.C, kSub))))
+    return rc;
+  const size_t sm = lif_bwd_smem_bytes<IO>();
+  const cudaError_t e = tma ? allow_smem(lif_bwd_kernel<IO, true>, sm) : allow_smem(lif_bwd_kernel<IO, false>, sm);
+  if (e != cudaSuccess) return cuda_fail(e, "setting the LIF kernel's shared memory size");
+  const unsigned grid = (unsigned)a.ncblk * (unsigned)a.B;
+  launch(K_LIF_BWD, st, [&] {
+    if (tma) lif_bwd_kernel<IO, true><<<grid, 32, sm, st>>>(a, mx, mg, mo);
+    else lif_bwd_kernel<IO, false><<<grid, 32, sm, st>>>(a, mx, mg, mo);
+  });
+  const cudaError_t le = cudaGetLastError();
+  return le == cudaSuccess ? WKV_OK : cuda_fail(le, "LIF backward launch");
+}
+
+}  // namespace
+
+extern "C" {
+
+int lif_forward(int dtype, const void* x, void* spikes, float* state, size_t state_bytes,
+                int64_t B, int64_t T, int64_t C, float tau, float threshold, float reset,
+                float slope, void* stream) {
+  g_last_error[0] = '\0';
+  LifArgs a;
+  int rc = lif_prepare(dtype, B, T, C, tau, threshold, reset, slope, a);
+  if (rc) return rc;
+  if (B == 0 || T == 0 || C == 0) return WKV_OK;
+  if (!x || !spikes) return fail(WKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (state != nullptr) {
+    const size_t need = lif_state_size(dtype, B, T, C);
+    if (state_bytes < need)
+      return fail(WKV_ERR_WORKSPACE_TOO_SMALL, "LIF state needs %zu bytes, got %zu", need, state_bytes);
+    if (!aligned16(state)) return fail(WKV_ERR_INVALID_ARGUMENT, "state must be 16-byte aligned");
+  }
+  a.x = x;
+  a.s = spikes;
+  a.state = state;
+  const bool tma = g_force_generic.load() == 0 && aligned16(x) && aligned16(spikes) &&
+                   (C * (int64_t)dtype_size(dtype)) % 16 == 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case WKV_DTYPE_F32: return lif_launch_forward<float>(a, tma, st);
+    case WKV_DTYPE_BF16: return lif_launch_forward<__nv_bfloat16>(a, tma, st);
+    default: return lif_launch_forward<__half>(a, tma, st);
+  }
+}
+
+int lif_backward(int dtype, const void* grad_spikes, const void* x, const float* state,
+                 size_t state_bytes, void* grad_x, int64_t B, int64_t T, int64_t C, float tau,
+                 float threshold, float reset, float slope, void* stream) {
+  g_last_error[0] = '\0';
+  LifArgs a;
+  int rc = lif_prepare(dtype, B, T, C, tau, threshold, reset, slope, a);
+  if (rc) return rc;
+  if (B == 0 || T == 0 || C == 0) return WKV_OK;
+  if (!grad_spikes || !x || !grad_x || !state)
+    return fail(WKV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  const size_t need = lif_state_size(dtype, B, T, C);
+  if (state_bytes < need)
+    return fail(WKV_ERR_WORKSPACE_TOO_SMALL, "LIF state needs %zu bytes, got %zu", need, state_bytes);
+  if (!aligned16(state)) return fail(WKV_ERR_INVALID_ARGUMENT, "state must be 16-byte aligned");
+  a.x = x;
+  a.gs = grad_spikes;
+  a.gx = grad_x;
+  a.state = const_cast<float*>(state);
+  const bool tma = g_force_generic.load() == 0 && aligned16(x) && aligned16(grad_spikes) &&
+                   aligned16(grad_x) && (C * (int64_t)dtype_size(dtype)) % 16 == 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case WKV_DTYPE_F32: return lif_launch_backward<float>(a, tma, st);
+    case WKV_DTYPE_BF16: return lif_launch_backward<__nv_bfloat16>(a, tma, st);
+    default: return lif_launch_backward<__half>(a, tma, st);
+  }
 }
 
 int wkv_kernel_kinds(void) { return K_COUNT; }

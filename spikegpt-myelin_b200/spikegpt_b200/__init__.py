@@ -12,11 +12,14 @@ from __future__ import annotations
 
 from . import _capi
 from ._ops import set_state_saving, state_saving_enabled, validate_wkv_inputs
+from .lif import SpikingSequenceLIF, surrogate_lif
 from .step import initial_step_state, weighted_key_value_step, weighted_key_value_step_
 from .wkv import weighted_key_value_cuda, weighted_key_value_triton
 from .wkv_bf16 import weighted_key_value_cuda_bf16io, weighted_key_value_triton_bf16io
 
 __all__ = [
+    "SpikingSequenceLIF",
+    "surrogate_lif",
     "initial_step_state",
     "weighted_key_value_step",
     "weighted_key_value_step_",

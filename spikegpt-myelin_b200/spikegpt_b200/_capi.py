@@ -75,6 +75,13 @@ def lib() -> ctypes.CDLL:
         handle.wkv_backward_noalloc.restype = ci
         handle.wkv_step.argtypes = [ci, ci, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]
         handle.wkv_step.restype = ci
+        f32 = ctypes.c_float
+        handle.lif_state_size.argtypes = [ci, i64, i64, i64]
+        handle.lif_state_size.restype = sz
+        handle.lif_forward.argtypes = [ci, vp, vp, vp, sz, i64, i64, i64, f32, f32, f32, f32, vp]
+        handle.lif_forward.restype = ci
+        handle.lif_backward.argtypes = [ci, vp, vp, vp, sz, vp, i64, i64, i64, f32, f32, f32, f32, vp]
+        handle.lif_backward.restype = ci
         handle.wkv_state_size.argtypes = [ci, i64, i64, i64]
         handle.wkv_state_size.restype = sz
         handle.wkv_forward_with_state.argtypes = [ci, vp, vp, vp, vp, vp, vp, sz, i64, i64, i64, vp, sz, vp]
@@ -166,4 +173,4 @@ def declared_symbols() -> list[str]:
     import re
 
     text = HEADER_PATH.read_text()
-    return sorted(set(re.findall(r"WKV_API\s+[\w\s\*]+?\b(wkv_\w+)\s*\(", text)))
+    return sorted(set(re.findall(r"WKV_API\s+[\w\s\*]+?\b((?:wkv|lif)_\w+)\s*\(", text)))

@@ -1,0 +1,124 @@
+"""GPU parity of the LIF sequence op (lif_forward / lif_backward through the
+registered ops) against the oracle and the reference-generated golden vectors.
+
+Spikes: exactly equal to the float32 oracle on the same (dtype-rounded)
+inputs, since the kernels keep the reference step's operation order. Input
+gradients: max|x - ref| / max(1, max|ref|) <= 1e-5 (float32 I/O), 2e-2
+(bf16/fp16, whose gradients are rounded on store)."""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+from _wkvtest import TOL_16BIT, TOL_FP32, scaled_err
+
+from oracle import oracle
+from spikegpt_b200 import SpikingSequenceLIF, _capi, surrogate_lif
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = np.load(Path(__file__).resolve().parent / "golden" / "lif_golden.npz")
+CASES = sorted({f.split("/")[0] for f in GOLDEN.files})
+
+
+def _params(name):
+    tau, thr, rst, sl = (float(x) for x in GOLDEN[f"{name}/params"])
+    return dict(tau=tau, threshold=thr, reset=rst, surrogate_slope=sl)
+
+
+def _run(x_np, gs_np, dtype, device, **params):
+    x = torch.as_tensor(np.asarray(x_np, np.float32)).to(device=device, dtype=dtype).requires_grad_()
+    s = surrogate_lif(x, **params)
+    s.backward(torch.as_tensor(np.asarray(gs_np, np.float32)).to(device=device, dtype=dtype))
+    return s.detach().double().cpu().numpy(), x.grad.double().cpu().numpy(), x.detach().double().cpu().numpy()
+
+
+def _oracle(x, gs, **p):
+    q = dict(tau=p["tau"], threshold=p["threshold"], reset=p["reset"], slope=p["surrogate_slope"])
+    return oracle.lif_forward(x, dtype=np.float32, **q), oracle.lif_backward(gs, x, **q)
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_golden_cases_float32(cuda, name):
+    s, gx, _ = _run(GOLDEN[f"{name}/x"], GOLDEN[f"{name}/gs"], torch.float32, cuda, **_params(name))
+    np.testing.assert_array_equal(s, GOLDEN[f"{name}/spikes"])
+    assert scaled_err(gx, GOLDEN[f"{name}/gx"]) <= TOL_FP32
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("name", CASES)
+def test_golden_cases_16bit(cuda, name, dtype):
+    p = _params(name)
+    s, gx, xr = _run(GOLDEN[f"{name}/x"], GOLDEN[f"{name}/gs"], dtype, cuda, **p)
+    gs_r = torch.as_tensor(GOLDEN[f"{name}/gs"]).to(dtype).double().numpy()
+    s_ref, gx_ref = _oracle(xr, gs_r, **p)
+    np.testing.assert_array_equal(s, s_ref)
+    assert scaled_err(gx, gx_ref) <= TOL_16BIT
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_config_shape(cuda, dtype):
+    """B=64 T=1024 C=512 (a SpikeGPT-41M block's activation)."""
+    rng = np.random.default_rng(5)
+    x = (rng.standard_normal((64, 1024, 512)) * 1.5 + 0.3).astype(np.float32)
+    gs = rng.standard_normal(x.shape).astype(np.float32)
+    s, gx, xr = _run(x, gs, dtype, cuda)
+    gs_r = torch.as_tensor(gs).to(dtype).double().numpy()
+    s_ref, gx_ref = _oracle(xr, gs_r, tau=2.0, threshold=1.0, reset=0.0, surrogate_slope=2.0)
+    np.testing.assert_array_equal(s, s_ref)
+    assert scaled_err(gx, gx_ref) <= (TOL_FP32 if dtype == torch.float32 else TOL_16BIT)
+
+
+@pytest.mark.parametrize("shape", [(2, 17, 70), (3, 1, 64), (1, 33, 8), (2, 40, 130)])
+@pytest.mark.parametrize("generic", [False, True])
+def test_shapes_tails_and_generic_path(cuda, shape, generic):
+    _capi.set_debug_overrides(force_generic=int(generic))
+    try:
+        rng = np.random.default_rng(sum(shape))
+        x = (rng.standard_normal(shape) * 2).astype(np.float32)
+        gs = rng.standard_normal(shape).astype(np.float32)
+        s, gx, xr = _run(x, gs, torch.float32, cuda)
+        s_ref, gx_ref = _oracle(xr, gs, tau=2.0, threshold=1.0, reset=0.0, surrogate_slope=2.0)
+        np.testing.assert_array_equal(s, s_ref)
+        assert scaled_err(gx, gx_ref) <= TOL_FP32
+    finally:
+        _capi.set_debug_overrides()
+
+
+def test_module_contract_and_errors(cuda):
+    lif = SpikingSequenceLIF(tau=3.0, threshold=0.5, reset=-0.1, surrogate_slope=4.0)
+    assert lif.decay == pytest.approx(1 - 1 / 3)
+    x = torch.randn(2, 9, 16, device=cuda)
+    out = lif(x)
+    assert out.shape == x.shape and out.dtype == x.dtype
+    assert set(out.unique().tolist()) <= {0.0, 1.0}
+    with pytest.raises(ValueError, match="tau must be positive"):
+        SpikingSequenceLIF(tau=0.0)
+    with pytest.raises(ValueError, match=r"inputs must have shape \[B, T, C\]"):
+        lif(torch.randn(4, 16, device=cuda))
+    y = lif(x.double())
+    assert y.dtype == torch.float64
+
+
+def test_no_state_without_grad_and_compile(cuda):
+    x = torch.randn(4, 64, 64, device=cuda, dtype=torch.bfloat16)
+    with torch.no_grad():
+        s0 = surrogate_lif(x)
+    fn = torch.compile(lambda t: surrogate_lif(t) * 1.0, fullgraph=True)
+    xg = x.clone().requires_grad_()
+    s1 = fn(xg)
+    assert torch.equal(s0, s1.detach())
+    s1.float().sum().backward()
+    assert xg.grad is not None and torch.isfinite(xg.grad.float()).all()
+
+
+def test_lif_kernels_are_counted(cuda):
+    before = _capi.launch_counts()
+    x = torch.randn(2, 32, 64, device=cuda, requires_grad=True)
+    surrogate_lif(x).sum().backward()
+    after = _capi.launch_counts()
+    assert after["lif_fwd_kernel"] == before["lif_fwd_kernel"] + 1
+    assert after["lif_bwd_kernel"] == before["lif_bwd_kernel"] + 1
