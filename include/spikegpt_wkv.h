@@ -160,8 +160,9 @@ WKV_API int wkv_step(int dtype, int state_dtype, const void* key, const void* va
  *   v = v * (1 - s_t) + reset * s_t,
  * membrane in float32, x and spikes [B, T, C] in `dtype`. lif_forward writes
  * the spikes and, when `state` is non-null (lif_state_size bytes, 16-byte
- * aligned), the membrane entering every 16-step tile, which lif_backward
- * needs. lif_backward gives grad_x from grad_spikes through the loop with the
+ * aligned), for every 16-step tile the membrane entering it times decay
+ * ([B][ceil(T/16)][C] float32), which lif_backward recomputes the tile from.
+ * lif_backward gives grad_x from grad_spikes through the loop with the
  * spike's surrogate derivative slope * 1 / (2 (1 + (pi/2 * centered)^2)) (the
  * published arc-tangent surrogate; the reference's own surrogate lives in
  * myelin@68b8ebb and is not available to pin against). tau > 0.

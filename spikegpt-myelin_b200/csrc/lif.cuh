@@ -4,19 +4,28 @@
 // Per (b, c) over t, in the operation order of the reference's step
 // (language.py:831-841), with the membrane carried in float32:
 //   v = v * decay + x_t;  centered = slope * (v - threshold);
-//   s_t = (centered >= 0);  v = s_t ? reset : v
-// (decay = 1 - 1/tau; the reset form v*(1-s) + reset*s is exactly this select).
+//   s_t = (centered >= 0);  v = v * (1 - s_t) + reset * s_t
+// (decay = 1 - 1/tau).
 // Backward (gradient of that loop under autograd, with the spike's surrogate
 // derivative slope * surrogate'(centered), surrogate'(x) = 1 / (2 (1 + (pi/2 x)^2))):
 //   dL/dv_t = ds/dv (gs_t + g (reset - v_t)) + g (1 - s_t);  dL/dx_t = dL/dv_t;
 //   g <- decay * dL/dv_t  (g = dL/d(membrane after step t), 0 after the last step).
 //
-// One warp per (64-channel block, batch row), two channels per lane; kSub-step
-// tiles stream through a ring of shared-memory stages with TMA (or plain loads
-// on the generic path); spikes / input gradients go out through staged tiles.
-// The forward stores the membrane at every tile start ([B][ntiles][C] float32);
-// the backward recomputes each tile's membranes from it, last tile first.
-// Memory-bound: forward 2 * sizeof(T) bytes per element, backward 3 *.
+// One warp per (64-channel block, batch row), two channels per lane, kLifWarps
+// independent warps per CTA (no CTA-wide synchronization). A warp alone on its
+// scheduler issues every instruction of its T steps, and most of them (packed
+// f32x2 arithmetic, compares, selects, logic) issue at one per two cycles, so
+// the step is written for the fewest instructions: the spike test, the two
+// reset branches and the selects in one block that keeps the predicates in
+// predicate registers, the branches' products with decay folded into single
+// fmas, spikes / gradients staged in shared memory with immediate offsets and
+// written by one TMA store per 8 KB tile, and every per-tile cost (barrier
+// wait, TMA issue) paid once per lif_rows<T>() steps. Sub-tiles of kSub steps
+// are the unit of computation and of the checkpoints the forward stores (the
+// membrane entering each sub-tile times decay, [B][ceil(T/kSub)][C] float32)
+// and the backward recomputes from, last sub-tile first. The generic path (unaligned tensors) stages kSub-row tiles
+// with plain loads and stores. Memory-bound target: forward 2 * sizeof(T)
+// bytes per element, backward 3 *.
 #pragma once
 
 #include "wkv_kernels.cuh"
@@ -28,58 +37,252 @@ struct LifArgs {
   const void* gs;
   void* s;
   void* gx;
-  float* state;  // [B][ntiles][C] membrane at each tile start (forward output, backward input)
+  float* state;  // [B][ntiles][C] membrane entering each kSub-step sub-tile times decay (forward output)
   float decay, threshold, reset, slope;
   int B, T, C, ncblk, ntiles;
   unsigned* err;
 };
 
-// Stages of the input ring: 24 KB of the forward's x (12 bf16 tiles) and 32 KB
-// of the backward's (x, grad) pairs in flight per warp whatever the dtype.
+// Rows of a TMA-staged tile: 8 KB of 64 channels (64 bf16/fp16 rows, 32 fp32 rows).
 template <typename T>
-__host__ __device__ constexpr int lif_fwd_stages() {
-  return 24 / static_cast<int>(sizeof(T));
+__host__ __device__ constexpr int lif_rows() {
+  return 8192 / (kLanes * static_cast<int>(sizeof(T)));
+}
+constexpr int kLifTileBytes = 8192;
+constexpr int kLifFwdStages = 4;  // x tiles in flight per warp (forward)
+constexpr int kLifBwdStages = 2;  // (x, grad, checkpoint) tiles in flight per warp (backward)
+constexpr int kLifOut = 2;        // staged output tiles per warp
+// Independent warps per CTA: one warp lands on each of an SM's 4 schedulers.
+constexpr int kLifWarps = 4;
+__host__ __device__ constexpr size_t lif_align128(size_t n) { return (n + 127) / 128 * 128; }
+// Shared memory of one warp (the CTA holds kLifWarps of these): the stage
+// ring, the staged output tiles, the stage barriers. The generic path's
+// kSub-row stages fit in the same space.
+__host__ __device__ constexpr size_t lif_fwd_smem_bytes() {
+  return lif_align128((size_t)(kLifFwdStages + kLifOut) * kLifTileBytes + 8 * kLifFwdStages);
 }
 template <typename T>
-__host__ __device__ constexpr int lif_bwd_stages() {
-  return 16 / static_cast<int>(sizeof(T));
+__host__ __device__ constexpr size_t lif_bwd_stage_bytes() {
+  return (size_t)2 * kLifTileBytes + (size_t)(lif_rows<T>() / kSub) * kLanes * sizeof(float);
 }
 template <typename T>
-constexpr size_t lif_fwd_smem_bytes() {
-  return (size_t)(lif_fwd_stages<T>() + 2) * kSub * kLanes * sizeof(T) + 8 * lif_fwd_stages<T>();
+__host__ __device__ constexpr size_t lif_bwd_smem_bytes() {
+  return lif_align128((size_t)kLifBwdStages * lif_bwd_stage_bytes<T>() + (size_t)kLifOut * kLifTileBytes +
+                      8 * kLifBwdStages);
 }
-template <typename T>
-constexpr size_t lif_bwd_smem_bytes() {
-  return (size_t)(2 * lif_bwd_stages<T>() + 2) * kSub * kLanes * sizeof(T) + 8 * lif_bwd_stages<T>();
+static_assert(lif_rows<float>() % kSub == 0 && lif_rows<__nv_bfloat16>() % kSub == 0, "sub-tiles");
+static_assert(lif_bwd_stage_bytes<float>() % 128 == 0 && lif_bwd_stage_bytes<__nv_bfloat16>() % 128 == 0,
+              "TMA stage alignment");
+static_assert(kLifWarps * lif_bwd_smem_bytes<float>() <= 227 * 1024, "LIF backward shared memory");
+static_assert(kLifWarps * lif_bwd_smem_bytes<__nv_bfloat16>() <= 227 * 1024, "LIF backward shared memory");
+static_assert(kLifWarps * lif_fwd_smem_bytes() <= 227 * 1024, "LIF forward shared memory");
+
+// Per-lane constants of the step for a pair of channels.
+struct LifK {
+  f2 decay, thr, slope, reset;
+  f2 reset0;  // reset * 0: what the non-spiking branch adds (zero unless reset is not finite)
+  f2 rd;      // reset * decay
+  f2 rz;      // reset0 * decay
+  f2 half_slope, half_pi, half_pi_slope, zero, one;
+};
+
+__device__ __forceinline__ LifK lif_constants(const LifArgs& a) {
+  LifK k;
+  k.decay = splat(a.decay);
+  k.thr = splat(a.threshold);
+  k.slope = splat(a.slope);
+  k.reset = splat(a.reset);
+  k.reset0 = splat(__fmul_rn(a.reset, 0.f));
+  k.rd = splat(__fmul_rn(a.reset, a.decay));
+  k.rz = splat(__fmul_rn(__fmul_rn(a.reset, 0.f), a.decay));
+  k.half_slope = splat(__fmul_rn(a.slope, 0.5f));
+  k.half_pi = splat(1.5707963267948966f);
+  k.half_pi_slope = splat(__fmul_rn(1.5707963267948966f, a.slope));
+  k.zero = splat(0.f);
+  k.one = splat(1.f);
+  return k;
 }
 
-__device__ __forceinline__ f2 lif_spike(f2 v, f2 thr, f2 slope) {
-  const f2 cen = mul2(slope, sub2(v, thr));
-  return f2{cen.x >= 0.f ? 1.f : 0.f, cen.y >= 0.f ? 1.f : 0.f};
+// Spike words of a lane's pair: a 16-bit type's one in each half, or two
+// float ones.
+template <typename T>
+struct LifOnes {
+  static constexpr uint32_t lo = 0x3f80u, hi = 0x3f800000u;  // bf16
+};
+template <>
+struct LifOnes<__half> {
+  static constexpr uint32_t lo = 0x3c00u, hi = 0x3c000000u;
+};
+template <>
+struct LifOnes<float> {
+  static constexpr uint32_t lo = 0x3f800000u, hi = 0x3f800000u;
+};
+
+// The spike test on vn (%2, %3) leaves predicates p0, p1. Exact form:
+// centered = slope * (vn - threshold) >= 0. Plain form, vn >= threshold: the
+// same predicate whenever slope >= 1 is finite and threshold is finite (then
+// vn - threshold rounds to zero only when vn == threshold, to the sign of the
+// exact difference otherwise, and slope * d neither flushes a nonzero d to
+// zero nor flips its sign, with NaNs comparing false in both).
+#define LIF_TEST_EXACT                                 \
+  "mov.b64 rk, {%8, %8};\n\t"                          \
+  "sub.rn.f32x2 ra, rv, rk;\n\t"                       \
+  "mov.b64 rk, {%9, %9};\n\t"                          \
+  "mul.rn.f32x2 ra, rk, ra;\n\t"                       \
+  "mov.b64 {c0, c1}, ra;\n\t"                          \
+  "setp.ge.f32 p0, c0, 0f00000000;\n\t"                \
+  "setp.ge.f32 p1, c1, 0f00000000;\n\t"
+#define LIF_TEST_PLAIN      \
+  "setp.ge.f32 p0, %2, %8;\n\t" \
+  "setp.ge.f32 p1, %3, %8;\n\t"
+// vn = m + x; spike test; next m = p ? vn * 0 + reset * decay : vn * decay + reset0 * decay
+// (the reference's branches times decay, each one fma: vn * 0 is exact, and
+// reset0 * decay is zero unless reset is not finite).
+#define LIF_STEP_BODY(TEST)                                                         \
+  "{\n\t.reg .pred p0, p1;\n\t.reg .b64 rm, rx, rv, ra, rb, rk;\n\t"                  \
+  ".reg .f32 a0, a1, b0, b1, c0, c1;\n\t"                                           \
+  "mov.b64 rm, {%0, %1};\n\tmov.b64 rx, {%6, %7};\n\t"                              \
+  "add.rn.f32x2 rv, rm, rx;\n\tmov.b64 {%2, %3}, rv;\n\t" TEST                        \
+  "mov.b64 rk, {%10, %11};\n\tmov.b64 ra, 0;\n\tfma.rn.f32x2 ra, rv, ra, rk;\n\t"  \
+  "mov.b64 rk, {%12, %13};\n\tmov.b64 rb, {%14, %15};\n\tfma.rn.f32x2 rb, rv, rk, rb;\n\t" \
+  "mov.b64 {a0, a1}, ra;\n\tmov.b64 {b0, b1}, rb;\n\t"                              \
+  "selp.f32 %0, a0, b0, p0;\n\tselp.f32 %1, a1, b1, p1;\n\t"
+#define LIF_SPIKES_16 "selp.b32 %4, %16, 0, p0;\n\t@p1 or.b32 %4, %4, %17;\n\tmov.b32 %5, 0;\n\t}"
+#define LIF_SPIKES_32 "selp.b32 %4, %16, 0, p0;\n\tselp.b32 %5, %17, 0, p1;\n\t}"
+#define LIF_STEP_OPERANDS(m, vn, w0, w1, x, k, T)                                             \
+  : "+f"(m.x), "+f"(m.y), "=f"(vn.x), "=f"(vn.y), "=r"(w0), "=r"(w1)                             \
+  : "f"(x.x), "f"(x.y), "f"(k.thr.x), "f"(k.slope.x), "f"(k.rd.x), "f"(k.rd.y), "f"(k.decay.x), \
+    "f"(k.decay.y), "f"(k.rz.x), "f"(k.rz.y), "n"(LifOnes<T>::lo), "n"(LifOnes<T>::hi)
+
+// One step for a lane's pair of channels: m = membrane * decay from the step
+// before (updated), vn = membrane before reset, w0 / w1 = spike words
+// (LifOnes<T>).
+template <typename T, bool kPlain>
+__device__ __forceinline__ void lif_step(f2& m, f2 x, const LifK& k, f2& vn, uint32_t& w0, uint32_t& w1) {
+  if constexpr (sizeof(T) == 2 && kPlain) {
+    asm(LIF_STEP_BODY(LIF_TEST_PLAIN) LIF_SPIKES_16 LIF_STEP_OPERANDS(m, vn, w0, w1, x, k, T));
+  } else if constexpr (sizeof(T) == 2) {
+    asm(LIF_STEP_BODY(LIF_TEST_EXACT) LIF_SPIKES_16 LIF_STEP_OPERANDS(m, vn, w0, w1, x, k, T));
+  } else if constexpr (kPlain) {
+    asm(LIF_STEP_BODY(LIF_TEST_PLAIN) LIF_SPIKES_32 LIF_STEP_OPERANDS(m, vn, w0, w1, x, k, T));
+  } else {
+    asm(LIF_STEP_BODY(LIF_TEST_EXACT) LIF_SPIKES_32 LIF_STEP_OPERANDS(m, vn, w0, w1, x, k, T));
+  }
 }
 
-template <typename T, bool kTma>
-__global__ void __launch_bounds__(32) lif_fwd_kernel(const LifArgs a,
-                                                     const __grid_constant__ CUtensorMap tx,
-                                                     const __grid_constant__ CUtensorMap ts) {
+// One sub-tile of the forward: rows steps (kSub when kWhole) from m = the
+// membrane entering it times decay; x from a staged tile and spikes to a
+// staged tile (row stride kLanes, lane offset applied). Returns m for the
+// step after the sub-tile.
+template <bool kWhole, bool kPlain, typename T>
+__device__ __forceinline__ f2 lif_fwd_tile(f2 m, const T* xr, T* out, int rows, const LifK& k) {
   using P = Pair<T>;
-  constexpr int S = lif_fwd_stages<T>();
-  constexpr int R = kSub;
-  constexpr int E = R * kLanes;
+  typename P::raw xin[kSub];
+#pragma unroll
+  for (int i = 0; i < kSub; ++i)
+    if (kWhole || i < rows) xin[i] = P::ld(xr + i * kLanes);
+#pragma unroll
+  for (int i = 0; i < kSub; ++i) {
+    if (kWhole || i < rows) {
+      uint32_t w0, w1;
+      f2 vn;
+      lif_step<T, kPlain>(m, P::unpack(xin[i]), k, vn, w0, w1);
+      if constexpr (sizeof(T) == 2) {
+        *reinterpret_cast<uint32_t*>(out + i * kLanes) = w0;
+      } else {
+        *reinterpret_cast<uint2*>(out + i * kLanes) = make_uint2(w0, w1);
+      }
+    }
+  }
+  return m;
+}
+
+// The membranes before reset (vp) of one sub-tile, recomputed from its
+// checkpoint m (the membrane entering it times decay).
+template <bool kWhole, bool kPlain, typename T>
+__device__ __forceinline__ void lif_recompute(f2 m, const T* xr, int rows, const LifK& k, f2 (&vp)[kSub]) {
+  using P = Pair<T>;
+  typename P::raw xin[kSub];
+#pragma unroll
+  for (int i = 0; i < kSub; ++i)
+    if (kWhole || i < rows) xin[i] = P::ld(xr + i * kLanes);
+#pragma unroll
+  for (int i = 0; i < kSub; ++i) {
+    if (kWhole || i < rows) {
+      uint32_t w0, w1;
+      lif_step<T, kPlain>(m, P::unpack(xin[i]), k, vp[i], w0, w1);
+    } else {
+      vp[i] = k.zero;
+    }
+  }
+}
+
+// The adjoint sweep of one sub-tile, last step first. g = dL/d(membrane after
+// the sub-tile's last step); per step
+//   dL/dvn = dsdv * (gs + g * (reset - vn)) + g * (1 - s);  dL/dx = dL/dvn;  g <- decay * dL/dvn
+// with dsdv = slope * 0.5 / (1 + (pi/2 * centered)^2) (the arc-tangent
+// surrogate's derivative; slope * (0.5 * r) == (slope * 0.5) * r exactly) and
+// g * (1 - s) as g * 0 or g. With the plain spike test (see lif_step) the
+// spike is d = vn - threshold >= 0 and pi/2 * centered is formed as
+// (pi/2 * slope) * d. Input gradients go to a staged tile (row stride kLanes,
+// lane offset applied). Returns g entering the sub-tile.
+template <bool kWhole, bool kPlain, typename T>
+__device__ __forceinline__ f2 lif_grad_tile(f2 g, const f2 (&vp)[kSub], const T* gr, T* out, int rows,
+                                            const LifK& k) {
+  using P = Pair<T>;
+  typename P::raw gin[kSub];
+#pragma unroll
+  for (int i = 0; i < kSub; ++i)
+    if (kWhole || i < rows) gin[i] = P::ld(gr + i * kLanes);
+#pragma unroll
+  for (int i = kSub - 1; i >= 0; --i) {
+    if (kWhole || i < rows) {
+      const f2 d = sub2(vp[i], k.thr);
+      const f2 cen = kPlain ? d : mul2(k.slope, d);  // carries the spike test's sign
+      const f2 h = kPlain ? mul2(k.half_pi_slope, d) : mul2(k.half_pi, cen);
+      const f2 dsdv = mul2(k.half_slope, rcpx2(fma2(h, h, k.one)));
+      const f2 g0 = mul2(g, k.zero);
+      const f2 gk = f2{cen.x >= 0.f ? g0.x : g.x, cen.y >= 0.f ? g0.y : g.y};
+      const f2 gv = fma2(dsdv, fma2(g, sub2(k.reset, vp[i]), P::unpack(gin[i])), gk);
+      P::st(out + i * kLanes, P::pack(gv));
+      g = mul2(k.decay, gv);
+    }
+  }
+  return g;
+}
+
+template <typename T, bool kTma, bool kPlain>
+__global__ void __launch_bounds__(32 * kLifWarps, 1) lif_fwd_kernel(const LifArgs a,
+                                                                 const __grid_constant__ CUtensorMap tx,
+                                                                 const __grid_constant__ CUtensorMap ts) {
+  constexpr int S = kTma ? kLifFwdStages : 1;
+  constexpr int RT = kTma ? lif_rows<T>() : kSub;  // rows per staged tile
+  constexpr int E = RT * kLanes;
   extern __shared__ __align__(128) unsigned char smem[];
-  T* xbuf = reinterpret_cast<T*>(smem);
-  T* sbuf = xbuf + S * E;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sbuf + 2 * E);
-  const int lane = threadIdx.x;
-  const int cb = blockIdx.x % a.ncblk, b = blockIdx.x / a.ncblk;
+  const int unit = blockIdx.x * kLifWarps + threadIdx.x / 32;  // (channel block, batch row)
+  if (unit >= a.ncblk * a.B) return;
+  T* xbuf = reinterpret_cast<T*>(smem + (threadIdx.x / 32) * lif_fwd_smem_bytes());
+  T* obuf = xbuf + S * E;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(obuf + kLifOut * E);
+  const int lane = threadIdx.x % 32;
+  const int cb = unit % a.ncblk, b = unit / a.ncblk;
   const int c = cb * kLanes + 2 * lane;
   const bool v0 = c < a.C, v1 = c + 1 < a.C;
-  const f2 decay = splat(a.decay), thr = splat(a.threshold), slope = splat(a.slope);
-  const int nt = a.ntiles;
+  const LifK k = lif_constants(a);
+  const int ntt = (a.T + RT - 1) / RT;
+  // checkpoints: the membrane entering each sub-tile times decay, the first
+  // operand of its first step
+  float* state = a.state == nullptr ? nullptr : a.state + (size_t)b * a.ntiles * a.C + c;
 
   auto issue = [&](int j) {
     mbar_arrive_expect_tx_if(lane == 0, &bars[j % S], E * sizeof(T));
-    tma_load_3d_if(lane == 0, xbuf + (j % S) * E, &tx, &bars[j % S], cb * kLanes, j * R, b);
+    tma_load_3d_if(lane == 0, xbuf + (j % S) * E, &tx, &bars[j % S], cb * kLanes, j * RT, b);
+  };
+  auto checkpoint = [&](int u0, f2 v) {  // for the sub-tile starting at step u0
+    if (state == nullptr) return;
+    float* st = state + (size_t)(u0 / kSub) * a.C;
+    if (v1) *reinterpret_cast<f2*>(st) = v;
+    else if (v0) *st = v.x;
   };
   if (kTma) {
     if (lane == 0) {
@@ -89,89 +292,134 @@ __global__ void __launch_bounds__(32) lif_fwd_kernel(const LifArgs a,
       prefetch_tensormap(&ts);
     }
     __syncwarp();
-    for (int j = 0; j < min(S, nt); ++j) issue(j);
+    for (int j = 0; j < min(S, ntt); ++j) issue(j);
   }
-  f2 v = splat(0.f);
+  f2 m = k.zero;  // the initial membrane (zero) times decay
 #pragma unroll 1
-  for (int j = 0; j < nt; ++j) {
-    const int t0 = j * R;
-    const int rows = min(R, a.T - t0);
-    T* xs = xbuf + (j % S) * E;
+  for (int j = 0; j < ntt; ++j) {
+    const int t0 = j * RT;
+    const T* xs = xbuf + (j % S) * E + 2 * lane;
+    T* os = obuf + (j % kLifOut) * E;
     if (kTma) {
       if (!__all_sync(kFull, mbar_wait_bounded(&bars[j % S], (j / S) & 1))) {
         if (lane == 0) {
           report_timeout(a.err);
-          for (int q = j + 1; q < min(j + S, nt); ++q) mbar_wait_bounded(&bars[q % S], (q / S) & 1);
+          for (int q = j + 1; q < min(j + S, ntt); ++q) mbar_wait_bounded(&bars[q % S], (q / S) & 1);
         }
         bulk_wait_all();
         return;
       }
+      bulk_wait_read<kLifOut - 1>();  // the store of tile j - kLifOut has read os
+      __syncwarp();
     } else {
-      fill_tile(xs, static_cast<const T*>(a.x), b, t0, rows, a.T, a.C, c, v0, v1, lane);
+      fill_tile(xbuf, static_cast<const T*>(a.x), b, t0, min(RT, a.T - t0), a.T, a.C, c, v0, v1, lane);
       __syncwarp();
     }
-    if (a.state != nullptr && v1) {  // membrane entering the tile
-      *reinterpret_cast<f2*>(a.state + ((size_t)b * nt + j) * a.C + c) = v;
-    } else if (a.state != nullptr && v0) {
-      a.state[((size_t)b * nt + j) * a.C + c] = v.x;
-    }
-    T* ss = sbuf + (j & 1) * E;
-    if (kTma) {
-      bulk_wait_read<1>();  // the store of tile j-2 has read ss
-      __syncwarp();
-    }
-    const T* xr = xs + 2 * lane;
-#pragma unroll
-    for (int i = 0; i < R; ++i) {
-      if (i < rows) {
-        v = add2(mul2(v, decay), P::unpack(P::ld(xr + i * kLanes)));
-        const f2 sp = lif_spike(v, thr, slope);
-        v = f2{sp.x != 0.f ? a.reset : v.x, sp.y != 0.f ? a.reset : v.y};
-        P::st(ss + 2 * lane + i * kLanes, P::pack(sp));
+    if (t0 + RT <= a.T) {  // whole sub-tiles only
+#pragma unroll 1
+      for (int q = 0; q < RT / kSub; ++q) {
+        checkpoint(t0 + q * kSub, m);
+        m = lif_fwd_tile<true, kPlain>(m, xs + q * kSub * kLanes, os + q * kSub * kLanes + 2 * lane, kSub, k);
+      }
+    } else {
+#pragma unroll 1
+      for (int q = 0; q < RT / kSub; ++q) {
+        const int u0 = t0 + q * kSub;
+        if (u0 >= a.T) break;
+        const int rows = min(kSub, a.T - u0);
+        checkpoint(u0, m);
+        m = rows == kSub
+                ? lif_fwd_tile<true, kPlain>(m, xs + q * kSub * kLanes, os + q * kSub * kLanes + 2 * lane, kSub, k)
+                : lif_fwd_tile<false, kPlain>(m, xs + q * kSub * kLanes, os + q * kSub * kLanes + 2 * lane, rows, k);
       }
     }
     if (kTma) {
       fence_proxy_async_smem();
-      __syncwarp();
-      tma_store_3d_if(lane == 0, &ts, ss, cb * kLanes, t0, b);
+      __syncwarp();  // every lane has read stage j % S and written os
+      tma_store_3d_if(lane == 0, &ts, os, cb * kLanes, t0, b);
       bulk_commit();
-      if (j + S < nt) issue(j + S);
+      if (j + S < ntt) issue(j + S);
     } else {
       __syncwarp();
-      drain_tile(ss, static_cast<T*>(a.s), b, t0, rows, a.T, a.C, c, v0, v1, lane);
+      drain_tile(os, static_cast<T*>(a.s), b, t0, min(RT, a.T - t0), a.T, a.C, c, v0, v1, lane);
+      __syncwarp();
     }
   }
   if (kTma) bulk_wait_all();
 }
 
-template <typename T, bool kTma>
-__global__ void __launch_bounds__(32) lif_bwd_kernel(const LifArgs a,
-                                                     const __grid_constant__ CUtensorMap tx,
-                                                     const __grid_constant__ CUtensorMap tgs,
-                                                     const __grid_constant__ CUtensorMap tgx) {
-  using P = Pair<T>;
-  constexpr int S = lif_bwd_stages<T>();
-  constexpr int R = kSub;
-  constexpr int E = R * kLanes;
+// Backward, last sub-tile first, software-pipelined by one sub-tile: while the
+// adjoint sweep of sub-tile q runs, the membranes of sub-tile q - 1 are
+// recomputed from its checkpoint, two independent dependency chains in one
+// straight-line block. A stage holds one staged tile's x, grad and the
+// membrane checkpoints of its sub-tiles; staged tiles are visited last first
+// (the vt-th visited is tile ntt - 1 - vt, in stage vt % S, its input
+// gradients staged in output tile vt % kLifOut).
+template <typename T, bool kTma, bool kPlain>
+__global__ void __launch_bounds__(32 * kLifWarps, 1) lif_bwd_kernel(const LifArgs a,
+                                                                 const __grid_constant__ CUtensorMap tx,
+                                                                 const __grid_constant__ CUtensorMap tgs,
+                                                                 const __grid_constant__ CUtensorMap tst,
+                                                                 const __grid_constant__ CUtensorMap tgx) {
+  constexpr int S = kTma ? kLifBwdStages : 2;
+  constexpr int RT = kTma ? lif_rows<T>() : kSub;  // rows per staged tile
+  constexpr int QT = RT / kSub;                    // sub-tiles per staged tile
+  constexpr int E = RT * kLanes;
+  constexpr int SE = 2 * E * sizeof(T) + QT * kLanes * sizeof(float);  // stage bytes
   extern __shared__ __align__(128) unsigned char smem[];
-  T* xbuf = reinterpret_cast<T*>(smem);
-  T* gbuf = xbuf + S * E;
-  T* obuf = gbuf + S * E;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(obuf + 2 * E);
-  const int lane = threadIdx.x;
-  const int cb = blockIdx.x % a.ncblk, b = blockIdx.x / a.ncblk;
+  const int unit = blockIdx.x * kLifWarps + threadIdx.x / 32;  // (channel block, batch row)
+  if (unit >= a.ncblk * a.B) return;
+  unsigned char* base = smem + (threadIdx.x / 32) * lif_bwd_smem_bytes<T>();
+  T* obuf = reinterpret_cast<T*>(base + S * SE);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(obuf + kLifOut * E);
+  const int lane = threadIdx.x % 32;
+  const int cb = unit % a.ncblk, b = unit / a.ncblk;
   const int c = cb * kLanes + 2 * lane;
   const bool v0 = c < a.C, v1 = c + 1 < a.C;
-  const f2 decay = splat(a.decay), thr = splat(a.threshold), slope = splat(a.slope);
-  const f2 reset = splat(a.reset), half_pi = splat(1.5707963267948966f), half = splat(0.5f);
-  const int nt = a.ntiles;
+  const LifK k = lif_constants(a);
+  const int nq = a.ntiles;
+  const int ntt = (a.T + RT - 1) / RT;
 
-  // the jj-th visited tile is j = nt - 1 - jj
-  auto issue = [&](int jj) {
-    const int s = jj % S, t0 = (nt - 1 - jj) * R;
-    mbar_arrive_expect_tx_if(lane == 0, &bars[s], 2 * E * sizeof(T));
-    tma_load_3d_if(lane == 0, xbuf + s * E, &tx, &bars[s], cb * kLanes, t0, b);
-    tma_load_3d_if(lane == 0, gbuf + s * E, &tgs, &bars[s], cb * kLanes, t0, b);
+  auto xs_of = [&](int vt) { return reinterpret_cast<T*>(base + (vt % S) * SE); };
+  auto gs_of = [&](int vt) { return xs_of(vt) + E; };
+  auto st_of = [&](int vt) { return reinterpret_cast<float*>(xs_of(vt) + 2 * E); };
+  auto issue = [&](int vt) {
+    const int jt = ntt - 1 - vt;
+    uint64_t* bar = &bars[vt % S];
+    mbar_arrive_expect_tx_if(lane == 0, bar, SE);
+    tma_load_3d_if(lane == 0, xs_of(vt), &tx, bar, cb * kLanes, jt * RT, b);
+    tma_load_3d_if(lane == 0, gs_of(vt), &tgs, bar, cb * kLanes, jt * RT, b);
+    tma_load_3d_if(lane == 0, st_of(vt), &tst, bar, cb * kLanes, jt * QT, b);
+  };
+  // waits for the vt-th visited staged tile (TMA) or stages it (plain loads)
+  auto acquire = [&](int vt) -> bool {
+    if (kTma) {
+      if (!__all_sync(kFull, mbar_wait_bounded(&bars[vt % S], (vt / S) & 1))) {
+        if (lane == 0) {
+          report_timeout(a.err);
+          for (int q = vt + 1; q < min(vt + S, ntt); ++q) mbar_wait_bounded(&bars[q % S], (q / S) & 1);
+        }
+        bulk_wait_all();
+        return false;
+      }
+    } else {
+      const int j = ntt - 1 - vt, t0 = j * RT, rows = min(RT, a.T - t0);
+      fill_tile(xs_of(vt), static_cast<const T*>(a.x), b, t0, rows, a.T, a.C, c, v0, v1, lane);
+      fill_tile(gs_of(vt), static_cast<const T*>(a.gs), b, t0, rows, a.T, a.C, c, v0, v1, lane);
+      const float* st = a.state + ((size_t)b * nq + j) * a.C + c;
+      st_of(vt)[2 * lane] = v0 ? st[0] : 0.f;
+      st_of(vt)[2 * lane + 1] = v1 ? st[1] : 0.f;
+      __syncwarp();
+    }
+    return true;
+  };
+  // sub-tile q lives in visited tile vt(q), at sub-tile index q % QT
+  auto vt_of = [&](int q) { return ntt - 1 - q / QT; };
+  auto x_sub = [&](int q) -> const T* { return xs_of(vt_of(q)) + (q % QT) * kSub * kLanes + 2 * lane; };
+  auto g_sub = [&](int q) -> const T* { return gs_of(vt_of(q)) + (q % QT) * kSub * kLanes + 2 * lane; };
+  auto o_sub = [&](int q) -> T* { return obuf + (vt_of(q) % kLifOut) * E + (q % QT) * kSub * kLanes + 2 * lane; };
+  auto v_sub = [&](int q) -> f2 {
+    return *reinterpret_cast<const f2*>(st_of(vt_of(q)) + (q % QT) * kLanes + 2 * lane);
   };
   if (kTma) {
     if (lane == 0) {
@@ -179,88 +427,53 @@ __global__ void __launch_bounds__(32) lif_bwd_kernel(const LifArgs a,
       fence_barrier_init();
       prefetch_tensormap(&tx);
       prefetch_tensormap(&tgs);
+      prefetch_tensormap(&tst);
       prefetch_tensormap(&tgx);
     }
     __syncwarp();
-    for (int jj = 0; jj < min(S, nt); ++jj) issue(jj);
+    for (int vt = 0; vt < min(S, ntt); ++vt) issue(vt);
   }
-  auto load_state = [&](int j) -> f2 {
-    f2 r = splat(0.f);
-    const float* p = a.state + ((size_t)b * nt + j) * a.C + c;
-    if (v1) r = *reinterpret_cast<const f2*>(p);
-    else if (v0) r.x = *p;
-    return r;
-  };
-  f2 g = splat(0.f);  // dL/d(membrane after the current step), from later steps
-  f2 vin_next = nt > 0 ? load_state(nt - 1) : splat(0.f);
-#pragma unroll 1
-  for (int jj = 0; jj < nt; ++jj) {
-    const int j = nt - 1 - jj;
-    const int s = jj % S;
-    const int t0 = j * R;
-    const int rows = min(R, a.T - t0);
-    const f2 vin = vin_next;
-    if (j > 0) vin_next = load_state(j - 1);
-    T* xs = xbuf + s * E;
-    T* gss = gbuf + s * E;
-    if (kTma) {
-      if (!__all_sync(kFull, mbar_wait_bounded(&bars[s], (jj / S) & 1))) {
-        if (lane == 0) {
-          report_timeout(a.err);
-          for (int q = jj + 1; q < min(jj + S, nt); ++q) mbar_wait_bounded(&bars[q % S], (q / S) & 1);
-        }
-        bulk_wait_all();
-        return;
-      }
+  if (nq == 0) return;
+  const int last_rows = a.T - (nq - 1) * kSub;
+  f2 va[kSub], vb[kSub];
+  if (!acquire(0)) return;
+  if (last_rows == kSub) lif_recompute<true, kPlain>(v_sub(nq - 1), x_sub(nq - 1), kSub, k, va);
+  else lif_recompute<false, kPlain>(v_sub(nq - 1), x_sub(nq - 1), last_rows, k, va);
+  f2 g = k.zero;  // dL/d(membrane after the current step), from later steps
+  // sub-tile q: its membranes are in cur; those of q - 1 are recomputed into nxt
+  auto body = [&](int q, const f2(&cur)[kSub], f2(&nxt)[kSub]) -> bool {
+    const int u0 = q * kSub;
+    const int rows = min(kSub, a.T - u0);
+    if (q > 0 && q % QT == 0 && !acquire(vt_of(q - 1))) return false;
+    if (kTma && (q == nq - 1 || q % QT == QT - 1)) {
+      bulk_wait_read<kLifOut - 1>();  // the store of visited tile vt - kLifOut has read this output tile
+      __syncwarp();
+    }
+    if (q > 0 && rows == kSub) {
+      lif_recompute<true, kPlain>(v_sub(q - 1), x_sub(q - 1), kSub, k, nxt);
+      g = lif_grad_tile<true, kPlain>(g, cur, g_sub(q), o_sub(q), kSub, k);
     } else {
-      fill_tile(xs, static_cast<const T*>(a.x), b, t0, rows, a.T, a.C, c, v0, v1, lane);
-      fill_tile(gss, static_cast<const T*>(a.gs), b, t0, rows, a.T, a.C, c, v0, v1, lane);
+      g = lif_grad_tile<false, kPlain>(g, cur, g_sub(q), o_sub(q), rows, k);
+      if (q > 0) lif_recompute<true, kPlain>(v_sub(q - 1), x_sub(q - 1), kSub, k, nxt);
+    }
+    if (!kTma) {
       __syncwarp();
-    }
-    // recompute the tile's membranes (before reset) from the state entering it
-    f2 vp[R];
-    {
-      f2 v = vin;
-#pragma unroll
-      for (int i = 0; i < R; ++i) {
-        if (i < rows) {
-          v = add2(mul2(v, decay), P::unpack(P::ld(xs + 2 * lane + i * kLanes)));
-          vp[i] = v;
-          const f2 sp = lif_spike(v, thr, slope);
-          v = f2{sp.x != 0.f ? a.reset : v.x, sp.y != 0.f ? a.reset : v.y};
-        } else {
-          vp[i] = splat(0.f);
-        }
-      }
-    }
-    T* os = obuf + (jj & 1) * E;
-    if (kTma) {
-      bulk_wait_read<1>();  // the store of tile jj-2 has read os
+      drain_tile(obuf + (vt_of(q) % kLifOut) * E, static_cast<T*>(a.gx), b, u0, rows, a.T, a.C, c, v0, v1, lane);
       __syncwarp();
-    }
-#pragma unroll
-    for (int i = R - 1; i >= 0; --i) {
-      if (i < rows) {
-        const f2 cen = mul2(slope, sub2(vp[i], thr));
-        const f2 sp = f2{cen.x >= 0.f ? 1.f : 0.f, cen.y >= 0.f ? 1.f : 0.f};
-        const f2 h = mul2(half_pi, cen);
-        const f2 dsdv = mul2(slope, mul2(half, rcpx2(fma2(h, h, splat(1.f)))));
-        const f2 gsi = P::unpack(P::ld(gss + 2 * lane + i * kLanes));
-        const f2 gv = fma2(dsdv, fma2(g, sub2(reset, vp[i]), gsi), mul2(g, sub2(splat(1.f), sp)));
-        P::st(os + 2 * lane + i * kLanes, P::pack(gv));
-        g = mul2(decay, gv);
-      }
-    }
-    if (kTma) {
+    } else if (q % QT == 0) {  // the visited tile is done: store its gradients, refill its stage
+      const int vt = vt_of(q);
       fence_proxy_async_smem();
       __syncwarp();
-      tma_store_3d_if(lane == 0, &tgx, os, cb * kLanes, t0, b);
+      tma_store_3d_if(lane == 0, &tgx, obuf + (vt % kLifOut) * E, cb * kLanes, (ntt - 1 - vt) * RT, b);
       bulk_commit();
-      if (jj + S < nt) issue(jj + S);
-    } else {
-      __syncwarp();
-      drain_tile(os, static_cast<T*>(a.gx), b, t0, rows, a.T, a.C, c, v0, v1, lane);
+      if (vt + S < ntt) issue(vt + S);
     }
+    return true;
+  };
+#pragma unroll 1
+  for (int q = nq - 1; q >= 0; q -= 2) {
+    if (!body(q, va, vb)) return;
+    if (q == 0 || !body(q - 1, vb, va)) break;
   }
   if (kTma) bulk_wait_all();
 }

@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -894,6 +895,19 @@ int lif_prepare(int dtype, int64_t B, int64_t T, int64_t C, float tau, float thr
   return WKV_OK;
 }
 
+// The spike test can compare the membrane with the threshold directly when
+// that gives the reference's slope * (v - threshold) >= 0 for every membrane:
+// a finite slope >= 1 and a finite threshold (see lif.cuh).
+bool lif_plain_test(const LifArgs& a) {
+  return a.slope >= 1.f && std::isfinite(a.slope) && std::isfinite(a.threshold);
+}
+
+template <typename IO, bool kTma, bool kPlain>
+void lif_fwd_go(const LifArgs& a, const CUtensorMap& mx, const CUtensorMap& ms, unsigned grid, size_t sm,
+                cudaStream_t st) {
+  lif_fwd_kernel<IO, kTma, kPlain><<<grid, 32 * kLifWarps, sm, st>>>(a, mx, ms);
+}
+
 template <typename IO>
 int lif_launch_forward(LifArgs& a, bool tma, cudaStream_t st) {
   const int dt = sizeof(IO) == 4 ? WKV_DTYPE_F32
@@ -903,19 +917,31 @@ int lif_launch_forward(LifArgs& a, bool tma, cudaStream_t st) {
   std::memset(&mx, 0, sizeof(mx));
   std::memset(&ms, 0, sizeof(ms));
   int rc;
-  if (tma && ((rc = make_map(&mx, dt, a.x, a.B, a.T, a.C, kSub)) ||
-              (rc = make_map(&ms, dt, a.s, a.B, a.T, a.C, kSub))))
+  if (tma && ((rc = make_map(&mx, dt, a.x, a.B, a.T, a.C, lif_rows<IO>())) ||
+              (rc = make_map(&ms, dt, a.s, a.B, a.T, a.C, lif_rows<IO>()))))
     return rc;
-  const size_t sm = lif_fwd_smem_bytes<IO>();
-  const cudaError_t e = tma ? allow_smem(lif_fwd_kernel<IO, true>, sm) : allow_smem(lif_fwd_kernel<IO, false>, sm);
+  const bool plain = lif_plain_test(a);
+  const size_t sm = kLifWarps * lif_fwd_smem_bytes();
+  cudaError_t e = tma ? (plain ? allow_smem(lif_fwd_kernel<IO, true, true>, sm)
+                               : allow_smem(lif_fwd_kernel<IO, true, false>, sm))
+                      : (plain ? allow_smem(lif_fwd_kernel<IO, false, true>, sm)
+                               : allow_smem(lif_fwd_kernel<IO, false, false>, sm));
   if (e != cudaSuccess) return cuda_fail(e, "setting the LIF kernel's shared memory size");
-  const unsigned grid = (unsigned)a.ncblk * (unsigned)a.B;
+  const unsigned grid = (unsigned)(((int64_t)a.ncblk * a.B + kLifWarps - 1) / kLifWarps);
   launch(K_LIF_FWD, st, [&] {
-    if (tma) lif_fwd_kernel<IO, true><<<grid, 32, sm, st>>>(a, mx, ms);
-    else lif_fwd_kernel<IO, false><<<grid, 32, sm, st>>>(a, mx, ms);
+    if (tma && plain) lif_fwd_go<IO, true, true>(a, mx, ms, grid, sm, st);
+    else if (tma) lif_fwd_go<IO, true, false>(a, mx, ms, grid, sm, st);
+    else if (plain) lif_fwd_go<IO, false, true>(a, mx, ms, grid, sm, st);
+    else lif_fwd_go<IO, false, false>(a, mx, ms, grid, sm, st);
   });
   const cudaError_t le = cudaGetLastError();
   return le == cudaSuccess ? WKV_OK : cuda_fail(le, "LIF forward launch");
+}
+
+template <typename IO, bool kTma, bool kPlain>
+void lif_bwd_go(const LifArgs& a, const CUtensorMap& mx, const CUtensorMap& mg, const CUtensorMap& mst,
+                const CUtensorMap& mo, unsigned grid, size_t sm, cudaStream_t st) {
+  lif_bwd_kernel<IO, kTma, kPlain><<<grid, 32 * kLifWarps, sm, st>>>(a, mx, mg, mst, mo);
 }
 
 template <typename IO>
@@ -923,22 +949,32 @@ int lif_launch_backward(LifArgs& a, bool tma, cudaStream_t st) {
   const int dt = sizeof(IO) == 4 ? WKV_DTYPE_F32
                  : std::is_same<IO, __nv_bfloat16>::value ? WKV_DTYPE_BF16
                                                          : WKV_DTYPE_F16;
-  CUtensorMap mx, mg, mo;
+  // x, grad and grad_x in lif_rows<IO>()-row boxes; the membrane checkpoints
+  // of a staged tile's sub-tiles in one [sub-tiles][kLanes] float box
+  CUtensorMap mx, mg, mst, mo;
   std::memset(&mx, 0, sizeof(mx));
   std::memset(&mg, 0, sizeof(mg));
+  std::memset(&mst, 0, sizeof(mst));
   std::memset(&mo, 0, sizeof(mo));
   int rc;
-  if (tma && ((rc = make_map(&mx, dt, a.x, a.B, a.T, a.C, kSub)) ||
-              (rc = make_map(&mg, dt, a.gs, a.B, a.T, a.C, kSub)) ||
-              (rc = make_map(&mo, dt, a.gx, a.B, a.T, a.C, kSub))))
+  if (tma && ((rc = make_map(&mx, dt, a.x, a.B, a.T, a.C, lif_rows<IO>())) ||
+              (rc = make_map(&mg, dt, a.gs, a.B, a.T, a.C, lif_rows<IO>())) ||
+              (rc = make_map(&mo, dt, a.gx, a.B, a.T, a.C, lif_rows<IO>())) ||
+              (rc = make_map(&mst, WKV_DTYPE_F32, a.state, a.B, a.ntiles, a.C, lif_rows<IO>() / kSub))))
     return rc;
-  const size_t sm = lif_bwd_smem_bytes<IO>();
-  const cudaError_t e = tma ? allow_smem(lif_bwd_kernel<IO, true>, sm) : allow_smem(lif_bwd_kernel<IO, false>, sm);
+  const bool plain = lif_plain_test(a);
+  const size_t sm = kLifWarps * lif_bwd_smem_bytes<IO>();
+  cudaError_t e = tma ? (plain ? allow_smem(lif_bwd_kernel<IO, true, true>, sm)
+                               : allow_smem(lif_bwd_kernel<IO, true, false>, sm))
+                      : (plain ? allow_smem(lif_bwd_kernel<IO, false, true>, sm)
+                               : allow_smem(lif_bwd_kernel<IO, false, false>, sm));
   if (e != cudaSuccess) return cuda_fail(e, "setting the LIF kernel's shared memory size");
-  const unsigned grid = (unsigned)a.ncblk * (unsigned)a.B;
+  const unsigned grid = (unsigned)(((int64_t)a.ncblk * a.B + kLifWarps - 1) / kLifWarps);
   launch(K_LIF_BWD, st, [&] {
-    if (tma) lif_bwd_kernel<IO, true><<<grid, 32, sm, st>>>(a, mx, mg, mo);
-    else lif_bwd_kernel<IO, false><<<grid, 32, sm, st>>>(a, mx, mg, mo);
+    if (tma && plain) lif_bwd_go<IO, true, true>(a, mx, mg, mst, mo, grid, sm, st);
+    else if (tma) lif_bwd_go<IO, true, false>(a, mx, mg, mst, mo, grid, sm, st);
+    else if (plain) lif_bwd_go<IO, false, true>(a, mx, mg, mst, mo, grid, sm, st);
+    else lif_bwd_go<IO, false, false>(a, mx, mg, mst, mo, grid, sm, st);
   });
   const cudaError_t le = cudaGetLastError();
   return le == cudaSuccess ? WKV_OK : cuda_fail(le, "LIF backward launch");

@@ -237,6 +237,10 @@ struct Pair<float> {
   static __device__ __forceinline__ void st(float* p, raw r) { *reinterpret_cast<float2*>(p) = r; }
   static __device__ __forceinline__ f2 unpack(raw r) { return f2{r.x, r.y}; }
   static __device__ __forceinline__ raw pack(f2 v) { return make_float2(v.x, v.y); }
+  // (p0 ? 1 : 0, p1 ? 1 : 0) by integer selects of the constant's bits
+  static __device__ __forceinline__ raw ones(bool p0, bool p1) {
+    return make_float2(__int_as_float(p0 ? 0x3f800000 : 0), __int_as_float(p1 ? 0x3f800000 : 0));
+  }
   static __device__ __forceinline__ float scalar(float x) { return x; }
   static __device__ __forceinline__ float from_float(float x) { return x; }
 };
@@ -259,6 +263,9 @@ struct Pair<__nv_bfloat16> {
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(v.y), "f"(v.x));
     return d;
   }
+  static __device__ __forceinline__ raw ones(bool p0, bool p1) {
+    return (p0 ? 0x3f80u : 0u) | (p1 ? 0x3f800000u : 0u);
+  }
   static __device__ __forceinline__ float scalar(__nv_bfloat16 x) { return __bfloat162float(x); }
   static __device__ __forceinline__ __nv_bfloat16 from_float(float x) { return __float2bfloat16_rn(x); }
 };
@@ -280,6 +287,9 @@ struct Pair<__half> {
     uint32_t d;
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(v.y), "f"(v.x));
     return d;
+  }
+  static __device__ __forceinline__ raw ones(bool p0, bool p1) {
+    return (p0 ? 0x3c00u : 0u) | (p1 ? 0x3c000000u : 0u);
   }
   static __device__ __forceinline__ float scalar(__half x) { return __half2float(x); }
   static __device__ __forceinline__ __half from_float(float x) { return __float2half_rn(x); }

@@ -72,7 +72,7 @@ def test_config_shape(cuda, dtype):
     assert scaled_err(gx, gx_ref) <= (TOL_FP32 if dtype == torch.float32 else TOL_16BIT)
 
 
-@pytest.mark.parametrize("shape", [(2, 17, 70), (3, 1, 64), (1, 33, 8), (2, 40, 130)])
+@pytest.mark.parametrize("shape", [(2, 17, 70), (3, 1, 64), (1, 33, 8), (2, 40, 130), (1, 16, 64), (2, 64, 66)])
 @pytest.mark.parametrize("generic", [False, True])
 def test_shapes_tails_and_generic_path(cuda, shape, generic):
     _capi.set_debug_overrides(force_generic=int(generic))
@@ -86,6 +86,47 @@ def test_shapes_tails_and_generic_path(cuda, shape, generic):
         assert scaled_err(gx, gx_ref) <= TOL_FP32
     finally:
         _capi.set_debug_overrides()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(2, 100, 72), (1, 65, 136), (3, 17, 8), (1, 200, 64), (2, 130, 200)])
+def test_tma_path_ragged_tiles_and_channels(cuda, shape, dtype):
+    """Aligned rows (TMA path) with a partial last staged tile, a partial last
+    sub-tile and a partial last channel block."""
+    rng = np.random.default_rng(sum(shape) + 1)
+    x = (rng.standard_normal(shape) * 2 + 0.2).astype(np.float32)
+    gs = rng.standard_normal(shape).astype(np.float32)
+    s, gx, xr = _run(x, gs, dtype, cuda)
+    gs_r = torch.as_tensor(gs).to(dtype).double().numpy()
+    s_ref, gx_ref = _oracle(xr, gs_r, tau=2.0, threshold=1.0, reset=0.0, surrogate_slope=2.0)
+    np.testing.assert_array_equal(s, s_ref)
+    assert scaled_err(gx, gx_ref) <= (TOL_FP32 if dtype == torch.float32 else TOL_16BIT)
+
+
+@pytest.mark.parametrize("generic", [False, True])
+def test_non_finite_inputs(cuda, generic):
+    """Infinite and NaN currents: a spike on +inf leaves a NaN membrane (the
+    reference's v * (1 - s) + reset * s gives inf * 0), which never spikes
+    again; -inf and NaN do not spike. Spikes equal the oracle's; gradients
+    match it with NaNs in the same places."""
+    rng = np.random.default_rng(11)
+    x = (rng.standard_normal((2, 40, 64)) * 1.5).astype(np.float32)
+    x[0, 3, 5] = np.inf
+    x[0, 20, 6] = -np.inf
+    x[1, 7, 7] = np.nan
+    x[1, 30, 8] = np.inf
+    gs = rng.standard_normal(x.shape).astype(np.float32)
+    _capi.set_debug_overrides(force_generic=int(generic))
+    try:
+        s, gx, _ = _run(x, gs, torch.float32, cuda)
+    finally:
+        _capi.set_debug_overrides(force_generic=0)
+    s_ref, gx_ref = _oracle(x, gs, tau=2.0, threshold=1.0, reset=0.0, surrogate_slope=2.0)
+    np.testing.assert_array_equal(s, s_ref)
+    assert s[0, 4:, 5].sum() == 0 and s[0, 3, 5] == 1
+    np.testing.assert_array_equal(np.isnan(gx), np.isnan(gx_ref))
+    ok = ~np.isnan(gx_ref)
+    assert scaled_err(gx[ok], gx_ref[ok]) <= TOL_FP32
 
 
 def test_module_contract_and_errors(cuda):
