@@ -50,7 +50,16 @@ __host__ __device__ constexpr int lif_rows() {
 }
 constexpr int kLifTileBytes = 8192;
 constexpr int kLifFwdStages = 4;  // x tiles in flight per warp (forward)
+// The backward's stages hold 8 KB of x and 8 KB of grad: two of them fit
+// beside the output tiles for four warps. (Smaller tiles in a deeper ring
+// measured slower: the per-tile costs of barrier waits and TMA issue weigh
+// more than the shorter look-ahead.)
+constexpr int kLifBwdTileBytes = 8192;
 constexpr int kLifBwdStages = 2;  // (x, grad, checkpoint) tiles in flight per warp (backward)
+template <typename T>
+__host__ __device__ constexpr int lif_bwd_rows() {
+  return kLifBwdTileBytes / (kLanes * static_cast<int>(sizeof(T)));
+}
 constexpr int kLifOut = 2;        // staged output tiles per warp
 // Independent warps per CTA: one warp lands on each of an SM's 4 schedulers.
 constexpr int kLifWarps = 4;
@@ -63,16 +72,22 @@ __host__ __device__ constexpr size_t lif_fwd_smem_bytes() {
 }
 template <typename T>
 __host__ __device__ constexpr size_t lif_bwd_stage_bytes() {
-  return (size_t)2 * kLifTileBytes + (size_t)(lif_rows<T>() / kSub) * kLanes * sizeof(float);
+  return (size_t)2 * kLifBwdTileBytes + (size_t)(lif_bwd_rows<T>() / kSub) * kLanes * sizeof(float);
 }
 template <typename T>
 __host__ __device__ constexpr size_t lif_bwd_smem_bytes() {
-  return lif_align128((size_t)kLifBwdStages * lif_bwd_stage_bytes<T>() + (size_t)kLifOut * kLifTileBytes +
+  return lif_align128((size_t)kLifBwdStages * lif_bwd_stage_bytes<T>() + (size_t)kLifOut * kLifBwdTileBytes +
                       8 * kLifBwdStages);
 }
 static_assert(lif_rows<float>() % kSub == 0 && lif_rows<__nv_bfloat16>() % kSub == 0, "sub-tiles");
+static_assert(lif_bwd_rows<float>() % kSub == 0 && lif_bwd_rows<__nv_bfloat16>() % kSub == 0, "sub-tiles");
 static_assert(lif_bwd_stage_bytes<float>() % 128 == 0 && lif_bwd_stage_bytes<__nv_bfloat16>() % 128 == 0,
               "TMA stage alignment");
+static_assert(3 * kSub * kLanes * sizeof(float) + 8 <= lif_fwd_smem_bytes(), "generic forward staging");
+static_assert(2 * (2 * kSub * kLanes * sizeof(float) + kLanes * sizeof(float)) + 2 * kSub * kLanes * sizeof(float) +
+                      16 <=
+                  lif_bwd_smem_bytes<float>(),
+              "generic backward staging");
 static_assert(kLifWarps * lif_bwd_smem_bytes<float>() <= 227 * 1024, "LIF backward shared memory");
 static_assert(kLifWarps * lif_bwd_smem_bytes<__nv_bfloat16>() <= 227 * 1024, "LIF backward shared memory");
 static_assert(kLifWarps * lif_fwd_smem_bytes() <= 227 * 1024, "LIF forward shared memory");
@@ -83,7 +98,7 @@ struct LifK {
   f2 reset0;  // reset * 0: what the non-spiking branch adds (zero unless reset is not finite)
   f2 rd;      // reset * decay
   f2 rz;      // reset0 * decay
-  f2 half_slope, half_pi, half_pi_slope, zero, one;
+  f2 half_slope, half_pi, hq, cq, zero, one;
 };
 
 __device__ __forceinline__ LifK lif_constants(const LifArgs& a) {
@@ -97,7 +112,8 @@ __device__ __forceinline__ LifK lif_constants(const LifArgs& a) {
   k.rz = splat(__fmul_rn(__fmul_rn(a.reset, 0.f), a.decay));
   k.half_slope = splat(__fmul_rn(a.slope, 0.5f));
   k.half_pi = splat(1.5707963267948966f);
-  k.half_pi_slope = splat(__fmul_rn(1.5707963267948966f, a.slope));
+  k.hq = splat(1.5707963267948966f * a.slope * rsqrtf(0.5f * a.slope));  // plain test only (slope >= 1)
+  k.cq = splat(2.f / a.slope);
   k.zero = splat(0.f);
   k.one = splat(1.f);
   return k;
@@ -223,8 +239,9 @@ __device__ __forceinline__ void lif_recompute(f2 m, const T* xr, int rows, const
 // with dsdv = slope * 0.5 / (1 + (pi/2 * centered)^2) (the arc-tangent
 // surrogate's derivative; slope * (0.5 * r) == (slope * 0.5) * r exactly) and
 // g * (1 - s) as g * 0 or g. With the plain spike test (see lif_step) the
-// spike is d = vn - threshold >= 0 and pi/2 * centered is formed as
-// (pi/2 * slope) * d. Input gradients go to a staged tile (row stride kLanes,
+// spike is d = vn - threshold >= 0 and dsdv is formed as 1 / (h'^2 + 2/slope)
+// with h' = (pi/2 * slope / sqrt(slope/2)) * d: the same quantity, to a few
+// roundings, with one multiply fewer (slope >= 1 there). Input gradients go to a staged tile (row stride kLanes,
 // lane offset applied). Returns g entering the sub-tile.
 template <bool kWhole, bool kPlain, typename T>
 __device__ __forceinline__ f2 lif_grad_tile(f2 g, const f2 (&vp)[kSub], const T* gr, T* out, int rows,
@@ -239,8 +256,14 @@ __device__ __forceinline__ f2 lif_grad_tile(f2 g, const f2 (&vp)[kSub], const T*
     if (kWhole || i < rows) {
       const f2 d = sub2(vp[i], k.thr);
       const f2 cen = kPlain ? d : mul2(k.slope, d);  // carries the spike test's sign
-      const f2 h = kPlain ? mul2(k.half_pi_slope, d) : mul2(k.half_pi, cen);
-      const f2 dsdv = mul2(k.half_slope, rcpx2(fma2(h, h, k.one)));
+      f2 dsdv;
+      if constexpr (kPlain) {  // slope / 2 / (1 + h^2) = 1 / (h'^2 + 2 / slope), h' = h / sqrt(slope / 2)
+        const f2 h = mul2(k.hq, d);
+        dsdv = rcpx2(fma2(h, h, k.cq));
+      } else {
+        const f2 h = mul2(k.half_pi, cen);
+        dsdv = mul2(k.half_slope, rcpx2(fma2(h, h, k.one)));
+      }
       const f2 g0 = mul2(g, k.zero);
       const f2 gk = f2{cen.x >= 0.f ? g0.x : g.x, cen.y >= 0.f ? g0.y : g.y};
       const f2 gv = fma2(dsdv, fma2(g, sub2(k.reset, vp[i]), P::unpack(gin[i])), gk);
@@ -362,7 +385,7 @@ __global__ void __launch_bounds__(32 * kLifWarps, 1) lif_bwd_kernel(const LifArg
                                                                  const __grid_constant__ CUtensorMap tst,
                                                                  const __grid_constant__ CUtensorMap tgx) {
   constexpr int S = kTma ? kLifBwdStages : 2;
-  constexpr int RT = kTma ? lif_rows<T>() : kSub;  // rows per staged tile
+  constexpr int RT = kTma ? lif_bwd_rows<T>() : kSub;  // rows per staged tile
   constexpr int QT = RT / kSub;                    // sub-tiles per staged tile
   constexpr int E = RT * kLanes;
   constexpr int SE = 2 * E * sizeof(T) + QT * kLanes * sizeof(float);  // stage bytes

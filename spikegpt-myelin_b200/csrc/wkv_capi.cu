@@ -949,7 +949,7 @@ int lif_launch_backward(LifArgs& a, bool tma, cudaStream_t st) {
   const int dt = sizeof(IO) == 4 ? WKV_DTYPE_F32
                  : std::is_same<IO, __nv_bfloat16>::value ? WKV_DTYPE_BF16
                                                          : WKV_DTYPE_F16;
-  // x, grad and grad_x in lif_rows<IO>()-row boxes; the membrane checkpoints
+  // x, grad and grad_x in lif_bwd_rows<IO>()-row boxes; the checkpoints
   // of a staged tile's sub-tiles in one [sub-tiles][kLanes] float box
   CUtensorMap mx, mg, mst, mo;
   std::memset(&mx, 0, sizeof(mx));
@@ -957,10 +957,10 @@ int lif_launch_backward(LifArgs& a, bool tma, cudaStream_t st) {
   std::memset(&mst, 0, sizeof(mst));
   std::memset(&mo, 0, sizeof(mo));
   int rc;
-  if (tma && ((rc = make_map(&mx, dt, a.x, a.B, a.T, a.C, lif_rows<IO>())) ||
-              (rc = make_map(&mg, dt, a.gs, a.B, a.T, a.C, lif_rows<IO>())) ||
-              (rc = make_map(&mo, dt, a.gx, a.B, a.T, a.C, lif_rows<IO>())) ||
-              (rc = make_map(&mst, WKV_DTYPE_F32, a.state, a.B, a.ntiles, a.C, lif_rows<IO>() / kSub))))
+  if (tma && ((rc = make_map(&mx, dt, a.x, a.B, a.T, a.C, lif_bwd_rows<IO>())) ||
+              (rc = make_map(&mg, dt, a.gs, a.B, a.T, a.C, lif_bwd_rows<IO>())) ||
+              (rc = make_map(&mo, dt, a.gx, a.B, a.T, a.C, lif_bwd_rows<IO>())) ||
+              (rc = make_map(&mst, WKV_DTYPE_F32, a.state, a.B, a.ntiles, a.C, lif_bwd_rows<IO>() / kSub))))
     return rc;
   const bool plain = lif_plain_test(a);
   const size_t sm = kLifWarps * lif_bwd_smem_bytes<IO>();
