@@ -226,10 +226,10 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// [B, T, C] tensor as a 3-D map with dims {C, T, B} and a [1][rows][kLanes] box,
+// [B, T, C] tensor as a 3-D map with dims {C, T, B} and a [1][rows][cols] box,
 // rows = box_rows, or the dtype's tile height (Pair<T>::kTileRows) when 0.
 int make_map(CUtensorMap* m, int dtype, const void* ptr, int64_t B, int64_t T, int64_t C,
-             int box_rows = 0) {
+             int box_rows = 0, int box_cols = kLanes) {
   std::memset(m, 0, sizeof(*m));
   if (ptr == nullptr) return WKV_OK;
   EncodeTiledFn fn = encode_fn();
@@ -243,7 +243,7 @@ int make_map(CUtensorMap* m, int dtype, const void* ptr, int64_t B, int64_t T, i
   const cuuint32_t rows = box_rows > 0                 ? (cuuint32_t)box_rows
                           : dtype == WKV_DTYPE_F32 ? Pair<float>::kTileRows
                                                    : Pair<__half>::kTileRows;
-  const cuuint32_t box[3] = {(cuuint32_t)kLanes, rows, 1u};
+  const cuuint32_t box[3] = {(cuuint32_t)box_cols, rows, 1u};
   const cuuint32_t estr[3] = {1u, 1u, 1u};
   const CUresult r = fn(m, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -254,14 +254,15 @@ int make_map(CUtensorMap* m, int dtype, const void* ptr, int64_t B, int64_t T, i
 
 // Checkpoint rows [rows][3][C] float32 as a 3-D map with dims {C, 3, rows} and a
 // [tiles][3][kLanes] box (the checkpoints of `tiles` consecutive tiles).
-int make_ckpt_map(CUtensorMap* m, const float* ptr, int64_t rows, int64_t C, int tiles) {
+int make_ckpt_map(CUtensorMap* m, const float* ptr, int64_t rows, int64_t C, int tiles,
+                  int box_cols = kLanes) {
   std::memset(m, 0, sizeof(*m));
   if (ptr == nullptr) return WKV_OK;
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(WKV_ERR_DRIVER, "cuTensorMapEncodeTiled is not available");
   const cuuint64_t dims[3] = {(cuuint64_t)C, 3u, (cuuint64_t)rows};
   const cuuint64_t strides[2] = {(cuuint64_t)(C * 4), (cuuint64_t)(3 * C * 4)};
-  const cuuint32_t box[3] = {(cuuint32_t)kLanes, 3u, (cuuint32_t)tiles};
+  const cuuint32_t box[3] = {(cuuint32_t)box_cols, 3u, (cuuint32_t)tiles};
   const cuuint32_t estr[3] = {1u, 1u, 1u};
   const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(ptr), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -318,6 +319,7 @@ cudaError_t allow_smem(K* kernel, size_t bytes) {
 }
 
 // ----------------------------------------------------------- launch helpers
+
 
 template <typename IO>
 int launch_forward(const void* k, const void* v, const float* decay, int decay_is_w,

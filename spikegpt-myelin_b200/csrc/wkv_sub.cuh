@@ -96,8 +96,9 @@ struct Pre {
 };
 
 // Tree max/min of k (and max |grad_y| when gys != nullptr) over rows [0, L) of a
-// sub-chunk in shared memory (rows past L excluded when kTail).
-template <typename T, bool kTail, bool kGy>
+// sub-chunk in shared memory, rows RS elements apart (rows past L excluded when
+// kTail).
+template <typename T, bool kTail, bool kGy, int RS = kLanes>
 __device__ __forceinline__ Pre prescan(const T* ks, const T* gys, int L) {
   using S = Scan<T>;
   using P = Pair<T>;
@@ -106,11 +107,11 @@ __device__ __forceinline__ Pre prescan(const T* ks, const T* gys, int L) {
 #pragma unroll
   for (int i = 0; i < kSub / 2; ++i) {
     const bool i0 = !kTail || i < L, i1 = !kTail || i + kSub / 2 < L;
-    const raw x0 = P::ld(ks + i * kLanes), x1 = P::ld(ks + (i + kSub / 2) * kLanes);
+    const raw x0 = P::ld(ks + i * RS), x1 = P::ld(ks + (i + kSub / 2) * RS);
     a[i] = S::vmax(i0 ? x0 : scan_lo<T>(), i1 ? x1 : scan_lo<T>());
     b[i] = S::vmin(i0 ? x0 : scan_hi<T>(), i1 ? x1 : scan_hi<T>());
     if (kGy) {
-      const raw g0 = P::ld(gys + i * kLanes), g1 = P::ld(gys + (i + kSub / 2) * kLanes);
+      const raw g0 = P::ld(gys + i * RS), g1 = P::ld(gys + (i + kSub / 2) * RS);
       g[i] = S::vmax(S::vabs(i0 ? g0 : scan_lo<T>()), S::vabs(i1 ? g1 : scan_lo<T>()));
     }
   }
@@ -220,14 +221,14 @@ __device__ __noinline__ void bwd_slow1(float S0, float p0, float q0, float (&adj
 // ------------------------------------------------------------- forward tile
 //
 // Advances st over the `rows` steps of one staged tile (k/v pairs at
-// ks[i*kLanes], vs[i*kLanes]); with kY writes y pairs to ys[i*kLanes]; with
+// ks[i*RS], vs[i*RS]); with kY writes y pairs to ys[i*RS]; with
 // ck != nullptr stores the state at every sub-chunk start (rows 0, kSub, ...)
 // to checkpoint rows ck_row0, ck_row0 + 1, ... The range check and the scale
 // choice are made once per tile. The fast path is computed unconditionally (it
 // cannot fault on any input); if any lane of the warp fails the range check the
 // exact path recomputes the tile and its results (and checkpoints) replace the
 // fast ones.
-template <typename T, bool kTail, bool kY>
+template <typename T, bool kTail, bool kY, int RS = kLanes>
 __device__ __forceinline__ void fwd_tile2(Fwd2& st, const T* ks, const T* vs, T* ys, int rows,
                                           const Lane2& lc, bool force_slow, float* ck,
                                           size_t ck_row0, int C, int c, bool v0, bool v1) {
@@ -238,8 +239,8 @@ __device__ __forceinline__ void fwd_tile2(Fwd2& st, const T* ks, const T* vs, T*
   raw kr[R], vr[R];
 #pragma unroll
   for (int i = 0; i < R; ++i) {
-    kr[i] = P::ld(ks + i * kLanes);
-    vr[i] = P::ld(vs + i * kLanes);
+    kr[i] = P::ld(ks + i * RS);
+    vr[i] = P::ld(vs + i * RS);
   }
   raw mx[R / 2], mn[R / 2];
 #pragma unroll
@@ -284,17 +285,17 @@ __device__ __forceinline__ void fwd_tile2(Fwd2& st, const T* ks, const T* vs, T*
     if (kY) {
 #pragma unroll
       for (int i = 0; i < R; ++i)
-        if (!kTail || i < rows) P::st(ys + i * kLanes, P::pack(yr[i]));
+        if (!kTail || i < rows) P::st(ys + i * RS, P::pack(yr[i]));
     }
   } else {
 #pragma unroll 1
     for (int r0 = 0; r0 < rows; r0 += kSub) {
       if (ck != nullptr) store_state(ck, ck_row0 + r0 / kSub, C, c, v0, v1, st.S, st.p, st.q);
       const int L = min(kSub, rows - r0);
-      const int o = r0 * kLanes;
-      fwd_slow1<T, kY>(st.S.x, st.p.x, st.q.x, ks + o, vs + o, ys + o, L, lc.w2.x, lc.u2.x);
+      const int o = r0 * RS;
+      fwd_slow1<T, kY>(st.S.x, st.p.x, st.q.x, ks + o, vs + o, ys + o, L, lc.w2.x, lc.u2.x, RS, RS);
       fwd_slow1<T, kY>(st.S.y, st.p.y, st.q.y, ks + o + 1, vs + o + 1, ys + o + 1, L, lc.w2.y,
-                       lc.u2.y);
+                       lc.u2.y, RS, RS);
     }
   }
 }
@@ -310,18 +311,11 @@ __device__ __forceinline__ void fwd_tile2(Fwd2& st, const T* ks, const T* vs, T*
 //   gk = A (v - y) + e^k (dL/dP_{t+1} v + dL/dQ_{t+1})
 //   dL/dP_t = gy/D_t + e^w dL/dP_{t+1},  dL/dQ_t = -gy y/D_t + e^w dL/dQ_{t+1}
 //   H_t = e^w (dL/dP_{t+1} + H_{t+1})    (likewise for Q)
-template <typename T, bool kTail, bool kOut>
+template <typename T, bool kTail, bool kOut, int RS = kLanes>
 __device__ __forceinline__ void bwd_sub2(const Fwd2& st0, const Pre& pre, Adj2& adj, const T* ks,
                                          const T* vs, const T* gys, T* gks, T* gvs, int L,
                                          const Lane2& lc, f2& gwacc, f2& gu, bool force_slow) {
   using P = Pair<T>;
-  typename P::raw kr[kSub], vr[kSub], gr[kSub];
-#pragma unroll
-  for (int i = 0; i < kSub; ++i) {
-    kr[i] = P::ld(ks + i * kLanes);
-    vr[i] = P::ld(vs + i * kLanes);
-    gr[i] = P::ld(gys + i * kLanes);
-  }
   const int n = kTail ? L : kSub;
   f2 s, p, q;
   bool ok =
@@ -337,33 +331,35 @@ __device__ __forceinline__ void bwd_sub2(const Fwd2& st0, const Pre& pre, Adj2& 
   const f2 ns = f2{-s.x, -s.y};
   const f2 l2e = splat(kL2E);
   const f2 gw0 = gwacc, gu0 = gu;
-  f2 ry[kSub], rg[kSub];
-  // forward recompute of the sub-chunk
+  f2 ry[kSub], rg[kSub], re[kSub];
+  // forward recompute of the sub-chunk (k, v, gy read from shared memory once
+  // here and v once more in the reverse sweep; e^{k-s} kept in registers)
 #pragma unroll
   for (int i = 0; i < kSub; ++i) {
     if (kTail && i >= L) break;
-    const f2 v = P::unpack(vr[i]);
-    const f2 ek = ex2x2(fma2(P::unpack(kr[i]), l2e, ns));
+    const f2 v = P::unpack(P::ld(vs + i * RS));
+    const f2 ek = ex2x2(fma2(P::unpack(P::ld(ks + i * RS)), l2e, ns));
+    re[i] = ek;
     const f2 eb = mul2(ek, lc.eu);
     const f2 rd = rcpx2(add2(q, eb));
     ry[i] = mul2(fma2(eb, v, p), rd);
-    rg[i] = mul2(P::unpack(gr[i]), rd);  // gy 2^s / D_t
+    rg[i] = mul2(P::unpack(P::ld(gys + i * RS)), rd);  // gy 2^s / D_t
     p = fma2(lc.ew, p, mul2(ek, v));
     q = fma2(lc.ew, q, ek);
   }
-  // reverse sweep (e^{k-s} recomputed rather than kept)
+  // reverse sweep
 #pragma unroll
   for (int i = kSub - 1; i >= 0; --i) {
     if (kTail && i >= L) continue;
-    const f2 v = P::unpack(vr[i]);
-    const f2 ek = ex2x2(fma2(P::unpack(kr[i]), l2e, ns));
+    const f2 v = P::unpack(P::ld(vs + i * RS));
+    const f2 ek = re[i];
     const f2 a = mul2(mul2(rg[i], ek), lc.eu);  // gy e^{u+k} / D
     const f2 av = mul2(a, sub2(v, ry[i]));
     gu = add2(gu, av);
     gwacc = fma2(ek, fma2(v, hp, hq), gwacc);
     if (kOut) {
-      P::st(gvs + i * kLanes, P::pack(fma2(ek, gp, a)));
-      P::st(gks + i * kLanes, P::pack(fma2(ek, fma2(gp, v, gq), av)));
+      P::st(gvs + i * RS, P::pack(fma2(ek, gp, a)));
+      P::st(gks + i * RS, P::pack(fma2(ek, fma2(gp, v, gq), av)));
     }
     hp = mul2(lc.ew, add2(gp, hp));
     hq = mul2(lc.ew, add2(gq, hq));
@@ -378,9 +374,9 @@ __device__ __forceinline__ void bwd_sub2(const Fwd2& st0, const Pre& pre, Adj2& 
     float ax[5] = {adj.G.x, adj.gp.x, adj.gq.x, adj.hp.x, adj.hq.x};
     float ay[5] = {adj.G.y, adj.gp.y, adj.gq.y, adj.hp.y, adj.hq.y};
     bwd_slow1<T, kOut>(st0.S.x, st0.p.x, st0.q.x, ax, ks, vs, gys, gks, gvs, L, lc.w2.x, lc.u2.x,
-                       gwacc.x, gu.x);
+                       gwacc.x, gu.x, RS, RS);
     bwd_slow1<T, kOut>(st0.S.y, st0.p.y, st0.q.y, ay, ks + 1, vs + 1, gys + 1, gks + 1, gvs + 1, L,
-                       lc.w2.y, lc.u2.y, gwacc.y, gu.y);
+                       lc.w2.y, lc.u2.y, gwacc.y, gu.y, RS, RS);
     adj = Adj2{f2{ax[0], ay[0]}, f2{ax[1], ay[1]}, f2{ax[2], ay[2]}, f2{ax[3], ay[3]},
                f2{ax[4], ay[4]}};
   }

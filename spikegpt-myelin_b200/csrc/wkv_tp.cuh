@@ -395,13 +395,13 @@ __device__ __forceinline__ f2 tile_absmax(const typename Pair<T>::raw (&gr)[kSub
 }
 
 // Forward recompute of a tile from its start state rescaled to the tile scale
-// s: ry = y_t, rg = gy_t 2^s / D_t.
+// s: ry = y_t, rg = gy_t 2^s / D_t, re = e^{k_t - s} (kept for the reverse pass).
 template <typename T, bool kTail>
 __device__ __forceinline__ void bwd_tp_recompute(const typename Pair<T>::raw (&kr)[kSub],
                                                  const typename Pair<T>::raw (&vr)[kSub],
                                                  const typename Pair<T>::raw (&gr)[kSub], int n,
                                                  const Lane2& lc, f2 s, f2 p, f2 q,
-                                                 f2 (&ry)[kSub], f2 (&rg)[kSub]) {
+                                                 f2 (&ry)[kSub], f2 (&rg)[kSub], f2 (&re)[kSub]) {
   using P = Pair<T>;
   const f2 l2e = splat(kL2E), ns = f2{-s.x, -s.y};
 #pragma unroll
@@ -409,10 +409,12 @@ __device__ __forceinline__ void bwd_tp_recompute(const typename Pair<T>::raw (&k
     if (kTail && i >= n) {
       ry[i] = splat(0.f);
       rg[i] = splat(0.f);
+      re[i] = splat(0.f);
       continue;
     }
     const f2 v = P::unpack(vr[i]);
     const f2 ek = ex2x2(fma2(P::unpack(kr[i]), l2e, ns));
+    re[i] = ek;
     const f2 eb = mul2(ek, lc.eu);
     const f2 rd = rcpx2(add2(q, eb));
     ry[i] = mul2(fma2(eb, v, p), rd);
@@ -441,18 +443,17 @@ __device__ __forceinline__ void bwd_tp_summary(const f2 (&ry)[kSub], const f2 (&
 // Reverse pass of a tile from the adjoint at its end (scaled by 2^s): grad_key /
 // grad_value of its rows (kOut) and dL/dw, dL/du accumulated into gw, gu.
 template <typename T, bool kTail, bool kOut>
-__device__ __forceinline__ void bwd_tp_outputs(const typename Pair<T>::raw (&kr)[kSub],
+__device__ __forceinline__ void bwd_tp_outputs(const f2 (&re)[kSub],
                                                const typename Pair<T>::raw (&vr)[kSub],
                                                const f2 (&ry)[kSub], const f2 (&rg)[kSub], int n,
                                                const Lane2& lc, f2 s, f2 gp, f2 gq, f2 hp, f2 hq,
                                                T* gks, T* gvs, f2& gw, f2& gu) {
   using P = Pair<T>;
-  const f2 l2e = splat(kL2E), ns = f2{-s.x, -s.y};
 #pragma unroll
   for (int i = kSub - 1; i >= 0; --i) {
     if (kTail && i >= n) continue;
     const f2 v = P::unpack(vr[i]);
-    const f2 ek = ex2x2(fma2(P::unpack(kr[i]), l2e, ns));
+    const f2 ek = re[i];
     const f2 a = mul2(mul2(rg[i], ek), lc.eu);  // gy e^{u+k} / D
     const f2 av = mul2(a, sub2(v, ry[i]));
     gu = add2(gu, av);
@@ -645,13 +646,13 @@ __global__ void __launch_bounds__(32 * W, 4)
                                   s.y, p.y, q.y) &&
                          fmaxf(gymax.x, gymax.y) <= 0x1p40f && !force_slow);
     if (n == 0) s = p = q = splat(0.f);
-    f2 ry[R], rg[R];
+    f2 ry[R], rg[R], re[R];
     Adj2 loc;
     if (n == R) {
-      bwd_tp_recompute<T, false>(kr, vr, gr, n, lc, s, p, q, ry, rg);
+      bwd_tp_recompute<T, false>(kr, vr, gr, n, lc, s, p, q, ry, rg, re);
       bwd_tp_summary<false>(ry, rg, n, lc, loc.gp, loc.gq, loc.hp, loc.hq);
     } else {
-      bwd_tp_recompute<T, true>(kr, vr, gr, n, lc, s, p, q, ry, rg);
+      bwd_tp_recompute<T, true>(kr, vr, gr, n, lc, s, p, q, ry, rg, re);
       bwd_tp_summary<true>(ry, rg, n, lc, loc.gp, loc.gq, loc.hp, loc.hq);
     }
     loc.G = f2{-s.x, -s.y};
@@ -705,10 +706,10 @@ __global__ void __launch_bounds__(32 * W, 4)
                                fmaxf(fmaxf(fabsf(hp.x), fabsf(hp.y)), fmaxf(fabsf(hq.x), fabsf(hq.y))));
       if (fast && __all_sync(kFull, amax <= 0x1p80f)) {
         if (n == R)
-          bwd_tp_outputs<T, false, kOut>(kr, vr, ry, rg, n, lc, s, gp, gq, hp, hq, gks + 2 * lane,
+          bwd_tp_outputs<T, false, kOut>(re, vr, ry, rg, n, lc, s, gp, gq, hp, hq, gks + 2 * lane,
                                          gvs + 2 * lane, gwacc, gu);
         else
-          bwd_tp_outputs<T, true, kOut>(kr, vr, ry, rg, n, lc, s, gp, gq, hp, hq, gks + 2 * lane,
+          bwd_tp_outputs<T, true, kOut>(re, vr, ry, rg, n, lc, s, gp, gq, hp, hq, gks + 2 * lane,
                                         gvs + 2 * lane, gwacc, gu);
       } else {
         bwd_tp_exact<T>(a, b, t0, c, v0, v1, n, st0, ein, lc, gks + 2 * lane, gvs + 2 * lane,
