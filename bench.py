@@ -62,7 +62,12 @@ WORKLOADS = {
 }
 WORKLOADS["lif"] = dict(kind="lif", B=64, T=1024, C=512, dtype="bf16", kscale=1.5,
                         desc="LIF fwd+bwd: B=64 T=1024 C=512 bf16 (a SpikeGPT-41M block activation)")
+WORKLOADS["train"] = dict(kind="train", global_batch=64, T=1024, zipf=1.1,
+                          desc="config 3: SpikeGPT-41M train step (12L/512d/V=256/ctx1024), global batch 64, "
+                               "bf16 autocast, AdamW wd 0.1")
 LIF_METRIC = "LIF fwd+bwd algorithmic HBM throughput"
+TRAIN_METRIC = "SpikeGPT-41M train tokens/s"
+PEAKS_FALLBACK_TFLOPS = 1590.0
 STEP_METRIC = "WKV recurrent step algorithmic HBM throughput"
 STEP_BYTES = {"bf16": 2, "fp16": 2, "fp32": 4}
 METRIC = "WKV fwd+bwd algorithmic HBM throughput"
@@ -874,10 +879,148 @@ def run_lif_reference(args, wl):
     print(json.dumps(out), flush=True)
 
 
+def zipf_tokens(rng, shape, vocab: int, s: float):
+    """iid token ids with P(rank r) proportional to r^-s over the vocabulary
+    (rank r -> id r - 1)."""
+    w = np.arange(1, vocab + 1, dtype=np.float64) ** -s
+    return rng.choice(vocab, size=shape, p=w / w.sum()).astype(np.int64)
+
+
+def run_train(args, wl):
+    """Data-parallel train step of SpikeGPT-41M (this package's model and ops):
+    global batch 64 x 1024 tokens split over the ranks (weak per-rank work
+    shrinks as ranks grow: strong scaling), bf16 autocast, fused AdamW with
+    weight decay 0.1, DDP gradient all-reduce over NCCL for N > 1. A step is
+    forward, backward and the optimizer step on resident synthetic tokens."""
+    import torch
+    import torch.distributed as dist
+
+    from spikegpt_b200 import _capi
+    from spikegpt_b200.model import SPIKEGPT_41M, SpikeGPT, flops_per_token
+    from spikegpt_b200.sharding import max_over_ranks
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    gb, t = wl["global_batch"], wl["T"]
+    if gb % world:
+        raise SystemExit(f"global batch {gb} does not split over {world} ranks")
+    b = gb // world
+    torch.manual_seed(0)
+    model = SpikeGPT(SPIKEGPT_41M).to(dev)
+    ddp = model
+    if world > 1:
+        ddp = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local], broadcast_buffers=False)
+    opt = torch.optim.AdamW(model.parameters(), lr=6e-4, weight_decay=0.1, fused=True)
+    rng = np.random.default_rng(rank)
+    ids_np = zipf_tokens(rng, (b, t + 1), SPIKEGPT_41M.vocab_size, wl["zipf"])
+    ids = torch.as_tensor(ids_np).to(dev)
+    x, y = ids[:, :-1].contiguous(), ids[:, 1:].contiguous()
+
+    def step(xb, yb):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = ddp(xb, yb)
+        loss.backward()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return loss
+
+    for _ in range(args.warmup):
+        loss = step(x, y)
+    torch.cuda.synchronize(dev)
+    sampler = None if args.profile else ClockSampler(local)
+    time.sleep(0.3 if sampler else 0)
+    launches0 = sum(_capi.launch_counts().values())
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    host0 = time.time()
+    ev0.record()
+    for _ in range(args.steps):
+        loss = step(x, y)
+    ev1.record()
+    torch.cuda.synchronize(dev)
+    host1 = time.time()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    launches = sum(_capi.launch_counts().values()) - launches0
+    ms = max_over_ranks(ev0.elapsed_time(ev1), dev)
+    if sampler:
+        time.sleep(0.25)
+        sampler.stop()
+    clocks = sampler.summary(host0, host1) if sampler else None
+    tokens = gb * t * args.steps
+    value = tokens / (ms * 1e-3)
+    fpt = flops_per_token(SPIKEGPT_41M)
+    pk = peaks()
+    peak = float(pk.get("bf16_tflops", PEAKS_FALLBACK_TFLOPS))
+    achieved = value * fpt / world / 1e12
+    result = {
+        "metric": TRAIN_METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic Zipf(1.1) token ids, seeded numpy PCG64 per rank",
+        "config": {"workload": wl["desc"], "global_batch": gb, "seq_len": t, "B_per_gpu": b,
+                   "params": sum(p.numel() for p in model.parameters()),
+                   "parallelism": f"dp{world}" + (" (DDP, NCCL all-reduce)" if world > 1 else ""),
+                   "l2": "model state and activations far above L2; no flush"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "flops_per_token": fpt,
+                     "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops)" if pk.get("source") == "measured"
+                     else "fallback 1.59 PFLOP/s", "traffic": None,
+                     "note": "model FLOPs utilisation (6 x matmul weights per token)"},
+        "loss": float(loss.item()), "gpu_launches": int(launches), "clocks": clocks,
+        "cpu_baseline": None,
+        "cpu_baseline_note": "no CPU leg: the model step runs only on this package's CUDA ops, and the "
+                             "reference's own CPU step needs myelin@68b8ebb, absent",
+    }
+    if not args.profile:
+        hx = torch.as_tensor(ids_np).pin_memory()
+
+        def e2e_step():
+            d = hx.to(dev, non_blocking=True)
+            return step(d[:, :-1], d[:, 1:]).detach().to("cpu", non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ems = max_over_ranks(e0.elapsed_time(e1), dev)
+        result["e2e"] = {"value": gb * t * args.e2e_steps / (ems * 1e-3), "unit": "tokens/s",
+                         "h2d_bytes_per_step": int(hx.numel() * 8), "d2h_bytes_per_step": 4,
+                         "steps": args.e2e_steps, "ms_per_step": ems / args.e2e_steps,
+                         "path": "token ids copied from pinned host memory each step, loss read back"}
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        del ddp
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     wl = WORKLOADS[args.workload]
-    if wl.get("kind") == "step":
+    if wl.get("kind") == "train":
+        if args.impl == "reference":
+            if int(os.environ.get("RANK", "0")) == 0:
+                print(json.dumps({"impl": "reference", "metric": TRAIN_METRIC,
+                                  "unavailable": "the reference's train step needs myelin@68b8ebb (absent) "
+                                                 "for its LIF and spike functions"}), flush=True)
+        else:
+            run_train(args, wl)
+    elif wl.get("kind") == "step":
         if args.impl == "reference":
             run_step_reference(args, wl)
         else:

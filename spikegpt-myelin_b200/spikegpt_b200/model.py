@@ -1,0 +1,215 @@
+"""SpikeGPT language model on this package's sm_100a ops (the train-step harness).
+
+The architecture of the reference's ``SpikeLanguageModel``
+(src/spikegpt/language.py:1361-1480) with its defaults (``model_type="rwkv"``,
+``attention="rwkv"``, ``spiking=True``, ``spike_embedding=True``,
+``spike_input=False``): a spiking token embedding, ``n_layer`` blocks of
+RWKV-4 time mixing and channel mixing each followed by a LIF activation on the
+residual branch, a final LayerNorm and a linear head. The WKV recurrence runs
+on ``weighted_key_value_cuda_bf16io`` / ``weighted_key_value_cuda`` and the LIF
+activations on ``surrogate_lif``; everything else is plain PyTorch (cuBLAS
+GEMMs under bf16 autocast). Parameter shapes and initial values follow the
+reference (language.py:920-955 time mixing, 1145-1160 channel mixing,
+1223-1270 block, 1364-1385 model and weight init), so the parameter count of
+the SpikeGPT-41M configuration (12 layers, 512 wide, vocabulary 256, context
+1024) is the reference's 41,226,240.
+
+The model needs CUDA tensors for its forward pass (the ops have no CPU path);
+building it on the CPU is fine.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+from torch import Tensor, nn
+
+from .lif import surrogate_lif
+from .wkv import weighted_key_value_cuda
+from .wkv_bf16 import weighted_key_value_cuda_bf16io
+
+
+@dataclass
+class SpikeGPTConfig:
+    """The reference's SpikeGPTConfig fields this model implements
+    (language.py:234-253)."""
+
+    vocab_size: int = 256
+    context_length: int = 1024
+    n_layer: int = 12
+    n_embd: int = 512
+    dropout: float = 0.0
+    lif_tau: float = 2.0
+    lif_threshold: float = 1.0
+    lif_reset: float = 0.0
+    surrogate_slope: float = 2.0
+    spike_embedding: bool = True
+
+    def validate(self) -> None:
+        for name in ("vocab_size", "context_length", "n_layer", "n_embd"):
+            if getattr(self, name) <= 0:
+                raise ValueError(f"{name} must be positive")
+        if not 0.0 <= self.dropout < 1.0:
+            raise ValueError("dropout must be in [0, 1)")
+        if self.lif_tau <= 0.0:
+            raise ValueError("lif_tau must be positive")
+
+
+SPIKEGPT_41M = SpikeGPTConfig(vocab_size=256, context_length=1024, n_layer=12, n_embd=512)
+
+
+class _HardSpike(torch.autograd.Function):
+    """Heaviside spike of ``x`` with the arc-tangent surrogate gradient
+    ``1 / (2 (1 + (pi/2 x)^2))``: the spiking embedding's activation (reference
+    ``hard_surrogate_spike(slope * e, atan_surrogate)``, language.py:1387-1395)."""
+
+    @staticmethod
+    def forward(ctx, x: Tensor) -> Tensor:
+        ctx.save_for_backward(x)
+        return (x >= 0).to(x.dtype)
+
+    @staticmethod
+    def backward(ctx, grad: Tensor) -> Tensor:
+        (x,) = ctx.saved_tensors
+        h = x * (math.pi / 2)
+        return grad * (0.5 / (1.0 + h * h))
+
+
+def _shift_mix(x: Tensor, mix: Tensor) -> Tensor:
+    """``x * mix + x_{t-1} * (1 - mix)`` with a zero row before t = 0
+    (reference _mix_with_previous, language.py:344-353)."""
+    prev = F.pad(x[:, :-1], (0, 0, 1, 0))
+    return x * mix + prev * (1.0 - mix)
+
+
+def _mix_profile(n_embd: int, power: float, offset: float = 0.0) -> Tensor:
+    position = torch.arange(n_embd, dtype=torch.float32) / n_embd
+    return (torch.pow(position, power) + offset).view(1, 1, -1)
+
+
+class TimeMix(nn.Module):
+    """RWKV-4 time mixing (reference SpikeTimeMix, language.py:920-1036)."""
+
+    def __init__(self, n_embd: int, n_layer: int, layer_id: int) -> None:
+        super().__init__()
+        r01 = layer_id / max(1, n_layer - 1)
+        r10 = 1.0 - layer_id / n_layer
+        idx = torch.arange(n_embd, dtype=torch.float32)
+        self.time_decay = nn.Parameter(-5.0 + 8.0 * torch.pow(idx / max(1, n_embd - 1), 0.7 + 1.3 * r01))
+        zigzag = torch.tensor([(i + 1) % 3 - 1 for i in range(n_embd)], dtype=torch.float32)
+        self.time_first = nn.Parameter(torch.full((n_embd,), -1.2039728) + 0.5 * zigzag)
+        self.time_mix_k = nn.Parameter(_mix_profile(n_embd, r10))
+        self.time_mix_v = nn.Parameter(_mix_profile(n_embd, r10, 0.3 * r01))
+        self.time_mix_r = nn.Parameter(_mix_profile(n_embd, 0.5 * r10))
+        self.key = nn.Linear(n_embd, n_embd, bias=False)
+        self.value = nn.Linear(n_embd, n_embd, bias=False)
+        self.receptance = nn.Linear(n_embd, n_embd, bias=False)
+        self.output = nn.Linear(n_embd, n_embd, bias=False)
+
+    def forward(self, x: Tensor) -> Tensor:
+        k = self.key(_shift_mix(x, self.time_mix_k))
+        v = self.value(_shift_mix(x, self.time_mix_v))
+        r = torch.sigmoid(self.receptance(_shift_mix(x, self.time_mix_r)))
+        if k.dtype in (torch.bfloat16, torch.float16):
+            wkv = weighted_key_value_cuda_bf16io(k, v, self.time_decay, self.time_first)
+        else:
+            wkv = weighted_key_value_cuda(k, v, self.time_decay, self.time_first)
+        return self.output(r * wkv)
+
+
+class ChannelMix(nn.Module):
+    """RWKV-4 channel mixing (reference SpikeChannelMix, language.py:1145-1196)."""
+
+    def __init__(self, n_embd: int, n_layer: int, layer_id: int) -> None:
+        super().__init__()
+        r10 = 1.0 - layer_id / n_layer
+        self.time_mix_k = nn.Parameter(_mix_profile(n_embd, r10))
+        self.time_mix_r = nn.Parameter(_mix_profile(n_embd, r10))
+        self.key = nn.Linear(n_embd, 4 * n_embd, bias=False)
+        self.receptance = nn.Linear(n_embd, n_embd, bias=False)
+        self.value = nn.Linear(4 * n_embd, n_embd, bias=False)
+
+    def forward(self, x: Tensor) -> Tensor:
+        k = torch.relu(self.key(_shift_mix(x, self.time_mix_k))).square()
+        r = torch.sigmoid(self.receptance(_shift_mix(x, self.time_mix_r)))
+        return r * self.value(k)
+
+
+class Block(nn.Module):
+    """Time mixing and channel mixing, each spiked by a LIF neuron before it
+    joins the residual stream (reference SpikeGPTBlock.forward with
+    spike_input=False, language.py:1325-1355)."""
+
+    def __init__(self, config: SpikeGPTConfig, layer_id: int) -> None:
+        super().__init__()
+        c = config.n_embd
+        self.config = config
+        self.ln0 = nn.LayerNorm(c) if layer_id == 0 else None
+        self.ln1 = nn.LayerNorm(c)
+        self.ln2 = nn.LayerNorm(c)
+        self.att = TimeMix(c, config.n_layer, layer_id)
+        self.ffn = ChannelMix(c, config.n_layer, layer_id)
+        self.dropout = nn.Dropout(config.dropout)
+
+    def _lif(self, x: Tensor) -> Tensor:
+        cfg = self.config
+        return surrogate_lif(x, tau=cfg.lif_tau, threshold=cfg.lif_threshold, reset=cfg.lif_reset,
+                             surrogate_slope=cfg.surrogate_slope)
+
+    def forward(self, x: Tensor) -> Tensor:
+        if self.ln0 is not None:
+            x = self.ln0(x)
+        x = x + self._lif(self.att(self.ln1(x)))
+        x = x + self._lif(self.ffn(self.ln2(x)))
+        return self.dropout(x)
+
+
+class SpikeGPT(nn.Module):
+    """Spiking embedding, blocks, final LayerNorm, head; ``forward(ids, targets)``
+    returns the mean cross-entropy (reference SpikeLanguageModel.forward /
+    loss_tail, language.py:1446-1480)."""
+
+    def __init__(self, config: SpikeGPTConfig = SPIKEGPT_41M) -> None:
+        super().__init__()
+        config.validate()
+        self.config = config
+        self.embedding = nn.Embedding(config.vocab_size, config.n_embd)
+        self.blocks = nn.ModuleList([Block(config, i) for i in range(config.n_layer)])
+        self.ln_out = nn.LayerNorm(config.n_embd)
+        self.head = nn.Linear(config.n_embd, config.vocab_size, bias=False)
+        for m in self.modules():  # reference _init_weights (language.py:1376-1382)
+            if isinstance(m, nn.Embedding):
+                nn.init.normal_(m.weight, mean=0.0, std=1.0e-3)
+            elif isinstance(m, nn.Linear):
+                nn.init.normal_(m.weight, mean=0.0, std=0.01)
+
+    def forward(self, input_ids: Tensor, targets: Tensor | None = None) -> Tensor:
+        if input_ids.ndim != 2:
+            raise ValueError(f"input_ids must have shape [B, T]; got {tuple(input_ids.shape)}")
+        if input_ids.shape[1] > self.config.context_length:
+            raise ValueError("input sequence length exceeds context_length")
+        x = self.embedding(input_ids)
+        if self.config.spike_embedding:
+            x = _HardSpike.apply(self.config.surrogate_slope * x)
+        for block in self.blocks:
+            x = block(x)
+        logits = self.head(self.ln_out(x))
+        if targets is None:
+            return logits
+        return F.cross_entropy(logits.reshape(-1, logits.shape[-1]).float(), targets.reshape(-1))
+
+
+def parameter_count(model: nn.Module) -> int:
+    return sum(p.numel() for p in model.parameters())
+
+
+def flops_per_token(config: SpikeGPTConfig) -> float:
+    """Model FLOPs per token for MFU: 6 x the weights of the matrix products
+    (forward and backward), 13 C^2 per layer (time mixing 4 C^2, channel
+    mixing 9 C^2) plus the head C x V; the embedding lookup, WKV, LIF and
+    elementwise terms are left out. 246.2 MFLOP for SpikeGPT-41M."""
+    c, v = config.n_embd, config.vocab_size
+    return 6.0 * (config.n_layer * 13 * c * c + c * v)

@@ -1,0 +1,125 @@
+"""SpikeGPT model and train step (spikegpt_b200.model) against the reference's
+own model (golden vectors from tests/golden/make_golden_model.py).
+
+CPU: parameter count and FLOPs of SpikeGPT-41M, the initial values of the
+non-matrix parameters (decays, bonuses, mixing profiles) against the
+reference's. GPU: with the reference's parameters loaded, the loss, logits and
+every gradient in float32 (the model runs on this package's WKV and LIF
+kernels, the reference on its CPU paths; both use the same spike rule, so the
+comparison is to float32 rounding of the whole network: loss to 1e-5, logits
+to 1e-4 and each gradient to 1e-3 of its own scale); a bf16-autocast train step; the
+data-parallel invariant (the gradient of the batch mean is the mean of the
+shards' gradients)."""
+
+from __future__ import annotations
+
+import math
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+from _wkvtest import scaled_err
+
+from spikegpt_b200.model import SPIKEGPT_41M, SpikeGPT, SpikeGPTConfig, flops_per_token, parameter_count
+
+GOLDEN = np.load(Path(__file__).resolve().parent / "golden" / "model_golden.npz")
+
+
+def _golden_config() -> SpikeGPTConfig:
+    v, ctx, nl, ne = (int(x) for x in GOLDEN["config"])
+    return SpikeGPTConfig(vocab_size=v, context_length=ctx, n_layer=nl, n_embd=ne)
+
+
+def _golden_model(device) -> SpikeGPT:
+    torch.manual_seed(0)
+    model = SpikeGPT(_golden_config())
+    state = {k[len("param/"):]: torch.as_tensor(GOLDEN[k]) for k in GOLDEN.files if k.startswith("param/")}
+    model.load_state_dict(state, strict=True)
+    return model.to(device)
+
+
+def test_41m_parameters_and_flops():
+    model = SpikeGPT(SPIKEGPT_41M)
+    assert parameter_count(model) == 41_226_240
+    assert flops_per_token(SPIKEGPT_41M) == pytest.approx(246.2e6, rel=1e-3)
+
+
+def test_initial_values_match_reference():
+    model = SpikeGPT(_golden_config())
+    params = dict(model.named_parameters())
+    checked = 0
+    for key in GOLDEN.files:
+        if not key.startswith("param/"):
+            continue
+        name = key[len("param/"):]
+        if name.endswith(".weight") and GOLDEN[key].ndim == 2:
+            continue  # matrices were redrawn by the golden script
+        np.testing.assert_allclose(params[name].detach().numpy(), GOLDEN[key], rtol=1e-6, atol=1e-7,
+                                   err_msg=name)
+        checked += 1
+    assert checked > 20
+
+
+def test_shapes_and_errors():
+    model = SpikeGPT(_golden_config())
+    with pytest.raises(ValueError):
+        model(torch.zeros(4, dtype=torch.long))
+    with pytest.raises(ValueError):
+        model(torch.zeros(1, 1000, dtype=torch.long))
+    with pytest.raises(ValueError):
+        SpikeGPTConfig(n_embd=0).validate()
+
+
+@pytest.mark.gpu
+def test_float32_parity_with_reference_model(cuda):
+    model = _golden_model(cuda)
+    ids = torch.as_tensor(GOLDEN["ids"]).to(cuda)
+    logits = model(ids[:, :-1])
+    loss = model(ids[:, :-1], ids[:, 1:])
+    loss.backward()
+    assert abs(loss.item() - float(GOLDEN["loss"])) <= 1e-5 * max(1.0, abs(float(GOLDEN["loss"])))
+    assert scaled_err(logits.detach().cpu().numpy(), GOLDEN["logits"]) <= 1e-4
+    for name, p in model.named_parameters():
+        ref = GOLDEN[f"grad/{name}"]
+        scale = max(float(np.abs(ref).max()), 1e-30)
+        assert float(np.abs(p.grad.cpu().numpy() - ref).max()) <= 1e-3 * scale, name
+
+
+@pytest.mark.gpu
+def test_bf16_train_step(cuda):
+    cfg = SpikeGPTConfig(vocab_size=256, context_length=256, n_layer=2, n_embd=128)
+    torch.manual_seed(1)
+    model = SpikeGPT(cfg).to(cuda)
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-3, weight_decay=0.1, fused=True)
+    ids = torch.randint(0, 256, (4, 257), device=cuda)
+    losses = []
+    for _ in range(8):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = model(ids[:, :-1], ids[:, 1:])
+        loss.backward()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        losses.append(loss.item())
+    assert all(math.isfinite(x) for x in losses)
+    assert abs(losses[0] - math.log(256)) < 0.05  # tiny initial weights: uniform prediction
+    assert losses[-1] < losses[0]
+
+
+@pytest.mark.gpu
+def test_data_parallel_gradient_is_mean_of_shards(cuda):
+    model = _golden_model(cuda)
+    rng = np.random.default_rng(9)
+    ids = torch.as_tensor(rng.integers(0, model.config.vocab_size, (4, model.config.context_length + 1))).to(cuda)
+
+    def grads(batch):
+        model.zero_grad(set_to_none=True)
+        model(batch[:, :-1], batch[:, 1:]).backward()
+        return {n: p.grad.detach().clone() for n, p in model.named_parameters()}
+
+    full = grads(ids)
+    a, b = grads(ids[:2]), grads(ids[2:])
+    for n in full:
+        ref = full[n].cpu().numpy()
+        mean = ((a[n] + b[n]) / 2).cpu().numpy()
+        assert scaled_err(mean, ref) <= 1e-4, n
