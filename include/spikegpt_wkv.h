@@ -176,6 +176,31 @@ WKV_API int lif_backward(int dtype, const void* grad_spikes, const void* x, cons
                          float tau, float threshold, float reset, float slope, void* stream);
 
 /*
+ * Fused LayerNorm + token-shift mixing: the GEMM inputs of the SpikeGPT
+ * blocks under bf16 autocast. Replaces, per sublayer, the reference's
+ * LayerNorm followed by `_mix_with_previous` once per projection
+ * (src/spikegpt/language.py:344-353; time mixing 1009-1012 with n = 3,
+ * channel mixing 1190-1192 with n = 2) and autocast's bf16 copy:
+ *   out_i[b,t,:] = bf16(h[t] * m_i + h[t-1] * (1 - m_i)),  h = LayerNorm(x; w, b, eps),
+ * h[-1] = 0, x [B,T,C] float32, w, b [C], mix [n][C] float32, outputs bf16.
+ * ln_mix_forward also writes the row mean and 1/std ([B*T] float32) that
+ * ln_mix_backward takes with the n bf16 output gradients to give grad_x
+ * [B,T,C], grad_w, grad_b [C] and grad_mix [n][C] (parameter gradients
+ * reduced in a fixed order through `workspace`, ln_mix_workspace_size
+ * bytes). n in 1..3, C a multiple of 128 up to 1024; x, w, b, mix, grad_x
+ * 16-byte aligned, bf16 tensors 8-byte aligned; unused output pointers null.
+ */
+WKV_API size_t ln_mix_workspace_size(int n, int64_t B, int64_t T, int64_t C);
+WKV_API int ln_mix_forward(int n, const float* x, const float* w, const float* b, const float* mix,
+                           void* out0, void* out1, void* out2, float* mean, float* rstd, int64_t B,
+                           int64_t T, int64_t C, float eps, void* stream);
+WKV_API int ln_mix_backward(int n, const void* grad_out0, const void* grad_out1,
+                            const void* grad_out2, const float* x, const float* w, const float* b,
+                            const float* mix, const float* mean, const float* rstd, float* grad_x,
+                            float* grad_w, float* grad_b, float* grad_mix, void* workspace,
+                            size_t workspace_bytes, int64_t B, int64_t T, int64_t C, void* stream);
+
+/*
  * Forward/backward with a saved forward state (no reference counterpart; an
  * optimisation of wkv_forward/wkv_backward). wkv_forward_with_state computes y exactly as
  * wkv_forward and also stores the recurrence state at every 16th step into

@@ -19,6 +19,7 @@
 
 #include "spikegpt_wkv.h"
 #include "lif.cuh"
+#include "ln_mix.cuh"
 #include "wkv_step.cuh"
 #include "wkv_tp.cuh"
 
@@ -41,12 +42,14 @@ __device__ unsigned g_device_error_flags = 0;
 
 enum Kind {
   K_FWD_Y, K_FWD_STATE, K_BWD_GRAD, K_BWD_ADJ, K_CARRY_FWD, K_CARRY_ADJ, K_STEP, K_LIF_FWD, K_LIF_BWD,
+  K_MIX_FWD, K_MIX_BWD, K_MIX_RED,
   K_COUNT
 };
 const char* const kKindNames[K_COUNT] = {
     "wkv_fwd_kernel<y>",      "wkv_fwd_kernel<state>", "wkv_bwd_kernel<grad>",
     "wkv_bwd_kernel<adjoint>", "wkv_carry_fwd_kernel",  "wkv_carry_adj_kernel",
-    "wkv_step_kernel",        "lif_fwd_kernel",        "lif_bwd_kernel"};
+    "wkv_step_kernel",        "lif_fwd_kernel",        "lif_bwd_kernel",
+    "ln_mix_fwd_kernel",      "ln_mix_bwd_kernel",     "ln_mix_reduce_kernel"};
 
 std::atomic<long long> g_launches[K_COUNT];
 std::atomic<bool> g_timing{false};
@@ -1040,6 +1043,158 @@ int lif_backward(int dtype, const void* grad_spikes, const void* x, const float*
     case WKV_DTYPE_BF16: return lif_launch_backward<__nv_bfloat16>(a, tma, st);
     default: return lif_launch_backward<__half>(a, tma, st);
   }
+}
+
+}  // extern "C"
+
+namespace {
+
+int mix_check(int n, int64_t B, int64_t T, int64_t C) {
+  if (n < 1 || n > kMixMax) return fail(WKV_ERR_INVALID_ARGUMENT, "n must be 1..%d, got %d", kMixMax, n);
+  if (B < 0 || T < 0 || C <= 0) return fail(WKV_ERR_INVALID_ARGUMENT, "bad sizes B=%lld T=%lld C=%lld",
+                                            (long long)B, (long long)T, (long long)C);
+  if (C % 128 != 0 || C > 128 * kMixMaxGroups)
+    return fail(WKV_ERR_INVALID_ARGUMENT, "C must be a multiple of 128 up to %d, got %lld", 128 * kMixMaxGroups,
+                (long long)C);
+  if (B * T > (1ll << 31) - 1) return fail(WKV_ERR_INVALID_ARGUMENT, "B*T out of range");
+  return WKV_OK;
+}
+
+template <int G>
+void mix_fwd_go(const MixArgs& a, unsigned grid, cudaStream_t st) {
+  ln_mix_fwd_kernel<G><<<grid, 32 * kMixWarps, 0, st>>>(a);
+}
+template <int G, int N>
+void mix_bwd_go(const MixArgs& a, unsigned grid, cudaStream_t st) {
+  ln_mix_bwd_kernel<G, N><<<grid, 32 * kMixWarps, 0, st>>>(a);
+}
+template <int G>
+void mix_bwd_n(const MixArgs& a, unsigned grid, cudaStream_t st) {
+  if (a.n == 1) mix_bwd_go<G, 1>(a, grid, st);
+  else if (a.n == 2) mix_bwd_go<G, 2>(a, grid, st);
+  else mix_bwd_go<G, 3>(a, grid, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t ln_mix_workspace_size(int n, int64_t B, int64_t T, int64_t C) {
+  if (mix_check(n, B, T, C)) return 0;
+  const int64_t chunks = B * ((T + kMixRows - 1) / kMixRows);
+  return round_up((size_t)chunks * (2 + n) * C * sizeof(float));
+}
+
+int ln_mix_forward(int n, const float* x, const float* w, const float* b, const float* mix, void* out0, void* out1,
+                   void* out2, float* mean, float* rstd, int64_t B, int64_t T, int64_t C, float eps, void* stream) {
+  g_last_error[0] = '\0';
+  int rc = mix_check(n, B, T, C);
+  if (rc) return rc;
+  if (B == 0 || T == 0) return WKV_OK;
+  void* outs[kMixMax] = {out0, out1, out2};
+  if (!x || !w || !b || !mix || !mean || !rstd) return fail(WKV_ERR_INVALID_ARGUMENT, "null pointer");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(b) || !aligned16(mix))
+    return fail(WKV_ERR_INVALID_ARGUMENT, "x, w, b and mix must be 16-byte aligned");
+  MixArgs a{};
+  for (int i = 0; i < n; ++i) {
+    if (!outs[i] || (reinterpret_cast<uintptr_t>(outs[i]) & 7u))
+      return fail(WKV_ERR_INVALID_ARGUMENT, "output %d must be non-null and 8-byte aligned", i);
+    a.out[i] = static_cast<__nv_bfloat16*>(outs[i]);
+  }
+  a.x = x;
+  a.w = w;
+  a.b = b;
+  a.mix = mix;
+  a.mean = mean;
+  a.rstd = rstd;
+  a.n = n;
+  a.B = (int)B;
+  a.T = (int)T;
+  a.C = (int)C;
+  a.nct = (int)((T + kMixRows - 1) / kMixRows);
+  a.eps = eps;
+  const unsigned grid = (unsigned)((B * a.nct + kMixWarps - 1) / kMixWarps);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  launch(K_MIX_FWD, st, [&] {
+    switch (C / 128) {
+      case 1: mix_fwd_go<1>(a, grid, st); break;
+      case 2: mix_fwd_go<2>(a, grid, st); break;
+      case 3: mix_fwd_go<3>(a, grid, st); break;
+      case 4: mix_fwd_go<4>(a, grid, st); break;
+      case 5: mix_fwd_go<5>(a, grid, st); break;
+      case 6: mix_fwd_go<6>(a, grid, st); break;
+      case 7: mix_fwd_go<7>(a, grid, st); break;
+      default: mix_fwd_go<8>(a, grid, st); break;
+    }
+  });
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? WKV_OK : cuda_fail(e, "ln_mix forward launch");
+}
+
+int ln_mix_backward(int n, const void* g0, const void* g1, const void* g2, const float* x, const float* w,
+                    const float* b, const float* mix, const float* mean, const float* rstd, float* gx, float* gw,
+                    float* gb, float* gmix, void* workspace, size_t workspace_bytes, int64_t B, int64_t T,
+                    int64_t C, void* stream) {
+  g_last_error[0] = '\0';
+  int rc = mix_check(n, B, T, C);
+  if (rc) return rc;
+  if (!gw || !gb || !gmix) return fail(WKV_ERR_INVALID_ARGUMENT, "null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (B == 0 || T == 0) {  // empty batch: zero parameter gradients
+    cudaMemsetAsync(gw, 0, C * sizeof(float), st);
+    cudaMemsetAsync(gb, 0, C * sizeof(float), st);
+    cudaMemsetAsync(gmix, 0, n * C * sizeof(float), st);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? WKV_OK : cuda_fail(e, "ln_mix backward");
+  }
+  const void* gs[kMixMax] = {g0, g1, g2};
+  if (!x || !w || !b || !mix || !mean || !rstd || !gx) return fail(WKV_ERR_INVALID_ARGUMENT, "null pointer");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(b) || !aligned16(mix) || !aligned16(gx))
+    return fail(WKV_ERR_INVALID_ARGUMENT, "x, w, b, mix and grad_x must be 16-byte aligned");
+  const size_t need = ln_mix_workspace_size(n, B, T, C);
+  if (workspace_bytes < need || !workspace)
+    return fail(WKV_ERR_WORKSPACE_TOO_SMALL, "ln_mix backward needs %zu workspace bytes, got %zu", need,
+                workspace_bytes);
+  MixArgs a{};
+  for (int i = 0; i < n; ++i) {
+    if (!gs[i] || (reinterpret_cast<uintptr_t>(gs[i]) & 7u))
+      return fail(WKV_ERR_INVALID_ARGUMENT, "gradient %d must be non-null and 8-byte aligned", i);
+    a.gout[i] = static_cast<const __nv_bfloat16*>(gs[i]);
+  }
+  a.x = x;
+  a.w = w;
+  a.b = b;
+  a.mix = mix;
+  a.mean = const_cast<float*>(mean);
+  a.rstd = const_cast<float*>(rstd);
+  a.gx = gx;
+  a.partial = static_cast<float*>(workspace);
+  a.n = n;
+  a.B = (int)B;
+  a.T = (int)T;
+  a.C = (int)C;
+  a.nct = (int)((T + kMixRows - 1) / kMixRows);
+  const int chunks = (int)(B * a.nct);
+  const unsigned grid = (unsigned)((chunks + kMixWarps - 1) / kMixWarps);
+  launch(K_MIX_BWD, st, [&] {
+    switch (C / 128) {
+      case 1: mix_bwd_n<1>(a, grid, st); break;
+      case 2: mix_bwd_n<2>(a, grid, st); break;
+      case 3: mix_bwd_n<3>(a, grid, st); break;
+      case 4: mix_bwd_n<4>(a, grid, st); break;
+      case 5: mix_bwd_n<5>(a, grid, st); break;
+      case 6: mix_bwd_n<6>(a, grid, st); break;
+      case 7: mix_bwd_n<7>(a, grid, st); break;
+      default: mix_bwd_n<8>(a, grid, st); break;
+    }
+  });
+  const int rows = 2 + n;
+  launch(K_MIX_RED, st, [&] {
+    ln_mix_reduce_kernel<<<(unsigned)((rows * C + 255) / 256), 256, 0, st>>>(a.partial, chunks, rows, (int)C, gw, gb,
+                                                                          gmix);
+  });
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? WKV_OK : cuda_fail(e, "ln_mix backward launch");
 }
 
 int wkv_kernel_kinds(void) { return K_COUNT; }

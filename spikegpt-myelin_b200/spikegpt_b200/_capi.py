@@ -82,6 +82,13 @@ def lib() -> ctypes.CDLL:
         handle.lif_forward.restype = ci
         handle.lif_backward.argtypes = [ci, vp, vp, vp, sz, vp, i64, i64, i64, f32, f32, f32, f32, vp]
         handle.lif_backward.restype = ci
+        handle.ln_mix_workspace_size.argtypes = [ci, i64, i64, i64]
+        handle.ln_mix_workspace_size.restype = sz
+        handle.ln_mix_forward.argtypes = [ci, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, f32, vp]
+        handle.ln_mix_forward.restype = ci
+        handle.ln_mix_backward.argtypes = [ci, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, sz,
+                                           i64, i64, i64, vp]
+        handle.ln_mix_backward.restype = ci
         handle.wkv_state_size.argtypes = [ci, i64, i64, i64]
         handle.wkv_state_size.restype = sz
         handle.wkv_forward_with_state.argtypes = [ci, vp, vp, vp, vp, vp, vp, sz, i64, i64, i64, vp, sz, vp]
@@ -173,4 +180,4 @@ def declared_symbols() -> list[str]:
     import re
 
     text = HEADER_PATH.read_text()
-    return sorted(set(re.findall(r"WKV_API\s+[\w\s\*]+?\b((?:wkv|lif)_\w+)\s*\(", text)))
+    return sorted(set(re.findall(r"WKV_API\s+[\w\s\*]+?\b((?:wkv|lif|ln_mix)_\w+)\s*\(", text)))

@@ -27,6 +27,7 @@ import torch
 import torch.nn.functional as F
 from torch import Tensor, nn
 
+from . import fused
 from .lif import surrogate_lif
 from .wkv import weighted_key_value_cuda
 from .wkv_bf16 import weighted_key_value_cuda_bf16io
@@ -110,9 +111,14 @@ class TimeMix(nn.Module):
         self.output = nn.Linear(n_embd, n_embd, bias=False)
 
     def forward(self, x: Tensor) -> Tensor:
-        k = self.key(_shift_mix(x, self.time_mix_k))
-        v = self.value(_shift_mix(x, self.time_mix_v))
-        r = torch.sigmoid(self.receptance(_shift_mix(x, self.time_mix_r)))
+        return self.from_mixed(_shift_mix(x, self.time_mix_k), _shift_mix(x, self.time_mix_v),
+                               _shift_mix(x, self.time_mix_r))
+
+    def from_mixed(self, xk: Tensor, xv: Tensor, xr: Tensor) -> Tensor:
+        """The sublayer from its three token-shift-mixed inputs."""
+        k = self.key(xk)
+        v = self.value(xv)
+        r = torch.sigmoid(self.receptance(xr))
         if k.dtype in (torch.bfloat16, torch.float16):
             wkv = weighted_key_value_cuda_bf16io(k, v, self.time_decay, self.time_first)
         else:
@@ -133,8 +139,12 @@ class ChannelMix(nn.Module):
         self.value = nn.Linear(4 * n_embd, n_embd, bias=False)
 
     def forward(self, x: Tensor) -> Tensor:
-        k = torch.relu(self.key(_shift_mix(x, self.time_mix_k))).square()
-        r = torch.sigmoid(self.receptance(_shift_mix(x, self.time_mix_r)))
+        return self.from_mixed(_shift_mix(x, self.time_mix_k), _shift_mix(x, self.time_mix_r))
+
+    def from_mixed(self, xk: Tensor, xr: Tensor) -> Tensor:
+        """The sublayer from its two token-shift-mixed inputs."""
+        k = torch.relu(self.key(xk)).square()
+        r = torch.sigmoid(self.receptance(xr))
         return r * self.value(k)
 
 
@@ -159,11 +169,27 @@ class Block(nn.Module):
         return surrogate_lif(x, tau=cfg.lif_tau, threshold=cfg.lif_threshold, reset=cfg.lif_reset,
                              surrogate_slope=cfg.surrogate_slope)
 
+    @staticmethod
+    def _fused(x: Tensor) -> bool:
+        # Under bf16 autocast the projections take bf16 inputs, which the fused
+        # LayerNorm + token-shift kernel produces directly.
+        return (torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16
+                and fused.supported(x))
+
     def forward(self, x: Tensor) -> Tensor:
         if self.ln0 is not None:
             x = self.ln0(x)
-        x = x + self._lif(self.att(self.ln1(x)))
-        x = x + self._lif(self.ffn(self.ln2(x)))
+        if self._fused(x):
+            att, ffn = self.att, self.ffn
+            xk, xv, xr = fused.ln_shift_mix(x, self.ln1.weight, self.ln1.bias,
+                                            [att.time_mix_k, att.time_mix_v, att.time_mix_r], self.ln1.eps)
+            x = x + self._lif(att.from_mixed(xk, xv, xr))
+            xk, xr = fused.ln_shift_mix(x, self.ln2.weight, self.ln2.bias, [ffn.time_mix_k, ffn.time_mix_r],
+                                        self.ln2.eps)
+            x = x + self._lif(ffn.from_mixed(xk, xr))
+        else:
+            x = x + self._lif(self.att(self.ln1(x)))
+            x = x + self._lif(self.ffn(self.ln2(x)))
         return self.dropout(x)
 
 

@@ -1,0 +1,90 @@
+"""GPU parity of the fused LayerNorm + token-shift mixing op against the
+eager float32 computation it replaces (LayerNorm, shift-mix, bf16 rounding):
+outputs within one bf16 rounding (2e-2 relative), input and parameter
+gradients within 1e-4 of their scale (float32 sums in a different order)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from spikegpt_b200 import _capi
+from spikegpt_b200.fused import ln_shift_mix
+
+pytestmark = pytest.mark.gpu
+
+
+def _eager(x, w, b, mixes, eps):
+    h = F.layer_norm(x, (x.shape[-1],), w, b, eps)
+    prev = F.pad(h[:, :-1], (0, 0, 1, 0))
+    return [(h * m + prev * (1.0 - m)).to(torch.bfloat16) for m in mixes]
+
+
+def _rel(a, b):
+    a, b = a.double(), b.double()
+    return float((a - b).abs().max() / max(float(b.abs().max()), 1e-30))
+
+
+@pytest.mark.parametrize("shape,n", [((2, 70, 128), 3), ((3, 200, 512), 3), ((1, 65, 512), 2), ((2, 33, 768), 3),
+                                     ((1, 1, 256), 1)])
+def test_forward_backward_match_eager(cuda, shape, n):
+    g = torch.Generator(device="cpu").manual_seed(sum(shape) + n)
+    b_, t, c = shape
+    x = (torch.randn(shape, generator=g) * 2 + 0.5).to(cuda).requires_grad_()
+    w = (1 + 0.3 * torch.randn(c, generator=g)).to(cuda).requires_grad_()
+    b = (0.2 * torch.randn(c, generator=g)).to(cuda).requires_grad_()
+    mixes = [torch.rand(1, 1, c, generator=g).to(cuda).requires_grad_() for _ in range(n)]
+    grads = [torch.randn(shape, generator=g).to(cuda).to(torch.bfloat16) for _ in range(n)]
+
+    outs = ln_shift_mix(x, w, b, mixes)
+    torch.autograd.backward(outs, grads)
+    got = [o.detach().float() for o in outs]
+    gx, gw, gb, gm = x.grad.clone(), w.grad.clone(), b.grad.clone(), [m.grad.clone() for m in mixes]
+    for p in [x, w, b, *mixes]:
+        p.grad = None
+    ref = _eager(x, w, b, mixes, 1e-5)
+    torch.autograd.backward(ref, grads)
+    for o, r in zip(got, ref):
+        assert _rel(o, r.float()) <= 2e-2
+    assert _rel(gx, x.grad) <= 1e-4
+    assert _rel(gw, w.grad) <= 1e-4
+    assert _rel(gb, b.grad) <= 1e-4
+    for a, m in zip(gm, mixes):
+        assert _rel(a, m.grad) <= 1e-4
+
+
+def test_deterministic_parameter_gradients(cuda):
+    x = torch.randn(4, 300, 512, device=cuda, requires_grad=True)
+    w = torch.ones(512, device=cuda, requires_grad=True)
+    b = torch.zeros(512, device=cuda, requires_grad=True)
+    m = torch.rand(512, device=cuda, requires_grad=True)
+    gr = torch.randn(4, 300, 512, device=cuda).to(torch.bfloat16)
+    res = []
+    for _ in range(2):
+        (o,) = ln_shift_mix(x, w, b, [m])
+        o.backward(gr)
+        res.append((w.grad.clone(), m.grad.clone()))
+        w.grad = m.grad = x.grad = None
+    assert torch.equal(res[0][0], res[1][0]) and torch.equal(res[0][1], res[1][1])
+
+
+def test_errors(cuda):
+    x = torch.randn(2, 8, 100, device=cuda)
+    with pytest.raises(ValueError):
+        ln_shift_mix(x, torch.ones(100, device=cuda), torch.zeros(100, device=cuda), [torch.zeros(100, device=cuda)])
+    x = torch.randn(2, 8, 128, device=cuda)
+    with pytest.raises(ValueError):
+        ln_shift_mix(x, torch.ones(128, device=cuda), torch.zeros(128, device=cuda), [])
+
+
+def test_kernels_are_counted(cuda):
+    before = _capi.launch_counts()
+    x = torch.randn(1, 64, 128, device=cuda, requires_grad=True)
+    (o,) = ln_shift_mix(x, torch.ones(128, device=cuda), torch.zeros(128, device=cuda), [torch.rand(128, device=cuda)])
+    o.float().sum().backward()
+    torch.cuda.synchronize()
+    after = _capi.launch_counts()
+    for k in ("ln_mix_fwd_kernel", "ln_mix_bwd_kernel", "ln_mix_reduce_kernel"):
+        assert after[k] > before.get(k, 0)
