@@ -245,17 +245,27 @@ __global__ void __launch_bounds__(32 * kMixWarps) ln_mix_bwd_kernel(const MixArg
   }
 }
 
-// Column sums of the per-chunk partials, chunks in order: out[k][c] for the
-// 2 + n rows k (dw, db, dm_i). One thread per (k, c).
-__global__ void ln_mix_reduce_kernel(const float* partial, int nchunks, int rows, int C, float* gw, float* gb,
-                                     float* gmix) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= rows * C) return;
-  const int k = i / C, c = i % C;
-  double s = 0.0;
-  for (int j = 0; j < nchunks; ++j) s += partial[((size_t)j * rows + k) * C + c];
+// Column sums of the per-chunk partials: out[k][c] for the 2 + n rows k (dw,
+// db, dm_i). A CTA of 32 x 32 threads takes 32 columns of one row k; thread
+// (y, x) sums the chunks y, y + 32, ... of column x, then the 32 partial sums
+// of a column are added in y order (a fixed order: the result does not depend
+// on timing).
+__global__ void __launch_bounds__(1024) ln_mix_reduce_kernel(const float* partial, int nchunks, int rows, int C,
+                                                             float* gw, float* gb, float* gmix) {
+  __shared__ float part[32][33];
+  const int k = blockIdx.y;
+  const int c = blockIdx.x * 32 + threadIdx.x;
+  float s = 0.f;
+  if (c < C)
+    for (int j = threadIdx.y; j < nchunks; j += 32) s += partial[((size_t)j * rows + k) * C + c];
+  part[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y != 0 || c >= C) return;
+  float t = 0.f;
+#pragma unroll 8
+  for (int y = 0; y < 32; ++y) t += part[y][threadIdx.x];
   float* dst = k == 0 ? gw + c : k == 1 ? gb + c : gmix + (size_t)(k - 2) * C + c;
-  *dst = static_cast<float>(s);
+  *dst = t;
 }
 
 }  // namespace wkv

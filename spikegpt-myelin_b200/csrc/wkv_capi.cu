@@ -1190,8 +1190,8 @@ int ln_mix_backward(int n, const void* g0, const void* g1, const void* g2, const
   });
   const int rows = 2 + n;
   launch(K_MIX_RED, st, [&] {
-    ln_mix_reduce_kernel<<<(unsigned)((rows * C + 255) / 256), 256, 0, st>>>(a.partial, chunks, rows, (int)C, gw, gb,
-                                                                          gmix);
+    ln_mix_reduce_kernel<<<dim3((unsigned)((C + 31) / 32), (unsigned)rows), dim3(32, 32), 0, st>>>(
+        a.partial, chunks, rows, (int)C, gw, gb, gmix);
   });
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? WKV_OK : cuda_fail(e, "ln_mix backward launch");

@@ -142,8 +142,13 @@ class ChannelMix(nn.Module):
         return self.from_mixed(_shift_mix(x, self.time_mix_k), _shift_mix(x, self.time_mix_r))
 
     def from_mixed(self, xk: Tensor, xr: Tensor) -> Tensor:
-        """The sublayer from its two token-shift-mixed inputs."""
-        k = torch.relu(self.key(xk)).square()
+        """The sublayer from its two token-shift-mixed inputs. The square is
+        taken in the key's dtype: under bf16 autocast, square (pow) would be
+        computed in float32 and cast back for the value projection, which
+        rounds the same exact square to bf16 once either way."""
+        k = torch.relu(self.key(xk))
+        with torch.autocast("cuda", enabled=False):
+            k = torch.square(k)
         r = torch.sigmoid(self.receptance(xr))
         return r * self.value(k)
 
