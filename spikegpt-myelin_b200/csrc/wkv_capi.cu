@@ -946,7 +946,8 @@ int lif_launch_forward(LifArgs& a, bool tma, cudaStream_t st) {
 template <typename IO, bool kTma, bool kPlain>
 void lif_bwd_go(const LifArgs& a, const CUtensorMap& mx, const CUtensorMap& mg, const CUtensorMap& mst,
                 const CUtensorMap& mo, unsigned grid, size_t sm, cudaStream_t st) {
-  lif_bwd_kernel<IO, kTma, kPlain><<<grid, 32 * kLifWarps, sm, st>>>(a, mx, mg, mst, mo);
+  if constexpr (kTma) lif_bwd_ws_kernel<IO, kPlain><<<grid, kLifWsThreads, sm, st>>>(a, mx, mg, mst, mo);
+  else lif_bwd_kernel<IO, false, kPlain><<<grid, 32 * kLifWarps, sm, st>>>(a, mx, mg, mst, mo);
 }
 
 template <typename IO>
@@ -962,19 +963,23 @@ int lif_launch_backward(LifArgs& a, bool tma, cudaStream_t st) {
   std::memset(&mst, 0, sizeof(mst));
   std::memset(&mo, 0, sizeof(mo));
   int rc;
-  if (tma && ((rc = make_map(&mx, dt, a.x, a.B, a.T, a.C, lif_bwd_rows<IO>())) ||
-              (rc = make_map(&mg, dt, a.gs, a.B, a.T, a.C, lif_bwd_rows<IO>())) ||
-              (rc = make_map(&mo, dt, a.gx, a.B, a.T, a.C, lif_bwd_rows<IO>())) ||
-              (rc = make_map(&mst, WKV_DTYPE_F32, a.state, a.B, a.ntiles, a.C, lif_bwd_rows<IO>() / kSub))))
+  constexpr int WR = lif_ws_rows<IO>();
+  if (tma && ((rc = make_map(&mx, dt, a.x, a.B, a.T, a.C, WR, kLifWsCols)) ||
+              (rc = make_map(&mg, dt, a.gs, a.B, a.T, a.C, WR, kLifWsCols)) ||
+              (rc = make_map(&mo, dt, a.gx, a.B, a.T, a.C, WR, kLifWsCols)) ||
+              (rc = make_map(&mst, WKV_DTYPE_F32, a.state, a.B, a.ntiles, a.C, WR / kSub, kLifWsCols))))
     return rc;
   const bool plain = lif_plain_test(a);
-  const size_t sm = kLifWarps * lif_bwd_smem_bytes<IO>();
-  cudaError_t e = tma ? (plain ? allow_smem(lif_bwd_kernel<IO, true, true>, sm)
-                               : allow_smem(lif_bwd_kernel<IO, true, false>, sm))
+  const size_t sm = tma ? lif_ws_bwd_smem_bytes<IO>() : kLifWarps * lif_bwd_smem_bytes<IO>();
+  cudaError_t e = tma ? (plain ? allow_smem(lif_bwd_ws_kernel<IO, true>, sm)
+                               : allow_smem(lif_bwd_ws_kernel<IO, false>, sm))
                       : (plain ? allow_smem(lif_bwd_kernel<IO, false, true>, sm)
                                : allow_smem(lif_bwd_kernel<IO, false, false>, sm));
   if (e != cudaSuccess) return cuda_fail(e, "setting the LIF kernel's shared memory size");
-  const unsigned grid = (unsigned)(((int64_t)a.ncblk * a.B + kLifWarps - 1) / kLifWarps);
+  // TMA path: one CTA per kLifWarps channel blocks of a batch row (channel
+  // groups fastest); generic path: kLifWarps consecutive units per CTA
+  const unsigned grid = tma ? (unsigned)((a.ncblk + kLifWarps - 1) / kLifWarps) * (unsigned)a.B
+                            : (unsigned)(((int64_t)a.ncblk * a.B + kLifWarps - 1) / kLifWarps);
   launch(K_LIF_BWD, st, [&] {
     if (tma && plain) lif_bwd_go<IO, true, true>(a, mx, mg, mst, mo, grid, sm, st);
     else if (tma) lif_bwd_go<IO, true, false>(a, mx, mg, mst, mo, grid, sm, st);
