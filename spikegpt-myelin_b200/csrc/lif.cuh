@@ -522,8 +522,8 @@ __global__ void __launch_bounds__(32 * kLifWarps, 1) lif_bwd_kernel(const LifArg
 
 constexpr int kLifWsCols = kLifWarps * kLanes;     // channels per CTA (one box wide)
 constexpr int kLifWsThreads = 32 * (kLifWarps + 1);
-constexpr int kLifWsBwdStages = 3;
-constexpr int kLifWsOut = 3;
+constexpr int kLifWsBwdStages = 4;
+constexpr int kLifWsOut = 4;
 // Rows of a staged tile: 16 KB boxes (32 bf16/fp16 rows, 16 fp32 rows).
 template <typename T>
 __host__ __device__ constexpr int lif_ws_rows() {
