@@ -51,17 +51,7 @@ __host__ __device__ constexpr int lif_rows() {
 }
 constexpr int kLifTileBytes = 8192;
 constexpr int kLifFwdStages = 4;  // x tiles in flight per warp (forward)
-// The backward's stages hold 8 KB of x and 8 KB of grad: two of them fit
-// beside the output tiles for four warps. (Smaller tiles in a deeper ring
-// measured slower: the per-tile costs of barrier waits and TMA issue weigh
-// more than the shorter look-ahead.)
-constexpr int kLifBwdTileBytes = 8192;
-constexpr int kLifBwdStages = 2;  // (x, grad, checkpoint) tiles in flight per warp (backward)
-template <typename T>
-__host__ __device__ constexpr int lif_bwd_rows() {
-  return kLifBwdTileBytes / (kLanes * static_cast<int>(sizeof(T)));
-}
-constexpr int kLifOut = 2;        // staged output tiles per warp
+constexpr int kLifOut = 2;        // staged output tiles per warp (forward)
 // Independent warps per CTA: one warp lands on each of an SM's 4 schedulers.
 constexpr int kLifWarps = 4;
 __host__ __device__ constexpr size_t lif_align128(size_t n) { return (n + 127) / 128 * 128; }
@@ -71,26 +61,16 @@ __host__ __device__ constexpr size_t lif_align128(size_t n) { return (n + 127) /
 __host__ __device__ constexpr size_t lif_fwd_smem_bytes() {
   return lif_align128((size_t)(kLifFwdStages + kLifOut) * kLifTileBytes + 8 * kLifFwdStages);
 }
-template <typename T>
-__host__ __device__ constexpr size_t lif_bwd_stage_bytes() {
-  return (size_t)2 * kLifBwdTileBytes + (size_t)(lif_bwd_rows<T>() / kSub) * kLanes * sizeof(float);
-}
+// Generic-path backward: two kSub-row stages of x, grad and the checkpoint,
+// and one staged gradient tile, per warp.
 template <typename T>
 __host__ __device__ constexpr size_t lif_bwd_smem_bytes() {
-  return lif_align128((size_t)kLifBwdStages * lif_bwd_stage_bytes<T>() + (size_t)kLifOut * kLifBwdTileBytes +
-                      8 * kLifBwdStages);
+  return lif_align128((size_t)2 * (2 * kSub * kLanes * sizeof(T) + kLanes * sizeof(float)) +
+                      (size_t)kSub * kLanes * sizeof(T));
 }
 static_assert(lif_rows<float>() % kSub == 0 && lif_rows<__nv_bfloat16>() % kSub == 0, "sub-tiles");
-static_assert(lif_bwd_rows<float>() % kSub == 0 && lif_bwd_rows<__nv_bfloat16>() % kSub == 0, "sub-tiles");
-static_assert(lif_bwd_stage_bytes<float>() % 128 == 0 && lif_bwd_stage_bytes<__nv_bfloat16>() % 128 == 0,
-              "TMA stage alignment");
+static_assert(kLifWarps * lif_bwd_smem_bytes<float>() <= 227 * 1024, "generic LIF backward shared memory");
 static_assert(3 * kSub * kLanes * sizeof(float) + 8 <= lif_fwd_smem_bytes(), "generic forward staging");
-static_assert(2 * (2 * kSub * kLanes * sizeof(float) + kLanes * sizeof(float)) + 2 * kSub * kLanes * sizeof(float) +
-                      16 <=
-                  lif_bwd_smem_bytes<float>(),
-              "generic backward staging");
-static_assert(kLifWarps * lif_bwd_smem_bytes<float>() <= 227 * 1024, "LIF backward shared memory");
-static_assert(kLifWarps * lif_bwd_smem_bytes<__nv_bfloat16>() <= 227 * 1024, "LIF backward shared memory");
 static_assert(kLifWarps * lif_fwd_smem_bytes() <= 227 * 1024, "LIF forward shared memory");
 
 // Per-lane constants of the step for a pair of channels.
@@ -372,134 +352,70 @@ __global__ void __launch_bounds__(32 * kLifWarps, 1) lif_fwd_kernel(const LifArg
   if (kTma) bulk_wait_all();
 }
 
-// Backward, last sub-tile first, software-pipelined by one sub-tile: while the
-// adjoint sweep of sub-tile q runs, the membranes of sub-tile q - 1 are
-// recomputed from its checkpoint, two independent dependency chains in one
-// straight-line block. A stage holds one staged tile's x, grad and the
-// membrane checkpoints of its sub-tiles; staged tiles are visited last first
-// (the vt-th visited is tile ntt - 1 - vt, in stage vt % S, its input
-// gradients staged in output tile vt % kLifOut).
-template <typename T, bool kTma, bool kPlain>
-__global__ void __launch_bounds__(32 * kLifWarps, 1) lif_bwd_kernel(const LifArgs a,
-                                                                 const __grid_constant__ CUtensorMap tx,
-                                                                 const __grid_constant__ CUtensorMap tgs,
-                                                                 const __grid_constant__ CUtensorMap tst,
-                                                                 const __grid_constant__ CUtensorMap tgx) {
-  constexpr int S = kTma ? kLifBwdStages : 2;
-  constexpr int RT = kTma ? lif_bwd_rows<T>() : kSub;  // rows per staged tile
-  constexpr int QT = RT / kSub;                    // sub-tiles per staged tile
-  constexpr int E = RT * kLanes;
-  constexpr int SE = 2 * E * sizeof(T) + QT * kLanes * sizeof(float);  // stage bytes
+// Backward on the generic path (unaligned tensors), last sub-tile first,
+// software-pipelined by one sub-tile: while the adjoint sweep of sub-tile q
+// runs, the membranes of sub-tile q - 1 are recomputed from its checkpoint,
+// two independent dependency chains in one straight-line block. Each
+// kSub-row sub-tile is staged with plain loads (x, grad, checkpoint) into one
+// of two stages and its input gradients leave through a staged tile.
+template <typename T, bool kPlain>
+__global__ void __launch_bounds__(32 * kLifWarps, 1) lif_bwd_kernel(const LifArgs a) {
+  constexpr int E = kSub * kLanes;
+  constexpr int SE = 2 * E * sizeof(T) + kLanes * sizeof(float);  // stage bytes
   extern __shared__ __align__(128) unsigned char smem[];
   const int unit = blockIdx.x * kLifWarps + threadIdx.x / 32;  // (channel block, batch row)
   if (unit >= a.ncblk * a.B) return;
   unsigned char* base = smem + (threadIdx.x / 32) * lif_bwd_smem_bytes<T>();
-  T* obuf = reinterpret_cast<T*>(base + S * SE);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(obuf + kLifOut * E);
+  T* obuf = reinterpret_cast<T*>(base + 2 * SE);
   const int lane = threadIdx.x % 32;
   const int cb = unit % a.ncblk, b = unit / a.ncblk;
   const int c = cb * kLanes + 2 * lane;
   const bool v0 = c < a.C, v1 = c + 1 < a.C;
   const LifK k = lif_constants(a);
   const int nq = a.ntiles;
-  const int ntt = (a.T + RT - 1) / RT;
 
-  auto xs_of = [&](int vt) { return reinterpret_cast<T*>(base + (vt % S) * SE); };
-  auto gs_of = [&](int vt) { return xs_of(vt) + E; };
-  auto st_of = [&](int vt) { return reinterpret_cast<float*>(xs_of(vt) + 2 * E); };
-  auto issue = [&](int vt) {
-    const int jt = ntt - 1 - vt;
-    uint64_t* bar = &bars[vt % S];
-    mbar_arrive_expect_tx_if(lane == 0, bar, SE);
-    tma_load_3d_if(lane == 0, xs_of(vt), &tx, bar, cb * kLanes, jt * RT, b);
-    tma_load_3d_if(lane == 0, gs_of(vt), &tgs, bar, cb * kLanes, jt * RT, b);
-    tma_load_3d_if(lane == 0, st_of(vt), &tst, bar, cb * kLanes, jt * QT, b);
-  };
-  // waits for the vt-th visited staged tile (TMA) or stages it (plain loads)
-  auto acquire = [&](int vt) -> bool {
-    if (kTma) {
-      if (!__all_sync(kFull, mbar_wait_bounded(&bars[vt % S], (vt / S) & 1))) {
-        if (lane == 0) {
-          report_timeout(a.err);
-          for (int q = vt + 1; q < min(vt + S, ntt); ++q) mbar_wait_bounded(&bars[q % S], (q / S) & 1);
-        }
-        bulk_wait_all();
-        return false;
-      }
-    } else {
-      const int j = ntt - 1 - vt, t0 = j * RT, rows = min(RT, a.T - t0);
-      fill_tile(xs_of(vt), static_cast<const T*>(a.x), b, t0, rows, a.T, a.C, c, v0, v1, lane);
-      fill_tile(gs_of(vt), static_cast<const T*>(a.gs), b, t0, rows, a.T, a.C, c, v0, v1, lane);
-      const float* st = a.state + ((size_t)b * nq + j) * a.C + c;
-      st_of(vt)[2 * lane] = v0 ? st[0] : 0.f;
-      st_of(vt)[2 * lane + 1] = v1 ? st[1] : 0.f;
-      __syncwarp();
-    }
-    return true;
-  };
-  // sub-tile q lives in visited tile vt(q), at sub-tile index q % QT
-  auto vt_of = [&](int q) { return ntt - 1 - q / QT; };
-  auto x_sub = [&](int q) -> const T* { return xs_of(vt_of(q)) + (q % QT) * kSub * kLanes + 2 * lane; };
-  auto g_sub = [&](int q) -> const T* { return gs_of(vt_of(q)) + (q % QT) * kSub * kLanes + 2 * lane; };
-  auto o_sub = [&](int q) -> T* { return obuf + (vt_of(q) % kLifOut) * E + (q % QT) * kSub * kLanes + 2 * lane; };
-  auto v_sub = [&](int q) -> f2 {
-    return *reinterpret_cast<const f2*>(st_of(vt_of(q)) + (q % QT) * kLanes + 2 * lane);
-  };
-  if (kTma) {
-    if (lane == 0) {
-      for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
-      fence_barrier_init();
-      prefetch_tensormap(&tx);
-      prefetch_tensormap(&tgs);
-      prefetch_tensormap(&tst);
-      prefetch_tensormap(&tgx);
-    }
+  auto xs_of = [&](int q) { return reinterpret_cast<T*>(base + (q & 1) * SE); };
+  auto gs_of = [&](int q) { return xs_of(q) + E; };
+  auto st_of = [&](int q) { return reinterpret_cast<float*>(xs_of(q) + 2 * E); };
+  auto stage = [&](int q) {  // sub-tile q into stage q & 1
+    const int t0 = q * kSub, rows = min(kSub, a.T - t0);
+    fill_tile(xs_of(q), static_cast<const T*>(a.x), b, t0, rows, a.T, a.C, c, v0, v1, lane);
+    fill_tile(gs_of(q), static_cast<const T*>(a.gs), b, t0, rows, a.T, a.C, c, v0, v1, lane);
+    const float* st = a.state + ((size_t)b * nq + q) * a.C + c;
+    st_of(q)[2 * lane] = v0 ? st[0] : 0.f;
+    st_of(q)[2 * lane + 1] = v1 ? st[1] : 0.f;
     __syncwarp();
-    for (int vt = 0; vt < min(S, ntt); ++vt) issue(vt);
-  }
+  };
+  auto v_sub = [&](int q) -> f2 { return *reinterpret_cast<const f2*>(st_of(q) + 2 * lane); };
   if (nq == 0) return;
   const int last_rows = a.T - (nq - 1) * kSub;
   f2 va[kSub], vb[kSub];
-  if (!acquire(0)) return;
-  if (last_rows == kSub) lif_recompute<true, kPlain>(v_sub(nq - 1), x_sub(nq - 1), kSub, k, va);
-  else lif_recompute<false, kPlain>(v_sub(nq - 1), x_sub(nq - 1), last_rows, k, va);
+  stage(nq - 1);
+  if (last_rows == kSub) lif_recompute<true, kPlain>(v_sub(nq - 1), xs_of(nq - 1) + 2 * lane, kSub, k, va);
+  else lif_recompute<false, kPlain>(v_sub(nq - 1), xs_of(nq - 1) + 2 * lane, last_rows, k, va);
   f2 g = k.zero;  // dL/d(membrane after the current step), from later steps
   // sub-tile q: its membranes are in cur; those of q - 1 are recomputed into nxt
-  auto body = [&](int q, const f2(&cur)[kSub], f2(&nxt)[kSub]) -> bool {
-    const int u0 = q * kSub;
-    const int rows = min(kSub, a.T - u0);
-    if (q > 0 && q % QT == 0 && !acquire(vt_of(q - 1))) return false;
-    if (kTma && (q == nq - 1 || q % QT == QT - 1)) {
-      bulk_wait_read<kLifOut - 1>();  // the store of visited tile vt - kLifOut has read this output tile
-      __syncwarp();
-    }
+  auto body = [&](int q, const f2(&cur)[kSub], f2(&nxt)[kSub]) {
+    const int rows = min(kSub, a.T - q * kSub);
+    if (q > 0) stage(q - 1);
+    T* out = obuf + 2 * lane;
     if (q > 0 && rows == kSub) {
-      lif_recompute<true, kPlain>(v_sub(q - 1), x_sub(q - 1), kSub, k, nxt);
-      g = lif_grad_tile<true, kPlain>(g, cur, g_sub(q), o_sub(q), kSub, k);
+      lif_recompute<true, kPlain>(v_sub(q - 1), xs_of(q - 1) + 2 * lane, kSub, k, nxt);
+      g = lif_grad_tile<true, kPlain>(g, cur, gs_of(q) + 2 * lane, out, kSub, k);
     } else {
-      g = lif_grad_tile<false, kPlain>(g, cur, g_sub(q), o_sub(q), rows, k);
-      if (q > 0) lif_recompute<true, kPlain>(v_sub(q - 1), x_sub(q - 1), kSub, k, nxt);
+      g = lif_grad_tile<false, kPlain>(g, cur, gs_of(q) + 2 * lane, out, rows, k);
+      if (q > 0) lif_recompute<true, kPlain>(v_sub(q - 1), xs_of(q - 1) + 2 * lane, kSub, k, nxt);
     }
-    if (!kTma) {
-      __syncwarp();
-      drain_tile(obuf + (vt_of(q) % kLifOut) * E, static_cast<T*>(a.gx), b, u0, rows, a.T, a.C, c, v0, v1, lane);
-      __syncwarp();
-    } else if (q % QT == 0) {  // the visited tile is done: store its gradients, refill its stage
-      const int vt = vt_of(q);
-      fence_proxy_async_smem();
-      __syncwarp();
-      tma_store_3d_if(lane == 0, &tgx, obuf + (vt % kLifOut) * E, cb * kLanes, (ntt - 1 - vt) * RT, b);
-      bulk_commit();
-      if (vt + S < ntt) issue(vt + S);
-    }
-    return true;
+    __syncwarp();
+    drain_tile(obuf, static_cast<T*>(a.gx), b, q * kSub, rows, a.T, a.C, c, v0, v1, lane);
+    __syncwarp();
   };
 #pragma unroll 1
   for (int q = nq - 1; q >= 0; q -= 2) {
-    if (!body(q, va, vb)) return;
-    if (q == 0 || !body(q - 1, vb, va)) break;
+    body(q, va, vb);
+    if (q == 0) break;
+    body(q - 1, vb, va);
   }
-  if (kTma) bulk_wait_all();
 }
 
 // ---------------------------------------------- warp-specialized backward (TMA)

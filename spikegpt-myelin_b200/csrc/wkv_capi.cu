@@ -947,7 +947,7 @@ template <typename IO, bool kTma, bool kPlain>
 void lif_bwd_go(const LifArgs& a, const CUtensorMap& mx, const CUtensorMap& mg, const CUtensorMap& mst,
                 const CUtensorMap& mo, unsigned grid, size_t sm, cudaStream_t st) {
   if constexpr (kTma) lif_bwd_ws_kernel<IO, kPlain><<<grid, kLifWsThreads, sm, st>>>(a, mx, mg, mst, mo);
-  else lif_bwd_kernel<IO, false, kPlain><<<grid, 32 * kLifWarps, sm, st>>>(a, mx, mg, mst, mo);
+  else lif_bwd_kernel<IO, kPlain><<<grid, 32 * kLifWarps, sm, st>>>(a);
 }
 
 template <typename IO>
@@ -955,8 +955,8 @@ int lif_launch_backward(LifArgs& a, bool tma, cudaStream_t st) {
   const int dt = sizeof(IO) == 4 ? WKV_DTYPE_F32
                  : std::is_same<IO, __nv_bfloat16>::value ? WKV_DTYPE_BF16
                                                          : WKV_DTYPE_F16;
-  // x, grad and grad_x in lif_bwd_rows<IO>()-row boxes; the checkpoints
-  // of a staged tile's sub-tiles in one [sub-tiles][kLanes] float box
+  // TMA path: x, grad and grad_x in lif_ws_rows<IO>() x kLifWsCols boxes; the
+  // checkpoints of a staged tile's sub-tiles in one [sub-tiles][kLifWsCols] float box
   CUtensorMap mx, mg, mst, mo;
   std::memset(&mx, 0, sizeof(mx));
   std::memset(&mg, 0, sizeof(mg));
@@ -973,8 +973,8 @@ int lif_launch_backward(LifArgs& a, bool tma, cudaStream_t st) {
   const size_t sm = tma ? lif_ws_bwd_smem_bytes<IO>() : kLifWarps * lif_bwd_smem_bytes<IO>();
   cudaError_t e = tma ? (plain ? allow_smem(lif_bwd_ws_kernel<IO, true>, sm)
                                : allow_smem(lif_bwd_ws_kernel<IO, false>, sm))
-                      : (plain ? allow_smem(lif_bwd_kernel<IO, false, true>, sm)
-                               : allow_smem(lif_bwd_kernel<IO, false, false>, sm));
+                      : (plain ? allow_smem(lif_bwd_kernel<IO, true>, sm)
+                               : allow_smem(lif_bwd_kernel<IO, false>, sm));
   if (e != cudaSuccess) return cuda_fail(e, "setting the LIF kernel's shared memory size");
   // TMA path: one CTA per kLifWarps channel blocks of a batch row (channel
   // groups fastest); generic path: kLifWarps consecutive units per CTA
