@@ -62,11 +62,15 @@ WORKLOADS = {
 }
 WORKLOADS["lif"] = dict(kind="lif", B=64, T=1024, C=512, dtype="bf16", kscale=1.5,
                         desc="LIF fwd+bwd: B=64 T=1024 C=512 bf16 (a SpikeGPT-41M block activation)")
-WORKLOADS["train"] = dict(kind="train", global_batch=64, T=1024, zipf=1.1,
+WORKLOADS["train"] = dict(kind="train", model="41m", global_batch=64, T=1024, zipf=1.1,
                           desc="config 3: SpikeGPT-41M train step (12L/512d/V=256/ctx1024), global batch 64, "
                                "bf16 autocast, AdamW wd 0.1")
+WORKLOADS["train216m"] = dict(kind="train", model="216m", global_batch=32, T=1024, zipf=1.05,
+                              desc="config 4: 216M-class SpikeGPT train step (18L/768d/V=50257/ctx1024), "
+                                   "global batch 32, bf16 autocast, AdamW wd 0.1")
 LIF_METRIC = "LIF fwd+bwd algorithmic HBM throughput"
 TRAIN_METRIC = "SpikeGPT-41M train tokens/s"
+TRAIN_METRICS = {"41m": TRAIN_METRIC, "216m": "SpikeGPT-216M train tokens/s"}
 PEAKS_FALLBACK_TFLOPS = 1590.0
 STEP_METRIC = "WKV recurrent step algorithmic HBM throughput"
 STEP_BYTES = {"bf16": 2, "fp16": 2, "fp32": 4}
@@ -86,6 +90,8 @@ def parse_args():
     ap.add_argument("--profile", action="store_true", help="device loop only (for ncu): no CPU leg, e2e or clocks")
     ap.add_argument("--no-state", action="store_true",
                     help="time the self-contained op pair (backward re-runs the forward sweep)")
+    ap.add_argument("--eager", action="store_true",
+                    help="train workloads: launch the step's kernels eagerly instead of replaying a CUDA graph")
     return ap.parse_args()
 
 
@@ -887,17 +893,19 @@ def zipf_tokens(rng, shape, vocab: int, s: float):
 
 
 def run_train(args, wl):
-    """Data-parallel train step of SpikeGPT-41M (this package's model and ops):
-    global batch 64 x 1024 tokens split over the ranks (weak per-rank work
-    shrinks as ranks grow: strong scaling), bf16 autocast, fused AdamW with
-    weight decay 0.1, DDP gradient all-reduce over NCCL for N > 1. A step is
-    forward, backward and the optimizer step on resident synthetic tokens."""
+    """Data-parallel train step of SpikeGPT (this package's model and ops): the
+    global batch split over the ranks (per-rank work shrinks as ranks grow:
+    strong scaling), bf16 autocast, fused AdamW with weight decay 0.1. A step
+    is forward, backward, the gradient all-reduce (NCCL, N > 1) and the
+    optimizer step on resident synthetic tokens; forward and backward replay
+    one CUDA graph (``spikegpt_b200.train.TrainStep``) unless --eager."""
     import torch
     import torch.distributed as dist
 
     from spikegpt_b200 import _capi
-    from spikegpt_b200.model import SPIKEGPT_41M, SpikeGPT, flops_per_token
+    from spikegpt_b200.model import SPIKEGPT_41M, SPIKEGPT_216M, SpikeGPT, flops_per_token
     from spikegpt_b200.sharding import max_over_ranks
+    from spikegpt_b200.train import TrainStep
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -908,28 +916,21 @@ def run_train(args, wl):
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    cfg = {"41m": SPIKEGPT_41M, "216m": SPIKEGPT_216M}[wl["model"]]
     gb, t = wl["global_batch"], wl["T"]
     if gb % world:
         raise SystemExit(f"global batch {gb} does not split over {world} ranks")
     b = gb // world
     torch.manual_seed(0)
-    model = SpikeGPT(SPIKEGPT_41M).to(dev)
-    ddp = model
-    if world > 1:
-        ddp = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local], broadcast_buffers=False)
+    model = SpikeGPT(cfg).to(dev)
     opt = torch.optim.AdamW(model.parameters(), lr=6e-4, weight_decay=0.1, fused=True)
     rng = np.random.default_rng(rank)
-    ids_np = zipf_tokens(rng, (b, t + 1), SPIKEGPT_41M.vocab_size, wl["zipf"])
+    ids_np = zipf_tokens(rng, (b, t + 1), cfg.vocab_size, wl["zipf"])
     ids = torch.as_tensor(ids_np).to(dev)
     x, y = ids[:, :-1].contiguous(), ids[:, 1:].contiguous()
-
-    def step(xb, yb):
-        with torch.autocast("cuda", dtype=torch.bfloat16):
-            loss = ddp(xb, yb)
-        loss.backward()
-        opt.step()
-        opt.zero_grad(set_to_none=True)
-        return loss
+    launches_before = sum(_capi.launch_counts().values())
+    step = TrainStep(model, opt, (b, t), device=dev, graph=not args.eager)
+    capture_launches = sum(_capi.launch_counts().values()) - launches_before
 
     for _ in range(args.warmup):
         loss = step(x, y)
@@ -950,7 +951,9 @@ def run_train(args, wl):
     host1 = time.time()
     if world > 1:
         dist.barrier(device_ids=[local])
-    launches = sum(_capi.launch_counts().values()) - launches0
+    # eager launches go through the C ABI's counters; a graph replay runs the
+    # kernels counted while it was captured
+    launches = sum(_capi.launch_counts().values()) - launches0 + args.steps * step.captured_launches
     ms = max_over_ranks(ev0.elapsed_time(ev1), dev)
     if sampler:
         time.sleep(0.25)
@@ -958,17 +961,21 @@ def run_train(args, wl):
     clocks = sampler.summary(host0, host1) if sampler else None
     tokens = gb * t * args.steps
     value = tokens / (ms * 1e-3)
-    fpt = flops_per_token(SPIKEGPT_41M)
+    fpt = flops_per_token(cfg)
     pk = peaks()
     peak = float(pk.get("bf16_tflops", PEAKS_FALLBACK_TFLOPS))
     achieved = value * fpt / world / 1e12
+    name = {"41m": "SpikeGPT-41M", "216m": "SpikeGPT-216M"}[wl["model"]]
     result = {
-        "metric": TRAIN_METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic Zipf(1.1) token ids, seeded numpy PCG64 per rank",
-        "config": {"workload": wl["desc"], "global_batch": gb, "seq_len": t, "B_per_gpu": b,
+        "metric": TRAIN_METRICS[wl["model"]], "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": f"synthetic Zipf({wl['zipf']}) token ids, seeded numpy PCG64 per rank",
+        "config": {"workload": wl["desc"], "model": name, "global_batch": gb, "seq_len": t, "B_per_gpu": b,
                    "params": sum(p.numel() for p in model.parameters()),
-                   "parallelism": f"dp{world}" + (" (DDP, NCCL all-reduce)" if world > 1 else ""),
+                   "parallelism": f"dp{world}" + (" (flat-gradient NCCL all-reduce, AVG)" if world > 1 else ""),
+                   "launch": "eager" if args.eager else "CUDA graph (forward + backward), eager all-reduce "
+                                                         "and fused AdamW",
                    "l2": "model state and activations far above L2; no flush"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "flops_per_token": fpt,
@@ -976,6 +983,7 @@ def run_train(args, wl):
                      else "fallback 1.59 PFLOP/s", "traffic": None,
                      "note": "model FLOPs utilisation (6 x matmul weights per token)"},
         "loss": float(loss.item()), "gpu_launches": int(launches), "clocks": clocks,
+        "graph_capture_launches": int(capture_launches),
         "cpu_baseline": None,
         "cpu_baseline_note": "no CPU leg: the model step runs only on this package's CUDA ops, and the "
                              "reference's own CPU step needs myelin@68b8ebb, absent",
@@ -985,7 +993,7 @@ def run_train(args, wl):
 
         def e2e_step():
             d = hx.to(dev, non_blocking=True)
-            return step(d[:, :-1], d[:, 1:]).detach().to("cpu", non_blocking=True)
+            return step(d[:, :-1], d[:, 1:]).to("cpu", non_blocking=True)
 
         for _ in range(3):
             e2e_step()
@@ -1003,9 +1011,9 @@ def run_train(args, wl):
                          "path": "token ids copied from pinned host memory each step, loss read back"}
     if rank == 0:
         print(json.dumps(result), flush=True)
+    step.release()
     if world > 1:
         dist.barrier(device_ids=[local])
-        del ddp
         dist.destroy_process_group()
 
 
@@ -1015,7 +1023,7 @@ def main():
     if wl.get("kind") == "train":
         if args.impl == "reference":
             if int(os.environ.get("RANK", "0")) == 0:
-                print(json.dumps({"impl": "reference", "metric": TRAIN_METRIC,
+                print(json.dumps({"impl": "reference", "metric": TRAIN_METRICS[wl["model"]],
                                   "unavailable": "the reference's train step needs myelin@68b8ebb (absent) "
                                                  "for its LIF and spike functions"}), flush=True)
         else:

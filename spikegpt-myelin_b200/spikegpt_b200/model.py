@@ -60,6 +60,8 @@ class SpikeGPTConfig:
 
 
 SPIKEGPT_41M = SpikeGPTConfig(vocab_size=256, context_length=1024, n_layer=12, n_embd=512)
+# The 216M-class configuration: 18 layers, 768 wide, the GPT-2 BPE vocabulary.
+SPIKEGPT_216M = SpikeGPTConfig(vocab_size=50257, context_length=1024, n_layer=18, n_embd=768)
 
 
 class _HardSpike(torch.autograd.Function):

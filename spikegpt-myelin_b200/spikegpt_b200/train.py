@@ -1,0 +1,122 @@
+"""Data-parallel train step of the SpikeGPT model with the forward and backward
+replayed from one CUDA graph.
+
+The reference trains with eager PyTorch under DDP (src/spikegpt/train.py and
+its model, language.py:1361-1480). An eager step of SpikeGPT-41M launches
+about 1100 kernels; at 64 sequences per GPU their device time dominates, but
+with the batch split over 2 to 8 GPUs each kernel shrinks while the host time
+to launch it does not, and the step turns launch-bound. Here the forward and
+backward are captured once and replayed, so the host issues one graph launch,
+one all-reduce and the fused optimizer per step.
+
+Gradients live in one flat float32 buffer: every parameter's ``.grad`` is a
+view of it, the captured backward accumulates into those views after the
+captured zero fill, and a data-parallel step averages them with a single
+all-reduce (DDP's average of the ranks' gradients of their shard-mean
+losses: ``ReduceOp.AVG`` over NCCL; gloo sums and divides). That all-reduce
+and the optimizer step run outside the graph, on the current stream.
+
+``graph=False`` runs the same step eagerly (any device, any process group:
+the CPU tests use it over gloo).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+from torch import Tensor, nn
+
+from . import _capi
+
+
+class TrainStep:
+    """One optimizer step of ``model(ids, targets) -> loss`` per call.
+
+    ``batch_shape`` is the (rows, T) shape of this rank's token ids and
+    targets; every call must pass that shape. ``group`` is the data-parallel
+    process group (None: the default group when one is initialized, else no
+    exchange). ``autocast_dtype`` None runs without autocast.
+    """
+
+    def __init__(self, model: nn.Module, optimizer: torch.optim.Optimizer, batch_shape: tuple[int, int], *,
+                 device: torch.device | str, autocast_dtype: torch.dtype | None = torch.bfloat16,
+                 graph: bool = True, group=None, warmup: int = 3) -> None:
+        self.model = model
+        self.optimizer = optimizer
+        self.device = torch.device(device)
+        self.autocast_dtype = autocast_dtype
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        # NCCL averages in the collective; gloo has no AVG, so it sums and divides
+        self.avg = self.world > 1 and dist.get_backend(group) == "nccl"
+        if graph and self.device.type != "cuda":
+            raise ValueError("graph capture needs a CUDA device")
+        params = [p for p in model.parameters() if p.requires_grad]
+        if any(p.device != self.device or p.dtype != torch.float32 for p in params):
+            raise ValueError("TrainStep expects float32 parameters on its device")
+        total = sum(p.numel() for p in params)
+        self.grads = torch.zeros(total, dtype=torch.float32, device=self.device)
+        off = 0
+        for p in params:
+            n = p.numel()
+            p.grad = self.grads[off:off + n].view_as(p)
+            off += n
+        self.ids = torch.zeros(batch_shape, dtype=torch.long, device=self.device)
+        self.targets = torch.zeros(batch_shape, dtype=torch.long, device=self.device)
+        self.graph = None
+        self.loss = None
+        self.captured_launches = 0  # this package's kernels in the graph (each replay runs them again)
+        if graph:
+            self._capture(warmup)
+
+    def _forward_backward(self) -> Tensor:
+        self.grads.zero_()
+        if self.autocast_dtype is None:
+            loss = self.model(self.ids, self.targets)
+        else:
+            with torch.autocast(self.device.type, dtype=self.autocast_dtype):
+                loss = self.model(self.ids, self.targets)
+        loss.backward()
+        return loss.detach()
+
+    def _capture(self, warmup: int) -> None:
+        # Warm-up on a side stream (as graph capture requires), then capture.
+        # Neither touches the parameters: the optimizer does not run here.
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(max(1, warmup)):
+                self._forward_backward()
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        before = sum(_capi.launch_counts().values())
+        with torch.cuda.graph(self.graph):
+            self.loss = self._forward_backward()
+        self.captured_launches = sum(_capi.launch_counts().values()) - before
+
+    def __call__(self, ids: Tensor, targets: Tensor) -> Tensor:
+        """Copy the batch in, run forward and backward, average the gradients
+        over the ranks, step the optimizer. Returns the loss of this rank's
+        shard (a device tensor; with a graph, the same tensor every call)."""
+        if tuple(ids.shape) != tuple(self.ids.shape) or tuple(targets.shape) != tuple(self.targets.shape):
+            raise ValueError(f"batch shape {tuple(ids.shape)} differs from the captured {tuple(self.ids.shape)}")
+        self.ids.copy_(ids, non_blocking=True)
+        self.targets.copy_(targets, non_blocking=True)
+        if self.graph is not None:
+            self.graph.replay()
+            loss = self.loss
+        else:
+            loss = self._forward_backward()
+        if self.world > 1:
+            if self.avg:
+                dist.all_reduce(self.grads, op=dist.ReduceOp.AVG, group=self.group)
+            else:
+                dist.all_reduce(self.grads, op=dist.ReduceOp.SUM, group=self.group)
+                self.grads.div_(self.world)
+        self.optimizer.step()
+        return loss
+
+    def release(self) -> None:
+        """Drop the captured graph (before the process group is destroyed)."""
+        self.graph = None
+        self.loss = None

@@ -21,7 +21,8 @@ import pytest
 import torch
 from _wkvtest import scaled_err
 
-from spikegpt_b200.model import SPIKEGPT_41M, SpikeGPT, SpikeGPTConfig, flops_per_token, parameter_count
+from spikegpt_b200.model import (SPIKEGPT_41M, SPIKEGPT_216M, SpikeGPT, SpikeGPTConfig, flops_per_token,
+                                 parameter_count)
 
 GOLDEN = np.load(Path(__file__).resolve().parent / "golden" / "model_golden.npz")
 
@@ -43,6 +44,12 @@ def test_41m_parameters_and_flops():
     model = SpikeGPT(SPIKEGPT_41M)
     assert parameter_count(model) == 41_226_240
     assert flops_per_token(SPIKEGPT_41M) == pytest.approx(246.2e6, rel=1e-3)
+
+
+def test_216m_class_parameters():
+    # 18 x 13 x 768^2 matrix weights + 2 x 50257 x 768 embedding and head + the vectors
+    assert parameter_count(SpikeGPT(SPIKEGPT_216M)) == 215_368_704
+    assert flops_per_token(SPIKEGPT_216M) == pytest.approx(1059.7e6, rel=1e-4)
 
 
 def test_initial_values_match_reference():
