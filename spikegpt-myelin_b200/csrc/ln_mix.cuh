@@ -12,24 +12,31 @@
 //   dh[t]  = sum_i m_i g_i[t] + (1 - m_i) g_i[t+1]
 //   dx     = rstd (dh w - mean(dh w) - xhat mean(dh w xhat))      (LayerNorm)
 //   dw     = sum_rows dh xhat,  db = sum_rows dh,  dm_i = sum_rows g_i[t] (h[t] - h[t-1])
-// the column sums as per-warp partials reduced in a fixed order by
+// the column sums as per-CTA partials reduced in a fixed order by
 // ln_mix_reduce (deterministic).
 //
-// Layout: one warp per chunk of kMixRows consecutive steps of one sequence;
-// lane l holds channels g*128 + 4l .. 4l+3 of each 128-channel group g
-// (float4 loads of x, 8-byte bf16 stores). C is a multiple of 128, at most
-// kMixMaxGroups * 128. Memory-bound: forward reads x (4 B) and writes n bf16
-// outputs (2n B) per element; backward reads x and n gradients, writes dx.
+// Layout: a CTA of C/4 threads takes `rows` consecutive steps of one sequence,
+// one row at a time; thread j holds channels 4j .. 4j+3 (a float4 of x, an
+// 8-byte bf16 word of each output or gradient), so a row is one coalesced
+// 4C-byte read. Row sums (the statistics in the forward, the two LayerNorm
+// backward means) are block reductions: a warp butterfly, then the warps'
+// sums added in warp order through shared memory, double-buffered so one
+// barrier per reduction suffices. The next row's loads are issued before the
+// current row is processed. A thread needs few registers, so many CTAs share
+// an SM; `rows` (8..64) is chosen per launch so that a launch has about 8 CTAs
+// per SM whatever the batch. C is a multiple of 128, at most kMixMaxC.
+// Memory-bound: forward reads x (4 B) and writes n bf16 outputs (2n B) per
+// element; backward reads x and n gradients, writes dx.
 #pragma once
 
 #include "wkv_device.cuh"
 
 namespace wkv {
 
-constexpr int kMixMax = 3;         // mixing vectors per call (time mixing: key, value, receptance)
-constexpr int kMixRows = 64;       // steps per warp chunk
-constexpr int kMixWarps = 4;       // warps per CTA
-constexpr int kMixMaxGroups = 8;   // C <= 1024
+constexpr int kMixMax = 3;        // mixing vectors per call (time mixing: key, value, receptance)
+constexpr int kMixMaxC = 1024;    // channels: a CTA has C/4 <= 256 threads
+constexpr int kMixMinRows = 8;    // steps per CTA, at least
+constexpr int kMixMaxRows = 64;   // and at most
 
 struct MixArgs {
   const float* x;    // [B*T][C]
@@ -41,8 +48,10 @@ struct MixArgs {
   float* mean;     // [B*T]
   float* rstd;     // [B*T]
   float* gx;       // [B*T][C]
-  float* partial;  // [nchunks][2 + n][C]: dw, db, dm_0 .. dm_{n-1} per chunk
-  int n, B, T, C, nct;  // nct = chunks per sequence
+  float* partial;  // [B*nct][2 + n][C]: dw, db, dm_0 .. dm_{n-1} per CTA
+  int n, B, T, C;
+  int rows;  // steps per CTA
+  int nct;   // CTAs per sequence
   float eps;
 };
 
@@ -52,26 +61,42 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-template <int G>
-__device__ __forceinline__ void mix_load_row(const float* row, int lane, float4 (&v)[G]) {
-#pragma unroll
-  for (int g = 0; g < G; ++g) v[g] = *reinterpret_cast<const float4*>(row + g * 128 + 4 * lane);
+// Sum over the CTA of one value per thread (all threads get it): warp sums,
+// then the warps' sums in warp order. `slot` alternates between calls (two
+// buffers): a buffer is rewritten only after every thread has passed the
+// barrier of the call in between, so its readers are done with it.
+__device__ __forceinline__ float block_sum(float v, float (*red)[kMixMaxC / 128], int slot) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) red[slot][threadIdx.x >> 5] = v;
+  __syncthreads();
+  float s = 0.f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += red[slot][w];
+  return s;
 }
 
-// Row statistics as PyTorch's LayerNorm defines them (biased variance).
-template <int G>
-__device__ __forceinline__ void mix_stats(const float4 (&v)[G], int C, float eps, float& mu, float& rs) {
-  float s = 0.f;
-#pragma unroll
-  for (int g = 0; g < G; ++g) s += (v[g].x + v[g].y) + (v[g].z + v[g].w);
-  mu = warp_sum(s) / C;
-  float q = 0.f;
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const float a = v[g].x - mu, b = v[g].y - mu, c = v[g].z - mu, d = v[g].w - mu;
-    q += (a * a + b * b) + (c * c + d * d);
+// Two sums at once (one barrier).
+__device__ __forceinline__ float2 block_sum2(float u, float v, float2 (*red)[kMixMaxC / 128], int slot) {
+  u = warp_sum(u);
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) red[slot][threadIdx.x >> 5] = make_float2(u, v);
+  __syncthreads();
+  float2 s = make_float2(0.f, 0.f);
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+    s.x += red[slot][w].x;
+    s.y += red[slot][w].y;
   }
-  rs = rsqrtf(warp_sum(q) / C + eps);
+  return s;
+}
+
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+// Row statistics as PyTorch's LayerNorm defines them (biased variance), two
+// passes (mean, then the centred squares); uses reduction slots 0 and 1.
+__device__ __forceinline__ void mix_stats(float4 v, int C, float eps, float (*red)[kMixMaxC / 128], float& mu,
+                                          float& rs) {
+  mu = block_sum((v.x + v.y) + (v.z + v.w), red, 0) / C;
+  const float a = v.x - mu, b = v.y - mu, c = v.z - mu, d = v.w - mu;
+  rs = rsqrtf(block_sum((a * a + b * b) + (c * c + d * d), red, 1) / C + eps);
 }
 
 __device__ __forceinline__ float4 mix_norm(float4 v, float mu, float rs, float4 w, float4 b) {
@@ -84,170 +109,164 @@ __device__ __forceinline__ float mix1(float h, float p, float m, float om) {
   return __fadd_rn(__fmul_rn(h, m), __fmul_rn(p, om));
 }
 
-template <int G>
-__global__ void __launch_bounds__(32 * kMixWarps) ln_mix_fwd_kernel(const MixArgs a) {
-  const int lane = threadIdx.x & 31;
-  const int chunk = blockIdx.x * kMixWarps + (threadIdx.x >> 5);
-  if (chunk >= a.B * a.nct) return;
-  const int bi = chunk / a.nct, t0 = (chunk % a.nct) * kMixRows;
-  const int t1 = min(a.T, t0 + kMixRows);
-  float4 wv[G], bv[G];
-  mix_load_row<G>(a.w, lane, wv);
-  mix_load_row<G>(a.b, lane, bv);
-  const size_t row0 = (size_t)bi * a.T;
-  float4 hp[G];  // h[t-1]
-  if (t0 > 0) {
-    float4 v[G];
-    mix_load_row<G>(a.x + (row0 + t0 - 1) * a.C, lane, v);
-    float mu, rs;
-    mix_stats<G>(v, a.C, a.eps, mu, rs);
-#pragma unroll
-    for (int g = 0; g < G; ++g) hp[g] = mix_norm(v[g], mu, rs, wv[g], bv[g]);
-  } else {
-#pragma unroll
-    for (int g = 0; g < G; ++g) hp[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-#pragma unroll 1
-  for (int t = t0; t < t1; ++t) {
-    const size_t r = row0 + t;
-    float4 v[G];
-    mix_load_row<G>(a.x + r * a.C, lane, v);
-    float mu, rs;
-    mix_stats<G>(v, a.C, a.eps, mu, rs);
-    if (lane == 0) {
-      a.mean[r] = mu;
-      a.rstd[r] = rs;
-    }
-    float4 h[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) h[g] = mix_norm(v[g], mu, rs, wv[g], bv[g]);
-#pragma unroll 1
-    for (int i = 0; i < a.n; ++i) {
-      const float* mrow = a.mix + (size_t)i * a.C;
-      __nv_bfloat16* orow = a.out[i] + r * a.C;
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float4 m = *reinterpret_cast<const float4*>(mrow + g * 128 + 4 * lane);
-        const float o0 = mix1(h[g].x, hp[g].x, m.x, 1.f - m.x), o1 = mix1(h[g].y, hp[g].y, m.y, 1.f - m.y);
-        const float o2 = mix1(h[g].z, hp[g].z, m.z, 1.f - m.z), o3 = mix1(h[g].w, hp[g].w, m.w, 1.f - m.w);
-        __nv_bfloat162 lo = __floats2bfloat162_rn(o0, o1), hi = __floats2bfloat162_rn(o2, o3);
-        uint2 pk;
-        pk.x = *reinterpret_cast<uint32_t*>(&lo);
-        pk.y = *reinterpret_cast<uint32_t*>(&hi);
-        *reinterpret_cast<uint2*>(orow + g * 128 + 4 * lane) = pk;
-      }
-    }
-#pragma unroll
-    for (int g = 0; g < G; ++g) hp[g] = h[g];
-  }
-}
-
-// Four bf16 values (8 bytes) as floats.
-__device__ __forceinline__ float4 mix_grad4(const __nv_bfloat16* p) {
-  const uint2 pk = *reinterpret_cast<const uint2*>(p);
+// Four bf16 values (8 bytes): loaded packed, unpacked to floats where used.
+__device__ __forceinline__ uint2 mix_ld8(const __nv_bfloat16* p) { return *reinterpret_cast<const uint2*>(p); }
+__device__ __forceinline__ float4 mix_unpack4(uint2 pk) {
   return make_float4(__uint_as_float(pk.x << 16), __uint_as_float(pk.x & 0xffff0000u),
                      __uint_as_float(pk.y << 16), __uint_as_float(pk.y & 0xffff0000u));
 }
 
-// Backward of one chunk. The mixing vectors and the output gradients are read
-// where used (the next row's gradients again as the current row's one step
-// later, from L1/L2); the column accumulators stay in registers.
-template <int G, int N>
-__global__ void __launch_bounds__(32 * kMixWarps) ln_mix_bwd_kernel(const MixArgs a) {
-  const int lane = threadIdx.x & 31;
-  const int chunk = blockIdx.x * kMixWarps + (threadIdx.x >> 5);
-  if (chunk >= a.B * a.nct) return;
-  const int bi = chunk / a.nct, t0 = (chunk % a.nct) * kMixRows;
-  const int t1 = min(a.T, t0 + kMixRows);
-  float4 wv[G], bv[G];
-  mix_load_row<G>(a.w, lane, wv);
-  mix_load_row<G>(a.b, lane, bv);
+// Steps [t0, t1) of sequence bi taken by this CTA.
+__device__ __forceinline__ void mix_span(const MixArgs& a, int& bi, int& t0, int& t1) {
+  bi = blockIdx.x / a.nct;
+  t0 = (blockIdx.x % a.nct) * a.rows;
+  t1 = min(a.T, t0 + a.rows);
+}
+
+__global__ void __launch_bounds__(kMixMaxC / 4) ln_mix_fwd_kernel(const MixArgs a) {
+  __shared__ float red[2][kMixMaxC / 128];
+  const int c = 4 * threadIdx.x;
+  int bi, t0, t1;
+  mix_span(a, bi, t0, t1);
+  const float4 wv = ld4(a.w + c), bv = ld4(a.b + c);
+  float4 m[kMixMax];
+#pragma unroll
+  for (int i = 0; i < kMixMax; ++i) m[i] = i < a.n ? ld4(a.mix + (size_t)i * a.C + c) : make_float4(0, 0, 0, 0);
   const size_t row0 = (size_t)bi * a.T;
-  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
-  float4 acc_w[G], acc_b[G], acc_m[N][G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    acc_w[g] = acc_b[g] = z4;
-#pragma unroll
-    for (int i = 0; i < N; ++i) acc_m[i][g] = z4;
-  }
-  float4 hp[G];  // h[t-1]
+  float4 hp = make_float4(0.f, 0.f, 0.f, 0.f);  // h[t-1]
   if (t0 > 0) {
-    float4 v[G];
-    const size_t r = row0 + t0 - 1;
-    mix_load_row<G>(a.x + r * a.C, lane, v);
-    const float mu = a.mean[r], rs = a.rstd[r];
-#pragma unroll
-    for (int g = 0; g < G; ++g) hp[g] = mix_norm(v[g], mu, rs, wv[g], bv[g]);
-  } else {
-#pragma unroll
-    for (int g = 0; g < G; ++g) hp[g] = z4;
+    const float4 v = ld4(a.x + (row0 + t0 - 1) * a.C + c);
+    float mu, rs;
+    mix_stats(v, a.C, a.eps, red, mu, rs);
+    hp = mix_norm(v, mu, rs, wv, bv);
   }
+  float4 v = ld4(a.x + (row0 + t0) * a.C + c);
 #pragma unroll 1
   for (int t = t0; t < t1; ++t) {
     const size_t r = row0 + t;
-    const bool has_next = t + 1 < a.T;
-    float4 xh[G], dw[G];
-    float s1 = 0.f, s2 = 0.f;
-    const float mu = a.mean[r], rs = a.rstd[r];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const int c = g * 128 + 4 * lane;
-      const float4 v = *reinterpret_cast<const float4*>(a.x + r * a.C + c);
-      const float4 h = mix_norm(v, mu, rs, wv[g], bv[g]);
-      xh[g] = make_float4(__fmul_rn(v.x - mu, rs), __fmul_rn(v.y - mu, rs), __fmul_rn(v.z - mu, rs),
-                          __fmul_rn(v.w - mu, rs));
-      float4 d = z4;
-#pragma unroll
-      for (int i = 0; i < N; ++i) {
-        const float4 m = *reinterpret_cast<const float4*>(a.mix + (size_t)i * a.C + c);
-        const float4 gc = mix_grad4(a.gout[i] + r * a.C + c);
-        const float4 gn = has_next ? mix_grad4(a.gout[i] + (r + 1) * a.C + c) : z4;
-        d.x += m.x * gc.x + (1.f - m.x) * gn.x;
-        d.y += m.y * gc.y + (1.f - m.y) * gn.y;
-        d.z += m.z * gc.z + (1.f - m.z) * gn.z;
-        d.w += m.w * gc.w + (1.f - m.w) * gn.w;
-        acc_m[i][g].x += gc.x * (h.x - hp[g].x);
-        acc_m[i][g].y += gc.y * (h.y - hp[g].y);
-        acc_m[i][g].z += gc.z * (h.z - hp[g].z);
-        acc_m[i][g].w += gc.w * (h.w - hp[g].w);
-      }
-      hp[g] = h;
-      acc_w[g].x += d.x * xh[g].x;
-      acc_w[g].y += d.y * xh[g].y;
-      acc_w[g].z += d.z * xh[g].z;
-      acc_w[g].w += d.w * xh[g].w;
-      acc_b[g].x += d.x;
-      acc_b[g].y += d.y;
-      acc_b[g].z += d.z;
-      acc_b[g].w += d.w;
-      dw[g] = make_float4(d.x * wv[g].x, d.y * wv[g].y, d.z * wv[g].z, d.w * wv[g].w);
-      s1 += (dw[g].x + dw[g].y) + (dw[g].z + dw[g].w);
-      s2 += (dw[g].x * xh[g].x + dw[g].y * xh[g].y) + (dw[g].z * xh[g].z + dw[g].w * xh[g].w);
+    const float4 vn = ld4(a.x + (row0 + min(t + 1, t1 - 1)) * a.C + c);  // next row (last row again at the end)
+    float mu, rs;
+    mix_stats(v, a.C, a.eps, red, mu, rs);
+    if (threadIdx.x == 0) {
+      a.mean[r] = mu;
+      a.rstd[r] = rs;
     }
-    s1 = warp_sum(s1) / a.C;
-    s2 = warp_sum(s2) / a.C;
-    float* gxr = a.gx + r * a.C;
+    const float4 h = mix_norm(v, mu, rs, wv, bv);
 #pragma unroll
-    for (int g = 0; g < G; ++g)
-      *reinterpret_cast<float4*>(gxr + g * 128 + 4 * lane) =
-          make_float4(rs * (dw[g].x - s1 - xh[g].x * s2), rs * (dw[g].y - s1 - xh[g].y * s2),
-                      rs * (dw[g].z - s1 - xh[g].z * s2), rs * (dw[g].w - s1 - xh[g].w * s2));
-  }
-  float* p = a.partial + (size_t)chunk * (2 + N) * a.C;
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const int c = g * 128 + 4 * lane;
-    *reinterpret_cast<float4*>(p + c) = acc_w[g];
-    *reinterpret_cast<float4*>(p + a.C + c) = acc_b[g];
-#pragma unroll
-    for (int i = 0; i < N; ++i) *reinterpret_cast<float4*>(p + (2 + i) * (size_t)a.C + c) = acc_m[i][g];
+    for (int i = 0; i < kMixMax; ++i) {
+      if (i < a.n) {
+        const float o0 = mix1(h.x, hp.x, m[i].x, 1.f - m[i].x), o1 = mix1(h.y, hp.y, m[i].y, 1.f - m[i].y);
+        const float o2 = mix1(h.z, hp.z, m[i].z, 1.f - m[i].z), o3 = mix1(h.w, hp.w, m[i].w, 1.f - m[i].w);
+        __nv_bfloat162 lo = __floats2bfloat162_rn(o0, o1), hi = __floats2bfloat162_rn(o2, o3);
+        uint2 pk;
+        pk.x = *reinterpret_cast<uint32_t*>(&lo);
+        pk.y = *reinterpret_cast<uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(a.out[i] + r * a.C + c) = pk;
+      }
+    }
+    hp = h;
+    v = vn;
   }
 }
 
-// Column sums of the per-chunk partials: out[k][c] for the 2 + n rows k (dw,
+// Backward of the CTA's steps. Row t needs g_i[t] and g_i[t+1]: g_i[t+1] is
+// carried to the next row in registers, and the loads of row t+1 (x, its
+// statistics, g_i[t+2]) are issued before row t is processed. The column
+// sums accumulate per thread and leave as the CTA's partial row set.
+template <int N>
+__global__ void __launch_bounds__(kMixMaxC / 4, 3) ln_mix_bwd_kernel(const MixArgs a) {
+  __shared__ float2 red[2][kMixMaxC / 128];
+  const int c = 4 * threadIdx.x;
+  int bi, t0, t1;
+  mix_span(a, bi, t0, t1);
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 wv = ld4(a.w + c), bv = ld4(a.b + c);
+  float4 m[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) m[i] = ld4(a.mix + (size_t)i * a.C + c);
+  const size_t row0 = (size_t)bi * a.T;
+  float4 acc_w = z4, acc_b = z4, acc_m[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) acc_m[i] = z4;
+  float4 hp = z4;  // h[t-1]
+  if (t0 > 0) {
+    const size_t r = row0 + t0 - 1;
+    hp = mix_norm(ld4(a.x + r * a.C + c), a.mean[r], a.rstd[r], wv, bv);
+  }
+  // row t0's operands and g_i[t0 + 1]
+  float4 v = ld4(a.x + (row0 + t0) * a.C + c);
+  float mu = a.mean[row0 + t0], rs = a.rstd[row0 + t0];
+  const uint2 z2 = make_uint2(0u, 0u);  // four bf16 zeros
+  uint2 gc[N], gn[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    gc[i] = mix_ld8(a.gout[i] + (row0 + t0) * a.C + c);
+    gn[i] = t0 + 1 < a.T ? mix_ld8(a.gout[i] + (row0 + t0 + 1) * a.C + c) : z2;
+  }
+  int slot = 0;
+#pragma unroll 1
+  for (int t = t0; t < t1; ++t) {
+    const size_t r = row0 + t;
+    // prefetch row t+1 (the last row again at the end) and g_i[t+2]
+    const size_t rn = row0 + min(t + 1, t1 - 1);
+    const float4 vn = ld4(a.x + rn * a.C + c);
+    const float mun = a.mean[rn], rsn = a.rstd[rn];
+    uint2 gnn[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) gnn[i] = t + 2 < a.T ? mix_ld8(a.gout[i] + (r + 2) * a.C + c) : z2;
+
+    const float4 h = mix_norm(v, mu, rs, wv, bv);
+    const float4 xh = make_float4(__fmul_rn(v.x - mu, rs), __fmul_rn(v.y - mu, rs), __fmul_rn(v.z - mu, rs),
+                                  __fmul_rn(v.w - mu, rs));
+    float4 d = z4;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      const float4 g = mix_unpack4(gc[i]), gq = mix_unpack4(gn[i]);
+      d.x += m[i].x * g.x + (1.f - m[i].x) * gq.x;
+      d.y += m[i].y * g.y + (1.f - m[i].y) * gq.y;
+      d.z += m[i].z * g.z + (1.f - m[i].z) * gq.z;
+      d.w += m[i].w * g.w + (1.f - m[i].w) * gq.w;
+      acc_m[i].x += g.x * (h.x - hp.x);
+      acc_m[i].y += g.y * (h.y - hp.y);
+      acc_m[i].z += g.z * (h.z - hp.z);
+      acc_m[i].w += g.w * (h.w - hp.w);
+    }
+    acc_w.x += d.x * xh.x;
+    acc_w.y += d.y * xh.y;
+    acc_w.z += d.z * xh.z;
+    acc_w.w += d.w * xh.w;
+    acc_b.x += d.x;
+    acc_b.y += d.y;
+    acc_b.z += d.z;
+    acc_b.w += d.w;
+    const float4 dw = make_float4(d.x * wv.x, d.y * wv.y, d.z * wv.z, d.w * wv.w);
+    const float2 s = block_sum2((dw.x + dw.y) + (dw.z + dw.w),
+                                (dw.x * xh.x + dw.y * xh.y) + (dw.z * xh.z + dw.w * xh.w), red, slot);
+    slot ^= 1;
+    const float s1 = s.x / a.C, s2 = s.y / a.C;
+    *reinterpret_cast<float4*>(a.gx + r * a.C + c) =
+        make_float4(rs * (dw.x - s1 - xh.x * s2), rs * (dw.y - s1 - xh.y * s2), rs * (dw.z - s1 - xh.z * s2),
+                    rs * (dw.w - s1 - xh.w * s2));
+    hp = h;
+    v = vn;
+    mu = mun;
+    rs = rsn;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      gc[i] = gn[i];
+      gn[i] = gnn[i];
+    }
+  }
+  float* p = a.partial + (size_t)blockIdx.x * (2 + N) * a.C + c;
+  *reinterpret_cast<float4*>(p) = acc_w;
+  *reinterpret_cast<float4*>(p + a.C) = acc_b;
+#pragma unroll
+  for (int i = 0; i < N; ++i) *reinterpret_cast<float4*>(p + (2 + i) * (size_t)a.C) = acc_m[i];
+}
+
+// Column sums of the per-CTA partials: out[k][c] for the 2 + n rows k (dw,
 // db, dm_i). A CTA of 32 x 32 threads takes 32 columns of one row k; thread
-// (y, x) sums the chunks y, y + 32, ... of column x, then the 32 partial sums
+// (y, x) sums the partials y, y + 32, ... of column x, then the 32 partial sums
 // of a column are added in y order (a fixed order: the result does not depend
 // on timing).
 __global__ void __launch_bounds__(1024) ln_mix_reduce_kernel(const float* partial, int nchunks, int rows, int C,

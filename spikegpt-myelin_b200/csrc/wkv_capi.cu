@@ -1058,26 +1058,30 @@ int mix_check(int n, int64_t B, int64_t T, int64_t C) {
   if (n < 1 || n > kMixMax) return fail(WKV_ERR_INVALID_ARGUMENT, "n must be 1..%d, got %d", kMixMax, n);
   if (B < 0 || T < 0 || C <= 0) return fail(WKV_ERR_INVALID_ARGUMENT, "bad sizes B=%lld T=%lld C=%lld",
                                             (long long)B, (long long)T, (long long)C);
-  if (C % 128 != 0 || C > 128 * kMixMaxGroups)
-    return fail(WKV_ERR_INVALID_ARGUMENT, "C must be a multiple of 128 up to %d, got %lld", 128 * kMixMaxGroups,
+  if (C % 128 != 0 || C > kMixMaxC)
+    return fail(WKV_ERR_INVALID_ARGUMENT, "C must be a multiple of 128 up to %d, got %lld", kMixMaxC,
                 (long long)C);
   if (B * T > (1ll << 31) - 1) return fail(WKV_ERR_INVALID_ARGUMENT, "B*T out of range");
   return WKV_OK;
 }
 
-template <int G>
-void mix_fwd_go(const MixArgs& a, unsigned grid, cudaStream_t st) {
-  ln_mix_fwd_kernel<G><<<grid, 32 * kMixWarps, 0, st>>>(a);
+// Steps per CTA of the LayerNorm-mix kernels: the largest power of two in
+// [kMixMinRows, kMixMaxRows] that still gives a launch about 8 CTAs per SM
+// (148 SMs), so small batches fill the GPU too; and the CTAs per sequence that
+// follow from it.
+int mix_rows_per_cta(int64_t B, int64_t T) {
+  int r = kMixMaxRows;
+  while (r > kMixMinRows && B * ((T + r - 1) / r) < 8 * 148) r /= 2;
+  return r;
 }
-template <int G, int N>
+int64_t mix_ctas_per_seq(int64_t B, int64_t T) {
+  const int r = mix_rows_per_cta(B, T);
+  return (T + r - 1) / r;
+}
+
+template <int N>
 void mix_bwd_go(const MixArgs& a, unsigned grid, cudaStream_t st) {
-  ln_mix_bwd_kernel<G, N><<<grid, 32 * kMixWarps, 0, st>>>(a);
-}
-template <int G>
-void mix_bwd_n(const MixArgs& a, unsigned grid, cudaStream_t st) {
-  if (a.n == 1) mix_bwd_go<G, 1>(a, grid, st);
-  else if (a.n == 2) mix_bwd_go<G, 2>(a, grid, st);
-  else mix_bwd_go<G, 3>(a, grid, st);
+  ln_mix_bwd_kernel<N><<<grid, a.C / 4, 0, st>>>(a);
 }
 
 }  // namespace
@@ -1086,8 +1090,8 @@ extern "C" {
 
 size_t ln_mix_workspace_size(int n, int64_t B, int64_t T, int64_t C) {
   if (mix_check(n, B, T, C)) return 0;
-  const int64_t chunks = B * ((T + kMixRows - 1) / kMixRows);
-  return round_up((size_t)chunks * (2 + n) * C * sizeof(float));
+  // one partial row set (dw, db, dm_i) per CTA
+  return round_up((size_t)(B * mix_ctas_per_seq(B, T)) * (2 + n) * C * sizeof(float));
 }
 
 int ln_mix_forward(int n, const float* x, const float* w, const float* b, const float* mix, void* out0, void* out1,
@@ -1116,22 +1120,12 @@ int ln_mix_forward(int n, const float* x, const float* w, const float* b, const 
   a.B = (int)B;
   a.T = (int)T;
   a.C = (int)C;
-  a.nct = (int)((T + kMixRows - 1) / kMixRows);
+  a.rows = mix_rows_per_cta(B, T);
+  a.nct = (int)mix_ctas_per_seq(B, T);
   a.eps = eps;
-  const unsigned grid = (unsigned)((B * a.nct + kMixWarps - 1) / kMixWarps);
+  const unsigned grid = (unsigned)(B * a.nct);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  launch(K_MIX_FWD, st, [&] {
-    switch (C / 128) {
-      case 1: mix_fwd_go<1>(a, grid, st); break;
-      case 2: mix_fwd_go<2>(a, grid, st); break;
-      case 3: mix_fwd_go<3>(a, grid, st); break;
-      case 4: mix_fwd_go<4>(a, grid, st); break;
-      case 5: mix_fwd_go<5>(a, grid, st); break;
-      case 6: mix_fwd_go<6>(a, grid, st); break;
-      case 7: mix_fwd_go<7>(a, grid, st); break;
-      default: mix_fwd_go<8>(a, grid, st); break;
-    }
-  });
+  launch(K_MIX_FWD, st, [&] { ln_mix_fwd_kernel<<<grid, (unsigned)(C / 4), 0, st>>>(a); });
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? WKV_OK : cuda_fail(e, "ln_mix forward launch");
 }
@@ -1178,20 +1172,14 @@ int ln_mix_backward(int n, const void* g0, const void* g1, const void* g2, const
   a.B = (int)B;
   a.T = (int)T;
   a.C = (int)C;
-  a.nct = (int)((T + kMixRows - 1) / kMixRows);
-  const int chunks = (int)(B * a.nct);
-  const unsigned grid = (unsigned)((chunks + kMixWarps - 1) / kMixWarps);
+  a.rows = mix_rows_per_cta(B, T);
+  a.nct = (int)mix_ctas_per_seq(B, T);
+  const int chunks = (int)(B * a.nct);  // CTAs, each leaving one partial row set
+  const unsigned grid = (unsigned)chunks;
   launch(K_MIX_BWD, st, [&] {
-    switch (C / 128) {
-      case 1: mix_bwd_n<1>(a, grid, st); break;
-      case 2: mix_bwd_n<2>(a, grid, st); break;
-      case 3: mix_bwd_n<3>(a, grid, st); break;
-      case 4: mix_bwd_n<4>(a, grid, st); break;
-      case 5: mix_bwd_n<5>(a, grid, st); break;
-      case 6: mix_bwd_n<6>(a, grid, st); break;
-      case 7: mix_bwd_n<7>(a, grid, st); break;
-      default: mix_bwd_n<8>(a, grid, st); break;
-    }
+    if (n == 1) mix_bwd_go<1>(a, grid, st);
+    else if (n == 2) mix_bwd_go<2>(a, grid, st);
+    else mix_bwd_go<3>(a, grid, st);
   });
   const int rows = 2 + n;
   launch(K_MIX_RED, st, [&] {

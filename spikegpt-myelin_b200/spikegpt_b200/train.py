@@ -9,12 +9,15 @@ to launch it does not, and the step turns launch-bound. Here the forward and
 backward are captured once and replayed, so the host issues one graph launch,
 one all-reduce and the fused optimizer per step.
 
-Gradients live in one flat float32 buffer: every parameter's ``.grad`` is a
-view of it, the captured backward accumulates into those views after the
-captured zero fill, and a data-parallel step averages them with a single
-all-reduce (DDP's average of the ranks' gradients of their shard-mean
-losses: ``ReduceOp.AVG`` over NCCL; gloo sums and divides). That all-reduce
-and the optimizer step run outside the graph, on the current stream.
+Gradients: the backward starts from ``.grad = None``, so autograd hands each
+parameter the gradient tensor it produced (no zero fill, no accumulation
+kernels). On one rank the optimizer reads those. On several, one
+concatenation (captured with the backward) gathers them into a flat float32
+buffer, a single all-reduce averages it (DDP's average of the ranks'
+gradients of their shard-mean losses: ``ReduceOp.AVG`` over NCCL; gloo sums
+and divides), and the parameters' ``.grad`` are views of that buffer for the
+optimizer. The all-reduce and the optimizer step run outside the graph, on
+the current stream.
 
 ``graph=False`` runs the same step eagerly (any device, any process group:
 the CPU tests use it over gloo).
@@ -54,29 +57,35 @@ class TrainStep:
         params = [p for p in model.parameters() if p.requires_grad]
         if any(p.device != self.device or p.dtype != torch.float32 for p in params):
             raise ValueError("TrainStep expects float32 parameters on its device")
-        total = sum(p.numel() for p in params)
-        self.grads = torch.zeros(total, dtype=torch.float32, device=self.device)
-        off = 0
-        for p in params:
-            n = p.numel()
-            p.grad = self.grads[off:off + n].view_as(p)
-            off += n
+        self.params = params
+        self.grads = None  # the flat gradient buffer (several ranks only)
+        self.grad_views = None
+        if self.world > 1:
+            self.grads = torch.zeros(sum(p.numel() for p in params), dtype=torch.float32, device=self.device)
+            self.grad_views, off = [], 0
+            for p in params:
+                self.grad_views.append(self.grads[off:off + p.numel()].view_as(p))
+                off += p.numel()
         self.ids = torch.zeros(batch_shape, dtype=torch.long, device=self.device)
         self.targets = torch.zeros(batch_shape, dtype=torch.long, device=self.device)
         self.graph = None
         self.loss = None
+        self.captured_grads = None
         self.captured_launches = 0  # this package's kernels in the graph (each replay runs them again)
         if graph:
             self._capture(warmup)
 
     def _forward_backward(self) -> Tensor:
-        self.grads.zero_()
+        for p in self.params:
+            p.grad = None
         if self.autocast_dtype is None:
             loss = self.model(self.ids, self.targets)
         else:
             with torch.autocast(self.device.type, dtype=self.autocast_dtype):
                 loss = self.model(self.ids, self.targets)
         loss.backward()
+        if self.grads is not None:
+            torch.cat([p.grad.reshape(-1) for p in self.params], out=self.grads)
         return loss.detach()
 
     def _capture(self, warmup: int) -> None:
@@ -93,6 +102,11 @@ class TrainStep:
         with torch.cuda.graph(self.graph):
             self.loss = self._forward_backward()
         self.captured_launches = sum(_capi.launch_counts().values()) - before
+        # every replay rewrites the gradient tensors the capture produced
+        self.captured_grads = [p.grad for p in self.params]
+        if self.grad_views is not None:
+            for p, g in zip(self.params, self.grad_views):
+                p.grad = g
 
     def __call__(self, ids: Tensor, targets: Tensor) -> Tensor:
         """Copy the batch in, run forward and backward, average the gradients
@@ -107,12 +121,15 @@ class TrainStep:
             loss = self.loss
         else:
             loss = self._forward_backward()
-        if self.world > 1:
+        if self.grads is not None:
             if self.avg:
                 dist.all_reduce(self.grads, op=dist.ReduceOp.AVG, group=self.group)
             else:
                 dist.all_reduce(self.grads, op=dist.ReduceOp.SUM, group=self.group)
                 self.grads.div_(self.world)
+            if self.graph is None:
+                for p, g in zip(self.params, self.grad_views):
+                    p.grad = g
         self.optimizer.step()
         return loss
 
@@ -120,3 +137,4 @@ class TrainStep:
         """Drop the captured graph (before the process group is destroyed)."""
         self.graph = None
         self.loss = None
+        self.captured_grads = None

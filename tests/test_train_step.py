@@ -1,10 +1,11 @@
 """spikegpt_b200.train.TrainStep: the data-parallel train step.
 
 CPU (gloo, world size 2, eager mode, a small stand-in model with the same
-``model(ids, targets) -> loss`` interface): every parameter's gradient is a
-view of one flat buffer, one all-reduce averages it over the ranks, and after
-a step both ranks hold the parameters that one process gets from the whole
-batch (the gradient of the batch-mean loss is the mean of the shards').
+``model(ids, targets) -> loss`` interface): the gradients are gathered into
+one flat buffer that one all-reduce averages over the ranks (the parameters'
+gradients are then views of it), and after a step both ranks hold the
+parameters that one process gets from the whole batch (the gradient of the
+batch-mean loss is the mean of the shards').
 
 GPU: the SpikeGPT model stepped by the captured CUDA graph follows the eager
 step of the same model from the same initial state: the same losses and
@@ -69,9 +70,10 @@ def _worker(rank, world, port, out):
         x, y = _batch()
         rows = x.shape[0] // world
         step = TrainStep(model, opt, (rows, x.shape[1]), device="cpu", autocast_dtype=None, graph=False)
-        views = all(p.grad.data_ptr() >= step.grads.data_ptr() for p in model.parameters())
         for _ in range(2):
             step(x[rank * rows:(rank + 1) * rows], y[rank * rows:(rank + 1) * rows])
+        lo, hi = step.grads.data_ptr(), step.grads.data_ptr() + step.grads.numel() * 4
+        views = all(lo <= p.grad.data_ptr() < hi for p in model.parameters())
         out.put((rank, views, [p.detach().clone().numpy() for p in model.parameters()]))
     finally:
         dist.destroy_process_group()
