@@ -201,6 +201,26 @@ WKV_API int ln_mix_backward(int n, const void* grad_out0, const void* grad_out1,
                             size_t workspace_bytes, int64_t B, int64_t T, int64_t C, void* stream);
 
 /*
+ * Elementwise gates of the SpikeGPT blocks under bf16 autocast, one pass each
+ * way (no reference C interface; they replace the eager ops the reference's
+ * modules run): the receptance gate `sigmoid(receptance(xr)) * x` of time and
+ * channel mixing (src/spikegpt/language.py:1022 and 1035, 1195-1196) and the
+ * channel-mixing activation `relu(k).square()` (language.py:1193), with the
+ * eager bf16 roundings:
+ *   gate_forward:         out = bf16(s * x),  s = bf16(1 / (1 + exp(-r)))
+ *   gate_backward:        grad_x = bf16(g * s),
+ *                         grad_r = bf16(bf16(bf16(g * x) * bf16(1 - s)) * s)
+ *   relu_square_forward:  out = bf16(relu(k)^2)
+ *   relu_square_backward: grad_k = k <= 0 ? 0 : bf16(g * 2k)
+ * All tensors bf16, n elements, 16-byte aligned.
+ */
+WKV_API int gate_forward(const void* r, const void* x, void* out, int64_t n, void* stream);
+WKV_API int gate_backward(const void* grad_out, const void* r, const void* x, void* grad_r, void* grad_x,
+                          int64_t n, void* stream);
+WKV_API int relu_square_forward(const void* k, void* out, int64_t n, void* stream);
+WKV_API int relu_square_backward(const void* grad_out, const void* k, void* grad_k, int64_t n, void* stream);
+
+/*
  * Forward/backward with a saved forward state (no reference counterpart; an
  * optimisation of wkv_forward/wkv_backward). wkv_forward_with_state computes y exactly as
  * wkv_forward and also stores the recurrence state at every 16th step into

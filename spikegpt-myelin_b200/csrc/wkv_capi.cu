@@ -13,11 +13,13 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <initializer_list>
 #include <mutex>
 #include <type_traits>
 #include <vector>
 
 #include "spikegpt_wkv.h"
+#include "gates.cuh"
 #include "lif.cuh"
 #include "ln_mix.cuh"
 #include "wkv_step.cuh"
@@ -43,13 +45,16 @@ __device__ unsigned g_device_error_flags = 0;
 enum Kind {
   K_FWD_Y, K_FWD_STATE, K_BWD_GRAD, K_BWD_ADJ, K_CARRY_FWD, K_CARRY_ADJ, K_STEP, K_LIF_FWD, K_LIF_BWD,
   K_MIX_FWD, K_MIX_BWD, K_MIX_RED,
+  K_GATE_FWD, K_GATE_BWD, K_RSQ_FWD, K_RSQ_BWD,
   K_COUNT
 };
 const char* const kKindNames[K_COUNT] = {
     "wkv_fwd_kernel<y>",      "wkv_fwd_kernel<state>", "wkv_bwd_kernel<grad>",
     "wkv_bwd_kernel<adjoint>", "wkv_carry_fwd_kernel",  "wkv_carry_adj_kernel",
     "wkv_step_kernel",        "lif_fwd_kernel",        "lif_bwd_kernel",
-    "ln_mix_fwd_kernel",      "ln_mix_bwd_kernel",     "ln_mix_reduce_kernel"};
+    "ln_mix_fwd_kernel",      "ln_mix_bwd_kernel",     "ln_mix_reduce_kernel",
+    "gate_fwd_kernel",        "gate_bwd_kernel",       "relu_square_fwd_kernel",
+    "relu_square_bwd_kernel"};
 
 std::atomic<long long> g_launches[K_COUNT];
 std::atomic<bool> g_timing{false};
@@ -1188,6 +1193,89 @@ int ln_mix_backward(int n, const void* g0, const void* g1, const void* g2, const
   });
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? WKV_OK : cuda_fail(e, "ln_mix backward launch");
+}
+
+}  // extern "C"
+
+namespace {
+
+// Grid of the elementwise gate kernels: one 8-element vector per thread per
+// iteration, at most 8 CTAs per SM (grid-stride beyond that).
+unsigned gate_grid(int64_t n) {
+  const int64_t v = (n / 8 + kGateThreads - 1) / kGateThreads;
+  return (unsigned)std::max<int64_t>(1, std::min<int64_t>(v, 8 * 148));
+}
+
+int gate_check(int64_t n, std::initializer_list<const void*> ptrs) {
+  if (n < 0) return fail(WKV_ERR_INVALID_ARGUMENT, "n must be >= 0, got %lld", (long long)n);
+  if (n == 0) return WKV_OK;
+  for (const void* p : ptrs) {
+    if (!p) return fail(WKV_ERR_INVALID_ARGUMENT, "null pointer");
+    if (!aligned16(p)) return fail(WKV_ERR_INVALID_ARGUMENT, "bf16 tensors must be 16-byte aligned");
+  }
+  return WKV_OK;
+}
+
+int launched(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? WKV_OK : cuda_fail(e, what);
+}
+
+}  // namespace
+
+extern "C" {
+
+int gate_forward(const void* r, const void* x, void* out, int64_t n, void* stream) {
+  g_last_error[0] = '\0';
+  const int rc = gate_check(n, {r, x, out});
+  if (rc || n == 0) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  launch(K_GATE_FWD, st, [&] {
+    gate_fwd_kernel<<<gate_grid(n), kGateThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(r),
+                                                            static_cast<const __nv_bfloat16*>(x),
+                                                            static_cast<__nv_bfloat16*>(out), n);
+  });
+  return launched("gate forward launch");
+}
+
+int gate_backward(const void* grad_out, const void* r, const void* x, void* grad_r, void* grad_x, int64_t n,
+                  void* stream) {
+  g_last_error[0] = '\0';
+  const int rc = gate_check(n, {grad_out, r, x, grad_r, grad_x});
+  if (rc || n == 0) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  launch(K_GATE_BWD, st, [&] {
+    gate_bwd_kernel<<<gate_grid(n), kGateThreads, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(grad_out), static_cast<const __nv_bfloat16*>(r),
+        static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(grad_r),
+        static_cast<__nv_bfloat16*>(grad_x), n);
+  });
+  return launched("gate backward launch");
+}
+
+int relu_square_forward(const void* k, void* out, int64_t n, void* stream) {
+  g_last_error[0] = '\0';
+  const int rc = gate_check(n, {k, out});
+  if (rc || n == 0) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  launch(K_RSQ_FWD, st, [&] {
+    relu_square_fwd_kernel<<<gate_grid(n), kGateThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(k),
+                                                                   static_cast<__nv_bfloat16*>(out), n);
+  });
+  return launched("relu_square forward launch");
+}
+
+int relu_square_backward(const void* grad_out, const void* k, void* grad_k, int64_t n, void* stream) {
+  g_last_error[0] = '\0';
+  const int rc = gate_check(n, {grad_out, k, grad_k});
+  if (rc || n == 0) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  launch(K_RSQ_BWD, st, [&] {
+    relu_square_bwd_kernel<<<gate_grid(n), kGateThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(grad_out),
+                                                                   static_cast<const __nv_bfloat16*>(k),
+                                                                   static_cast<__nv_bfloat16*>(grad_k), n);
+  });
+  return launched("relu_square backward launch");
 }
 
 int wkv_kernel_kinds(void) { return K_COUNT; }

@@ -113,3 +113,118 @@ def ln_shift_mix(x: Tensor, weight: Tensor, bias: Tensor, mixes: list[Tensor], e
     outs = torch.ops.spikegpt_b200.ln_shift_mix(x.contiguous(), weight.float().contiguous(),
                                                 bias.float().contiguous(), mix.contiguous(), float(eps))
     return list(outs[: len(mixes)])
+
+
+# ------------------------------------------------------------------ gates
+#
+# The receptance gate ``sigmoid(r) * x`` of time and channel mixing
+# (language.py:1022 and 1035, 1195-1196) and the channel-mixing activation
+# ``relu(k).square()`` (language.py:1193) on bf16 GEMM outputs, one kernel
+# pass forward and one backward each (``gate_*`` and ``relu_square_*`` in the
+# C ABI), with the eager bf16 roundings, so the results equal the eager ops'.
+
+
+def _aligned(t: Tensor) -> Tensor:
+    t = t.contiguous()
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
+def _stream(t: Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+@torch.library.custom_op("spikegpt_b200::gate", mutates_args=(), device_types="cuda")
+def _gate(r: Tensor, x: Tensor) -> Tensor:
+    out = torch.empty_like(x)
+    _capi.check(_capi.lib().gate_forward(r.data_ptr(), x.data_ptr(), out.data_ptr(), x.numel(), _stream(x)),
+                "gate_forward")
+    return out
+
+
+@_gate.register_fake
+def _(r, x):
+    return torch.empty_like(x)
+
+
+@torch.library.custom_op("spikegpt_b200::gate_backward", mutates_args=(), device_types="cuda")
+def _gate_backward(grad: Tensor, r: Tensor, x: Tensor) -> list[Tensor]:
+    gr, gx = torch.empty_like(r), torch.empty_like(x)
+    _capi.check(_capi.lib().gate_backward(grad.data_ptr(), r.data_ptr(), x.data_ptr(), gr.data_ptr(), gx.data_ptr(),
+                                          x.numel(), _stream(x)), "gate_backward")
+    return [gr, gx]
+
+
+@_gate_backward.register_fake
+def _(grad, r, x):
+    return [torch.empty_like(r), torch.empty_like(x)]
+
+
+def _gate_setup(ctx, inputs, output):
+    ctx.save_for_backward(*inputs)
+
+
+def _gate_grad(ctx, grad):
+    r, x = ctx.saved_tensors
+    gr, gx = torch.ops.spikegpt_b200.gate_backward(_aligned(grad.to(torch.bfloat16)), r, x)
+    return gr, gx
+
+
+_gate.register_autograd(_gate_grad, setup_context=_gate_setup)
+
+
+@torch.library.custom_op("spikegpt_b200::relu_square", mutates_args=(), device_types="cuda")
+def _relu_square(k: Tensor) -> Tensor:
+    out = torch.empty_like(k)
+    _capi.check(_capi.lib().relu_square_forward(k.data_ptr(), out.data_ptr(), k.numel(), _stream(k)),
+                "relu_square_forward")
+    return out
+
+
+@_relu_square.register_fake
+def _(k):
+    return torch.empty_like(k)
+
+
+@torch.library.custom_op("spikegpt_b200::relu_square_backward", mutates_args=(), device_types="cuda")
+def _relu_square_backward(grad: Tensor, k: Tensor) -> Tensor:
+    gk = torch.empty_like(k)
+    _capi.check(_capi.lib().relu_square_backward(grad.data_ptr(), k.data_ptr(), gk.data_ptr(), k.numel(),
+                                                 _stream(k)), "relu_square_backward")
+    return gk
+
+
+@_relu_square_backward.register_fake
+def _(grad, k):
+    return torch.empty_like(k)
+
+
+def _rsq_setup(ctx, inputs, output):
+    ctx.save_for_backward(inputs[0])
+
+
+def _rsq_grad(ctx, grad):
+    (k,) = ctx.saved_tensors
+    return torch.ops.spikegpt_b200.relu_square_backward(_aligned(grad.to(torch.bfloat16)), k)
+
+
+_relu_square.register_autograd(_rsq_grad, setup_context=_rsq_setup)
+
+
+def gates_supported(*ts: Tensor) -> bool:
+    """bf16 CUDA tensors of one shape: what ``gate`` and ``relu_square`` take."""
+    return all(t.is_cuda and t.dtype == torch.bfloat16 and t.shape == ts[0].shape for t in ts)
+
+
+def gate(r: Tensor, x: Tensor) -> Tensor:
+    """bf16 ``sigmoid(r) * x`` (the receptance gate), r and x bf16 CUDA tensors
+    of one shape."""
+    if not gates_supported(r, x):
+        raise ValueError("gate needs bf16 CUDA tensors of one shape")
+    return torch.ops.spikegpt_b200.gate(_aligned(r), _aligned(x))
+
+
+def relu_square(k: Tensor) -> Tensor:
+    """bf16 ``relu(k) ** 2``, k a bf16 CUDA tensor."""
+    if not gates_supported(k):
+        raise ValueError("relu_square needs a bf16 CUDA tensor")
+    return torch.ops.spikegpt_b200.relu_square(_aligned(k))

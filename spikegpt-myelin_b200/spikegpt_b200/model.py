@@ -120,12 +120,14 @@ class TimeMix(nn.Module):
         """The sublayer from its three token-shift-mixed inputs."""
         k = self.key(xk)
         v = self.value(xv)
-        r = torch.sigmoid(self.receptance(xr))
+        rl = self.receptance(xr)
         if k.dtype in (torch.bfloat16, torch.float16):
             wkv = weighted_key_value_cuda_bf16io(k, v, self.time_decay, self.time_first)
         else:
             wkv = weighted_key_value_cuda(k, v, self.time_decay, self.time_first)
-        return self.output(r * wkv)
+        if fused.gates_supported(rl, wkv):  # bf16 autocast: one kernel each way
+            return self.output(fused.gate(rl, wkv))
+        return self.output(torch.sigmoid(rl) * wkv)
 
 
 class ChannelMix(nn.Module):
@@ -147,8 +149,13 @@ class ChannelMix(nn.Module):
         """The sublayer from its two token-shift-mixed inputs. The square is
         taken in the key's dtype: under bf16 autocast, square (pow) would be
         computed in float32 and cast back for the value projection, which
-        rounds the same exact square to bf16 once either way."""
-        k = torch.relu(self.key(xk))
+        rounds the same exact square to bf16 once either way. With bf16
+        projections the activation and the gate are the fused kernels."""
+        k = self.key(xk)
+        if fused.gates_supported(k):  # bf16 autocast: one kernel each way
+            v = self.value(fused.relu_square(k))
+            return fused.gate(self.receptance(xr), v)
+        k = torch.relu(k)
         with torch.autocast("cuda", enabled=False):
             k = torch.square(k)
         r = torch.sigmoid(self.receptance(xr))
