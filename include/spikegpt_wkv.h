@@ -221,6 +221,15 @@ WKV_API int relu_square_forward(const void* k, void* out, int64_t n, void* strea
 WKV_API int relu_square_backward(const void* grad_out, const void* k, void* grad_k, int64_t n, void* stream);
 
 /*
+ * The residual connection around a LIF sublayer under bf16 autocast
+ * (src/spikegpt/language.py:1353-1358, `residual + lif(...)`):
+ * out = x + float(spikes), x and out float32, spikes bf16, n elements,
+ * 16-byte aligned; the same values as PyTorch's type-promoting add. Its
+ * backward is the identity for x and a cast to bf16 for the spikes.
+ */
+WKV_API int residual_add_forward(const float* x, const void* spikes, float* out, int64_t n, void* stream);
+
+/*
  * Forward/backward with a saved forward state (no reference counterpart; an
  * optimisation of wkv_forward/wkv_backward). wkv_forward_with_state computes y exactly as
  * wkv_forward and also stores the recurrence state at every 16th step into

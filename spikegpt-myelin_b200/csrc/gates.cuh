@@ -13,12 +13,15 @@
 //                operation, as PyTorch evaluates it for 16-bit types)
 //   relu_square: out = bf16(relu(k)^2)
 //                grad_k = k <= 0 ? 0 : bf16(g * (2 k))
+//   residual_add: out = x + float(s)   (float32 residual stream plus the bf16
+//                spikes of a LIF sublayer, language.py:1353-1358; PyTorch's
+//                type-promoting add, which converts s exactly and rounds once)
 // (products in float32; relu keeps NaN, and its backward zeroes the
 // gradient where its output is <= 0, so a NaN key passes g * 2k = NaN on, as
 // eagerly). Eight elements per thread per
 // iteration (16-byte loads and stores), grid-stride; a scalar tail handles
 // n % 8. Memory-bound: gate forward 6 B per element, backward 10 B;
-// relu_square 4 B and 6 B.
+// relu_square 4 B and 6 B; residual_add 10 B.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -132,6 +135,21 @@ __global__ void __launch_bounds__(kGateThreads) relu_square_bwd_kernel(const __n
   }
   if (blockIdx.x == 0)
     for (int64_t i = 8 * nv + threadIdx.x; i < n; i += blockDim.x) ReluSquare::bwd(g, k, gk, i);
+}
+
+__global__ void __launch_bounds__(kGateThreads) residual_add_kernel(const float* x, const __nv_bfloat16* s,
+                                                                    float* out, int64_t n) {
+  const int64_t nv = n / 8, stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += stride) {
+    const float4 a = *reinterpret_cast<const float4*>(x + 8 * v), b = *reinterpret_cast<const float4*>(x + 8 * v + 4);
+    const Bf8 sp = ld8(s + 8 * v);
+    *reinterpret_cast<float4*>(out + 8 * v) =
+        make_float4(a.x + bf(sp.h[0]), a.y + bf(sp.h[1]), a.z + bf(sp.h[2]), a.w + bf(sp.h[3]));
+    *reinterpret_cast<float4*>(out + 8 * v + 4) =
+        make_float4(b.x + bf(sp.h[4]), b.y + bf(sp.h[5]), b.z + bf(sp.h[6]), b.w + bf(sp.h[7]));
+  }
+  if (blockIdx.x == 0)
+    for (int64_t i = 8 * nv + threadIdx.x; i < n; i += blockDim.x) out[i] = x[i] + bf(s[i]);
 }
 
 }  // namespace wkv

@@ -45,7 +45,7 @@ __device__ unsigned g_device_error_flags = 0;
 enum Kind {
   K_FWD_Y, K_FWD_STATE, K_BWD_GRAD, K_BWD_ADJ, K_CARRY_FWD, K_CARRY_ADJ, K_STEP, K_LIF_FWD, K_LIF_BWD,
   K_MIX_FWD, K_MIX_BWD, K_MIX_RED,
-  K_GATE_FWD, K_GATE_BWD, K_RSQ_FWD, K_RSQ_BWD,
+  K_GATE_FWD, K_GATE_BWD, K_RSQ_FWD, K_RSQ_BWD, K_RESID,
   K_COUNT
 };
 const char* const kKindNames[K_COUNT] = {
@@ -54,7 +54,7 @@ const char* const kKindNames[K_COUNT] = {
     "wkv_step_kernel",        "lif_fwd_kernel",        "lif_bwd_kernel",
     "ln_mix_fwd_kernel",      "ln_mix_bwd_kernel",     "ln_mix_reduce_kernel",
     "gate_fwd_kernel",        "gate_bwd_kernel",       "relu_square_fwd_kernel",
-    "relu_square_bwd_kernel"};
+    "relu_square_bwd_kernel", "residual_add_kernel"};
 
 std::atomic<long long> g_launches[K_COUNT];
 std::atomic<bool> g_timing{false};
@@ -1276,6 +1276,18 @@ int relu_square_backward(const void* grad_out, const void* k, void* grad_k, int6
                                                                    static_cast<__nv_bfloat16*>(grad_k), n);
   });
   return launched("relu_square backward launch");
+}
+
+int residual_add_forward(const float* x, const void* spikes, float* out, int64_t n, void* stream) {
+  g_last_error[0] = '\0';
+  const int rc = gate_check(n, {x, spikes, out});
+  if (rc || n == 0) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  launch(K_RESID, st, [&] {
+    residual_add_kernel<<<gate_grid(n), kGateThreads, 0, st>>>(x, static_cast<const __nv_bfloat16*>(spikes), out,
+                                                                n);
+  });
+  return launched("residual_add launch");
 }
 
 int wkv_kernel_kinds(void) { return K_COUNT; }

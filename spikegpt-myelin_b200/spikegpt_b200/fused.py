@@ -228,3 +228,45 @@ def relu_square(k: Tensor) -> Tensor:
     if not gates_supported(k):
         raise ValueError("relu_square needs a bf16 CUDA tensor")
     return torch.ops.spikegpt_b200.relu_square(_aligned(k))
+
+
+# --------------------------------------------------------- residual add
+#
+# ``residual + lif(sublayer(...))`` (language.py:1353-1358): the float32
+# residual stream plus bf16 spikes. PyTorch's type-promoting add takes its
+# mixed-dtype (unvectorized) path; ``residual_add_forward`` is one vectorized
+# pass with the same values (the bf16 spike converts exactly, one rounded
+# add). The backward is the identity for the residual and a cast to bf16 for
+# the spikes, as autograd's.
+
+
+@torch.library.custom_op("spikegpt_b200::residual_add", mutates_args=(), device_types="cuda")
+def _residual_add(x: Tensor, spikes: Tensor) -> Tensor:
+    out = torch.empty_like(x)
+    _capi.check(_capi.lib().residual_add_forward(x.data_ptr(), spikes.data_ptr(), out.data_ptr(), x.numel(),
+                                                 _stream(x)), "residual_add_forward")
+    return out
+
+
+@_residual_add.register_fake
+def _(x, spikes):
+    return torch.empty_like(x)
+
+
+def _resid_setup(ctx, inputs, output):
+    pass
+
+
+def _resid_grad(ctx, grad):
+    return grad, grad.to(torch.bfloat16)
+
+
+_residual_add.register_autograd(_resid_grad, setup_context=_resid_setup)
+
+
+def residual_add(x: Tensor, spikes: Tensor) -> Tensor:
+    """float32 ``x + spikes`` for a float32 x and bf16 spikes of one shape (CUDA)."""
+    if not (x.is_cuda and x.dtype == torch.float32 and spikes.dtype == torch.bfloat16
+            and spikes.is_cuda and x.shape == spikes.shape):
+        raise ValueError("residual_add needs a float32 x and bf16 spikes of one shape on CUDA")
+    return torch.ops.spikegpt_b200.residual_add(_aligned(x), _aligned(spikes))

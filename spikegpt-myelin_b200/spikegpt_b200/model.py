@@ -184,6 +184,13 @@ class Block(nn.Module):
                              surrogate_slope=cfg.surrogate_slope)
 
     @staticmethod
+    def _residual(x: Tensor, spikes: Tensor) -> Tensor:
+        # float32 residual stream + bf16 spikes: one vectorized kernel
+        if x.dtype == torch.float32 and spikes.dtype == torch.bfloat16 and x.shape == spikes.shape:
+            return fused.residual_add(x, spikes)
+        return x + spikes
+
+    @staticmethod
     def _fused(x: Tensor) -> bool:
         # Under bf16 autocast the projections take bf16 inputs, which the fused
         # LayerNorm + token-shift kernel produces directly.
@@ -197,10 +204,10 @@ class Block(nn.Module):
             att, ffn = self.att, self.ffn
             xk, xv, xr = fused.ln_shift_mix(x, self.ln1.weight, self.ln1.bias,
                                             [att.time_mix_k, att.time_mix_v, att.time_mix_r], self.ln1.eps)
-            x = x + self._lif(att.from_mixed(xk, xv, xr))
+            x = self._residual(x, self._lif(att.from_mixed(xk, xv, xr)))
             xk, xr = fused.ln_shift_mix(x, self.ln2.weight, self.ln2.bias, [ffn.time_mix_k, ffn.time_mix_r],
                                         self.ln2.eps)
-            x = x + self._lif(ffn.from_mixed(xk, xr))
+            x = self._residual(x, self._lif(ffn.from_mixed(xk, xr)))
         else:
             x = x + self._lif(self.att(self.ln1(x)))
             x = x + self._lif(self.ffn(self.ln2(x)))

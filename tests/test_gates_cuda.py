@@ -1,7 +1,7 @@
-"""GPU parity of the fused gate ops (``spikegpt_b200.fused.gate`` and
-``relu_square``) against the eager bf16 PyTorch ops they replace:
-``torch.sigmoid(r) * x`` and ``torch.relu(k).square()`` with their autograd
-backward. Both compute the same float32 products with the same bf16
+"""GPU parity of the fused gate ops (``spikegpt_b200.fused.gate``,
+``relu_square`` and ``residual_add``) against the eager PyTorch ops they
+replace: ``torch.sigmoid(r) * x`` and ``torch.relu(k).square()`` on bf16, and
+the float32 + bf16 residual add, with their autograd backward. Both compute the same float32 products with the same bf16
 roundings, so outputs and gradients are compared bit for bit, including
 special values (NaN, infinities, signed zeros), sizes that are not a
 multiple of the 8-element vector, and an empty tensor."""
@@ -12,7 +12,7 @@ import pytest
 import torch
 
 from spikegpt_b200 import _capi
-from spikegpt_b200.fused import gate, relu_square
+from spikegpt_b200.fused import gate, relu_square, residual_add
 
 pytestmark = pytest.mark.gpu
 
@@ -84,3 +84,25 @@ def test_gate_kernels_are_counted(cuda):
     after = _capi.launch_counts()
     for name in ("gate_fwd_kernel", "gate_bwd_kernel", "relu_square_fwd_kernel", "relu_square_bwd_kernel"):
         assert after[name] - before[name] == 1, name
+    residual_add(torch.zeros(8, 16, device=cuda), x.detach())
+    assert _capi.launch_counts()["residual_add_kernel"] - after["residual_add_kernel"] == 1
+
+
+@pytest.mark.parametrize("shape", [(4, 64, 512), (3, 5, 7), (0, 3)])
+def test_residual_add_matches_eager(cuda, shape):
+    g = torch.Generator(device="cpu").manual_seed(8)
+    x0 = (torch.randn(shape, generator=g) * 5).to(cuda)
+    s0 = _bf16(shape, 9, cuda)
+    go = torch.randn(shape, generator=g).to(cuda)
+    x, s = x0.clone().requires_grad_(), s0.clone().requires_grad_()
+    out = residual_add(x, s)
+    out.backward(go)
+    xe, se = x0.clone().requires_grad_(), s0.clone().requires_grad_()
+    ref = xe + se
+    ref.backward(go)
+    assert ref.dtype == torch.float32
+    nan = torch.isnan(ref)
+    assert torch.equal(nan, torch.isnan(out))
+    assert torch.equal(out.detach()[~nan].view(torch.int32), ref.detach()[~nan].view(torch.int32))
+    assert torch.equal(x.grad, xe.grad)
+    _same(s.grad, se.grad)
