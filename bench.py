@@ -92,6 +92,11 @@ def parse_args():
                     help="time the self-contained op pair (backward re-runs the forward sweep)")
     ap.add_argument("--eager", action="store_true",
                     help="train workloads: launch the step's kernels eagerly instead of replaying a CUDA graph")
+    ap.add_argument("--global-batch", type=int, default=None,
+                    help="train workloads: override the global batch (e.g. the per-rank share of an N-GPU run on one GPU)")
+    ap.add_argument("--kernel-split", type=int, default=0, metavar="TOP",
+                    help="train workloads: after timing, print the TOP kernels of two eager steps by device time "
+                         "(torch profiler, CUDA activity) to stderr")
     return ap.parse_args()
 
 
@@ -892,6 +897,32 @@ def zipf_tokens(rng, shape, vocab: int, s: float):
     return rng.choice(vocab, size=shape, p=w / w.sum()).astype(np.int64)
 
 
+def train_kernel_split(model, opt, x, y, dev, top: int) -> None:
+    """Per-kernel device time of the train step: two eager steps (the same
+    kernels a graph replay runs) under the torch profiler's CUDA activity,
+    averaged per step, printed to stderr."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    from spikegpt_b200.train import TrainStep
+
+    step = TrainStep(model, opt, tuple(x.shape), device=dev, graph=False)
+    for _ in range(2):
+        step(x, y)
+    torch.cuda.synchronize(dev)
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(2):
+            step(x, y)
+        torch.cuda.synchronize(dev)
+    rows = sorted(((e.device_time_total, e.count, e.key) for e in prof.key_averages() if e.device_time_total > 0),
+                  reverse=True)
+    total = sum(r[0] for r in rows)
+    print(f"device time per step {total / 2e3:.2f} ms over {sum(r[1] for r in rows) // 2} kernels "
+          f"(batch {x.shape[0]} x {x.shape[1]})", file=sys.stderr)
+    for t_us, n, key in rows[:top]:
+        print(f"  {t_us / 2e3:8.3f} ms {n // 2:5d}  {key[:110]}", file=sys.stderr)
+
+
 def run_train(args, wl):
     """Data-parallel train step of SpikeGPT (this package's model and ops): the
     global batch split over the ranks (per-rank work shrinks as ranks grow:
@@ -917,7 +948,7 @@ def run_train(args, wl):
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
     cfg = {"41m": SPIKEGPT_41M, "216m": SPIKEGPT_216M}[wl["model"]]
-    gb, t = wl["global_batch"], wl["T"]
+    gb, t = args.global_batch or wl["global_batch"], wl["T"]
     if gb % world:
         raise SystemExit(f"global batch {gb} does not split over {world} ranks")
     b = gb // world
@@ -1012,6 +1043,8 @@ def run_train(args, wl):
     if rank == 0:
         print(json.dumps(result), flush=True)
     step.release()
+    if args.kernel_split and rank == 0:
+        train_kernel_split(model, opt, x, y, dev, args.kernel_split)
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
