@@ -166,12 +166,19 @@ WKV_API int wkv_step(int dtype, int state_dtype, const void* key, const void* va
  * spike's surrogate derivative slope * 1 / (2 (1 + (pi/2 * centered)^2)) (the
  * published arc-tangent surrogate; the reference's own surrogate lives in
  * myelin@68b8ebb and is not available to pin against). tau > 0.
+ * With few sequences for the GPU (the 256-channel groups times B under half
+ * the SMs) lif_backward splits T into segments that run at once (each
+ * segment's adjoint map composed first); the per-segment maps go into
+ * scratch at the end of `state` (lif_state_size includes it), so backward
+ * calls that share one state buffer concurrently race. The last segment's
+ * gradients are bit-identical to the one-sweep ones, the others agree to
+ * float32 rounding.
  */
 WKV_API size_t lif_state_size(int dtype, int64_t B, int64_t T, int64_t C);
 WKV_API int lif_forward(int dtype, const void* x, void* spikes, float* state, size_t state_bytes,
                         int64_t B, int64_t T, int64_t C, float tau, float threshold, float reset,
                         float slope, void* stream);
-WKV_API int lif_backward(int dtype, const void* grad_spikes, const void* x, const float* state,
+WKV_API int lif_backward(int dtype, const void* grad_spikes, const void* x, float* state,
                          size_t state_bytes, void* grad_x, int64_t B, int64_t T, int64_t C,
                          float tau, float threshold, float reset, float slope, void* stream);
 

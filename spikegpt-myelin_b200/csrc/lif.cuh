@@ -42,6 +42,12 @@ struct LifArgs {
   float decay, threshold, reset, slope;
   int B, T, C, ncblk, ntiles;
   unsigned* err;
+  // Time-segmented backward (TMA path, few sequences): nseg segments of
+  // seg_tiles staged tiles each (nseg 1: one segment, seg_sum unused), and
+  // the affine map g_start = A * g_end + B of the adjoint over each segment,
+  // [B][nseg][2][C] (A, then B).
+  int nseg, seg_tiles;
+  float* seg_sum;
 };
 
 // Rows of a TMA-staged tile: 8 KB of 64 channels (64 bf16/fp16 rows, 32 fp32 rows).
@@ -481,8 +487,13 @@ __global__ void __launch_bounds__(kLifWsThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ncg = (a.ncblk + kLifWarps - 1) / kLifWarps;
   const int cg = blockIdx.x % ncg, b = blockIdx.x / ncg;
-  const int nq = a.ntiles;
-  const int ntt = (a.T + RT - 1) / RT;
+  // this CTA's time segment: staged tiles [tt0, tt0 + ntt), sub-tiles [q0, q0 + nq)
+  const int seg = blockIdx.y;
+  const int ntt_all = (a.T + RT - 1) / RT;
+  const int tt0 = a.nseg > 1 ? seg * a.seg_tiles : 0;
+  const int ntt = a.nseg > 1 ? min(ntt_all, tt0 + a.seg_tiles) - tt0 : ntt_all;
+  const int q0 = tt0 * QT;
+  const int nq = min(a.ntiles, q0 + ntt * QT) - q0;
   auto xs_of = [&](int vt) { return reinterpret_cast<T*>(smem + (vt % S) * SE); };
   auto gs_of = [&](int vt) { return xs_of(vt) + E; };
   auto st_of = [&](int vt) { return reinterpret_cast<float*>(xs_of(vt) + 2 * E); };
@@ -506,7 +517,7 @@ __global__ void __launch_bounds__(kLifWsThreads, 1)
     prefetch_tensormap(&tst);
     prefetch_tensormap(&tgx);
     auto issue = [&](int vt) {
-      const int jt = ntt - 1 - vt;
+      const int jt = tt0 + ntt - 1 - vt;
       uint64_t* bar = &full[vt % S];
       mbar_arrive_expect_tx(bar, SE);
       tma_load_3d(xs_of(vt), &tx, bar, cg * kLifWsCols, jt * RT, b);
@@ -528,7 +539,7 @@ __global__ void __launch_bounds__(kLifWsThreads, 1)
         report_timeout(a.err);
         break;
       }
-      tma_store_3d(&tgx, obuf + (vt % NO) * E, cg * kLifWsCols, (ntt - 1 - vt) * RT, b);
+      tma_store_3d(&tgx, obuf + (vt % NO) * E, cg * kLifWsCols, (tt0 + ntt - 1 - vt) * RT, b);
       bulk_commit();
       if (vt > 0) {
         bulk_wait_read<1>();
@@ -559,14 +570,25 @@ __global__ void __launch_bounds__(kLifWsThreads, 1)
     return false;
   };
   if (nq == 0) return;
-  const int last_rows = a.T - (nq - 1) * kSub;
+  const int last_rows = a.T - (q0 + nq - 1) * kSub;
   f2 va[kSub], vb[kSub];
+  // the adjoint entering the segment from its end: zero for the last one,
+  // else the later segments' affine maps applied to zero, last first
+  f2 g = k.zero;
+  if (a.nseg > 1) {
+    const int c = cg * kLifWsCols + off;
+    if (c < a.C) {
+      for (int s2 = a.nseg - 1; s2 > seg; --s2) {
+        const float* p = a.seg_sum + ((size_t)b * a.nseg + s2) * 2 * a.C + c;
+        g = fma2(*reinterpret_cast<const f2*>(p), g, *reinterpret_cast<const f2*>(p + a.C));
+      }
+    }
+  }
   if (!wait_full(0)) return;
   if (last_rows == kSub) lif_recompute<true, kPlain, T, kLifWsCols>(v_sub(nq - 1), x_sub(nq - 1), kSub, k, va);
   else lif_recompute<false, kPlain, T, kLifWsCols>(v_sub(nq - 1), x_sub(nq - 1), last_rows, k, va);
-  f2 g = k.zero;
   auto body = [&](int q, const f2(&cur)[kSub], f2(&nxt)[kSub]) -> bool {
-    const int u0 = q * kSub;
+    const int u0 = (q0 + q) * kSub;
     const int rows = min(kSub, a.T - u0);
     const int vt = vt_of(q);
     if (q > 0 && q % QT == 0 && !wait_full(vt + 1)) return false;
@@ -597,6 +619,113 @@ __global__ void __launch_bounds__(kLifWsThreads, 1)
     if (!body(q, va, vb)) return;
     if (q == 0 || !body(q - 1, vb, va)) return;
   }
+}
+
+// ------------------------------------------ time-segmented backward (summary)
+//
+// With few sequences the backward has few units (one per 256-channel group
+// and sequence) and each is a serial sweep over T. The adjoint recurrence is
+// affine in g: per step, with the membrane recomputed from the checkpoints,
+//   g_prev = decay * (dsdv * (g * (reset - vn) + gs) + (spike ? g * 0 : g))
+// so a segment of steps maps the adjoint entering from its end, G, to
+// g_start = A * G + B. This kernel composes (A, B) for segments 1 .. nseg-1,
+// with the operations of lif_grad_tile. A CTA takes one 64-channel block,
+// sequence and segment; its kLifWarps warps compose consecutive quarters of
+// the segment's sub-tiles (plain coalesced loads, the next sub-tile's loads
+// issued before the current one is processed) and warp 0 chains the quarters'
+// maps, latest first. The warp-specialized kernel then runs every segment at
+// once from its entering adjoint (the later segments' maps applied to zero):
+// the last segment's gradients are bit-identical to the one-segment sweep,
+// the others agree to rounding.
+template <typename T, bool kPlain>
+__global__ void __launch_bounds__(32 * kLifWarps) lif_bwd_summary_kernel(const LifArgs a) {
+  using P = Pair<T>;
+  using raw = typename P::raw;
+  __shared__ f2 part[kLifWarps][2][kLanes / 2];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cb = blockIdx.x % a.ncblk, b = blockIdx.x / a.ncblk;  // (channel block, sequence)
+  const int c = cb * kLanes + 2 * lane;
+  const bool on = c < a.C;  // the TMA path has C a multiple of 4: a pair is in or out
+  const int s = blockIdx.y + 1;
+  constexpr int QT = lif_ws_rows<T>() / kSub;
+  const int s_begin = s * a.seg_tiles * QT, s_end = min(a.ntiles, (s + 1) * a.seg_tiles * QT);
+  const int per_warp = (s_end - s_begin + kLifWarps - 1) / kLifWarps;
+  const int q_begin = min(s_end, s_begin + warp * per_warp), q_end = min(s_end, q_begin + per_warp);
+  const LifK k = lif_constants(a);
+  const T* xg = static_cast<const T*>(a.x);
+  const T* gg = static_cast<const T*>(a.gs);
+  const raw zero{};
+  auto load = [&](int q, raw (&xo)[kSub], raw (&go)[kSub], f2& m) {
+    const int t0 = q * kSub;
+#pragma unroll
+    for (int i = 0; i < kSub; ++i) {
+      const bool ok = on && t0 + i < a.T;
+      const size_t r = ((size_t)b * a.T + t0 + i) * a.C + c;
+      xo[i] = ok ? P::ld(xg + r) : zero;
+      go[i] = ok ? P::ld(gg + r) : zero;
+    }
+    m = on ? *reinterpret_cast<const f2*>(a.state + ((size_t)b * a.ntiles + q) * a.C + c) : k.zero;
+  };
+  f2 A = k.one, B = k.zero;
+  auto compose = [&](int q, const raw (&xi)[kSub], const raw (&gi)[kSub], f2 m) {
+    const int rows = min(kSub, a.T - q * kSub);
+    f2 vp[kSub];
+#pragma unroll
+    for (int i = 0; i < kSub; ++i) {
+      if (i < rows) {
+        uint32_t w0, w1;
+        lif_step<T, kPlain>(m, P::unpack(xi[i]), k, vp[i], w0, w1);
+      }
+    }
+#pragma unroll
+    for (int i = kSub - 1; i >= 0; --i) {
+      if (i < rows) {
+        const f2 d = sub2(vp[i], k.thr);
+        const f2 cen = kPlain ? d : mul2(k.slope, d);
+        f2 dsdv;
+        if constexpr (kPlain) {
+          const f2 h = mul2(k.hq, d);
+          dsdv = rcpx2(fma2(h, h, k.cq));
+        } else {
+          const f2 h = mul2(k.half_pi, cen);
+          dsdv = mul2(k.half_slope, rcpx2(fma2(h, h, k.one)));
+        }
+        const f2 rv = sub2(k.reset, vp[i]);
+        const f2 a0 = mul2(A, k.zero), b0 = mul2(B, k.zero);
+        const f2 as = f2{cen.x >= 0.f ? a0.x : A.x, cen.y >= 0.f ? a0.y : A.y};
+        const f2 bs = f2{cen.x >= 0.f ? b0.x : B.x, cen.y >= 0.f ? b0.y : B.y};
+        A = mul2(k.decay, fma2(dsdv, mul2(A, rv), as));
+        B = mul2(k.decay, fma2(dsdv, fma2(B, rv, P::unpack(gi[i])), bs));
+      }
+    }
+  };
+  if (q_begin < q_end) {
+    raw xa[kSub], ga[kSub], xb[kSub], gb[kSub];
+    f2 ma, mb;
+    load(q_end - 1, xa, ga, ma);
+#pragma unroll 1
+    for (int q = q_end - 1; q >= q_begin; q -= 2) {
+      if (q - 1 >= q_begin) load(q - 1, xb, gb, mb);
+      compose(q, xa, ga, ma);
+      if (q - 1 < q_begin) break;
+      if (q - 2 >= q_begin) load(q - 2, xa, ga, ma);
+      compose(q - 1, xb, gb, mb);
+    }
+  }
+  part[warp][0][lane] = A;
+  part[warp][1][lane] = B;
+  __syncthreads();
+  if (warp != 0 || !on) return;
+  // g_start = A_0 (A_1 ( ... (A_last G + B_last) ... ) + B_1) + B_0
+  f2 At = k.one, Bt = k.zero;
+  for (int w = kLifWarps - 1; w >= 0; --w) {
+    const f2 Aw = part[w][0][lane], Bw = part[w][1][lane];
+    Bt = fma2(Aw, Bt, Bw);
+    At = mul2(Aw, At);
+  }
+  float* p = a.seg_sum + ((size_t)b * a.nseg + s) * 2 * a.C + c;
+  *reinterpret_cast<f2*>(p) = At;
+  *reinterpret_cast<f2*>(p + a.C) = Bt;
 }
 
 }  // namespace wkv

@@ -45,7 +45,7 @@ __device__ unsigned g_device_error_flags = 0;
 enum Kind {
   K_FWD_Y, K_FWD_STATE, K_BWD_GRAD, K_BWD_ADJ, K_CARRY_FWD, K_CARRY_ADJ, K_STEP, K_LIF_FWD, K_LIF_BWD,
   K_MIX_FWD, K_MIX_BWD, K_MIX_RED,
-  K_GATE_FWD, K_GATE_BWD, K_RSQ_FWD, K_RSQ_BWD, K_RESID,
+  K_GATE_FWD, K_GATE_BWD, K_RSQ_FWD, K_RSQ_BWD, K_RESID, K_LIF_SUM,
   K_COUNT
 };
 const char* const kKindNames[K_COUNT] = {
@@ -54,7 +54,7 @@ const char* const kKindNames[K_COUNT] = {
     "wkv_step_kernel",        "lif_fwd_kernel",        "lif_bwd_kernel",
     "ln_mix_fwd_kernel",      "ln_mix_bwd_kernel",     "ln_mix_reduce_kernel",
     "gate_fwd_kernel",        "gate_bwd_kernel",       "relu_square_fwd_kernel",
-    "relu_square_bwd_kernel", "residual_add_kernel"};
+    "relu_square_bwd_kernel", "residual_add_kernel",   "lif_bwd_summary_kernel"};
 
 std::atomic<long long> g_launches[K_COUNT];
 std::atomic<bool> g_timing{false};
@@ -877,9 +877,45 @@ int wkv_step(int dtype, int state_dtype, const void* key, const void* value,
   return WKV_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+// Time segments of the LIF backward's TMA path: with few units (256-channel
+// groups x sequences) for the SMs, the sweep over T is split into up to 16
+// segments of at least two staged tiles (segment summaries, then every
+// segment at once); 1 when the units fill half the GPU or the shape has no
+// TMA path. seg_tiles: staged tiles per segment. The debug override
+// force_segments (> 1) sets the count.
+int lif_bwd_segments(int dtype, int64_t B, int64_t T, int64_t C, int* seg_tiles) {
+  const int64_t rt = dtype == WKV_DTYPE_F32 ? lif_ws_rows<float>() : lif_ws_rows<__nv_bfloat16>();
+  const int64_t tiles = (T + rt - 1) / rt;
+  *seg_tiles = (int)tiles;
+  if ((C * (int64_t)dtype_size(dtype)) % 16 != 0 || tiles < 4) return 1;
+  const int64_t units = ((C + kLanes - 1) / kLanes + kLifWarps - 1) / kLifWarps * B;
+  const int forced = g_force_segments.load();
+  int64_t nseg = forced > 1 ? forced : (2 * units <= 148 ? std::min<int64_t>(16, 148 / std::max<int64_t>(1, units)) : 1);
+  nseg = std::min<int64_t>(nseg, tiles / 2);
+  if (nseg < 2) return 1;
+  const int64_t per = (tiles + nseg - 1) / nseg;
+  *seg_tiles = (int)per;
+  return (int)((tiles + per - 1) / per);
+}
+
+size_t lif_ckpt_bytes(int64_t B, int64_t T, int64_t C) {
+  return round_up((size_t)B * ((T + kSub - 1) / kSub) * C * sizeof(float));
+}
+
+}  // namespace
+
+extern "C" {
+
 size_t lif_state_size(int dtype, int64_t B, int64_t T, int64_t C) {
   if (check_dims(dtype, B, T, C)) return 0;
-  return round_up((size_t)B * ((T + kSub - 1) / kSub) * C * sizeof(float));
+  int per = 0;
+  const int nseg = lif_bwd_segments(dtype, B, T, C, &per);
+  const size_t sums = nseg > 1 ? round_up((size_t)B * nseg * 2 * C * sizeof(float)) : 0;
+  return lif_ckpt_bytes(B, T, C) + sums;
 }
 
 }  // extern "C"
@@ -951,7 +987,8 @@ int lif_launch_forward(LifArgs& a, bool tma, cudaStream_t st) {
 template <typename IO, bool kTma, bool kPlain>
 void lif_bwd_go(const LifArgs& a, const CUtensorMap& mx, const CUtensorMap& mg, const CUtensorMap& mst,
                 const CUtensorMap& mo, unsigned grid, size_t sm, cudaStream_t st) {
-  if constexpr (kTma) lif_bwd_ws_kernel<IO, kPlain><<<grid, kLifWsThreads, sm, st>>>(a, mx, mg, mst, mo);
+  if constexpr (kTma)
+    lif_bwd_ws_kernel<IO, kPlain><<<dim3(grid, (unsigned)a.nseg), kLifWsThreads, sm, st>>>(a, mx, mg, mst, mo);
   else lif_bwd_kernel<IO, kPlain><<<grid, 32 * kLifWarps, sm, st>>>(a);
 }
 
@@ -985,6 +1022,18 @@ int lif_launch_backward(LifArgs& a, bool tma, cudaStream_t st) {
   // groups fastest); generic path: kLifWarps consecutive units per CTA
   const unsigned grid = tma ? (unsigned)((a.ncblk + kLifWarps - 1) / kLifWarps) * (unsigned)a.B
                             : (unsigned)(((int64_t)a.ncblk * a.B + kLifWarps - 1) / kLifWarps);
+  a.nseg = 1;
+  if (tma) {
+    a.nseg = lif_bwd_segments(dt, a.B, a.T, a.C, &a.seg_tiles);
+    a.seg_sum = reinterpret_cast<float*>(reinterpret_cast<char*>(a.state) + lif_ckpt_bytes(a.B, a.T, a.C));
+  }
+  if (a.nseg > 1) {
+    const dim3 sg((unsigned)((int64_t)a.ncblk * a.B), (unsigned)(a.nseg - 1));  // CTA: block, sequence, segment
+    launch(K_LIF_SUM, st, [&] {
+      if (plain) lif_bwd_summary_kernel<IO, true><<<sg, 32 * kLifWarps, 0, st>>>(a);
+      else lif_bwd_summary_kernel<IO, false><<<sg, 32 * kLifWarps, 0, st>>>(a);
+    });
+  }
   launch(K_LIF_BWD, st, [&] {
     if (tma && plain) lif_bwd_go<IO, true, true>(a, mx, mg, mst, mo, grid, sm, st);
     else if (tma) lif_bwd_go<IO, true, false>(a, mx, mg, mst, mo, grid, sm, st);
@@ -1027,7 +1076,7 @@ int lif_forward(int dtype, const void* x, void* spikes, float* state, size_t sta
   }
 }
 
-int lif_backward(int dtype, const void* grad_spikes, const void* x, const float* state,
+int lif_backward(int dtype, const void* grad_spikes, const void* x, float* state,
                  size_t state_bytes, void* grad_x, int64_t B, int64_t T, int64_t C, float tau,
                  float threshold, float reset, float slope, void* stream) {
   g_last_error[0] = '\0';
@@ -1044,7 +1093,7 @@ int lif_backward(int dtype, const void* grad_spikes, const void* x, const float*
   a.x = x;
   a.gs = grad_spikes;
   a.gx = grad_x;
-  a.state = const_cast<float*>(state);
+  a.state = state;
   const bool tma = g_force_generic.load() == 0 && aligned16(x) && aligned16(grad_spikes) &&
                    aligned16(grad_x) && (C * (int64_t)dtype_size(dtype)) % 16 == 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);

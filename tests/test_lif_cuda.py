@@ -163,3 +163,72 @@ def test_lif_kernels_are_counted(cuda):
     after = _capi.launch_counts()
     assert after["lif_fwd_kernel"] == before["lif_fwd_kernel"] + 1
     assert after["lif_bwd_kernel"] == before["lif_bwd_kernel"] + 1
+
+
+def _lif_grad(x_np, gs_np, dtype, device, generic=False, segments=0):
+    _capi.set_debug_overrides(force_segments=segments, force_generic=int(generic))
+    try:
+        return _run(x_np, gs_np, dtype, device)
+    finally:
+        _capi.set_debug_overrides()
+
+
+@pytest.mark.parametrize("dtype,shape", [(torch.float32, (4, 512, 256)), (torch.bfloat16, (3, 1000, 512)),
+                                         (torch.float32, (1, 333, 64))])
+def test_segmented_backward(cuda, dtype, shape):
+    """Few sequences: the TMA backward splits T into segments (per-segment
+    adjoint maps, then all segments at once). The last segment's gradients
+    equal the one-sweep generic kernel's bit for bit (same operations from a
+    zero adjoint), the earlier ones agree to float32 rounding, and both match
+    the oracle."""
+    rng = np.random.default_rng(sum(shape) + 7)
+    x = (rng.standard_normal(shape) * 1.5 + 0.3).astype(np.float32)
+    gs = rng.standard_normal(shape).astype(np.float32)
+    s_seg, gx_seg, xr = _lif_grad(x, gs, dtype, cuda)
+    s_one, gx_one, _ = _lif_grad(x, gs, dtype, cuda, generic=True)
+    np.testing.assert_array_equal(s_seg, s_one)
+    rt = 16 if dtype == torch.float32 else 32
+    tiles = -(-shape[1] // rt)
+    units = -(-(-(-shape[2] // 64)) // 4) * shape[0]
+    nseg = min(16, 148 // units, tiles // 2)
+    per = -(-tiles // nseg)
+    last0 = (-(-tiles // per) - 1) * per * rt  # first step of the last segment
+    assert 0 < last0 < shape[1]
+    np.testing.assert_array_equal(gx_seg[:, last0:], gx_one[:, last0:])
+    tol = TOL_FP32 if dtype == torch.float32 else TOL_16BIT
+    assert scaled_err(gx_seg, gx_one) <= tol
+    gs_r = torch.as_tensor(gs).to(dtype).double().numpy()
+    s_ref, gx_ref = _oracle(xr, gs_r, tau=2.0, threshold=1.0, reset=0.0, surrogate_slope=2.0)
+    np.testing.assert_array_equal(s_seg, s_ref)
+    assert scaled_err(gx_seg, gx_ref) <= tol
+
+
+@pytest.mark.parametrize("segments", [2, 3, 7])
+def test_forced_segment_counts(cuda, segments):
+    shape = (2, 230, 72)  # 15 staged tiles of 16 rows, a ragged last one; 72 channels: a partial block
+    rng = np.random.default_rng(segments)
+    x = (rng.standard_normal(shape) * 2).astype(np.float32)
+    gs = rng.standard_normal(shape).astype(np.float32)
+    s, gx, xr = _lif_grad(x, gs, torch.float32, cuda, segments=segments)
+    s_ref, gx_ref = _oracle(xr, gs, tau=2.0, threshold=1.0, reset=0.0, surrogate_slope=2.0)
+    np.testing.assert_array_equal(s, s_ref)
+    assert scaled_err(gx, gx_ref) <= TOL_FP32
+
+
+def test_segmented_non_finite_inputs(cuda):
+    """Non-finite currents in different segments: NaNs of the gradients in the
+    oracle's places (a NaN adjoint in a later segment reaches every earlier
+    segment through its map, as it does through the sweep)."""
+    rng = np.random.default_rng(12)
+    x = (rng.standard_normal((2, 128, 64)) * 1.5).astype(np.float32)
+    x[0, 3, 5] = np.inf
+    x[0, 70, 6] = -np.inf
+    x[1, 40, 7] = np.nan
+    x[1, 100, 8] = np.inf
+    gs = rng.standard_normal(x.shape).astype(np.float32)
+    s, gx, _ = _lif_grad(x, gs, torch.float32, cuda, segments=4)
+    s_ref, gx_ref = _oracle(x, gs, tau=2.0, threshold=1.0, reset=0.0, surrogate_slope=2.0)
+    np.testing.assert_array_equal(s, s_ref)
+    np.testing.assert_array_equal(np.isnan(gx), np.isnan(gx_ref))
+    ok = ~np.isnan(gx_ref)
+    assert scaled_err(gx[ok], gx_ref[ok]) <= TOL_FP32
