@@ -266,17 +266,31 @@ __global__ void __launch_bounds__(kMixMaxC / 4, 3) ln_mix_bwd_kernel(const MixAr
 
 // Column sums of the per-CTA partials: out[k][c] for the 2 + n rows k (dw,
 // db, dm_i). A CTA of 32 x 32 threads takes 32 columns of one row k; thread
-// (y, x) sums the partials y, y + 32, ... of column x, then the 32 partial sums
-// of a column are added in y order (a fixed order: the result does not depend
-// on timing).
+// (y, x) sums the partials j = y (mod 32) of column x into four accumulators
+// by j / 32 mod 4 (four independent load chains), adds them in order, then the
+// 32 partial sums of a column are added in y order (a fixed order: the result
+// does not depend on timing).
 __global__ void __launch_bounds__(1024) ln_mix_reduce_kernel(const float* partial, int nchunks, int rows, int C,
                                                              float* gw, float* gb, float* gmix) {
   __shared__ float part[32][33];
   const int k = blockIdx.y;
   const int c = blockIdx.x * 32 + threadIdx.x;
   float s = 0.f;
-  if (c < C)
-    for (int j = threadIdx.y; j < nchunks; j += 32) s += partial[((size_t)j * rows + k) * C + c];
+  if (c < C) {
+    const float* col = partial + (size_t)k * C + c;
+    const size_t step = (size_t)32 * rows * C;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    int j = threadIdx.y;
+    for (; j + 96 < nchunks; j += 128) {
+      const float* p = col + (size_t)j * rows * C;
+      a0 += p[0];
+      a1 += p[step];
+      a2 += p[2 * step];
+      a3 += p[3 * step];
+    }
+    for (; j < nchunks; j += 32) a0 += col[(size_t)j * rows * C];
+    s = (a0 + a1) + (a2 + a3);
+  }
   part[threadIdx.y][threadIdx.x] = s;
   __syncthreads();
   if (threadIdx.y != 0 || c >= C) return;
