@@ -68,6 +68,9 @@ WORKLOADS["train"] = dict(kind="train", model="41m", global_batch=64, T=1024, zi
 WORKLOADS["train216m"] = dict(kind="train", model="216m", global_batch=32, T=1024, zipf=1.05,
                               desc="config 4: 216M-class SpikeGPT train step (18L/768d/V=50257/ctx1024), "
                                    "global batch 32, bf16 autocast, AdamW wd 0.1")
+WORKLOADS["rwkv7"] = dict(kind="rwkv7", B=16, T=1024, H=12, dtype="fp32",
+                          desc="config 4 extra: RWKV-7 DPLR forward, H=12 heads of 64, B=16, T=1024, float32")
+RWKV7_METRIC = "RWKV-7 DPLR forward algorithmic HBM throughput"
 LIF_METRIC = "LIF fwd+bwd algorithmic HBM throughput"
 TRAIN_METRIC = "SpikeGPT-41M train tokens/s"
 TRAIN_METRICS = {"41m": TRAIN_METRIC, "216m": "SpikeGPT-216M train tokens/s"}
@@ -670,6 +673,155 @@ def run_lif(args, wl):
         dist.destroy_process_group()
 
 
+def run_rwkv7(args, wl):
+    """RWKV-7 DPLR forward: one rwkv7_forward per step through the C ABI on
+    device-resident inputs. Algorithmic bytes per element: r, w, k, v, a, b in
+    and y out, 7 x 4 B (the per-head state stays on chip)."""
+    import torch
+    import torch.distributed as dist
+
+    from spikegpt_b200 import _capi
+    from spikegpt_b200.rwkv7 import HEAD_SIZE, dplr_inputs, rwkv7_forward_op
+    from spikegpt_b200.sharding import max_over_ranks
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    b, t, h = wl["B"], wl["T"], wl["H"]
+    host = dplr_inputs(b, t, h, seed=rank)
+    ins = [x.to(dev) for x in host]
+    y = torch.empty_like(ins[0])
+    s_out = torch.empty((b, h, HEAD_SIZE, HEAD_SIZE), dtype=torch.float32, device=dev)
+    lib = _capi.lib()
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    ptrs = [x.data_ptr() for x in ins]
+
+    def step():
+        _capi.check(lib.rwkv7_forward(*ptrs, None, y.data_ptr(), s_out.data_ptr(), b, t, h, HEAD_SIZE, sp),
+                    "rwkv7_forward")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    sampler = None if args.profile else ClockSampler(local)
+    time.sleep(0.3 if sampler else 0)
+    _capi.timing_collect()
+    _capi.timing_enable(True)
+    launches0 = sum(_capi.launch_counts().values())
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    host0 = time.time()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    host1 = time.time()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    _capi.timing_enable(False)
+    launches = sum(_capi.launch_counts().values()) - launches0
+    per_kernel = _capi.timing_collect()
+    ms = max_over_ranks(ev0.elapsed_time(ev1), dev)
+    if sampler:
+        time.sleep(0.25)
+        sampler.stop()
+    clocks = sampler.summary(host0, host1) if sampler else None
+    elems = b * t * h * HEAD_SIZE
+    alg = 7 * 4 * elems
+    value = alg * args.steps * world / (ms * 1e-3) / 1e9
+    tot, cnt = per_kernel["rwkv7_fwd_kernel"]
+    pk = peaks()
+    hbm = float(pk.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+    achieved = alg / (tot / cnt * 1e-3) / 1e9
+    result = {
+        "metric": RWKV7_METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded torch; rwkv7.dplr_inputs)",
+        "tokens_per_s": b * t * args.steps * world / (ms * 1e-3),
+        "config": {"workload": wl["desc"], "B_per_gpu": b, "T": t, "H": h, "head_size": HEAD_SIZE,
+                   "parallelism": f"{world} batch-sharded replica(s), no collective",
+                   "l2": f"{alg / 1e6:.0f} MB moved per step (> L2); no flush",
+                   "form": "sequential over T on CUDA cores (the chunked tensor-core form is not built)"},
+        "roofline": {"kernel": "rwkv7_fwd_kernel", "bound": "hbm", "achieved": achieved, "peak": hbm,
+                     "unit": "GB/s", "frac": achieved / hbm, "alg_bytes_per_launch": alg,
+                     "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if pk.get("source") == "measured"
+                     else "fallback 6.65 TB/s", "traffic": ncu_traffic("rwkv7_fwd_kernel", args.workload)},
+        "gpu_launches": int(launches), "clocks": clocks,
+    }
+    if not args.profile:
+        pins = [x.pin_memory() for x in host]
+        hy = torch.empty_like(pins[0]).pin_memory()
+
+        def e2e_step():
+            yd, _ = rwkv7_forward_op(*(x.to(dev, non_blocking=True) for x in pins))
+            hy.copy_(yd, non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ems = max_over_ranks(e0.elapsed_time(e1), dev)
+        result["e2e"] = {"value": alg * args.e2e_steps * world / (ems * 1e-3) / 1e9, "unit": "GB/s",
+                         "h2d_bytes_per_step": 6 * 4 * elems, "d2h_bytes_per_step": 4 * elems,
+                         "steps": args.e2e_steps, "ms_per_step": ems / args.e2e_steps,
+                         "path": "spikegpt_b200.rwkv7.rwkv7_forward_op, pinned host buffers"}
+        if world == 1 and rank == 0:
+            result["cpu_baseline"] = cpu_rwkv7_throughput(wl)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def cpu_rwkv7_throughput(wl: dict, seconds: float = 3.0):
+    """The float64 numpy restatement (oracle) on one sequence of the workload."""
+    from oracle import oracle
+    from spikegpt_b200.rwkv7 import HEAD_SIZE, dplr_inputs
+
+    ins = [x.numpy() for x in dplr_inputs(1, wl["T"], wl["H"], seed=0)]
+    n, t0 = 0, time.perf_counter()
+    while True:
+        oracle.rwkv7_forward_numpy(*ins)
+        n += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": 7 * 4 * wl["T"] * wl["H"] * HEAD_SIZE * n / dt / 1e9, "unit": "GB/s", "cores": 1,
+            "kind": "port", "sample": f"{n} x (1 of {wl['B']} sequences, T={wl['T']}, H={wl['H']}), numpy float64",
+            "note": "the reference has no RWKV-7 code; the oracle restates the published recurrence"}
+
+
+def run_rwkv7_reference(args, wl):
+    """Reference arm of the RWKV-7 workload: the reference ships no
+    implementation, so the arm times the oracle restatement on the host."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    base = cpu_rwkv7_throughput(wl, seconds=2.0)
+    print(json.dumps({"metric": RWKV7_METRIC, "value": base["value"], "unit": "GB/s",
+                      "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
+                      "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                      "dtype": "fp32", "data": "synthetic", "config": {"workload": wl["desc"]},
+                      "impl": "reference", "cpu_baseline": base,
+                      "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
+                              "d2h_bytes_per_step": 0}}), flush=True)
+
+
 def cpu_lif_throughput(wl: dict, seconds: float = 5.0):
     """The float32 LIF oracle fwd+bwd (a single-threaded C loop) on one batch row."""
     from oracle import oracle
@@ -1066,6 +1218,11 @@ def main():
             run_step_reference(args, wl)
         else:
             run_step(args, wl)
+    elif wl.get("kind") == "rwkv7":
+        if args.impl == "reference":
+            run_rwkv7_reference(args, wl)
+        else:
+            run_rwkv7(args, wl)
     elif wl.get("kind") == "lif":
         if args.impl == "reference":
             run_lif_reference(args, wl)

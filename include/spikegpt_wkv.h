@@ -237,6 +237,21 @@ WKV_API int relu_square_backward(const void* grad_out, const void* k, void* grad
 WKV_API int residual_add_forward(const float* x, const void* spikes, float* out, int64_t n, void* stream);
 
 /*
+ * RWKV-7 diagonal-plus-low-rank time mixing, forward (the optional op of the
+ * 216M configuration; the reference has no code for it, only prose about an
+ * external library's kernel, so the restatement is the published state update):
+ * per sequence b and head h, with S [N][N] (rows value channels, columns key
+ * channels), S_0 = state_in (or zero when null),
+ *   S_t = S_{t-1} diag(w_t) + (S_{t-1} a_t) b_t^T + v_t k_t^T,   y_t = S_t r_t.
+ * r, w, k, v, a, b, y: [B, T, H, N] float32, 16-byte aligned; N = 64;
+ * state_in / state_out [B, H, N, N] float32 or null. Sequential over T
+ * (one CTA per sequence and head, the state in registers).
+ */
+WKV_API int rwkv7_forward(const float* r, const float* w, const float* k, const float* v, const float* a,
+                          const float* b, const float* state_in, float* y, float* state_out, int64_t B,
+                          int64_t T, int64_t H, int64_t N, void* stream);
+
+/*
  * Forward/backward with a saved forward state (no reference counterpart; an
  * optimisation of wkv_forward/wkv_backward). wkv_forward_with_state computes y exactly as
  * wkv_forward and also stores the recurrence state at every 16th step into

@@ -282,3 +282,22 @@ def backward_numpy(gy, w, u, k, v):
             gq = a * gq - e * yt
             o = no
     return gk, gv, (gw * w).sum(0), gu.sum(0)
+
+
+def rwkv7_forward_numpy(r, w, k, v, a, b, s0=None):
+    """RWKV-7 diagonal-plus-low-rank recurrence in numpy float64 (parity
+    unpinned: the reference ships no code for it; this restates the published
+    state update). Tensors [B, T, H, N]; per (b, h) with S [N, N] (rows value
+    channels, columns key channels):
+        S_t = S_{t-1} diag(w_t) + (S_{t-1} a_t) b_t^T + v_t k_t^T,   y_t = S_t r_t.
+    Returns (y [B, T, H, N], final state [B, H, N, N])."""
+    r, w, k, v, a, b = (np.asarray(x, np.float64) for x in (r, w, k, v, a, b))
+    bsz, t, h, n = r.shape
+    s = np.zeros((bsz, h, n, n)) if s0 is None else np.array(s0, np.float64)
+    y = np.empty_like(r)
+    for i in range(t):
+        sa = np.einsum("bhij,bhj->bhi", s, a[:, i])
+        s = s * w[:, i][:, :, None, :] + sa[..., None] * b[:, i][:, :, None, :] \
+            + v[:, i][..., None] * k[:, i][:, :, None, :]
+        y[:, i] = np.einsum("bhij,bhj->bhi", s, r[:, i])
+    return y, s

@@ -22,6 +22,7 @@
 #include "gates.cuh"
 #include "lif.cuh"
 #include "ln_mix.cuh"
+#include "rwkv7.cuh"
 #include "wkv_step.cuh"
 #include "wkv_tp.cuh"
 
@@ -45,7 +46,7 @@ __device__ unsigned g_device_error_flags = 0;
 enum Kind {
   K_FWD_Y, K_FWD_STATE, K_BWD_GRAD, K_BWD_ADJ, K_CARRY_FWD, K_CARRY_ADJ, K_STEP, K_LIF_FWD, K_LIF_BWD,
   K_MIX_FWD, K_MIX_BWD, K_MIX_RED,
-  K_GATE_FWD, K_GATE_BWD, K_RSQ_FWD, K_RSQ_BWD, K_RESID, K_LIF_SUM,
+  K_GATE_FWD, K_GATE_BWD, K_RSQ_FWD, K_RSQ_BWD, K_RESID, K_LIF_SUM, K_R7_FWD,
   K_COUNT
 };
 const char* const kKindNames[K_COUNT] = {
@@ -54,7 +55,8 @@ const char* const kKindNames[K_COUNT] = {
     "wkv_step_kernel",        "lif_fwd_kernel",        "lif_bwd_kernel",
     "ln_mix_fwd_kernel",      "ln_mix_bwd_kernel",     "ln_mix_reduce_kernel",
     "gate_fwd_kernel",        "gate_bwd_kernel",       "relu_square_fwd_kernel",
-    "relu_square_bwd_kernel", "residual_add_kernel",   "lif_bwd_summary_kernel"};
+    "relu_square_bwd_kernel", "residual_add_kernel",   "lif_bwd_summary_kernel",
+    "rwkv7_fwd_kernel"};
 
 std::atomic<long long> g_launches[K_COUNT];
 std::atomic<bool> g_timing{false};
@@ -1337,6 +1339,27 @@ int residual_add_forward(const float* x, const void* spikes, float* out, int64_t
                                                                 n);
   });
   return launched("residual_add launch");
+}
+
+int rwkv7_forward(const float* r, const float* w, const float* k, const float* v, const float* a,
+                  const float* b, const float* state_in, float* y, float* state_out, int64_t B, int64_t T,
+                  int64_t H, int64_t N, void* stream) {
+  g_last_error[0] = '\0';
+  if (N != kR7N) return fail(WKV_ERR_INVALID_ARGUMENT, "head size must be %d, got %lld", kR7N, (long long)N);
+  if (B < 0 || T < 0 || H < 0) return fail(WKV_ERR_INVALID_ARGUMENT, "negative size");
+  if (B * H > (1ll << 31) - 1 || B * T * H * N > (1ll << 40))
+    return fail(WKV_ERR_INVALID_ARGUMENT, "sizes out of range");
+  if (B == 0 || H == 0) return WKV_OK;
+  if (T > 0 && (!r || !w || !k || !v || !a || !b || !y))  // an empty sequence reads no step vectors
+    return fail(WKV_ERR_INVALID_ARGUMENT, "null pointer");
+  for (const void* q : {static_cast<const void*>(r), static_cast<const void*>(w), static_cast<const void*>(k),
+                        static_cast<const void*>(v), static_cast<const void*>(a), static_cast<const void*>(b),
+                        static_cast<const void*>(y)})
+    if (!aligned16(q)) return fail(WKV_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
+  R7Args p{r, w, k, v, a, b, state_in, y, state_out, (int)B, (int)T, (int)H};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  launch(K_R7_FWD, st, [&] { rwkv7_fwd_kernel<<<(unsigned)(B * H), kR7Threads, 0, st>>>(p); });
+  return launched("rwkv7 forward launch");
 }
 
 int wkv_kernel_kinds(void) { return K_COUNT; }
