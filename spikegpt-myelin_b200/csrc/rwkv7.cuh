@@ -10,27 +10,27 @@
 //
 // Layout: one CTA of 64 threads per (b, h); thread (rb, q) = (tid / 4, tid % 4)
 // keeps the 4 x 16 block S[4rb .. 4rb+3][16q .. 16q+15] in registers, so each
-// step vector read from shared memory serves four state rows. Per step it
-// forms its part of (S a) and of y for its four rows, the four partial sums
-// of a row meet in two xor shuffles (fixed order), and it updates its 64
-// entries with two fused multiply-adds and a multiply each. The step vectors
-// of kChunk steps at a time are staged in shared memory by coalesced float4
-// loads; y leaves the same way. Serial in T by construction: this is the
-// sequential form of the op on CUDA cores (the chunked tensor-core form is not
-// built).
+// step vector read from shared memory serves four state rows (two rows a
+// thread measured slower: twice the shared-memory reads per entry). Per step it
+// forms its part of (S a) and of y for its rows, the four partial sums of a
+// row meet in two xor shuffles (fixed order), and it updates its 64 entries
+// with two fused multiply-adds and a multiply each. The step vectors of
+// kChunk steps at a time are staged in shared memory by asynchronous 16-byte
+// copies, double-buffered (chunk c+1 lands while chunk c is computed); y
+// leaves through shared memory by coalesced float4 stores. Serial in T by
+// construction: this is the sequential form of the op on CUDA cores (the
+// chunked tensor-core form is not built).
 #pragma once
 
-#include <cuda_runtime.h>
-
-#include <cstdint>
+#include "wkv_device.cuh"
 
 namespace wkv {
 
 constexpr int kR7N = 64;           // head size
-constexpr int kR7Threads = 64;     // 16 row blocks x 4 column blocks
-constexpr int kR7Chunk = 16;       // steps staged per pass
 constexpr int kR7Rows = 4;         // state rows per thread
 constexpr int kR7Cols = kR7N / 4;  // state columns per thread
+constexpr int kR7Threads = (kR7N / kR7Rows) * 4;
+constexpr int kR7Chunk = 8;        // steps staged per pass
 
 struct R7Args {
   const float* r;
@@ -45,9 +45,13 @@ struct R7Args {
   int B, T, H;
 };
 
+__device__ __forceinline__ void r7_cp16(float* dst, const float* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
 __global__ void __launch_bounds__(kR7Threads) rwkv7_fwd_kernel(const R7Args p) {
-  // staged step vectors: [r, w, k, a, b, v][kChunk][N], then y [kChunk][N]
-  __shared__ __align__(16) float st[6][kR7Chunk][kR7N];
+  // staged step vectors, two buffers: [r, w, k, a, b, v][kChunk][N]; y [kChunk][N]
+  __shared__ __align__(16) float st[2][6][kR7Chunk][kR7N];
   __shared__ __align__(16) float ys[kR7Chunk][kR7N];
   const int tid = threadIdx.x;
   const int rb = tid >> 2, q = tid & 3;
@@ -64,32 +68,41 @@ __global__ void __launch_bounds__(kR7Threads) rwkv7_fwd_kernel(const R7Args p) {
     for (int j = 0; j < kR7Cols; ++j) S[r][j] = s0 != nullptr ? s0[j] : 0.f;
   }
   const float* src[6] = {p.r, p.w, p.k, p.a, p.b, p.v};
-#pragma unroll 1
-  for (int t0 = 0; t0 < p.T; t0 += kR7Chunk) {
-    const int n = min(kR7Chunk, p.T - t0);
-    __syncthreads();  // the previous chunk's vectors and y are consumed
-    // loader: 6 x kChunk x 16 float4 over 64 threads; thread -> column float4 tid % 16, steps tid / 16 + 4m
+  const int nch = (p.T + kR7Chunk - 1) / kR7Chunk;
+  // 6 x kChunk x 16 float4 per chunk over the CTA: thread -> float4 column
+  // tid % 16, steps tid / 16 + kR7Threads / 16 * m
+  constexpr int kSteps = kR7Threads / 16;  // steps one pass of the CTA covers
+  auto issue = [&](int c) {
+    const int col = 4 * (tid & 15);
 #pragma unroll
-    for (int s6 = 0; s6 < 6; ++s6) {
+    for (int m = 0; m < kR7Chunk / kSteps; ++m) {
+      const int u = (tid >> 4) + kSteps * m, t = c * kR7Chunk + u;
+      if (t < p.T) {
 #pragma unroll
-      for (int m = 0; m < kR7Chunk / 4; ++m) {
-        const int u = (tid >> 4) + 4 * m, col = 4 * (tid & 15);
-        if (u < n)
-          *reinterpret_cast<float4*>(&st[s6][u][col]) =
-              *reinterpret_cast<const float4*>(src[s6] + seq + (size_t)(t0 + u) * row_stride + head + col);
+        for (int s6 = 0; s6 < 6; ++s6)
+          r7_cp16(&st[c & 1][s6][u][col], src[s6] + seq + (size_t)t * row_stride + head + col);
       }
     }
-    __syncthreads();
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  if (nch > 0) issue(0);
+#pragma unroll 1
+  for (int c = 0; c < nch; ++c) {
+    const int t0 = c * kR7Chunk, n = min(kR7Chunk, p.T - t0);
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();  // chunk c landed; chunk c-1's buffer and y are consumed
+    if (c + 1 < nch) issue(c + 1);
+    float(*sv)[kR7Chunk][kR7N] = st[c & 1];
 #pragma unroll 1
     for (int u = 0; u < n; ++u) {
-      const float* rr = &st[0][u][j0];
-      const float* ww = &st[1][u][j0];
-      const float* kk = &st[2][u][j0];
-      const float* aa = &st[3][u][j0];
-      const float* bb = &st[4][u][j0];
-      const float4 v4 = *reinterpret_cast<const float4*>(&st[5][u][i0]);
+      const float* rr = &sv[0][u][j0];
+      const float* ww = &sv[1][u][j0];
+      const float* kk = &sv[2][u][j0];
+      const float* aa = &sv[3][u][j0];
+      const float* bb = &sv[4][u][j0];
+      const float4 v4 = *reinterpret_cast<const float4*>(&sv[5][u][i0]);
       const float vi[kR7Rows] = {v4.x, v4.y, v4.z, v4.w};
-      // (S a) for the four rows over this thread's columns (two chains a row),
+      // (S a) for the rows over this thread's columns (two chains a row),
       // then over the row's four column blocks
       float sa[kR7Rows];
 #pragma unroll
@@ -129,8 +142,8 @@ __global__ void __launch_bounds__(kR7Threads) rwkv7_fwd_kernel(const R7Args p) {
     }
     __syncthreads();
 #pragma unroll
-    for (int m = 0; m < kR7Chunk / 4; ++m) {
-      const int u = (tid >> 4) + 4 * m, col = 4 * (tid & 15);
+    for (int m = 0; m < kR7Chunk / kSteps; ++m) {
+      const int u = (tid >> 4) + kSteps * m, col = 4 * (tid & 15);
       if (u < n)
         *reinterpret_cast<float4*>(p.y + seq + (size_t)(t0 + u) * row_stride + head + col) =
             *reinterpret_cast<const float4*>(&ys[u][col]);
