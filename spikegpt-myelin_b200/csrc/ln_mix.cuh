@@ -13,7 +13,9 @@
 //   dx     = rstd (dh w - mean(dh w) - xhat mean(dh w xhat))      (LayerNorm)
 //   dw     = sum_rows dh xhat,  db = sum_rows dh,  dm_i = sum_rows g_i[t] (h[t] - h[t-1])
 // the column sums as per-CTA partials reduced in a fixed order by
-// ln_mix_reduce (deterministic).
+// ln_mix_reduce (deterministic). When the sublayer's residual connection
+// passes its gradient in (gres), dx also takes that gradient, so the residual
+// stream's two gradient contributions need no separate add.
 //
 // Layout: a CTA of C/4 threads takes `rows` consecutive steps of one sequence,
 // one row at a time; thread j holds channels 4j .. 4j+3 (a float4 of x, an
@@ -48,6 +50,7 @@ struct MixArgs {
   float* mean;     // [B*T]
   float* rstd;     // [B*T]
   float* gx;       // [B*T][C]
+  const float* gres;  // [B*T][C] or null: the residual connection's gradient, added to gx
   float* partial;  // [B*nct][2 + n][C]: dw, db, dm_0 .. dm_{n-1} per CTA
   int n, B, T, C;
   int rows;  // steps per CTA
@@ -244,9 +247,13 @@ __global__ void __launch_bounds__(kMixMaxC / 4, 3) ln_mix_bwd_kernel(const MixAr
                                 (dw.x * xh.x + dw.y * xh.y) + (dw.z * xh.z + dw.w * xh.w), red, slot);
     slot ^= 1;
     const float s1 = s.x / a.C, s2 = s.y / a.C;
-    *reinterpret_cast<float4*>(a.gx + r * a.C + c) =
-        make_float4(rs * (dw.x - s1 - xh.x * s2), rs * (dw.y - s1 - xh.y * s2), rs * (dw.z - s1 - xh.z * s2),
-                    rs * (dw.w - s1 - xh.w * s2));
+    float4 o = make_float4(__fmul_rn(rs, dw.x - s1 - xh.x * s2), __fmul_rn(rs, dw.y - s1 - xh.y * s2),
+                           __fmul_rn(rs, dw.z - s1 - xh.z * s2), __fmul_rn(rs, dw.w - s1 - xh.w * s2));
+    if (a.gres != nullptr) {  // the skip connection's gradient, one rounded add as autograd's sum
+      const float4 g = ld4(a.gres + r * a.C + c);
+      o = make_float4(__fadd_rn(o.x, g.x), __fadd_rn(o.y, g.y), __fadd_rn(o.z, g.z), __fadd_rn(o.w, g.w));
+    }
+    *reinterpret_cast<float4*>(a.gx + r * a.C + c) = o;
     hp = h;
     v = vn;
     mu = mun;

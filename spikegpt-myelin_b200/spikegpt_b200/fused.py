@@ -16,6 +16,8 @@ multiple of 128 up to 1024; outputs bf16.
 
 from __future__ import annotations
 
+import itertools
+
 import torch
 from torch import Tensor
 
@@ -29,8 +31,23 @@ def supported(x: Tensor) -> bool:
     return x.is_cuda and x.dtype == torch.float32 and x.ndim == 3 and c % 128 == 0 and c <= 1024
 
 
+# The residual connection x + sublayer(ln_shift_mix(x)) gives x two gradient
+# contributions that autograd would sum with one more kernel. A sublayer built
+# with a residual token instead hands the skip connection's gradient from
+# residual_add's backward (which runs first: the sublayer lies between the
+# two) to ln_shift_mix's backward, which adds it to grad x inside its kernel.
+_RESIDUAL_GRADS: dict[int, Tensor] = {}
+_TOKENS = itertools.count(1)
+
+
+def new_residual_token() -> int:
+    """A token pairing one ln_shift_mix with the residual_add that closes its
+    sublayer (0 means no pairing)."""
+    return next(_TOKENS)
+
+
 @torch.library.custom_op("spikegpt_b200::ln_shift_mix", mutates_args=(), device_types="cuda")
-def _ln_shift_mix(x: Tensor, weight: Tensor, bias: Tensor, mix: Tensor, eps: float) -> list[Tensor]:
+def _ln_shift_mix(x: Tensor, weight: Tensor, bias: Tensor, mix: Tensor, eps: float, token: int) -> list[Tensor]:
     b, t, c = x.shape
     n = mix.shape[0]
     outs = [torch.empty((b, t, c), dtype=torch.bfloat16, device=x.device) for _ in range(n)]
@@ -47,7 +64,7 @@ def _ln_shift_mix(x: Tensor, weight: Tensor, bias: Tensor, mix: Tensor, eps: flo
 
 
 @_ln_shift_mix.register_fake
-def _(x, weight, bias, mix, eps):
+def _(x, weight, bias, mix, eps, token):
     b, t, c = x.shape
     return [x.new_empty((b, t, c), dtype=torch.bfloat16) for _ in range(mix.shape[0])] + [
         x.new_empty((b, t)), x.new_empty((b, t))]
@@ -55,7 +72,7 @@ def _(x, weight, bias, mix, eps):
 
 @torch.library.custom_op("spikegpt_b200::ln_shift_mix_backward", mutates_args=(), device_types="cuda")
 def _ln_shift_mix_backward(grads: list[Tensor], x: Tensor, weight: Tensor, bias: Tensor, mix: Tensor,
-                           mean: Tensor, rstd: Tensor) -> list[Tensor]:
+                           mean: Tensor, rstd: Tensor, grad_residual: Tensor | None) -> list[Tensor]:
     b, t, c = x.shape
     n = mix.shape[0]
     gs = [g.to(torch.bfloat16).contiguous() for g in grads]
@@ -69,7 +86,8 @@ def _ln_shift_mix_backward(grads: list[Tensor], x: Tensor, weight: Tensor, bias:
     ptrs = [g.data_ptr() for g in gs] + [None] * (MAX_MIX - n)
     _capi.check(
         lib.ln_mix_backward(n, *ptrs, x.data_ptr(), weight.data_ptr(), bias.data_ptr(), mix.data_ptr(),
-                            mean.data_ptr(), rstd.data_ptr(), gx.data_ptr(), gw.data_ptr(), gb.data_ptr(),
+                            mean.data_ptr(), rstd.data_ptr(),
+                            None if grad_residual is None else grad_residual.data_ptr(), gx.data_ptr(), gw.data_ptr(), gb.data_ptr(),
                             gm.data_ptr(), ws.data_ptr(), nws, b, t, c,
                             torch.cuda.current_stream(x.device).cuda_stream),
         "ln_mix_backward",
@@ -78,15 +96,16 @@ def _ln_shift_mix_backward(grads: list[Tensor], x: Tensor, weight: Tensor, bias:
 
 
 @_ln_shift_mix_backward.register_fake
-def _(grads, x, weight, bias, mix, mean, rstd):
+def _(grads, x, weight, bias, mix, mean, rstd, grad_residual):
     return [torch.empty_like(x), torch.empty_like(weight), torch.empty_like(bias), torch.empty_like(mix)]
 
 
 def _setup(ctx, inputs, output):
-    x, weight, bias, mix, _eps = inputs
+    x, weight, bias, mix, _eps, token = inputs
     n = mix.shape[0]
     ctx.save_for_backward(x, weight, bias, mix, output[n], output[n + 1])
     ctx.n = n
+    ctx.token = token
     ctx.mark_non_differentiable(output[n], output[n + 1])
 
 
@@ -94,16 +113,23 @@ def _backward(ctx, grads):
     x, weight, bias, mix, mean, rstd = ctx.saved_tensors
     gouts = [g if g is not None else torch.zeros(x.shape, dtype=torch.bfloat16, device=x.device)
              for g in grads[: ctx.n]]
-    gx, gw, gb, gm = torch.ops.spikegpt_b200.ln_shift_mix_backward(gouts, x, weight, bias, mix, mean, rstd)
-    return gx, gw, gb, gm, None
+    gres = _RESIDUAL_GRADS.pop(ctx.token, None) if ctx.token else None
+    if gres is not None:
+        gres = _aligned(gres.float())
+    gx, gw, gb, gm = torch.ops.spikegpt_b200.ln_shift_mix_backward(gouts, x, weight, bias, mix, mean, rstd, gres)
+    return gx, gw, gb, gm, None, None
 
 
 _ln_shift_mix.register_autograd(_backward, setup_context=_setup)
 
 
-def ln_shift_mix(x: Tensor, weight: Tensor, bias: Tensor, mixes: list[Tensor], eps: float = 1e-5) -> list[Tensor]:
+def ln_shift_mix(x: Tensor, weight: Tensor, bias: Tensor, mixes: list[Tensor], eps: float = 1e-5,
+                 residual_token: int = 0) -> list[Tensor]:
     """bf16 ``LayerNorm(x) * m + shift(LayerNorm(x)) * (1 - m)`` for each m in
-    ``mixes`` (each [C] or [1, 1, C]); x [B, T, C] float32 CUDA, contiguous."""
+    ``mixes`` (each [C] or [1, 1, C]); x [B, T, C] float32 CUDA, contiguous.
+    ``residual_token`` (from :func:`new_residual_token`) pairs it with the
+    ``residual_add(x, ...)`` that closes the sublayer: the skip connection's
+    gradient is then added to grad x in this op's backward kernel."""
     if not supported(x):
         raise ValueError("ln_shift_mix needs a contiguous float32 CUDA [B, T, C] tensor with C % 128 == 0, C <= 1024")
     if not 1 <= len(mixes) <= MAX_MIX:
@@ -111,7 +137,8 @@ def ln_shift_mix(x: Tensor, weight: Tensor, bias: Tensor, mixes: list[Tensor], e
     c = x.shape[-1]
     mix = torch.cat([m.reshape(1, c).float() for m in mixes], 0)
     outs = torch.ops.spikegpt_b200.ln_shift_mix(x.contiguous(), weight.float().contiguous(),
-                                                bias.float().contiguous(), mix.contiguous(), float(eps))
+                                                bias.float().contiguous(), mix.contiguous(), float(eps),
+                                                int(residual_token))
     return list(outs[: len(mixes)])
 
 
@@ -241,7 +268,7 @@ def relu_square(k: Tensor) -> Tensor:
 
 
 @torch.library.custom_op("spikegpt_b200::residual_add", mutates_args=(), device_types="cuda")
-def _residual_add(x: Tensor, spikes: Tensor) -> Tensor:
+def _residual_add(x: Tensor, spikes: Tensor, token: int) -> Tensor:
     out = torch.empty_like(x)
     _capi.check(_capi.lib().residual_add_forward(x.data_ptr(), spikes.data_ptr(), out.data_ptr(), x.numel(),
                                                  _stream(x)), "residual_add_forward")
@@ -249,24 +276,29 @@ def _residual_add(x: Tensor, spikes: Tensor) -> Tensor:
 
 
 @_residual_add.register_fake
-def _(x, spikes):
+def _(x, spikes, token):
     return torch.empty_like(x)
 
 
 def _resid_setup(ctx, inputs, output):
-    pass
+    ctx.token = inputs[2]
 
 
 def _resid_grad(ctx, grad):
-    return grad, grad.to(torch.bfloat16)
+    if ctx.token:  # the paired ln_shift_mix adds it to grad x in its kernel
+        _RESIDUAL_GRADS[ctx.token] = grad
+        return None, grad.to(torch.bfloat16), None
+    return grad, grad.to(torch.bfloat16), None
 
 
 _residual_add.register_autograd(_resid_grad, setup_context=_resid_setup)
 
 
-def residual_add(x: Tensor, spikes: Tensor) -> Tensor:
-    """float32 ``x + spikes`` for a float32 x and bf16 spikes of one shape (CUDA)."""
+def residual_add(x: Tensor, spikes: Tensor, residual_token: int = 0) -> Tensor:
+    """float32 ``x + spikes`` for a float32 x and bf16 spikes of one shape (CUDA).
+    With the ``residual_token`` of the ln_shift_mix that reads this x, the
+    gradient for x goes to that op's backward instead of a separate sum."""
     if not (x.is_cuda and x.dtype == torch.float32 and spikes.dtype == torch.bfloat16
             and spikes.is_cuda and x.shape == spikes.shape):
         raise ValueError("residual_add needs a float32 x and bf16 spikes of one shape on CUDA")
-    return torch.ops.spikegpt_b200.residual_add(_aligned(x), _aligned(spikes))
+    return torch.ops.spikegpt_b200.residual_add(_aligned(x), _aligned(spikes), int(residual_token))

@@ -184,10 +184,11 @@ class Block(nn.Module):
                              surrogate_slope=cfg.surrogate_slope)
 
     @staticmethod
-    def _residual(x: Tensor, spikes: Tensor) -> Tensor:
-        # float32 residual stream + bf16 spikes: one vectorized kernel
+    def _residual(x: Tensor, spikes: Tensor, token: int = 0) -> Tensor:
+        # float32 residual stream + bf16 spikes: one vectorized kernel; with the
+        # token of the sublayer's ln_shift_mix, x's gradient is summed in there
         if x.dtype == torch.float32 and spikes.dtype == torch.bfloat16 and x.shape == spikes.shape:
-            return fused.residual_add(x, spikes)
+            return fused.residual_add(x, spikes, token)
         return x + spikes
 
     @staticmethod
@@ -202,12 +203,14 @@ class Block(nn.Module):
             x = self.ln0(x)
         if self._fused(x):
             att, ffn = self.att, self.ffn
+            tok = fused.new_residual_token()
             xk, xv, xr = fused.ln_shift_mix(x, self.ln1.weight, self.ln1.bias,
-                                            [att.time_mix_k, att.time_mix_v, att.time_mix_r], self.ln1.eps)
-            x = self._residual(x, self._lif(att.from_mixed(xk, xv, xr)))
+                                            [att.time_mix_k, att.time_mix_v, att.time_mix_r], self.ln1.eps, tok)
+            x = self._residual(x, self._lif(att.from_mixed(xk, xv, xr)), tok)
+            tok = fused.new_residual_token()
             xk, xr = fused.ln_shift_mix(x, self.ln2.weight, self.ln2.bias, [ffn.time_mix_k, ffn.time_mix_r],
-                                        self.ln2.eps)
-            x = self._residual(x, self._lif(ffn.from_mixed(xk, xr)))
+                                        self.ln2.eps, tok)
+            x = self._residual(x, self._lif(ffn.from_mixed(xk, xr)), tok)
         else:
             x = x + self._lif(self.att(self.ln1(x)))
             x = x + self._lif(self.ffn(self.ln2(x)))

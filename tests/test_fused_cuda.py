@@ -89,3 +89,29 @@ def test_kernels_are_counted(cuda):
     after = _capi.launch_counts()
     for k in ("ln_mix_fwd_kernel", "ln_mix_bwd_kernel", "ln_mix_reduce_kernel"):
         assert after[k] > before.get(k, 0)
+
+
+def test_residual_gradient_summed_in_kernel(cuda):
+    """A sublayer closed by residual_add with the ln_shift_mix's token: the
+    skip connection's gradient reaches x through the LayerNorm-mix backward
+    kernel instead of autograd's sum, with the same value bit for bit."""
+    from spikegpt_b200 import fused
+
+    g = torch.Generator(device="cpu").manual_seed(21)
+    shape = (3, 90, 256)
+    x0 = (torch.randn(shape, generator=g) * 2).to(cuda)
+    w = (1 + 0.3 * torch.randn(256, generator=g)).to(cuda)
+    b = (0.2 * torch.randn(256, generator=g)).to(cuda)
+    m = [torch.rand(1, 1, 256, generator=g).to(cuda) for _ in range(2)]
+    go = torch.randn(shape, generator=g).to(cuda)
+
+    def run(paired):
+        x = x0.clone().requires_grad_()
+        tok = fused.new_residual_token() if paired else 0
+        xk, xr = fused.ln_shift_mix(x, w, b, m, 1e-5, tok)
+        out = fused.residual_add(x, fused.gate(xk, xr), tok)
+        out.backward(go)
+        return x.grad
+
+    assert torch.equal(run(True), run(False))
+    assert not fused._RESIDUAL_GRADS  # every handed-over gradient was consumed
