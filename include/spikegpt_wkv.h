@@ -250,6 +250,23 @@ WKV_API int residual_add_forward(const float* x, const void* spikes, float* out,
  * state_in / state_out [B, H, N, N] float32 or null. Sequential over T
  * (one CTA per sequence and head, the state in registers).
  */
+/*
+ * Cross-entropy over bf16 logits (the language-model loss under bf16
+ * autocast; replaces F.cross_entropy(logits.float(), targets) of
+ * src/spikegpt/language.py:1475-1480 and its backward): per row i of a
+ * [rows, ld] bf16 logits buffer whose first V columns are the classes,
+ * loss[i] = logsumexp_j x_ij - x_i,t_i and lse[i] = logsumexp_j x_ij
+ * (float32); rows whose target lies outside [0, V) are ignored (loss 0,
+ * gradient 0). cross_entropy_backward writes grad_logits [rows, ld] bf16:
+ * grad_loss[i] * (softmax_ij - [j == t_i]) for j < V, zero beyond. ld a
+ * multiple of 8, logits and grad_logits 16-byte aligned.
+ */
+WKV_API int cross_entropy_forward(const void* logits, int64_t ld, const int64_t* targets, int64_t rows,
+                                  int64_t V, float* loss, float* lse, void* stream);
+WKV_API int cross_entropy_backward(const void* logits, int64_t ld, const int64_t* targets, const float* lse,
+                                   const float* grad_loss, void* grad_logits, int64_t rows, int64_t V,
+                                   void* stream);
+
 WKV_API int rwkv7_forward(const float* r, const float* w, const float* k, const float* v, const float* a,
                           const float* b, const float* state_in, float* y, float* state_out, int64_t B,
                           int64_t T, int64_t H, int64_t N, void* stream);

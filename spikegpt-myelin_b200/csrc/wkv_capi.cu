@@ -23,6 +23,7 @@
 #include "lif.cuh"
 #include "ln_mix.cuh"
 #include "rwkv7.cuh"
+#include "xent.cuh"
 #include "wkv_step.cuh"
 #include "wkv_tp.cuh"
 
@@ -46,7 +47,7 @@ __device__ unsigned g_device_error_flags = 0;
 enum Kind {
   K_FWD_Y, K_FWD_STATE, K_BWD_GRAD, K_BWD_ADJ, K_CARRY_FWD, K_CARRY_ADJ, K_STEP, K_LIF_FWD, K_LIF_BWD,
   K_MIX_FWD, K_MIX_BWD, K_MIX_RED,
-  K_GATE_FWD, K_GATE_BWD, K_RSQ_FWD, K_RSQ_BWD, K_RESID, K_LIF_SUM, K_R7_FWD,
+  K_GATE_FWD, K_GATE_BWD, K_RSQ_FWD, K_RSQ_BWD, K_RESID, K_LIF_SUM, K_R7_FWD, K_XENT_FWD, K_XENT_BWD,
   K_COUNT
 };
 const char* const kKindNames[K_COUNT] = {
@@ -56,7 +57,7 @@ const char* const kKindNames[K_COUNT] = {
     "ln_mix_fwd_kernel",      "ln_mix_bwd_kernel",     "ln_mix_reduce_kernel",
     "gate_fwd_kernel",        "gate_bwd_kernel",       "relu_square_fwd_kernel",
     "relu_square_bwd_kernel", "residual_add_kernel",   "lif_bwd_summary_kernel",
-    "rwkv7_fwd_kernel"};
+    "rwkv7_fwd_kernel",       "xent_fwd_kernel",       "xent_bwd_kernel"};
 
 std::atomic<long long> g_launches[K_COUNT];
 std::atomic<bool> g_timing{false};
@@ -1362,6 +1363,47 @@ int rwkv7_forward(const float* r, const float* w, const float* k, const float* v
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   launch(K_R7_FWD, st, [&] { rwkv7_fwd_kernel<<<(unsigned)(B * H), kR7Threads, 0, st>>>(p); });
   return launched("rwkv7 forward launch");
+}
+
+namespace {
+int xent_check(const void* logits, int64_t ld, const int64_t* targets, int64_t rows, int64_t V) {
+  if (rows < 0 || V < 1 || ld < V || ld % 8 != 0 || rows > (1ll << 31) - 1)
+    return fail(WKV_ERR_INVALID_ARGUMENT, "bad sizes rows=%lld V=%lld ld=%lld (ld >= V, a multiple of 8)",
+                (long long)rows, (long long)V, (long long)ld);
+  if (rows > 0 && (!logits || !targets)) return fail(WKV_ERR_INVALID_ARGUMENT, "null pointer");
+  if (!aligned16(logits)) return fail(WKV_ERR_INVALID_ARGUMENT, "logits must be 16-byte aligned");
+  return WKV_OK;
+}
+}  // namespace
+
+int cross_entropy_forward(const void* logits, int64_t ld, const int64_t* targets, int64_t rows, int64_t V,
+                          float* loss, float* lse, void* stream) {
+  g_last_error[0] = '\0';
+  int rc = xent_check(logits, ld, targets, rows, V);
+  if (rc || rows == 0) return rc;
+  if (!loss || !lse) return fail(WKV_ERR_INVALID_ARGUMENT, "null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  launch(K_XENT_FWD, st, [&] {
+    xent_fwd_kernel<<<(unsigned)rows, kXentThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(logits), ld, targets,
+                                                              V, loss, lse);
+  });
+  return launched("cross_entropy forward launch");
+}
+
+int cross_entropy_backward(const void* logits, int64_t ld, const int64_t* targets, const float* lse,
+                           const float* grad_loss, void* grad_logits, int64_t rows, int64_t V, void* stream) {
+  g_last_error[0] = '\0';
+  int rc = xent_check(logits, ld, targets, rows, V);
+  if (rc || rows == 0) return rc;
+  if (!lse || !grad_loss || !grad_logits) return fail(WKV_ERR_INVALID_ARGUMENT, "null pointer");
+  if (!aligned16(grad_logits)) return fail(WKV_ERR_INVALID_ARGUMENT, "grad_logits must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  launch(K_XENT_BWD, st, [&] {
+    xent_bwd_kernel<<<(unsigned)rows, kXentThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(logits), ld, targets,
+                                                              lse, grad_loss,
+                                                              static_cast<__nv_bfloat16*>(grad_logits), V);
+  });
+  return launched("cross_entropy backward launch");
 }
 
 int wkv_kernel_kinds(void) { return K_COUNT; }

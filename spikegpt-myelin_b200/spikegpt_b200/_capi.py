@@ -101,6 +101,10 @@ def lib() -> ctypes.CDLL:
         handle.residual_add_forward.restype = ci
         handle.rwkv7_forward.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, vp]
         handle.rwkv7_forward.restype = ci
+        handle.cross_entropy_forward.argtypes = [vp, i64, vp, i64, i64, vp, vp, vp]
+        handle.cross_entropy_forward.restype = ci
+        handle.cross_entropy_backward.argtypes = [vp, i64, vp, vp, vp, vp, i64, i64, vp]
+        handle.cross_entropy_backward.restype = ci
         handle.wkv_state_size.argtypes = [ci, i64, i64, i64]
         handle.wkv_state_size.restype = sz
         handle.wkv_forward_with_state.argtypes = [ci, vp, vp, vp, vp, vp, vp, sz, i64, i64, i64, vp, sz, vp]
@@ -192,4 +196,4 @@ def declared_symbols() -> list[str]:
     import re
 
     text = HEADER_PATH.read_text()
-    return sorted(set(re.findall(r"WKV_API\s+[\w\s\*]+?\b((?:wkv|lif|ln_mix|gate|relu_square|residual_add|rwkv7)_\w+)\s*\(", text)))
+    return sorted(set(re.findall(r"WKV_API\s+[\w\s\*]+?\b((?:wkv|lif|ln_mix|gate|relu_square|residual_add|rwkv7|cross_entropy)_\w+)\s*\(", text)))

@@ -302,3 +302,83 @@ def residual_add(x: Tensor, spikes: Tensor, residual_token: int = 0) -> Tensor:
             and spikes.is_cuda and x.shape == spikes.shape):
         raise ValueError("residual_add needs a float32 x and bf16 spikes of one shape on CUDA")
     return torch.ops.spikegpt_b200.residual_add(_aligned(x), _aligned(spikes), int(residual_token))
+
+
+# ------------------------------------------------------------ cross-entropy
+#
+# The language-model loss under bf16 autocast, F.cross_entropy(logits.float(),
+# targets) (language.py:1475-1480): a float32 copy of the [rows, V] logits, a
+# log-softmax forward and backward, and the gradient cast back to bf16.
+# ``cross_entropy_forward`` / ``_backward`` read the bf16 logits in place
+# (rows of pitch ld >= V, so a head padded to an aligned width needs no
+# slicing copy) and write the bf16 gradient directly. Targets outside [0, V)
+# (PyTorch's ignore_index -100) contribute nothing; the mean divides by the
+# count of targets != -100, as PyTorch's does.
+
+
+@torch.library.custom_op("spikegpt_b200::cross_entropy_rows", mutates_args=(), device_types="cuda")
+def _xent(logits: Tensor, targets: Tensor, classes: int) -> list[Tensor]:
+    rows, ld = logits.shape
+    loss = torch.empty(rows, dtype=torch.float32, device=logits.device)
+    lse = torch.empty_like(loss)
+    _capi.check(_capi.lib().cross_entropy_forward(logits.data_ptr(), ld, targets.data_ptr(), rows, classes,
+                                                  loss.data_ptr(), lse.data_ptr(), _stream(logits)),
+                "cross_entropy_forward")
+    return [loss, lse]
+
+
+@_xent.register_fake
+def _(logits, targets, classes):
+    rows = logits.shape[0]
+    return [logits.new_empty(rows, dtype=torch.float32), logits.new_empty(rows, dtype=torch.float32)]
+
+
+@torch.library.custom_op("spikegpt_b200::cross_entropy_rows_backward", mutates_args=(), device_types="cuda")
+def _xent_backward(logits: Tensor, targets: Tensor, lse: Tensor, grad_loss: Tensor, classes: int) -> Tensor:
+    rows, ld = logits.shape
+    gx = torch.empty_like(logits)
+    _capi.check(_capi.lib().cross_entropy_backward(logits.data_ptr(), ld, targets.data_ptr(), lse.data_ptr(),
+                                                   grad_loss.data_ptr(), gx.data_ptr(), rows, classes,
+                                                   _stream(logits)), "cross_entropy_backward")
+    return gx
+
+
+@_xent_backward.register_fake
+def _(logits, targets, lse, grad_loss, classes):
+    return torch.empty_like(logits)
+
+
+def _xent_setup(ctx, inputs, output):
+    logits, targets, classes = inputs
+    ctx.save_for_backward(logits, targets, output[1])
+    ctx.classes = classes
+    ctx.mark_non_differentiable(output[1])
+
+
+def _xent_grad(ctx, grads):
+    logits, targets, lse = ctx.saved_tensors
+    g = grads[0]
+    if g is None:
+        g = torch.zeros(logits.shape[0], dtype=torch.float32, device=logits.device)
+    gx = torch.ops.spikegpt_b200.cross_entropy_rows_backward(logits, targets, lse, g.float().contiguous(),
+                                                             ctx.classes)
+    return gx, None, None
+
+
+_xent.register_autograd(_xent_grad, setup_context=_xent_setup)
+
+
+def cross_entropy(logits: Tensor, targets: Tensor, classes: int | None = None) -> Tensor:
+    """Mean cross-entropy of bf16 logits [rows, ld] (the first ``classes``
+    columns are the classes, default all) against int64 targets [rows], with
+    PyTorch's ignore_index -100 semantics."""
+    if logits.ndim != 2 or logits.dtype != torch.bfloat16 or not logits.is_cuda:
+        raise ValueError("cross_entropy takes bf16 CUDA logits [rows, ld]")
+    classes = logits.shape[1] if classes is None else int(classes)
+    if logits.shape[1] % 8 or not 1 <= classes <= logits.shape[1]:
+        raise ValueError("the logits' row pitch must be a multiple of 8 and hold the classes")
+    targets = targets.reshape(-1).to(torch.int64).contiguous()
+    if targets.numel() != logits.shape[0]:
+        raise ValueError("one target per row")
+    loss, _ = torch.ops.spikegpt_b200.cross_entropy_rows(_aligned(logits), targets, classes)
+    return loss.sum() / (targets != -100).sum()

@@ -246,10 +246,28 @@ class SpikeGPT(nn.Module):
             x = _HardSpike.apply(self.config.surrogate_slope * x)
         for block in self.blocks:
             x = block(x)
-        logits = self.head(self.ln_out(x))
+        full, v = _head(self.ln_out(x), self.head.weight)
         if targets is None:
-            return logits
-        return F.cross_entropy(logits.reshape(-1, logits.shape[-1]).float(), targets.reshape(-1))
+            return full[..., :v]
+        if full.dtype == torch.bfloat16 and full.is_cuda:  # bf16 autocast: the fused loss, logits read in place
+            return fused.cross_entropy(full.reshape(-1, full.shape[-1]), targets, v)
+        logits = full[..., :v]
+        return F.cross_entropy(logits.reshape(-1, v).float(), targets.reshape(-1))
+
+
+def _head(h: Tensor, weight: Tensor, multiple: int = 64) -> tuple[Tensor, int]:
+    """The output projection ``h @ weight.T``: (logits [.., Vp], V), the first V
+    columns the classes. When V is not a multiple of 64 (the GPT-2 BPE
+    vocabulary, 50257) on CUDA, the weight is zero-padded to Vp, a multiple of
+    64, for the product: with an odd V the library GEMM falls back to an
+    alignment-1 kernel at a few percent of the tensor peak (54 of 115 ms of the
+    216M-class step). The padded columns are never read as classes, so values
+    and gradients are those of the plain projection."""
+    v = weight.shape[0]
+    pad = (-v) % multiple
+    if pad == 0 or not h.is_cuda:
+        return F.linear(h, weight), v
+    return F.linear(h, F.pad(weight, (0, 0, 0, pad))), v
 
 
 def parameter_count(model: nn.Module) -> int:

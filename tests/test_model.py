@@ -130,3 +130,26 @@ def test_data_parallel_gradient_is_mean_of_shards(cuda):
         ref = full[n].cpu().numpy()
         mean = ((a[n] + b[n]) / 2).cpu().numpy()
         assert scaled_err(mean, ref) <= 1e-4, n
+
+
+@pytest.mark.gpu
+def test_padded_head_matches_plain_projection(cuda):
+    """The output projection of an unaligned vocabulary runs on a weight padded
+    to 64 rows: logits and the weight's gradient are those of the plain
+    projection (float32: to rounding of the GEMM's own order)."""
+    from spikegpt_b200.model import _head
+
+    g = torch.Generator(device="cpu").manual_seed(5)
+    h = torch.randn(4, 33, 96, generator=g).to(cuda)
+    w = torch.randn(50257 // 64 + 5, 96, generator=g).to(cuda).requires_grad_()  # 790 rows: not a multiple of 64
+    w2 = w.detach().clone().requires_grad_()
+    full, v = _head(h, w)
+    assert v == w.shape[0] and full.shape[-1] % 64 == 0
+    out = full[..., :v]
+    ref = h @ w2.T
+    assert out.shape == ref.shape
+    go = torch.randn(out.shape, generator=g).to(cuda)
+    out.backward(go)
+    ref.backward(go)
+    assert scaled_err(out.detach().cpu().numpy(), ref.detach().cpu().numpy()) <= 1e-5
+    assert scaled_err(w.grad.cpu().numpy(), w2.grad.cpu().numpy()) <= 1e-5
