@@ -47,6 +47,11 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "spikegpt-myelin_b200"))
 sys.path.insert(0, str(ROOT))
+# The reference itself (baseline/install_ref.py puts it in the git-ignored
+# baseline/_ref; its absent dependency myelin is replaced by the test-only
+# stand-in). Used only by the reference arm and the incumbent leg.
+REF_DIR = ROOT / "baseline" / "_ref"
+MYELIN_SHIM = ROOT / "tests" / "golden" / "_myelin_shim"
 
 BYTES_PER_ELEM = {"bf16": 16, "fp16": 16, "fp32": 32}  # fwd 3 tensors + bwd 5 tensors
 WORKLOADS = {
@@ -54,7 +59,15 @@ WORKLOADS = {
     "cfg1-fp32": dict(B=64, T=1024, C=512, dtype="fp32", kscale=4.0, desc="config 1 with fp32 I/O"),
     "cfg2": dict(B=24, T=3072, C=512, dtype="bf16", kscale=4.0, desc="config 2: B=24 T=3072 C=512 bf16, k/v x4"),
     "cfg2b-1": dict(B=1, T=3072, C=512, dtype="bf16", kscale=4.0, desc="config 2b: B=1 T=3072 C=512 bf16"),
+    "cfg2b-2": dict(B=2, T=3072, C=512, dtype="bf16", kscale=4.0, desc="config 2b: B=2 T=3072 C=512 bf16"),
+    "cfg2b-4": dict(B=4, T=3072, C=512, dtype="bf16", kscale=4.0, desc="config 2b: B=4 T=3072 C=512 bf16"),
     "cfg2b-8": dict(B=8, T=3072, C=512, dtype="bf16", kscale=4.0, desc="config 2b: B=8 T=3072 C=512 bf16"),
+    "cfg2-b12": dict(B=12, T=3072, C=512, dtype="bf16", kscale=4.0,
+                     desc="long context B=12 T=3072 C=512 bf16 (the reference's published row)"),
+    "cfg1-b12": dict(B=12, T=1024, C=512, dtype="bf16", kscale=4.0,
+                     desc="B=12 T=1024 C=512 bf16 (the reference's published row)"),
+    "cfg1-b24": dict(B=24, T=1024, C=512, dtype="bf16", kscale=4.0,
+                     desc="B=24 T=1024 C=512 bf16 (the reference's published row)"),
     # recurrent (generation) step: B decode streams, one token each per step,
     # bf16 keys/values with a float32 state (the autocast case)
     "decode": dict(kind="step", B=16384, T=1, C=512, dtype="bf16", state="fp32", kscale=4.0,
@@ -78,6 +91,7 @@ PEAKS_FALLBACK_TFLOPS = 1590.0
 STEP_METRIC = "WKV recurrent step algorithmic HBM throughput"
 STEP_BYTES = {"bf16": 2, "fp16": 2, "fp32": 4}
 METRIC = "WKV fwd+bwd algorithmic HBM throughput"
+TRAIN_LEG_STEPS, TRAIN_LEG_WARMUP = 20, 5  # the train_step object of the op bench line
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "source": "fallback"}
 
 
@@ -97,6 +111,14 @@ def parse_args():
                     help="train workloads: launch the step's kernels eagerly instead of replaying a CUDA graph")
     ap.add_argument("--global-batch", type=int, default=None,
                     help="train workloads: override the global batch (e.g. the per-rank share of an N-GPU run on one GPU)")
+    ap.add_argument("--no-train-leg", dest="train_leg", action="store_false",
+                    help="WKV workloads: skip the SpikeGPT-41M train-step object of the line")
+    ap.add_argument("--no-incumbent", dest="incumbent", action="store_false",
+                    help="WKV workloads: skip timing the reference's Triton WKV (incumbent object)")
+    ap.add_argument("--incumbent-child", action="store_true", help=argparse.SUPPRESS)
+    ap.add_argument("--sweep-segments", default="", metavar="LIST",
+                    help="WKV workloads: time the op pair once per forced segment count (e.g. 1,2,4,8) and print "
+                         "one JSON line each")
     ap.add_argument("--kernel-split", type=int, default=0, metavar="TOP",
                     help="train workloads: after timing, print the TOP kernels of two eager steps by device time "
                          "(torch profiler, CUDA activity) to stderr")
@@ -223,7 +245,153 @@ def cpu_oracle_throughput(wl: dict, *, seconds: float = 10.0, steps: int | None 
     }
 
 
+def reference_available() -> bool:
+    return (REF_DIR / "spikegpt" / "language.py").exists()
+
+
+def _import_reference_language():
+    for p in (str(REF_DIR), str(MYELIN_SHIM)):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import spikegpt.language as language
+
+    return language
+
+
+def reference_cpu_throughput(wl: dict, *, steps: int, warmup: int, min_seconds: float = 5.0):
+    """Time the reference's own CPU WKV path, ``weighted_key_value`` (the
+    associative scan of src/spikegpt/language.py:452-527, what SpikeTimeMix
+    runs off CUDA), forward + autograd backward in float32 on all host threads,
+    one batch row of the workload per step, for at least ``steps`` steps and
+    ``min_seconds``."""
+    import torch
+
+    language = _import_reference_language()
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    k, v, td, tf, gy = make_inputs(dict(wl, B=1), seed=0)
+    leaves = [torch.tensor(x, requires_grad=True) for x in (k, v, td, tf)]
+    gyt = torch.tensor(gy)
+
+    def run():
+        for x in leaves:
+            x.grad = None
+        language.weighted_key_value(*leaves).backward(gyt)
+
+    for _ in range(max(1, warmup)):
+        run()
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        run()
+        n += 1
+        el = time.perf_counter() - t0
+        if n >= steps and el >= min_seconds:
+            break
+    value = BYTES_PER_ELEM[wl["dtype"]] * wl["T"] * wl["C"] * n / el / 1e9
+    return {
+        "value": value,
+        "unit": "GB/s",
+        "cores": torch.get_num_threads(),
+        "kind": "reference",
+        "sample": f"{n} x (1 of {wl['B']} batch rows: T={wl['T']} C={wl['C']}), float32 forward + backward "
+                  f"of the reference's weighted_key_value (associative scan, language.py:452-527), {el:.1f} s",
+        "host_cpus": os.cpu_count(),
+    }
+
+
+def run_incumbent_child(args, wl):
+    """Child process: the reference's own Triton WKV kernels (src/spikegpt/
+    wkv_triton.py, wkv_bf16.py) on this GPU, through its public wrappers and
+    autograd, as its model calls them. A separate process because the
+    reference registers the same myelin:: op names this package does."""
+    os.environ["MYELIN_SHIM_HAS_TRITON"] = "1"
+    import torch
+
+    for p in (str(REF_DIR), str(MYELIN_SHIM)):
+        sys.path.insert(0, p)
+    from spikegpt.wkv_bf16 import weighted_key_value_triton_bf16io
+    from spikegpt.wkv_triton import weighted_key_value_triton
+
+    dev = torch.device("cuda", 0)
+    k_np, v_np, td_np, tf_np, gy_np = make_inputs(wl, seed=0)
+    k = torch.as_tensor(k_np).to(dev, torch.bfloat16)
+    v = torch.as_tensor(v_np).to(dev, torch.bfloat16)
+    gy = torch.as_tensor(gy_np).to(dev, torch.bfloat16)
+    td = torch.as_tensor(td_np).to(dev)
+    tf = torch.as_tensor(tf_np).to(dev)
+    elems = k.numel()
+    out = {"workload": wl["desc"], "gpu": torch.cuda.get_device_name(dev)}
+    for name, fn in (("bf16io", weighted_key_value_triton_bf16io), ("fp32io_fed_bf16", weighted_key_value_triton)):
+        leaves = [x.detach().clone().requires_grad_() for x in (k, v, td, tf)]
+
+        def step(with_backward=True):
+            y = fn(*leaves)
+            if with_backward:
+                y.backward(gy)
+
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize(dev)
+        res = {}
+        for label, bwd, steps in (("fwd_bwd", True, args.steps), ("fwd", False, args.steps)):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(steps):
+                if bwd:
+                    step(True)
+                else:
+                    with torch.no_grad():
+                        step(False)
+            e1.record()
+            torch.cuda.synchronize(dev)
+            res[f"{label}_ms"] = e0.elapsed_time(e1) / steps
+        res["gbs"] = BYTES_PER_ELEM[wl["dtype"]] * elems / (res["fwd_bwd_ms"] * 1e-3) / 1e9
+        out[name] = res
+    print(json.dumps(out), flush=True)
+
+
+def incumbent_leg(args, wl) -> dict:
+    """The reference's Triton WKV on this GPU (run_incumbent_child in a
+    subprocess), or why it could not run."""
+    if not reference_available():
+        return {"unavailable": "baseline/_ref has no reference install (baseline/install_ref.py)"}
+    try:
+        import triton  # noqa: F401
+    except ImportError:
+        return {"unavailable": "triton is not installed"}
+    cmd = [sys.executable, str(ROOT / "bench.py"), "--incumbent-child", "--workload", args.workload,
+           "--steps", str(max(5, min(args.steps, 50)))]
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": "the incumbent child did not finish in 600 s"}
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    if r.returncode != 0 or not lines:
+        tail = (r.stderr or r.stdout).strip().splitlines()[-1:] or ["no output"]
+        return {"unavailable": f"rc={r.returncode}: {tail[0][:200]}"}
+    d = json.loads(lines[-1])
+    d["method"] = ("reference wrappers (weighted_key_value_triton_bf16io / weighted_key_value_triton) forward + "
+                   "autograd backward on resident bf16 inputs, CUDA events, mean over the steps")
+    return d
+
+
 # ------------------------------------------------------------- native arm
+
+
+def native_config(wl: dict, b: int, t: int, c: int, world: int) -> dict:
+    """The config keys both arms of the WKV workloads report."""
+    mb = 3 * BYTES_PER_ELEM[wl["dtype"]] // 8 * b * t * c / 1e6
+    return {
+        "workload": wl["desc"],
+        "B_per_gpu": b,
+        "T": t,
+        "C": c,
+        "global_batch": b * world,
+        "parallelism": f"{world} batch-sharded replica(s), no data-path collective",
+        "l2": (f"inputs larger than L2 ({mb:.0f} MB of k,v,grad_y read per step); no flush" if mb > 126 else
+               f"inputs ({mb:.1f} MB of k,v,grad_y per step) fit in the 126 MB L2; no flush: warm-L2 figure"),
+    }
 
 
 def run_native(args, wl):
@@ -367,19 +535,11 @@ def run_native(args, wl):
         "vs_baseline": None,
         "dtype": wl["dtype"],
         "data": "synthetic (seeded numpy PCG64; config distributions)",
-        "config": {
-            "workload": wl["desc"],
-            "B_per_gpu": b,
-            "T": t,
-            "C": c,
-            "global_batch": b * world,
-            "parallelism": f"{world} batch-sharded replica(s), no data-path collective",
-            "l2": "inputs larger than L2 (201 MB of k,v,grad_y read per step); no flush",
-            "frac_of_hbm_peak": value / world / hbm,
-            "plan": dict(zip(("tma", "segments"), _capi.plan(code, b, t, c), strict=True)),
-            "path": ("wkv_forward + wkv_backward (backward re-runs the forward sweep)" if args.no_state else
-                     "wkv_forward_with_state + wkv_backward_from_state (the autograd path)"),
-        },
+        "config": dict(native_config(wl, b, t, c, world),
+                       frac_of_hbm_peak=value / world / hbm,
+                       plan=dict(zip(("tma", "segments"), _capi.plan(code, b, t, c), strict=True)),
+                       path=("wkv_forward + wkv_backward (backward re-runs the forward sweep)" if args.no_state
+                             else "wkv_forward_with_state + wkv_backward_from_state (the autograd path)")),
         "roofline": roofline,
         "kernels": kernels,
         "gpu_launches": int(launches),
@@ -387,13 +547,119 @@ def run_native(args, wl):
     }
     if not args.profile:
         result["e2e"] = run_e2e(args, wl, dev, k_np, v_np, td_np, tf_np, gy_np, tdt, world)
+        # the other op pair: the schema-pure ops (the backward re-runs the forward sweep)
+        other = step_state if args.no_state else step_plain
+        n_other = max(5, min(args.steps, 200))
+        for _ in range(3):
+            other()
+        _capi.timing_collect()
+        _capi.timing_enable(True)
+        torch.cuda.synchronize(dev)
+        o0, o1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        o0.record(stream)
+        for _ in range(n_other):
+            other()
+        o1.record(stream)
+        torch.cuda.synchronize(dev)
+        _capi.timing_enable(False)
+        oms = max_over_ranks(o0.elapsed_time(o1), dev) / n_other
+        result["state" if args.no_state else "no_state"] = {
+            "value": step_bytes * world / (oms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": oms,
+            "steps": n_other,
+            "path": ("wkv_forward_with_state + wkv_backward_from_state" if args.no_state else
+                     "wkv_forward + wkv_backward: the reference's self-contained op contract (the backward "
+                     "re-runs the forward sweep); what a direct caller of the myelin:: ops gets"),
+            "kernels": {n: {"ms_per_launch": tot / cnt, "launches": cnt}
+                        for n, (tot, cnt) in _capi.timing_collect().items() if cnt},
+        }
         if world == 1 and rank == 0:
             result["cpu_baseline"] = cpu_oracle_throughput(wl, seconds=10.0)
+        if args.train_leg and "kind" not in wl:
+            # the data-parallel SpikeGPT-41M train step (config 3) at this N:
+            # global batch 64 over the ranks, gradients all-reduced over NCCL
+            tr, tstep, *_ = measure_train(WORKLOADS["train"], steps=TRAIN_LEG_STEPS, warmup=TRAIN_LEG_WARMUP,
+                                          world=world, rank=rank, dev=dev, clocks=False)
+            tstep.release()
+            result["train_step"] = {k: tr[k] for k in (
+                "metric", "value", "unit", "ms_per_step", "allreduce_ms_per_step", "nccl_ranks", "steps", "warmup",
+                "scaling", "loss", "gpu_launches")}
+            result["train_step"].update(
+                model=tr["config"]["model"], global_batch=tr["config"]["global_batch"],
+                B_per_gpu=tr["config"]["B_per_gpu"], seq_len=tr["config"]["seq_len"],
+                parallelism=tr["config"]["parallelism"], launch=tr["config"]["launch"],
+                mfu=tr["roofline"]["frac"], mfu_peak_tflops=tr["roofline"]["peak"],
+                mfu_peak_source=tr["roofline"]["peak_source"],
+                tokens_per_s_per_gpu=tr["value"] / world)
+        if world == 1 and rank == 0 and args.incumbent and "kind" not in wl:
+            result["incumbent"] = incumbent_leg(args, wl)
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+
+
+def run_segment_sweep(args, wl):
+    """One JSON line per time-segment count for the WKV op pair (saved-state
+    forward + backward) on this workload: the measurement behind the plan
+    choice of the C ABI (make_plan). 0 in the list means the default plan."""
+    import torch
+
+    from spikegpt_b200 import _capi
+
+    dev = torch.device("cuda", 0)
+    tdt = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}[wl["dtype"]]
+    code = {"bf16": _capi.DTYPE_BF16, "fp16": _capi.DTYPE_F16, "fp32": _capi.DTYPE_F32}[wl["dtype"]]
+    b, t, c = wl["B"], wl["T"], wl["C"]
+    k_np, v_np, td_np, tf_np, gy_np = make_inputs(wl, seed=0)
+    k, v, gy = (torch.as_tensor(x).to(dev, tdt) for x in (k_np, v_np, gy_np))
+    td, tf = torch.as_tensor(td_np).to(dev), torch.as_tensor(tf_np).to(dev)
+    w = -torch.exp(td)
+    y, gk, gv = torch.empty_like(k), torch.empty_like(k), torch.empty_like(k)
+    gtd, gtf = torch.empty_like(td), torch.empty_like(td)
+    lib = _capi.lib()
+    sp = torch.cuda.current_stream(dev).cuda_stream
+    step_bytes = BYTES_PER_ELEM[wl["dtype"]] * b * t * c
+    for nseg in [int(x) for x in args.sweep_segments.split(",")]:
+        _capi.set_debug_overrides(force_segments=nseg)
+        try:
+            fws_n = int(lib.wkv_forward_workspace_size(code, b, t, c))
+            bws_n = int(lib.wkv_backward_workspace_size(code, b, t, c))
+            st_n = int(lib.wkv_state_size(code, b, t, c))
+            fws = torch.empty(max(fws_n, 1), dtype=torch.uint8, device=dev)
+            bws = torch.empty(max(bws_n, 1), dtype=torch.uint8, device=dev)
+            state = torch.empty(max(st_n, 16), dtype=torch.uint8, device=dev)
+            plan = _capi.plan(code, b, t, c)
+
+            def step():
+                _capi.check(lib.wkv_forward_with_state(code, k.data_ptr(), v.data_ptr(), td.data_ptr(),
+                                                       tf.data_ptr(), y.data_ptr(), state.data_ptr(), st_n, b, t,
+                                                       c, fws.data_ptr(), fws_n, sp), "wkv_forward_with_state")
+                _capi.check(lib.wkv_backward_from_state(code, gy.data_ptr(), w.data_ptr(), tf.data_ptr(),
+                                                        k.data_ptr(), v.data_ptr(), state.data_ptr(), st_n,
+                                                        gk.data_ptr(), gv.data_ptr(), gtd.data_ptr(),
+                                                        gtf.data_ptr(), b, t, c, bws.data_ptr(), bws_n, sp),
+                            "wkv_backward_from_state")
+
+            for _ in range(max(3, args.warmup)):
+                step()
+            torch.cuda.synchronize(dev)
+            _capi.timing_collect()
+            _capi.timing_enable(True)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                step()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            _capi.timing_enable(False)
+            ms = e0.elapsed_time(e1) / args.steps
+            kernels = {n: round(tot / cnt * 1e3, 2) for n, (tot, cnt) in _capi.timing_collect().items() if cnt}
+        finally:
+            _capi.set_debug_overrides()
+        print(json.dumps({"workload": args.workload, "B": b, "T": t, "C": c, "forced_segments": nseg,
+                          "plan": {"tma": bool(plan[0]), "segments": int(plan[1])}, "ms_per_step": ms,
+                          "GB_s": step_bytes / (ms * 1e-3) / 1e9, "us_per_launch": kernels}), flush=True)
 
 
 def run_step(args, wl):
@@ -983,11 +1249,22 @@ def run_e2e(args, wl, dev, k_np, v_np, td_np, tf_np, gy_np, tdt, world):
 
 
 def run_reference(args, wl):
+    """Reference arm: the reference's own CPU WKV path on the host cores
+    (weighted_key_value, rank 0 only), or the C restatement of its arithmetic
+    (oracle/wkv_oracle.c) when the reference is not installed."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    base = cpu_oracle_throughput(wl, steps=args.steps, warmup=args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    if reference_available():
+        base = reference_cpu_throughput(wl, steps=args.steps, warmup=args.warmup)
+        note = ("the reference's own CPU implementation of the path: weighted_key_value "
+                "(src/spikegpt/language.py:452-527) from baseline/_ref, fp32, torch threads = host cores")
+    else:
+        base = cpu_oracle_throughput(wl, steps=args.steps, warmup=args.warmup)
+        note = ("baseline/_ref absent: the C restatement of the reference's WKV arithmetic "
+                "(oracle/wkv_oracle.c), float32, on the host cores")
+    b, t, c = wl["B"], wl["T"], wl["C"]
     out = {
         "metric": METRIC,
         "value": base["value"],
@@ -1000,12 +1277,11 @@ def run_reference(args, wl):
         "vs_baseline": None,
         "dtype": wl["dtype"],
         "data": "synthetic (seeded numpy PCG64; config distributions)",
-        "config": {"workload": wl["desc"], "B_per_gpu": wl["B"], "T": wl["T"], "C": wl["C"]},
+        "config": native_config(wl, b, t, c, world),
         "impl": "reference",
         "cpu_baseline": base,
         "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "the reference is pure Python (its only GPU code is Triton); this arm times the C "
-                "restatement of its WKV arithmetic (oracle/wkv_oracle.c), float32, on the host cores",
+        "note": note,
     }
     print(json.dumps(out), flush=True)
 
@@ -1075,32 +1351,22 @@ def train_kernel_split(model, opt, x, y, dev, top: int) -> None:
         print(f"  {t_us / 2e3:8.3f} ms {n // 2:5d}  {key[:110]}", file=sys.stderr)
 
 
-def run_train(args, wl):
-    """Data-parallel train step of SpikeGPT (this package's model and ops): the
-    global batch split over the ranks (per-rank work shrinks as ranks grow:
-    strong scaling), bf16 autocast, fused AdamW with weight decay 0.1. A step
-    is forward, backward, the gradient all-reduce (NCCL, N > 1) and the
-    optimizer step on resident synthetic tokens; forward and backward replay
-    one CUDA graph (``spikegpt_b200.train.TrainStep``) unless --eager."""
+def measure_train(wl, *, steps: int, warmup: int, world: int, rank: int, dev, global_batch=None,
+                  eager: bool = False, clocks: bool = True, e2e_steps: int = 0):
+    """Time the data-parallel train step (the process group, if any, is already
+    initialized). Returns (result dict, TrainStep, model, optimizer, x, y); the
+    caller releases the step before destroying the process group."""
     import torch
-    import torch.distributed as dist
 
     from spikegpt_b200 import _capi
     from spikegpt_b200.model import SPIKEGPT_41M, SPIKEGPT_216M, SpikeGPT, flops_per_token
     from spikegpt_b200.sharding import max_over_ranks
     from spikegpt_b200.train import TrainStep
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
+    import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
     cfg = {"41m": SPIKEGPT_41M, "216m": SPIKEGPT_216M}[wl["model"]]
-    gb, t = args.global_batch or wl["global_batch"], wl["T"]
+    gb, t = global_batch or wl["global_batch"], wl["T"]
     if gb % world:
         raise SystemExit(f"global batch {gb} does not split over {world} ranks")
     b = gb // world
@@ -1112,66 +1378,70 @@ def run_train(args, wl):
     ids = torch.as_tensor(ids_np).to(dev)
     x, y = ids[:, :-1].contiguous(), ids[:, 1:].contiguous()
     launches_before = sum(_capi.launch_counts().values())
-    step = TrainStep(model, opt, (b, t), device=dev, graph=not args.eager)
+    step = TrainStep(model, opt, (b, t), device=dev, graph=not eager)
     capture_launches = sum(_capi.launch_counts().values()) - launches_before
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         loss = step(x, y)
     torch.cuda.synchronize(dev)
-    sampler = None if args.profile else ClockSampler(local)
+    local = dev.index or 0
+    sampler = ClockSampler(local) if clocks else None
     time.sleep(0.3 if sampler else 0)
     launches0 = sum(_capi.launch_counts().values())
     if world > 1:
         dist.barrier(device_ids=[local])
     torch.cuda.synchronize(dev)
+    step.time_allreduce(world > 1)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     host0 = time.time()
     ev0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         loss = step(x, y)
     ev1.record()
     torch.cuda.synchronize(dev)
     host1 = time.time()
+    ar_ms, ar_n = step.allreduce_ms()
+    step.time_allreduce(False)
     if world > 1:
         dist.barrier(device_ids=[local])
     # eager launches go through the C ABI's counters; a graph replay runs the
     # kernels counted while it was captured
-    launches = sum(_capi.launch_counts().values()) - launches0 + args.steps * step.captured_launches
+    launches = sum(_capi.launch_counts().values()) - launches0 + steps * step.captured_launches
     ms = max_over_ranks(ev0.elapsed_time(ev1), dev)
+    ar = max_over_ranks(ar_ms / ar_n if ar_n else 0.0, dev)
     if sampler:
         time.sleep(0.25)
         sampler.stop()
-    clocks = sampler.summary(host0, host1) if sampler else None
-    tokens = gb * t * args.steps
+    tokens = gb * t * steps
     value = tokens / (ms * 1e-3)
     fpt = flops_per_token(cfg)
     pk = peaks()
-    peak = float(pk.get("bf16_tflops", PEAKS_FALLBACK_TFLOPS))
+    peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops", PEAKS_FALLBACK_TFLOPS)))
     achieved = value * fpt / world / 1e12
     name = {"41m": "SpikeGPT-41M", "216m": "SpikeGPT-216M"}[wl["model"]]
     result = {
         "metric": TRAIN_METRICS[wl["model"]], "value": value, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "steps": steps, "warmup": warmup, "ms_per_step": ms / steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": f"synthetic Zipf({wl['zipf']}) token ids, seeded numpy PCG64 per rank",
         "config": {"workload": wl["desc"], "model": name, "global_batch": gb, "seq_len": t, "B_per_gpu": b,
                    "params": sum(p.numel() for p in model.parameters()),
                    "parallelism": f"dp{world}" + (" (flat-gradient NCCL all-reduce, AVG)" if world > 1 else ""),
-                   "launch": "eager" if args.eager else "CUDA graph (forward + backward), eager all-reduce "
-                                                         "and fused AdamW",
+                   "launch": "eager" if eager else "CUDA graph (forward + backward), eager all-reduce "
+                                                   "and fused AdamW",
                    "l2": "model state and activations far above L2; no flush"},
+        "allreduce_ms_per_step": ar if world > 1 else 0.0,
+        "nccl_ranks": world if world > 1 else 0,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "flops_per_token": fpt,
-                     "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops)" if pk.get("source") == "measured"
-                     else "fallback 1.59 PFLOP/s", "traffic": None,
-                     "note": "model FLOPs utilisation (6 x matmul weights per token)"},
-        "loss": float(loss.item()), "gpu_launches": int(launches), "clocks": clocks,
+                     "peak_source": "measured sustained (MEASURED_PEAKS.json bf16_tflops_sustained)"
+                     if pk.get("source") == "measured" else "fallback 1.59 PFLOP/s", "traffic": None,
+                     "note": "model FLOPs utilisation (6 x matmul weights per token) per GPU"},
+        "loss": float(loss.item()), "gpu_launches": int(launches),
+        "clocks": sampler.summary(host0, host1) if sampler else None,
         "graph_capture_launches": int(capture_launches),
-        "cpu_baseline": None,
-        "cpu_baseline_note": "no CPU leg: the model step runs only on this package's CUDA ops, and the "
-                             "reference's own CPU step needs myelin@68b8ebb, absent",
     }
-    if not args.profile:
+    if e2e_steps:
         hx = torch.as_tensor(ids_np).pin_memory()
 
         def e2e_step():
@@ -1183,15 +1453,44 @@ def run_train(args, wl):
         torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(args.e2e_steps):
+        for _ in range(e2e_steps):
             e2e_step()
         e1.record()
         torch.cuda.synchronize(dev)
         ems = max_over_ranks(e0.elapsed_time(e1), dev)
-        result["e2e"] = {"value": gb * t * args.e2e_steps / (ems * 1e-3), "unit": "tokens/s",
+        result["e2e"] = {"value": gb * t * e2e_steps / (ems * 1e-3), "unit": "tokens/s",
                          "h2d_bytes_per_step": int(hx.numel() * 8), "d2h_bytes_per_step": 4,
-                         "steps": args.e2e_steps, "ms_per_step": ems / args.e2e_steps,
+                         "steps": e2e_steps, "ms_per_step": ems / e2e_steps,
                          "path": "token ids copied from pinned host memory each step, loss read back"}
+    return result, step, model, opt, x, y
+
+
+def run_train(args, wl):
+    """Data-parallel train step of SpikeGPT (this package's model and ops): the
+    global batch split over the ranks (per-rank work shrinks as ranks grow:
+    strong scaling), bf16 autocast, fused AdamW with weight decay 0.1. A step
+    is forward, backward, the gradient all-reduce (NCCL, N > 1) and the
+    optimizer step on resident synthetic tokens; forward and backward replay
+    one CUDA graph (``spikegpt_b200.train.TrainStep``) unless --eager."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    result, step, model, opt, x, y = measure_train(
+        wl, steps=args.steps, warmup=args.warmup, world=world, rank=rank, dev=dev,
+        global_batch=args.global_batch, eager=args.eager, clocks=not args.profile,
+        e2e_steps=0 if args.profile else args.e2e_steps)
+    result["cpu_baseline"] = None
+    result["cpu_baseline_note"] = ("no CPU leg: the model step runs only on this package's CUDA ops, and the "
+                                   "reference's own CPU step needs myelin@68b8ebb, absent")
     if rank == 0:
         print(json.dumps(result), flush=True)
     step.release()
@@ -1228,8 +1527,12 @@ def main():
             run_lif_reference(args, wl)
         else:
             run_lif(args, wl)
+    elif args.incumbent_child:
+        run_incumbent_child(args, wl)
     elif args.impl == "reference":
         run_reference(args, wl)
+    elif args.sweep_segments:
+        run_segment_sweep(args, wl)
     else:
         run_native(args, wl)
 

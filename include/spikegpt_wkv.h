@@ -53,6 +53,7 @@ extern "C" {
 
 /* Sticky device-side error flags (see wkv_device_error_flags). */
 #define WKV_DEVERR_PIPELINE_TIMEOUT 1u /* a bounded wait on a copy barrier expired */
+#define WKV_DEVERR_BAD_TARGET 2u       /* cross_entropy_*: a target outside [0, V) other than -100 */
 
 /* ABI version of this header; bumped on incompatible changes. */
 #define WKV_ABI_VERSION 1
@@ -115,8 +116,9 @@ WKV_API int wkv_backward(int dtype, const void* grad_y, const float* w, const fl
  *   element) fail with WKV_ERR_INVALID_ARGUMENT and a message naming the
  *   bytes needed; use wkv_backward for those.
  * - The first call on a device looks up the array's device address (once per
- *   device, with that device current); make that first call before any stream
- *   capture begins on the device.
+ *   device and CUDA context, with that device current); make that first call
+ *   before any stream capture begins on the device. After a device reset the
+ *   next call looks the address up again in the new context.
  * - Every call shares the one array and it keeps the previous call's
  *   contents; the call clears what must start at zero itself. Calls that
  *   overlap on the GPU (different streams, or different host threads on one
@@ -256,8 +258,11 @@ WKV_API int residual_add_forward(const float* x, const void* spikes, float* out,
  * src/spikegpt/language.py:1475-1480 and its backward): per row i of a
  * [rows, ld] bf16 logits buffer whose first V columns are the classes,
  * loss[i] = logsumexp_j x_ij - x_i,t_i and lse[i] = logsumexp_j x_ij
- * (float32); rows whose target lies outside [0, V) are ignored (loss 0,
- * gradient 0). cross_entropy_backward writes grad_logits [rows, ld] bf16:
+ * (float32); rows whose target is -100 (PyTorch's ignore_index) are
+ * ignored (loss 0, gradient 0); a target outside [0, V) other than -100
+ * gives that row a NaN loss and NaN gradient and sets
+ * WKV_DEVERR_BAD_TARGET (PyTorch raises for such a target).
+ * cross_entropy_backward writes grad_logits [rows, ld] bf16:
  * grad_loss[i] * (softmax_ij - [j == t_i]) for j < V, zero beyond. ld a
  * multiple of 8, logits and grad_logits 16-byte aligned.
  */
@@ -312,6 +317,17 @@ WKV_API int wkv_plan(int dtype, int64_t B, int64_t T, int64_t C, int* tma, int* 
  * rescaling path. Pass zeros to restore the defaults.
  */
 WKV_API int wkv_set_debug_overrides(int force_segments, int force_generic, int force_slow);
+
+/*
+ * Failure-path test hook (process-wide; no reference counterpart). The
+ * time-parallel forward kernels wait on copy barriers with a bounded wait;
+ * wait_limit_cycles > 0 shortens the consumers' limit (0 restores the default,
+ * about 2 s), and withhold_first_copies != 0 makes every CTA skip issuing its
+ * first round's copies, so that wait runs out: the kernel then sets
+ * WKV_DEVERR_PIPELINE_TIMEOUT, waits for the copies it did issue, and returns
+ * without finishing its outputs. For tests of the error path only.
+ */
+WKV_API int wkv_set_debug_pipeline(long long wait_limit_cycles, int withhold_first_copies);
 
 /*
  * Launch accounting and per-kernel device timing (no reference counterpart; the

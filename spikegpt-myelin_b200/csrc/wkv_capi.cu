@@ -35,6 +35,8 @@ thread_local char g_last_error[512] = "";
 std::atomic<int> g_force_segments{0};
 std::atomic<int> g_force_generic{0};
 std::atomic<int> g_force_slow{0};
+std::atomic<long long> g_wait_limit{kWaitLimitCycles};
+std::atomic<int> g_withhold_first{0};
 
 __device__ unsigned g_device_error_flags = 0;
 
@@ -284,20 +286,62 @@ int make_ckpt_map(CUtensorMap* m, const float* ptr, int64_t rows, int64_t C, int
   return WKV_OK;
 }
 
-// Device address of g_device_error_flags for the current device (looked up once
-// per device; the host-side symbol itself is not a device address).
-unsigned* device_err_ptr() {
-  static std::atomic<unsigned*> cached[64];
+// The current CUDA context (driver API through the runtime's entry-point
+// query, so the library needs no -lcuda). Device addresses of this module's
+// __device__ symbols are cached per (device, context): a device reset creates
+// a new primary context, reloads the module and moves the symbols.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CUcontext current_context() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  CUcontext c = nullptr;
+  if (fn == nullptr || fn(&c) != CUDA_SUCCESS) return nullptr;
+  return c;
+}
+
+struct SymbolCache {
+  std::mutex mu;
+  CUcontext ctx[64] = {};
+  void* ptr[64] = {};
+};
+
+// Device address of `symbol` in the current context, looked up with
+// cudaGetSymbolAddress when the device's context differs from the cached one.
+template <class S>
+cudaError_t symbol_address(SymbolCache& cache, const S& symbol, void** out) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  unsigned* p = cached[dev].load();
-  if (p == nullptr) {
-    void* q = nullptr;
-    if (cudaGetSymbolAddress(&q, g_device_error_flags) != cudaSuccess) return nullptr;
-    p = static_cast<unsigned*>(q);
-    cached[dev].store(p);
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  // (null before the runtime has bound a context to this thread: the lookup
+  // below binds one, and the next call caches again under the real context)
+  const CUcontext ctx = current_context();
+  std::lock_guard<std::mutex> lk(cache.mu);
+  if (cache.ptr[dev] == nullptr || cache.ctx[dev] != ctx) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, symbol);
+    if (e != cudaSuccess) return e;
+    cache.ptr[dev] = p;
+    cache.ctx[dev] = ctx;
   }
-  return p;
+  *out = cache.ptr[dev];
+  return cudaSuccess;
+}
+
+// Device address of g_device_error_flags for the current device and context
+// (the host-side symbol itself is not a device address).
+SymbolCache g_err_cache;
+unsigned* device_err_ptr() {
+  void* p = nullptr;
+  if (symbol_address(g_err_cache, g_device_error_flags, &p) != cudaSuccess) return nullptr;
+  return static_cast<unsigned*>(p);
 }
 
 int check_dims(int dtype, int64_t B, int64_t T, int64_t C) {
@@ -368,6 +412,8 @@ int launch_forward(const void* k, const void* v, const float* decay, int decay_i
   a.nsub = (T + kSub - 1) / kSub;
   a.force_slow = g_force_slow.load();
   a.err = device_err_ptr();
+  a.wait_limit = g_wait_limit.load();
+  a.withhold_first = g_withhold_first.load();
   const unsigned gx = (unsigned)a.ncblk * (unsigned)B;
   if (p.nseg > 1) {
     // summaries of segments 0..nseg-2, then the carry
@@ -592,6 +638,14 @@ int wkv_set_debug_overrides(int force_segments, int force_generic, int force_slo
   return WKV_OK;
 }
 
+int wkv_set_debug_pipeline(long long wait_limit_cycles, int withhold_first_copies) {
+  g_last_error[0] = '\0';
+  if (wait_limit_cycles < 0) return fail(WKV_ERR_INVALID_ARGUMENT, "negative wait limit");
+  g_wait_limit.store(wait_limit_cycles == 0 ? kWaitLimitCycles : wait_limit_cycles);
+  g_withhold_first.store(withhold_first_copies != 0);
+  return WKV_OK;
+}
+
 int wkv_plan(int dtype, int64_t B, int64_t T, int64_t C, int* tma, int* segments) {
   int rc = check_dims(dtype, B, T, C);
   if (rc) return rc;
@@ -732,25 +786,14 @@ int backward_impl(int dtype, const void* grad_y, const float* w, const float* u,
 // the gradient kernel reads them; checkpoints and partial sums are overwritten).
 __device__ __align__(256) unsigned char g_noalloc_scratch[WKV_NOALLOC_SCRATCH_BYTES];
 
-std::mutex g_noalloc_mu;
-void* g_noalloc_base[64] = {};
+SymbolCache g_noalloc_cache;
 
 // In host code `g_noalloc_scratch` names a host-side shadow of the symbol, not
-// device memory: the device address comes from cudaGetSymbolAddress, asked once
-// per device with that device current, and is cached.
+// device memory: the device address comes from cudaGetSymbolAddress, asked
+// with the device current, and is cached per device and context.
 int noalloc_scratch(void** base) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  if (dev < 0 || dev >= 64) return fail(WKV_ERR_INVALID_ARGUMENT, "device ordinal %d unsupported", dev);
-  std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (g_noalloc_base[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
-    g_noalloc_base[dev] = p;
-  }
-  *base = g_noalloc_base[dev];
+  const cudaError_t e = symbol_address(g_noalloc_cache, g_noalloc_scratch, base);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
   return WKV_OK;
 }
 
@@ -1385,7 +1428,7 @@ int cross_entropy_forward(const void* logits, int64_t ld, const int64_t* targets
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   launch(K_XENT_FWD, st, [&] {
     xent_fwd_kernel<<<(unsigned)rows, kXentThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(logits), ld, targets,
-                                                              V, loss, lse);
+                                                              V, loss, lse, device_err_ptr());
   });
   return launched("cross_entropy forward launch");
 }

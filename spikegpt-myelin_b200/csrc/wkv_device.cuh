@@ -140,13 +140,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait on an mbarrier phase: returns false (and never spins forever)
-// when the phase has not completed within kWaitLimitCycles.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+// when the phase has not completed within `limit` cycles.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  long long limit = kWaitLimitCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long start = clock64();
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (clock64() - start > kWaitLimitCycles) return false;
+    if (clock64() - start > limit) return false;
   }
 }
 

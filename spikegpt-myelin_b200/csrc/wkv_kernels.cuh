@@ -74,6 +74,10 @@ struct FwdArgs {
   int nzero;
   int force_slow;
   unsigned* err;
+  // Debug (wkv_set_debug_pipeline): the consumers' copy-wait limit in cycles,
+  // and withholding the first round's copies so that wait runs out.
+  long long wait_limit;
+  int withhold_first;
 };
 
 struct BwdArgs {

@@ -207,8 +207,11 @@ __global__ void __launch_bounds__(32 * W, 4)
   if (a.seg_start != nullptr)
     load3(a.seg_start, (size_t)b * a.nseg + seg, a.C, c, v0, v1, start.S, start.p, start.q);
 
+  // (a.withhold_first: debug only, the first round's copies are never issued)
+  auto withheld = [&](int r) { return a.withhold_first != 0 && r == 0; };
   auto issue = [&](bool on, int r) {  // by the threads with `on` (one per CTA)
     const int s = r % NS;
+    on = on && !withheld(r);
     mbar_arrive_expect_tx_if(on, &bars[s], 2 * G::kBoxBytes);
     const int t0 = t_begin + r * G::kRoundRows;
     tma_load_3d_if(on, kbuf + s * G::kBoxElems, &tk, &bars[s], cb * kLanes, t0, b);
@@ -232,7 +235,7 @@ __global__ void __launch_bounds__(32 * W, 4)
     const int t0 = rt0 + warp * R;  // this warp's tile
     const int n = max(0, min(R, t_end - t0));
     float* sr = sum + (r & 1) * (W + 1) * 3 * kLanes;  // this round's summaries
-    const bool arrived = mbar_wait_bounded(&bars[s], (r / NS) & 1);
+    const bool arrived = mbar_wait_bounded(&bars[s], (r / NS) & 1, a.wait_limit);
 
     // A. summary of the tile from a zero state, scaled by 2^-sj, sj = ceil(max k log2 e)
     raw kr[R], vr[R];
@@ -261,7 +264,9 @@ __global__ void __launch_bounds__(32 * W, 4)
     if (!__syncthreads_and(arrived)) {
       if (threadIdx.x == 0) {
         report_timeout(a.err);
-        for (int q = r; q < min(r + NS, nrounds); ++q) mbar_wait_bounded(&bars[q % NS], (q / NS) & 1);
+        // every copy this CTA issued lands before it exits
+        for (int q = r; q < min(r + NS, nrounds); ++q)
+          if (!withheld(q)) mbar_wait_bounded(&bars[q % NS], (q / NS) & 1);
       }
       if (kY) bulk_wait_all();
       return;

@@ -4,7 +4,10 @@
 // (src/spikegpt/language.py:1475-1480): under bf16 autocast that is a float32
 // copy of the [rows, V] logits, a log-softmax forward and backward over the
 // copy, and a cast of the gradient back to bf16. Here, per row i with target
-// t_i (rows whose target lies outside [0, V) are ignored: loss 0, gradient 0):
+// t_i (rows whose target is PyTorch's ignore_index -100 are ignored: loss 0,
+// gradient 0; any other target outside [0, V), which PyTorch rejects, gives
+// the row a NaN loss and a NaN gradient and sets kXentBadTarget in the sticky
+// device error flags, so the mean loss is NaN instead of silently lower):
 //   forward:  lse_i = log sum_j exp(x_ij),  loss_i = lse_i - x_i,t_i
 //   backward: dx_ij = bf16(g_i * (exp(x_ij - lse_i) - [j == t_i]))
 // in float32 from the bf16 logits, read in place (row pitch ld >= V, a
@@ -21,6 +24,8 @@
 namespace wkv {
 
 constexpr int kXentThreads = 256;
+constexpr int64_t kXentIgnore = -100;
+constexpr unsigned kXentBadTarget = 2u;  // WKV_DEVERR_BAD_TARGET
 
 __device__ __forceinline__ void xent_merge(float& m, float& s, float m2, float s2) {
   // (m, s) represents s * exp(m); merge two such sums (an empty one is
@@ -40,7 +45,7 @@ __device__ __forceinline__ void xent_merge(float& m, float& s, float m2, float s
 
 __global__ void __launch_bounds__(kXentThreads) xent_fwd_kernel(const __nv_bfloat16* logits, int64_t ld,
                                                                const int64_t* targets, int64_t V, float* loss,
-                                                               float* lse_out) {
+                                                               float* lse_out, unsigned* err) {
   __shared__ float sm[kXentThreads], ss[kXentThreads];
   const int64_t row = blockIdx.x;
   const __nv_bfloat16* x = logits + row * ld;
@@ -73,7 +78,14 @@ __global__ void __launch_bounds__(kXentThreads) xent_fwd_kernel(const __nv_bfloa
     const float lse = sm[0] + logf(ss[0]);
     const int64_t t = targets[row];
     lse_out[row] = lse;
-    loss[row] = (t >= 0 && t < V) ? lse - __bfloat162float(x[t]) : 0.f;
+    if (t >= 0 && t < V) {
+      loss[row] = lse - __bfloat162float(x[t]);
+    } else if (t == kXentIgnore) {
+      loss[row] = 0.f;
+    } else {
+      loss[row] = __int_as_float(0x7fffffff);
+      if (err) atomicOr(err, kXentBadTarget);
+    }
   }
 }
 
@@ -86,7 +98,8 @@ __global__ void __launch_bounds__(kXentThreads) xent_bwd_kernel(const __nv_bfloa
   __nv_bfloat16* d = dx + row * ld;
   const int64_t t = targets[row];
   const bool on = t >= 0 && t < V;
-  const float g = on ? grad[row] : 0.f, lse = lse_in[row];
+  const float g = on ? grad[row] : (t == kXentIgnore ? 0.f : __int_as_float(0x7fffffff));
+  const float lse = lse_in[row];
   const int64_t nv = ld / 8;
   for (int64_t v = threadIdx.x; v < nv; v += kXentThreads) {
     const uint4 u = *reinterpret_cast<const uint4*>(x + 8 * v);

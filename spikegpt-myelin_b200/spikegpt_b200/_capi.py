@@ -23,6 +23,7 @@ WKV_ERR_WORKSPACE_TOO_SMALL = 2
 WKV_ERR_CUDA = 3
 WKV_ERR_DRIVER = 4
 WKV_DEVERR_PIPELINE_TIMEOUT = 1
+WKV_DEVERR_BAD_TARGET = 2
 
 
 class WKVError(RuntimeError):
@@ -115,6 +116,8 @@ def lib() -> ctypes.CDLL:
         handle.wkv_backward_from_state.restype = ci
         handle.wkv_plan.argtypes = [ci, i64, i64, i64, ctypes.POINTER(ci), ctypes.POINTER(ci)]
         handle.wkv_plan.restype = ci
+        handle.wkv_set_debug_pipeline.argtypes = [ctypes.c_longlong, ci]
+        handle.wkv_set_debug_pipeline.restype = ci
         handle.wkv_set_debug_overrides.argtypes = [ci, ci, ci]
         handle.wkv_set_debug_overrides.restype = ci
         handle.wkv_kernel_kinds.argtypes = []
@@ -158,6 +161,11 @@ def plan(dtype_code: int, b: int, t: int, c: int) -> tuple[bool, int]:
 
 def set_debug_overrides(force_segments: int = 0, force_generic: bool = False, force_slow: bool = False) -> None:
     check(lib().wkv_set_debug_overrides(int(force_segments), int(force_generic), int(force_slow)), "overrides")
+
+
+def set_debug_pipeline(wait_limit_cycles: int = 0, withhold_first_copies: bool = False) -> None:
+    """Failure-path test hook of the forward's copy pipeline (0, False: defaults)."""
+    check(lib().wkv_set_debug_pipeline(int(wait_limit_cycles), int(withhold_first_copies)), "wkv_set_debug_pipeline")
 
 
 def device_error_flags(clear: bool = False) -> int:

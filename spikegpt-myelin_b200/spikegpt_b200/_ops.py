@@ -9,7 +9,6 @@ and float16 I/O natively and always computes in float32.
 from __future__ import annotations
 
 import os
-import threading
 
 import torch
 from torch import Tensor
@@ -70,16 +69,18 @@ def _workspace(nbytes: int, device: torch.device) -> tuple[Tensor | None, int]:
 # Saved forward state (the autograd hand-off)
 #
 # The reference's backward op takes only (grad_y, w, u, k, v), so on its own it
-# must re-run the forward recurrence to recover the state. When the forward is
-# called through this package's model-facing wrappers in eager mode with
-# gradients required, the forward also stores the recurrence state every 16
-# steps (float32, 0.75 bytes per element of key) and hands it to the backward
-# through the autograd context; the backward then reads key/value once instead
-# of twice. Calls of the ops themselves, and everything traced by
-# torch.compile, use the self-contained schema path.
+# must re-run the forward recurrence to recover the state. When gradients are
+# needed, the model-facing wrappers (weighted_key_value_triton[_bf16io]) call
+# ``spikegpt_b200::wkv_forward_with_state`` instead: the same forward, which
+# also returns the recurrence state every 16 steps (float32, 0.75 bytes per
+# element of key) as a second output. Its autograd formula hands that state to
+# ``spikegpt_b200::wkv_backward_from_state``, which reads key/value once instead
+# of twice. Both are traceable custom ops with fake impls, so eager autograd
+# and torch.compile graphs (the state becomes a saved activation of the
+# compiled forward) take the same path. Calls of the ``myelin::`` ops
+# themselves keep the reference's self-contained contract.
 # ---------------------------------------------------------------------------
 
-_TLS = threading.local()
 _SAVE_STATE = os.environ.get("SPIKEGPT_WKV_SAVE_STATE", "1") != "0"
 
 
@@ -93,31 +94,25 @@ def state_saving_enabled() -> bool:
     return _SAVE_STATE
 
 
+def state_nbytes(b, t, c) -> int:
+    """Bytes of the saved forward state (``wkv_state_size`` of the C ABI): float32
+    checkpoint rows [B][ceil(T/16)][3][C], then one 32-bit counter per 64-channel
+    block, each part rounded up to 256 bytes; at least 16 bytes."""
+    ckpt = (b * ((t + 15) // 16) * 3 * c * 4 + 255) // 256 * 256
+    counters = (((c + 63) // 64) * 4 + 255) // 256 * 256
+    return max(ckpt + counters, 16)
+
+
 def call_saving_state(op, key: Tensor, value: Tensor, time_decay: Tensor, time_first: Tensor) -> Tensor:
-    """Call a forward custom op, asking it to keep the state for the backward
-    when autograd will record this call (eager, grad mode on, an input that
-    requires grad)."""
-    if not (_SAVE_STATE and torch.is_grad_enabled() and any(
+    """y of a forward custom op; when autograd will record the call (grad mode
+    on, an input that requires grad), through the state-keeping forward so the
+    backward skips the forward sweep."""
+    if _SAVE_STATE and torch.is_grad_enabled() and any(
         t.requires_grad for t in (key, value, time_decay, time_first)
-    )):
-        return op(key, value, time_decay, time_first)
-    _TLS.want = True
-    try:
-        return op(key, value, time_decay, time_first)
-    finally:
-        _TLS.want = False
-        _TLS.pending = None
-
-
-def _take_pending(output: Tensor) -> Tensor | None:
-    pending = getattr(_TLS, "pending", None)
-    _TLS.pending = None
-    if pending is None or torch.compiler.is_compiling():
-        return None
-    ptr, shape, state = pending
-    if output.data_ptr() != ptr or tuple(output.shape) != shape:
-        return None
-    return state
+    ):
+        y, _state = torch.ops.spikegpt_b200.wkv_forward_with_state(key, value, time_decay, time_first)
+        return y
+    return op(key, value, time_decay, time_first)
 
 
 def forward(
@@ -141,8 +136,10 @@ def forward(
         nbytes = int(lib.wkv_forward_workspace_size(code, b, t, c))
         ws, ws_ptr = _workspace(nbytes, k.device)
         if save_state:
-            sbytes = int(lib.wkv_state_size(code, b, t, c))
-            state = torch.empty(max(sbytes, 16), dtype=torch.uint8, device=k.device)
+            sbytes = state_nbytes(b, t, c)
+            if sbytes < int(lib.wkv_state_size(code, b, t, c)):
+                raise RuntimeError("spikegpt_b200: state size formula disagrees with wkv_state_size")
+            state = torch.empty(sbytes, dtype=torch.uint8, device=k.device)
             rc = lib.wkv_forward_with_state(
                 code, k.data_ptr(), v.data_ptr(), td.data_ptr(), tf.data_ptr(), y.data_ptr(),
                 state.data_ptr(), state.numel(), b, t, c, ws_ptr, nbytes, stream,
@@ -220,11 +217,6 @@ def register(namespace_op_fwd: str, namespace_op_bwd: str):
 
     @torch.library.custom_op(namespace_op_fwd, mutates_args=(), device_types="cuda")
     def wkv_forward_op(key: Tensor, value: Tensor, time_decay: Tensor, time_first: Tensor) -> Tensor:
-        if getattr(_TLS, "want", False):
-            _TLS.want = False
-            y, state = forward(key, value, time_decay, time_first, save_state=True)
-            _TLS.pending = (y.data_ptr(), tuple(y.shape), state)
-            return y
         return forward(key, value, time_decay, time_first)
 
     @wkv_forward_op.register_fake
@@ -242,27 +234,16 @@ def register(namespace_op_fwd: str, namespace_op_bwd: str):
     bwd_name = namespace_op_bwd.split("::")[1]
 
     def setup_context(ctx, inputs, output):
-        key, value, time_decay, time_first = inputs
-        state = _take_pending(output)
-        if state is None:
-            ctx.save_for_backward(key, value, time_decay, time_first)
-        else:
-            ctx.save_for_backward(key, value, time_decay, time_first, state)
+        ctx.save_for_backward(*inputs)
 
     def backward_fn(ctx, grad_y):
-        saved = ctx.saved_tensors
-        key, value, time_decay, time_first = saved[:4]
+        key, value, time_decay, time_first = ctx.saved_tensors
         w = -torch.exp(time_decay.float())
         u = time_first.float()
         # The kernels read key/value/grad_y in their own dtype, so the fp32
         # copies the reference glue makes (wkv_triton.py:206-210) are not needed;
         # the float32 results are identical.
-        if len(saved) == 5:
-            gk, gv, gtd, gtf = torch.ops.spikegpt_b200.wkv_backward_from_state(
-                grad_y, w, u, key, value, saved[4]
-            )
-        else:
-            gk, gv, gtd, gtf = getattr(torch.ops.myelin, bwd_name)(grad_y, w, u, key, value)
+        gk, gv, gtd, gtf = getattr(torch.ops.myelin, bwd_name)(grad_y, w, u, key, value)
         return (
             gk.to(key.dtype),
             gv.to(value.dtype),
@@ -285,3 +266,34 @@ def wkv_backward_from_state_op(
 @wkv_backward_from_state_op.register_fake
 def _(grad_y, w, u, k, v, state):
     return [torch.empty_like(k), torch.empty_like(k), torch.empty_like(w), torch.empty_like(u)]
+
+
+@torch.library.custom_op("spikegpt_b200::wkv_forward_with_state", mutates_args=(), device_types="cuda")
+def wkv_forward_with_state_op(
+    key: Tensor, value: Tensor, time_decay: Tensor, time_first: Tensor
+) -> tuple[Tensor, Tensor]:
+    """The forward op's contract (wkv_triton.py:147-158) plus the saved state
+    (uint8, ``state_nbytes`` long) for ``wkv_backward_from_state``."""
+    return forward(key, value, time_decay, time_first, save_state=True)
+
+
+@wkv_forward_with_state_op.register_fake
+def _(key, value, time_decay, time_first):
+    b, t, c = key.shape
+    return torch.empty_like(key), key.new_empty(state_nbytes(b, t, c), dtype=torch.uint8)
+
+
+def _with_state_setup_context(ctx, inputs, output):
+    ctx.save_for_backward(*inputs, output[1])
+    ctx.mark_non_differentiable(output[1])
+
+
+def _with_state_backward(ctx, grad_y, _grad_state):
+    key, value, time_decay, time_first, state = ctx.saved_tensors
+    w = -torch.exp(time_decay.float())
+    u = time_first.float()
+    gk, gv, gtd, gtf = torch.ops.spikegpt_b200.wkv_backward_from_state(grad_y, w, u, key, value, state)
+    return gk.to(key.dtype), gv.to(value.dtype), gtd.to(time_decay.dtype), gtf.to(time_first.dtype)
+
+
+wkv_forward_with_state_op.register_autograd(_with_state_backward, setup_context=_with_state_setup_context)

@@ -16,7 +16,9 @@ multiple of 128 up to 1024; outputs bf16.
 
 from __future__ import annotations
 
+import contextlib
 import itertools
+import threading
 
 import torch
 from torch import Tensor
@@ -36,14 +38,47 @@ def supported(x: Tensor) -> bool:
 # with a residual token instead hands the skip connection's gradient from
 # residual_add's backward (which runs first: the sublayer lies between the
 # two) to ln_shift_mix's backward, which adds it to grad x inside its kernel.
+# That is only sound when both backwards are certain to run in the same
+# backward pass, so tokens are handed out only inside ``residual_handoff()``
+# (which TrainStep opens around its forward and full ``loss.backward()``),
+# outside torch.compile, and for an x that requires grad; everywhere else the
+# token is 0 and residual_add returns x's gradient itself.
 _RESIDUAL_GRADS: dict[int, Tensor] = {}
 _TOKENS = itertools.count(1)
+_HANDOFF = threading.local()
 
 
-def new_residual_token() -> int:
+@contextlib.contextmanager
+def residual_handoff():
+    """Allow residual tokens for sublayers built in this thread while the
+    context is open. The caller must run one full backward of everything built
+    inside, then check ``pending_residual_grads() == 0``."""
+    prev = getattr(_HANDOFF, "on", False)
+    _HANDOFF.on = True
+    try:
+        yield
+    finally:
+        _HANDOFF.on = prev
+
+
+def new_residual_token(x: Tensor | None = None) -> int:
     """A token pairing one ln_shift_mix with the residual_add that closes its
-    sublayer (0 means no pairing)."""
+    sublayer, or 0 (no pairing) outside ``residual_handoff()``, under
+    torch.compile, or when ``x`` does not require grad."""
+    if not getattr(_HANDOFF, "on", False) or torch.compiler.is_compiling():
+        return 0
+    if x is not None and not x.requires_grad:
+        return 0
     return next(_TOKENS)
+
+
+def pending_residual_grads() -> int:
+    """Handed-over skip gradients that no ln_shift_mix backward has consumed."""
+    return len(_RESIDUAL_GRADS)
+
+
+def drop_residual_grads() -> None:
+    _RESIDUAL_GRADS.clear()
 
 
 @torch.library.custom_op("spikegpt_b200::ln_shift_mix", mutates_args=(), device_types="cuda")
@@ -311,9 +346,11 @@ def residual_add(x: Tensor, spikes: Tensor, residual_token: int = 0) -> Tensor:
 # log-softmax forward and backward, and the gradient cast back to bf16.
 # ``cross_entropy_forward`` / ``_backward`` read the bf16 logits in place
 # (rows of pitch ld >= V, so a head padded to an aligned width needs no
-# slicing copy) and write the bf16 gradient directly. Targets outside [0, V)
-# (PyTorch's ignore_index -100) contribute nothing; the mean divides by the
-# count of targets != -100, as PyTorch's does.
+# slicing copy) and write the bf16 gradient directly. Targets equal to
+# PyTorch's ignore_index -100 contribute nothing and the mean divides by the
+# count of the others, as PyTorch's does; any other target outside [0, V)
+# (which PyTorch rejects) makes the loss NaN and sets the device error flag
+# WKV_DEVERR_BAD_TARGET.
 
 
 @torch.library.custom_op("spikegpt_b200::cross_entropy_rows", mutates_args=(), device_types="cuda")

@@ -203,11 +203,11 @@ class Block(nn.Module):
             x = self.ln0(x)
         if self._fused(x):
             att, ffn = self.att, self.ffn
-            tok = fused.new_residual_token()
+            tok = fused.new_residual_token(x)
             xk, xv, xr = fused.ln_shift_mix(x, self.ln1.weight, self.ln1.bias,
                                             [att.time_mix_k, att.time_mix_v, att.time_mix_r], self.ln1.eps, tok)
             x = self._residual(x, self._lif(att.from_mixed(xk, xv, xr)), tok)
-            tok = fused.new_residual_token()
+            tok = fused.new_residual_token(x)
             xk, xr = fused.ln_shift_mix(x, self.ln2.weight, self.ln2.bias, [ffn.time_mix_k, ffn.time_mix_r],
                                         self.ln2.eps, tok)
             x = self._residual(x, self._lif(ffn.from_mixed(xk, xr)), tok)

@@ -29,7 +29,7 @@ import torch
 import torch.distributed as dist
 from torch import Tensor, nn
 
-from . import _capi
+from . import _capi, fused
 
 
 class TrainStep:
@@ -72,18 +72,25 @@ class TrainStep:
         self.loss = None
         self.captured_grads = None
         self.captured_launches = 0  # this package's kernels in the graph (each replay runs them again)
+        self._ar_events: list[tuple[torch.cuda.Event, torch.cuda.Event]] | None = None
         if graph:
             self._capture(warmup)
 
     def _forward_backward(self) -> Tensor:
         for p in self.params:
             p.grad = None
-        if self.autocast_dtype is None:
-            loss = self.model(self.ids, self.targets)
-        else:
-            with torch.autocast(self.device.type, dtype=self.autocast_dtype):
+        # the full backward below consumes every skip gradient handed over
+        # between a residual_add and its LayerNorm-mix (fused.residual_handoff)
+        with fused.residual_handoff():
+            if self.autocast_dtype is None:
                 loss = self.model(self.ids, self.targets)
-        loss.backward()
+            else:
+                with torch.autocast(self.device.type, dtype=self.autocast_dtype):
+                    loss = self.model(self.ids, self.targets)
+            loss.backward()
+        if fused.pending_residual_grads():
+            fused.drop_residual_grads()
+            raise RuntimeError("TrainStep: a residual gradient was handed over but never consumed")
         if self.grads is not None:
             torch.cat([p.grad.reshape(-1) for p in self.params], out=self.grads)
         return loss.detach()
@@ -122,16 +129,39 @@ class TrainStep:
         else:
             loss = self._forward_backward()
         if self.grads is not None:
+            ev = None
+            if self._ar_events is not None:
+                ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                ev[0].record()
             if self.avg:
                 dist.all_reduce(self.grads, op=dist.ReduceOp.AVG, group=self.group)
             else:
                 dist.all_reduce(self.grads, op=dist.ReduceOp.SUM, group=self.group)
                 self.grads.div_(self.world)
+            if ev is not None:
+                ev[1].record()
+                self._ar_events.append(ev)
             if self.graph is None:
                 for p, g in zip(self.params, self.grad_views):
                     p.grad = g
         self.optimizer.step()
         return loss
+
+    def time_allreduce(self, on: bool = True) -> None:
+        """Record CUDA events around each call's gradient all-reduce (on the
+        current stream) until ``allreduce_ms`` collects them."""
+        self._ar_events = [] if on else None
+
+    def allreduce_ms(self) -> tuple[float, int]:
+        """(summed device ms, count) of the all-reduces timed since
+        ``time_allreduce(True)``; synchronizes on the last one."""
+        evs = self._ar_events or []
+        if evs:
+            evs[-1][1].synchronize()
+        total = sum(a.elapsed_time(b) for a, b in evs)
+        if self._ar_events is not None:
+            self._ar_events = []
+        return total, len(evs)
 
     def release(self) -> None:
         """Drop the captured graph (before the process group is destroyed)."""

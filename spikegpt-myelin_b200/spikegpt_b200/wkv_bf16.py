@@ -25,9 +25,8 @@ def weighted_key_value_cuda_bf16io(
     time_first: Tensor,
 ) -> Tensor:
     """RWKV WKV via the native-dtype-I/O sm_100a custom op (CUDA only)."""
-    if torch.compiler.is_compiling():
-        return torch.ops.myelin.wkv_forward_bf16io(key, value, time_decay, time_first)
-    # eager: keep the forward state for the backward when autograd records
+    # with gradients: the state-keeping forward, whose backward skips the
+    # forward sweep (eager and torch.compile alike)
     return _ops.call_saving_state(torch.ops.myelin.wkv_forward_bf16io, key, value, time_decay, time_first)
 
 

@@ -5,6 +5,8 @@ gradients within 1e-4 of their scale (float32 sums in a different order)."""
 
 from __future__ import annotations
 
+import contextlib
+
 import numpy as np
 import pytest
 import torch
@@ -107,11 +109,34 @@ def test_residual_gradient_summed_in_kernel(cuda):
 
     def run(paired):
         x = x0.clone().requires_grad_()
-        tok = fused.new_residual_token() if paired else 0
-        xk, xr = fused.ln_shift_mix(x, w, b, m, 1e-5, tok)
-        out = fused.residual_add(x, fused.gate(xk, xr), tok)
-        out.backward(go)
+        with fused.residual_handoff() if paired else contextlib.nullcontext():
+            tok = fused.new_residual_token(x)
+            assert (tok != 0) == paired
+            xk, xr = fused.ln_shift_mix(x, w, b, m, 1e-5, tok)
+            out = fused.residual_add(x, fused.gate(xk, xr), tok)
+            out.backward(go)
         return x.grad
 
     assert torch.equal(run(True), run(False))
-    assert not fused._RESIDUAL_GRADS  # every handed-over gradient was consumed
+    assert fused.pending_residual_grads() == 0  # every handed-over gradient was consumed
+
+
+def test_residual_token_only_inside_the_handoff_context(cuda):
+    """Outside residual_handoff(), for inputs without grad, and under
+    torch.compile no token is handed out, so a partial backward
+    (torch.autograd.grad on a subset) loses no skip gradient."""
+    from spikegpt_b200 import fused
+
+    x = torch.randn(2, 8, 128, device=cuda, requires_grad=True)
+    assert fused.new_residual_token(x) == 0
+    with fused.residual_handoff():
+        assert fused.new_residual_token(x.detach()) == 0
+        assert fused.new_residual_token(x) != 0
+    assert fused.new_residual_token(x) == 0
+    w = torch.ones(128, device=cuda)
+    b = torch.zeros(128, device=cuda)
+    m = [torch.full((1, 1, 128), 0.5, device=cuda)]
+    xk, = fused.ln_shift_mix(x, w, b, m, 1e-5, fused.new_residual_token(x))
+    out = fused.residual_add(x, xk.float().to(torch.bfloat16), 0)
+    (gx,) = torch.autograd.grad(out.sum(), [x])
+    assert torch.isfinite(gx).all() and fused.pending_residual_grads() == 0

@@ -68,6 +68,32 @@ def test_autograd_formula_traces_on_fake_tensors():
     assert k.grad.shape == k.shape and td.grad.shape == td.shape
 
 
+def test_state_keeping_forward_traces_on_fake_tensors():
+    """The wrappers' state-keeping forward and its backward (through the saved
+    state) trace on meta tensors, as torch.compile's AOTAutograd does."""
+    from spikegpt_b200 import weighted_key_value_triton_bf16io
+
+    k = _meta(2, 37, 72, dtype=torch.bfloat16).requires_grad_()
+    v = _meta(2, 37, 72, dtype=torch.bfloat16).requires_grad_()
+    td = _meta(72).requires_grad_()
+    tf = _meta(72).requires_grad_()
+    y, state = torch.ops.spikegpt_b200.wkv_forward_with_state(k, v, td, tf)
+    assert y.shape == k.shape and y.dtype == k.dtype and state.dtype == torch.uint8
+    weighted_key_value_triton_bf16io(k, v, td, tf).sum().backward()
+    assert k.grad.shape == k.shape and tf.grad.shape == tf.shape
+
+
+@pytest.mark.parametrize("shape", [(64, 1024, 512), (1, 1, 1), (3, 17, 70), (0, 5, 8), (2, 0, 8), (5, 3072, 96)])
+def test_state_size_formula_matches_the_library(shape):
+    from spikegpt_b200 import _capi
+    from spikegpt_b200._ops import state_nbytes
+
+    for code in (_capi.DTYPE_F32, _capi.DTYPE_BF16):
+        assert state_nbytes(*shape) >= int(_capi.lib().wkv_state_size(code, *shape))
+        if all(shape):
+            assert state_nbytes(*shape) == int(_capi.lib().wkv_state_size(code, *shape))
+
+
 def test_dropin_install_aliases_reference_module_names(monkeypatch):
     import sys
 

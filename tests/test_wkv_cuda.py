@@ -257,10 +257,9 @@ def test_no_state_is_saved_without_grad(cuda):
     before = _capi.launch_counts()
     with torch.no_grad():
         weighted_key_value_cuda_bf16io(kt, vt, torch.as_tensor(td).cuda(), torch.as_tensor(tf).cuda())
-    from spikegpt_b200 import _ops
-
-    assert getattr(_ops._TLS, "pending", None) is None
-    assert _capi.launch_counts()["wkv_fwd_kernel<y>"] == before["wkv_fwd_kernel<y>"] + 1
+    after = _capi.launch_counts()
+    assert after["wkv_fwd_kernel<y>"] == before["wkv_fwd_kernel<y>"] + 1
+    assert after["wkv_fwd_kernel<state>"] == before["wkv_fwd_kernel<state>"]
 
 
 def test_results_are_deterministic(cuda):
@@ -348,13 +347,37 @@ def test_torch_compile_fullgraph_matches_eager(cuda):
     outs = []
     for fn in (block, compiled):
         leaves = [torch.as_tensor(x).cuda().requires_grad_() for x in (k, v, td, tf)]
-        fn(*leaves).sum().backward()
-        outs.append([leaves[0].grad, leaves[2].grad])
-    # eager takes the saved-state backward, the compiled graph the self-contained
-    # one (segment-local checkpoints for this small B*C), so agreement is to
-    # float32 rounding of the per-channel sums
+        out = fn(*leaves).sum()
+        torch.cuda.synchronize()
+        before = _capi.launch_counts()
+        out.backward()
+        torch.cuda.synchronize()
+        after = _capi.launch_counts()
+        # both take the saved-state backward: no state sweep, one gradient launch
+        assert after["wkv_fwd_kernel<state>"] == before["wkv_fwd_kernel<state>"]
+        assert after["wkv_bwd_kernel<grad>"] == before["wkv_bwd_kernel<grad>"] + 1
+        outs.append([leaves[0].grad, leaves[1].grad, leaves[2].grad, leaves[3].grad])
     for a, b in zip(*outs, strict=True):
         assert scaled_err(a.cpu().numpy(), b.cpu().numpy()) <= TOL_FP32
+
+
+def test_torch_compile_without_state_saving_uses_the_schema_backward(cuda):
+    """With the hand-off disabled the compiled graph calls the reference's
+    self-contained backward op, which runs its own state sweep."""
+    k, v, td, tf, gy = config_inputs(4, 128, 64, seed=16)
+    spikegpt_b200.set_state_saving(False)
+    try:
+        torch._dynamo.reset()
+        compiled = torch.compile(lambda *a: weighted_key_value_cuda_bf16io(*a).sum(), fullgraph=True)
+        leaves = [torch.as_tensor(x).cuda().requires_grad_() for x in (k, v, td, tf)]
+        out = compiled(*leaves)
+        before = _capi.launch_counts()
+        out.backward()
+        torch.cuda.synchronize()
+        assert _capi.launch_counts()["wkv_fwd_kernel<state>"] > before["wkv_fwd_kernel<state>"]
+    finally:
+        spikegpt_b200.set_state_saving(True)
+        torch._dynamo.reset()
 
 
 def test_no_device_side_errors_were_raised(cuda):

@@ -66,3 +66,21 @@ def test_errors_and_launch_counts(cuda):
     after = _capi.launch_counts()
     assert after["xent_fwd_kernel"] - before["xent_fwd_kernel"] == 1
     assert after["xent_bwd_kernel"] - before["xent_bwd_kernel"] == 1
+
+
+@pytest.mark.parametrize("bad", [-1, 40, 1000])
+def test_out_of_range_target_makes_the_loss_nan_and_sets_the_flag(cuda, bad):
+    """PyTorch rejects a target outside [0, V) other than ignore_index -100;
+    the fused loss makes that row (so the mean) NaN and its gradient row NaN,
+    and records WKV_DEVERR_BAD_TARGET, instead of silently lowering the mean."""
+    full, t = _case(4, 40, 40, 5, cuda)
+    t[2] = bad
+    t[0] = -100
+    assert _capi.device_error_flags(clear=True) == 0
+    x = full.clone().requires_grad_()
+    loss = fused.cross_entropy(x, t)
+    loss.backward()
+    assert torch.isnan(loss)
+    assert torch.isnan(x.grad[2].float()).all()
+    assert torch.count_nonzero(x.grad[0]) == 0 and torch.isfinite(x.grad[[1, 3]].float()).all()
+    assert _capi.device_error_flags(clear=True) == _capi.WKV_DEVERR_BAD_TARGET

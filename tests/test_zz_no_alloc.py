@@ -33,7 +33,8 @@ pytestmark = pytest.mark.gpu
 # one (B*C fills the GPU); both fit in the static scratch.
 CALLS = [(4, 300, 192, 11), (64, 256, 512, 12)]
 DTYPES = {"float32": (torch.float32, _capi.DTYPE_F32, TOL_FP32),
-          "bfloat16": (torch.bfloat16, _capi.DTYPE_BF16, TOL_16BIT)}
+          "bfloat16": (torch.bfloat16, _capi.DTYPE_BF16, TOL_16BIT),
+          "float16": (torch.float16, _capi.DTYPE_F16, TOL_16BIT)}
 
 
 def _inputs(b, t, c, seed, dtype, device):
