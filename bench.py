@@ -64,6 +64,11 @@ WORKLOADS = {
     "cfg2b-8": dict(B=8, T=3072, C=512, dtype="bf16", kscale=4.0, desc="config 2b: B=8 T=3072 C=512 bf16"),
     "cfg2-b12": dict(B=12, T=3072, C=512, dtype="bf16", kscale=4.0,
                      desc="long context B=12 T=3072 C=512 bf16 (the reference's published row)"),
+    "cfg1-b1": dict(B=1, T=1024, C=512, dtype="bf16", kscale=4.0, desc="B=1 T=1024 C=512 bf16"),
+    "cfg1-b2": dict(B=2, T=1024, C=512, dtype="bf16", kscale=4.0, desc="B=2 T=1024 C=512 bf16"),
+    "cfg1-b4": dict(B=4, T=1024, C=512, dtype="bf16", kscale=4.0, desc="B=4 T=1024 C=512 bf16"),
+    "cfg1-b8": dict(B=8, T=1024, C=512, dtype="bf16", kscale=4.0,
+                    desc="B=8 T=1024 C=512 bf16 (the per-GPU batch of config 3 on 8 GPUs)"),
     "cfg1-b12": dict(B=12, T=1024, C=512, dtype="bf16", kscale=4.0,
                      desc="B=12 T=1024 C=512 bf16 (the reference's published row)"),
     "cfg1-b24": dict(B=24, T=1024, C=512, dtype="bf16", kscale=4.0,

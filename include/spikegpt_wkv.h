@@ -329,6 +329,7 @@ WKV_API int wkv_set_debug_overrides(int force_segments, int force_generic, int f
  */
 WKV_API int wkv_set_debug_pipeline(long long wait_limit_cycles, int withhold_first_copies);
 
+
 /*
  * Launch accounting and per-kernel device timing (no reference counterpart; the
  * benchmark uses them for its launch count and roofline figures).

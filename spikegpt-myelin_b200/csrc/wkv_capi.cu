@@ -142,17 +142,27 @@ struct Plan {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Segments: one sequential sweep per lane when B*C lanes give every SM enough
-// warps; otherwise split time so that lanes * segments reaches that count.
+// Segments (the chunked two-level scan across CTAs) against one sequential
+// sweep per lane set, chosen from a sweep of measured step times (forward +
+// backward, B200, C = 512, bf16, T in {1024, 3072}, B from 1 to 64, every
+// segment count from 1 to 24). A CTA covers one (batch row, 64-channel block,
+// segment); about 512 CTAs (3.46 per SM: the resident limit of the time-parallel
+// kernels is 4) fill the GPU. Segmenting adds a state sweep, an adjoint sweep
+// and two carries, which pays when the sweep alone leaves most SMs idle: at
+// T = 1024 up to 64 lane sets (B = 8: 99 us with 8 segments against 108 us with
+// one), not from 96 (B = 12: 109 us with one, 113-117 us with 4-6); at T = 3072
+// down to 192 lane sets (B = 24: 276 us with 3 against 295 us). The segment
+// count is then 512 / lane sets rounded up, with segments of at least 128 steps
+// (measured best within 3 % on every swept shape).
 Plan make_plan(int dtype, int64_t B, int64_t T, int64_t C, bool ptrs_aligned) {
   Plan p;
   const size_t es = dtype_size(dtype);
   p.tma = g_force_generic.load() == 0 && ptrs_aligned && (C * (int64_t)es) % 16 == 0;
-  const int64_t lanes = B * ((C + kLanes - 1) / kLanes) * kLanes;
-  const int64_t want = (int64_t)sm_count() * 3 * kLanes;  // ~3 single-warp CTAs per SM
+  const int64_t sets = B * ((C + kLanes - 1) / kLanes);  // CTAs of one sweep
+  const int64_t want = (int64_t)sm_count() * 346 / 100;     // 512 on 148 SMs
   int64_t nseg = 1;
-  if (lanes > 0 && lanes < want) nseg = (want + lanes - 1) / lanes;
-  const int64_t max_seg = T / (2 * kSegAlign);  // keep >= 2 alignment units per segment
+  if (sets > 0 && sets < want && (T >= 2048 || sets <= 64)) nseg = (want + sets - 1) / sets;
+  const int64_t max_seg = T / 128;
   if (nseg > max_seg) nseg = max_seg;
   if (g_force_segments.load() > 0) nseg = g_force_segments.load();
   if (nseg < 1) nseg = 1;

@@ -549,17 +549,30 @@ __global__ void wkv_carry_fwd_kernel(float* seg, const float* decay, int decay_i
   const int b = static_cast<int>(i / C), c = static_cast<int>(i % C);
   const float d = decay[c];
   const float ew = expf(decay_is_w ? d : -expf(d));  // as make_lane2
+  // every combined segment is a full one (only the last may be shorter, and
+  // nothing follows it)
+  const Decay1 dfull = ew_decay(ew, seg_len);
   float S = kNegBig, p = 0.f, q = 0.f;
-  for (int s = 0; s < nseg; ++s) {
-    const size_t row = (size_t)b * nseg + s;
-    float lS = kNegBig, lp = 0.f, lq = 0.f;
-    if (s + 1 < nseg) load3s(seg, row, C, c, lS, lp, lq);
-    store3s(seg, row, C, c, S, p, q);
-    if (s + 1 < nseg) {
-      fwd_combine1(S, p, q, ew_decay(ew, min(seg_len, T - s * seg_len)), lS, lp, lq);
-      S = lS;
-      p = lp;
-      q = lq;
+  constexpr int K = 8;  // summaries loaded K at a time, ahead of the serial chain
+  for (int s0 = 0; s0 < nseg; s0 += K) {
+    float lS[K], lp[K], lq[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      lS[k] = kNegBig;
+      lp[k] = lq[k] = 0.f;
+      if (s0 + k + 1 < nseg) load3s(seg, (size_t)b * nseg + s0 + k, C, c, lS[k], lp[k], lq[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int s = s0 + k;
+      if (s >= nseg) break;
+      store3s(seg, (size_t)b * nseg + s, C, c, S, p, q);
+      if (s + 1 < nseg) {
+        fwd_combine1(S, p, q, dfull, lS[k], lp[k], lq[k]);
+        S = lS[k];
+        p = lp[k];
+        q = lq[k];
+      }
     }
   }
 }
@@ -573,16 +586,34 @@ __global__ void wkv_carry_adj_kernel(float* adj, const float* w, int B, int T, i
   if (i >= (int64_t)B * C) return;
   const int b = static_cast<int>(i / C), c = static_cast<int>(i % C);
   const float ew = expf(w[c]);  // as make_lane2
+  const int last_len = T - (nseg - 1) * seg_len;  // the last segment may be shorter
+  const Decay1 dfull = ew_decay(ew, seg_len), dlast = ew_decay(ew, last_len);
   float e[5] = {kNegBig, 0.f, 0.f, 0.f, 0.f};
-  for (int s = nseg - 1; s >= 0; --s) {
-    float* r = adj + ((size_t)b * nseg + s) * 5 * (size_t)C + c;
-    float l[5] = {kNegBig, 0.f, 0.f, 0.f, 0.f};
-    if (s > 0)
-      for (int f = 0; f < 5; ++f) l[f] = r[f * (size_t)C];
-    for (int f = 0; f < 5; ++f) r[f * (size_t)C] = e[f];
-    if (s > 0) {
-      const int len = min(seg_len, T - s * seg_len);
-      adj_combine1(l, e, len, ew_decay(ew, len));
+  constexpr int K = 4;  // summaries loaded K at a time, ahead of the serial chain
+  for (int s0 = nseg - 1; s0 >= 0; s0 -= K) {
+    float l[K][5];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int s = s0 - k;
+      l[k][0] = kNegBig;
+      l[k][1] = l[k][2] = l[k][3] = l[k][4] = 0.f;
+      if (s > 0) {
+        const float* r = adj + ((size_t)b * nseg + s) * 5 * (size_t)C + c;
+#pragma unroll
+        for (int f = 0; f < 5; ++f) l[k][f] = r[f * (size_t)C];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int s = s0 - k;
+      if (s < 0) break;
+      float* r = adj + ((size_t)b * nseg + s) * 5 * (size_t)C + c;
+#pragma unroll
+      for (int f = 0; f < 5; ++f) r[f * (size_t)C] = e[f];
+      if (s > 0) {
+        const bool last = s == nseg - 1;
+        adj_combine1(l[k], e, last ? last_len : seg_len, last ? dlast : dfull);
+      }
     }
   }
 }

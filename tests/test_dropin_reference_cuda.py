@@ -59,7 +59,9 @@ def _run(block, x, gy, *, autocast: bool):
     with torch.autocast("cuda", dtype=torch.bfloat16, enabled=autocast):
         out = block(x)
     out.float().backward(gy)
-    grads = {n: p.grad.detach().float().cpu().numpy() for n, p in block.named_parameters() if p.grad is not None}
+    # (a compiled block names its parameters "_orig_mod.<name>")
+    grads = {n.removeprefix("_orig_mod."): p.grad.detach().float().cpu().numpy()
+             for n, p in block.named_parameters() if p.grad is not None}
     grads["input"] = x.grad.detach().float().cpu().numpy()
     return out.detach().float().cpu().numpy(), grads
 
