@@ -114,6 +114,8 @@ def parse_args():
                     help="time the self-contained op pair (backward re-runs the forward sweep)")
     ap.add_argument("--eager", action="store_true",
                     help="train workloads: launch the step's kernels eagerly instead of replaying a CUDA graph")
+    ap.add_argument("--no-overlap", dest="overlap", action="store_false",
+                    help="train workloads: one gradient all-reduce after the backward instead of buckets during it")
     ap.add_argument("--global-batch", type=int, default=None,
                     help="train workloads: override the global batch (e.g. the per-rank share of an N-GPU run on one GPU)")
     ap.add_argument("--no-train-leg", dest="train_leg", action="store_false",
@@ -586,8 +588,8 @@ def run_native(args, wl):
                                           world=world, rank=rank, dev=dev, clocks=False)
             tstep.release()
             result["train_step"] = {k: tr[k] for k in (
-                "metric", "value", "unit", "ms_per_step", "allreduce_ms_per_step", "nccl_ranks", "steps", "warmup",
-                "scaling", "loss", "gpu_launches")}
+                "metric", "value", "unit", "ms_per_step", "allreduce", "allreduce_ms_per_step", "nccl_ranks",
+                "steps", "warmup", "scaling", "loss", "gpu_launches")}
             result["train_step"].update(
                 model=tr["config"]["model"], global_batch=tr["config"]["global_batch"],
                 B_per_gpu=tr["config"]["B_per_gpu"], seq_len=tr["config"]["seq_len"],
@@ -1357,7 +1359,7 @@ def train_kernel_split(model, opt, x, y, dev, top: int) -> None:
 
 
 def measure_train(wl, *, steps: int, warmup: int, world: int, rank: int, dev, global_batch=None,
-                  eager: bool = False, clocks: bool = True, e2e_steps: int = 0):
+                  eager: bool = False, clocks: bool = True, e2e_steps: int = 0, overlap: bool = True):
     """Time the data-parallel train step (the process group, if any, is already
     initialized). Returns (result dict, TrainStep, model, optimizer, x, y); the
     caller releases the step before destroying the process group."""
@@ -1383,7 +1385,7 @@ def measure_train(wl, *, steps: int, warmup: int, world: int, rank: int, dev, gl
     ids = torch.as_tensor(ids_np).to(dev)
     x, y = ids[:, :-1].contiguous(), ids[:, 1:].contiguous()
     launches_before = sum(_capi.launch_counts().values())
-    step = TrainStep(model, opt, (b, t), device=dev, graph=not eager)
+    step = TrainStep(model, opt, (b, t), device=dev, graph=not eager, overlap=overlap)
     capture_launches = sum(_capi.launch_counts().values()) - launches_before
 
     for _ in range(warmup):
@@ -1431,11 +1433,14 @@ def measure_train(wl, *, steps: int, warmup: int, world: int, rank: int, dev, gl
         "data": f"synthetic Zipf({wl['zipf']}) token ids, seeded numpy PCG64 per rank",
         "config": {"workload": wl["desc"], "model": name, "global_batch": gb, "seq_len": t, "B_per_gpu": b,
                    "params": sum(p.numel() for p in model.parameters()),
-                   "parallelism": f"dp{world}" + (" (flat-gradient NCCL all-reduce, AVG)" if world > 1 else ""),
+                   "parallelism": f"dp{world}" + (" (bucketed NCCL all-reduce, AVG)" if world > 1 else ""),
                    "launch": "eager" if eager else "CUDA graph (forward + backward), eager all-reduce "
                                                    "and fused AdamW",
                    "l2": "model state and activations far above L2; no flush"},
-        "allreduce_ms_per_step": ar if world > 1 else 0.0,
+        "allreduce_ms_per_step": ar if world > 1 and not step.overlap else None,
+        "allreduce": (f"{len(step.buckets)} buckets of about 25 MB, all-reduced asynchronously during the backward "
+                      "(captured in the graph)" if step.overlap else
+                      "one all-reduce of the flat gradients after the backward" if world > 1 else "none (one rank)"),
         "nccl_ranks": world if world > 1 else 0,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "flops_per_token": fpt,
@@ -1492,7 +1497,7 @@ def run_train(args, wl):
     result, step, model, opt, x, y = measure_train(
         wl, steps=args.steps, warmup=args.warmup, world=world, rank=rank, dev=dev,
         global_batch=args.global_batch, eager=args.eager, clocks=not args.profile,
-        e2e_steps=0 if args.profile else args.e2e_steps)
+        e2e_steps=0 if args.profile else args.e2e_steps, overlap=args.overlap)
     result["cpu_baseline"] = None
     result["cpu_baseline_note"] = ("no CPU leg: the model step runs only on this package's CUDA ops, and the "
                                    "reference's own CPU step needs myelin@68b8ebb, absent")

@@ -11,13 +11,17 @@ one all-reduce and the fused optimizer per step.
 
 Gradients: the backward starts from ``.grad = None``, so autograd hands each
 parameter the gradient tensor it produced (no zero fill, no accumulation
-kernels). On one rank the optimizer reads those. On several, one
-concatenation (captured with the backward) gathers them into a flat float32
-buffer, a single all-reduce averages it (DDP's average of the ranks'
-gradients of their shard-mean losses: ``ReduceOp.AVG`` over NCCL; gloo sums
-and divides), and the parameters' ``.grad`` are views of that buffer for the
-optimizer. The all-reduce and the optimizer step run outside the graph, on
-the current stream.
+kernels). On one rank the optimizer reads those. On several, the gradients
+are averaged (DDP's average of the ranks' gradients of their shard-mean
+losses: ``ReduceOp.AVG`` over NCCL; gloo sums and divides) in buckets of about
+25 MB of float32 while the backward runs: the parameters are laid out in one
+flat buffer in backward order, a hook on each parameter counts the gradients
+of its bucket, and the bucket's last gradient gathers them into its slice and
+starts an asynchronous all-reduce, which overlaps the backward of the earlier
+layers (DDP's bucketing). With a CUDA graph the all-reduces are captured with
+the backward. The parameters' ``.grad`` are then views of the flat buffer for
+the optimizer, which runs outside the graph on the current stream.
+``overlap=False`` keeps one all-reduce of the whole buffer after the backward.
 
 ``graph=False`` runs the same step eagerly (any device, any process group:
 the CPU tests use it over gloo).
@@ -43,7 +47,8 @@ class TrainStep:
 
     def __init__(self, model: nn.Module, optimizer: torch.optim.Optimizer, batch_shape: tuple[int, int], *,
                  device: torch.device | str, autocast_dtype: torch.dtype | None = torch.bfloat16,
-                 graph: bool = True, group=None, warmup: int = 3) -> None:
+                 graph: bool = True, group=None, warmup: int = 3, overlap: bool = True,
+                 bucket_mb: float = 25.0) -> None:
         self.model = model
         self.optimizer = optimizer
         self.device = torch.device(device)
@@ -60,12 +65,10 @@ class TrainStep:
         self.params = params
         self.grads = None  # the flat gradient buffer (several ranks only)
         self.grad_views = None
+        self.overlap = overlap and self.world > 1
+        self.buckets: list[tuple[list[nn.Parameter], Tensor]] = []
         if self.world > 1:
-            self.grads = torch.zeros(sum(p.numel() for p in params), dtype=torch.float32, device=self.device)
-            self.grad_views, off = [], 0
-            for p in params:
-                self.grad_views.append(self.grads[off:off + p.numel()].view_as(p))
-                off += p.numel()
+            self._layout(bucket_mb)
         self.ids = torch.zeros(batch_shape, dtype=torch.long, device=self.device)
         self.targets = torch.zeros(batch_shape, dtype=torch.long, device=self.device)
         self.graph = None
@@ -76,23 +79,84 @@ class TrainStep:
         if graph:
             self._capture(warmup)
 
+    def _layout(self, bucket_mb: float) -> None:
+        """Flat gradient buffer in backward order (the reverse of registration,
+        which follows the forward), cut into buckets of about bucket_mb MB."""
+        order = list(reversed(self.params))
+        self.grads = torch.zeros(sum(p.numel() for p in order), dtype=torch.float32, device=self.device)
+        limit = max(1, int(bucket_mb * 2**20 / 4))
+        view_of: dict[int, Tensor] = {}
+        off, start, members = 0, 0, []
+        for p in order:
+            view_of[id(p)] = self.grads[off:off + p.numel()].view_as(p)
+            members.append(p)
+            off += p.numel()
+            if off - start >= limit or p is order[-1]:
+                self.buckets.append((members, self.grads[start:off]))
+                start, members = off, []
+        self.grad_views = [view_of[id(p)] for p in self.params]
+        self._bucket_of = {id(p): i for i, (ms, _) in enumerate(self.buckets) for p in ms}
+        self._ready = [0] * len(self.buckets)
+        self._works: list = []
+        self._collecting = False
+        if self.overlap:
+            for p in self.params:
+                p.register_post_accumulate_grad_hook(self._grad_ready)
+
+    def _grad_ready(self, p: Tensor) -> None:
+        # autograd hook: p.grad is final for this backward
+        if not self._collecting:
+            return
+        i = self._bucket_of[id(p)]
+        self._ready[i] += 1
+        if self._ready[i] == len(self.buckets[i][0]):
+            self._reduce_bucket(i)
+
+    def _reduce_bucket(self, i: int) -> None:
+        members, flat = self.buckets[i]
+        grads = [p.grad.reshape(-1) if p.grad is not None else torch.zeros(p.numel(), device=self.device)
+                 for p in members]
+        torch.cat(grads, out=flat)
+        op = dist.ReduceOp.AVG if self.avg else dist.ReduceOp.SUM
+        self._works.append((i, dist.all_reduce(flat, op=op, group=self.group, async_op=True)))
+        self._ready[i] = -1  # launched
+
+    def _finish_buckets(self) -> None:
+        """Launch the buckets the hooks did not (parameters without a gradient)
+        and make the current stream wait for every bucket's all-reduce."""
+        for i, n in enumerate(self._ready):
+            if n != -1:
+                self._reduce_bucket(i)
+        for i, work in self._works:
+            work.wait()
+            if not self.avg:
+                self.buckets[i][1].div_(self.world)
+        self._works = []
+        self._ready = [0] * len(self.buckets)
+
     def _forward_backward(self) -> Tensor:
         for p in self.params:
             p.grad = None
         # the full backward below consumes every skip gradient handed over
         # between a residual_add and its LayerNorm-mix (fused.residual_handoff)
-        with fused.residual_handoff():
-            if self.autocast_dtype is None:
-                loss = self.model(self.ids, self.targets)
-            else:
-                with torch.autocast(self.device.type, dtype=self.autocast_dtype):
+        self._collecting = self.overlap
+        try:
+            with fused.residual_handoff():
+                if self.autocast_dtype is None:
                     loss = self.model(self.ids, self.targets)
-            loss.backward()
+                else:
+                    with torch.autocast(self.device.type, dtype=self.autocast_dtype):
+                        loss = self.model(self.ids, self.targets)
+                loss.backward()
+        finally:
+            self._collecting = False
         if fused.pending_residual_grads():
             fused.drop_residual_grads()
             raise RuntimeError("TrainStep: a residual gradient was handed over but never consumed")
-        if self.grads is not None:
-            torch.cat([p.grad.reshape(-1) for p in self.params], out=self.grads)
+        if self.overlap:
+            self._finish_buckets()
+        elif self.grads is not None:
+            torch.cat([p.grad.reshape(-1) for p in reversed(self.params)], out=self.grads)
         return loss.detach()
 
     def _capture(self, warmup: int) -> None:
@@ -128,7 +192,7 @@ class TrainStep:
             loss = self.loss
         else:
             loss = self._forward_backward()
-        if self.grads is not None:
+        if self.grads is not None and not self.overlap:
             ev = None
             if self._ar_events is not None:
                 ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -141,6 +205,7 @@ class TrainStep:
             if ev is not None:
                 ev[1].record()
                 self._ar_events.append(ev)
+        if self.grads is not None:
             if self.graph is None:
                 for p, g in zip(self.params, self.grad_views):
                     p.grad = g
@@ -149,7 +214,8 @@ class TrainStep:
 
     def time_allreduce(self, on: bool = True) -> None:
         """Record CUDA events around each call's gradient all-reduce (on the
-        current stream) until ``allreduce_ms`` collects them."""
+        current stream) until ``allreduce_ms`` collects them; only the
+        all-reduce after the backward (overlap=False) is timed."""
         self._ar_events = [] if on else None
 
     def allreduce_ms(self) -> tuple[float, int]:

@@ -58,7 +58,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, out):
+def _worker(rank, world, port, out, overlap=True, bucket_mb=25.0):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     from datetime import timedelta
 
@@ -69,21 +69,29 @@ def _worker(rank, world, port, out):
         opt = torch.optim.SGD(model.parameters(), lr=0.5)
         x, y = _batch()
         rows = x.shape[0] // world
-        step = TrainStep(model, opt, (rows, x.shape[1]), device="cpu", autocast_dtype=None, graph=False)
+        step = TrainStep(model, opt, (rows, x.shape[1]), device="cpu", autocast_dtype=None, graph=False,
+                         overlap=overlap, bucket_mb=bucket_mb)
+        nbuckets = len(step.buckets)
         for _ in range(2):
             step(x[rank * rows:(rank + 1) * rows], y[rank * rows:(rank + 1) * rows])
         lo, hi = step.grads.data_ptr(), step.grads.data_ptr() + step.grads.numel() * 4
         views = all(lo <= p.grad.data_ptr() < hi for p in model.parameters())
-        out.put((rank, views, [p.detach().clone().numpy() for p in model.parameters()]))
+        out.put((rank, views, nbuckets, [p.detach().clone().numpy() for p in model.parameters()]))
     finally:
         dist.destroy_process_group()
 
 
-def test_gradients_average_over_gloo_ranks():
+@pytest.mark.parametrize("overlap,bucket_mb,nbuckets", [(True, 25.0, 1), (True, 1e-4, 3), (False, 25.0, 1)],
+                         ids=["one-bucket", "small-buckets", "after-backward"])
+def test_gradients_average_over_gloo_ranks(overlap, bucket_mb, nbuckets):
+    """Bucketed all-reduces during the backward (one bucket, or buckets of 26
+    elements: three all-reduces in flight over the four parameters) and the
+    single all-reduce after it give the same parameters as one process on the
+    whole batch."""
     ctx = mp.get_context("spawn")
     out = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, out)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, out, overlap, bucket_mb)) for r in range(WORLD)]
     for p in procs:
         p.start()
     results = sorted(out.get(timeout=120) for _ in range(WORLD))
@@ -98,8 +106,9 @@ def test_gradients_average_over_gloo_ranks():
         opt.zero_grad()
         model(x, y).backward()
         opt.step()
-    for rank, views, params in results:
+    for rank, views, got_buckets, params in results:
         assert views, rank
+        assert got_buckets == nbuckets
         for got, ref in zip(params, model.parameters()):
             np.testing.assert_allclose(got, ref.detach().numpy(), rtol=1e-5, atol=1e-6)
 
