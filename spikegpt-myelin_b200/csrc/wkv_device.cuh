@@ -379,18 +379,31 @@ __device__ __forceinline__ void fwd_combine1(float gS, float gp, float gq, Decay
   lS = s;
 }
 
+// The decay ew^delta of both lanes as (mantissas, integer exponents).
+__device__ __forceinline__ void ew_decay2(const Lane2& lc, int delta, f2& m, f2& e) {
+  if (delta == kSub) {
+    m = lc.dm16;
+    e = lc.de16;
+  } else {
+    const Decay1 dx = ew_decay(lc.ew.x, delta), dy = ew_decay(lc.ew.y, delta);
+    m = f2{dx.m, dy.m};
+    e = f2{dx.e, dy.e};
+  }
+}
+
+// fwd_combine1 for both lanes of the pair with packed arithmetic (the same
+// roundings lane by lane).
 __device__ __forceinline__ Fwd2 fwd_combine2(const Fwd2& g, int delta, const Lane2& lc,
                                              Fwd2 l) {
-  Decay1 dx, dy;
-  if (delta == kSub) {
-    dx = Decay1{lc.dm16.x, lc.de16.x};
-    dy = Decay1{lc.dm16.y, lc.de16.y};
-  } else {
-    dx = ew_decay(lc.ew.x, delta);
-    dy = ew_decay(lc.ew.y, delta);
-  }
-  fwd_combine1(g.S.x, g.p.x, g.q.x, dx, l.S.x, l.p.x, l.q.x);
-  fwd_combine1(g.S.y, g.p.y, g.q.y, dy, l.S.y, l.p.y, l.q.y);
+  f2 dm, de;
+  ew_decay2(lc, delta, dm, de);
+  const f2 ge = add2(g.S, de);
+  const f2 s = f2{fmaxf(ge.x, l.S.x), fmaxf(ge.y, l.S.y)};
+  const f2 a = mul2(dm, ex2x2(sub2(ge, s)));
+  const f2 b = ex2x2(sub2(l.S, s));
+  l.p = fma2(g.p, a, mul2(l.p, b));
+  l.q = fma2(g.q, a, mul2(l.q, b));
+  l.S = s;
   return l;
 }
 

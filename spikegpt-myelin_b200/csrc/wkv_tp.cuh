@@ -110,8 +110,10 @@ __device__ __forceinline__ void fwd_tp_summary(const typename Pair<T>::raw (&kr)
 }
 
 // Phase C of the forward: y for the n rows of the tile from the carry-in
-// (sc, p, q), with e^{k_i - sc} = ek[i] * c2, into a staged tile.
-template <typename T, bool kTail>
+// (sc, p, q), with e^{k_i - sc} = ek[i] * c2 (kScale; else c2 = 1), into a
+// staged tile. Per step: ekv = e v; y = (p + u' ekv) / (q + u' e) with u' = e^u,
+// both as one fused multiply-add; then p, q decay and take the step's terms.
+template <typename T, bool kTail, bool kScale>
 __device__ __forceinline__ void fwd_tp_y(const typename Pair<T>::raw (&vr)[kSub],
                                          const f2 (&ek)[kSub], int n, const Lane2& lc, f2 c2, f2 p,
                                          f2 q, T* ys) {
@@ -120,11 +122,11 @@ __device__ __forceinline__ void fwd_tp_y(const typename Pair<T>::raw (&vr)[kSub]
   for (int i = 0; i < kSub; ++i) {
     if (kTail && i >= n) break;
     const f2 v = P::unpack(vr[i]);
-    const f2 e = mul2(ek[i], c2);
-    const f2 eb = mul2(e, lc.eu);
-    const f2 y = mul2(fma2(eb, v, p), rcpx2(add2(q, eb)));
+    const f2 e = kScale ? mul2(ek[i], c2) : ek[i];
+    const f2 ekv = mul2(e, v);
+    const f2 y = mul2(fma2(lc.eu, ekv, p), rcpx2(fma2(e, lc.eu, q)));
     P::st(ys + i * kLanes, P::pack(y));  // staged [kSub][kLanes] tile
-    p = fma2(lc.ew, p, mul2(e, v));
+    p = fma2(lc.ew, p, ekv);
     q = fma2(lc.ew, q, e);
   }
 }
@@ -311,12 +313,21 @@ __global__ void __launch_bounds__(32 * W, 4)
                         fast_ok1(sin.S.y, sin.p.y, sin.q.y, kmax.y, kmin.y, n, lc.w2.y, lc.u2.y,
                                  sc.y, p.y, q.y) &&
                         !force_slow;
-        const f2 c2 = ex2x2(sub2(sj, sc));  // e^{k - sj} -> e^{k - sc}; integer exponents
         if (__all_sync(kFull, ok)) {
-          if (n == R)
-            fwd_tp_y<T, false>(vr, ek, n, lc, c2, p, q, ys + 2 * lane);
-          else
-            fwd_tp_y<T, true>(vr, ek, n, lc, c2, p, q, ys + 2 * lane);
+          // e^{k - sj} -> e^{k - sc}: an exact power of two, 1 unless the
+          // carried state's scale exceeds the tile's own
+          if (__all_sync(kFull, sc.x == sj.x && sc.y == sj.y)) {
+            if (n == R)
+              fwd_tp_y<T, false, false>(vr, ek, n, lc, splat(1.f), p, q, ys + 2 * lane);
+            else
+              fwd_tp_y<T, true, false>(vr, ek, n, lc, splat(1.f), p, q, ys + 2 * lane);
+          } else {
+            const f2 c2 = ex2x2(sub2(sj, sc));  // integer exponents: exact
+            if (n == R)
+              fwd_tp_y<T, false, true>(vr, ek, n, lc, c2, p, q, ys + 2 * lane);
+            else
+              fwd_tp_y<T, true, true>(vr, ek, n, lc, c2, p, q, ys + 2 * lane);
+          }
         } else {
           fwd_tp_exact<T>(a, b, t0, c, v0, v1, n, sin, lc, ys + 2 * lane);
         }
@@ -420,11 +431,11 @@ __device__ __forceinline__ void bwd_tp_recompute(const typename Pair<T>::raw (&k
     const f2 v = P::unpack(vr[i]);
     const f2 ek = ex2x2(fma2(P::unpack(kr[i]), l2e, ns));
     re[i] = ek;
-    const f2 eb = mul2(ek, lc.eu);
-    const f2 rd = rcpx2(add2(q, eb));
-    ry[i] = mul2(fma2(eb, v, p), rd);
+    const f2 ekv = mul2(ek, v);
+    const f2 rd = rcpx2(fma2(ek, lc.eu, q));  // 1 / D
+    ry[i] = mul2(fma2(lc.eu, ekv, p), rd);
     rg[i] = mul2(P::unpack(gr[i]), rd);
-    p = fma2(lc.ew, p, mul2(ek, v));
+    p = fma2(lc.ew, p, ekv);
     q = fma2(lc.ew, q, ek);
   }
 }
@@ -474,22 +485,23 @@ __device__ __forceinline__ void bwd_tp_outputs(const f2 (&re)[kSub],
   }
 }
 
+// adj_combine1 for both lanes of the pair with packed arithmetic (the same
+// roundings lane by lane).
 __device__ __forceinline__ Adj2 adj_combine2(const Adj2& l, Adj2 e, int len, const Lane2& lc) {
-  Decay1 dx, dy;
-  if (len == kSub) {
-    dx = Decay1{lc.dm16.x, lc.de16.x};
-    dy = Decay1{lc.dm16.y, lc.de16.y};
-  } else {
-    dx = ew_decay(lc.ew.x, len);
-    dy = ew_decay(lc.ew.y, len);
-  }
-  float lx[5] = {l.G.x, l.gp.x, l.gq.x, l.hp.x, l.hq.x};
-  float ly[5] = {l.G.y, l.gp.y, l.gq.y, l.hp.y, l.hq.y};
-  float ex[5] = {e.G.x, e.gp.x, e.gq.x, e.hp.x, e.hq.x};
-  float ey[5] = {e.G.y, e.gp.y, e.gq.y, e.hp.y, e.hq.y};
-  adj_combine1(lx, ex, len, dx);
-  adj_combine1(ly, ey, len, dy);
-  return Adj2{f2{ex[0], ey[0]}, f2{ex[1], ey[1]}, f2{ex[2], ey[2]}, f2{ex[3], ey[3]}, f2{ex[4], ey[4]}};
+  f2 dm, de;
+  ew_decay2(lc, len, dm, de);
+  const f2 fl = splat(static_cast<float>(len));
+  const f2 ge = add2(e.G, de);
+  const f2 g = f2{fmaxf(ge.x, l.G.x), fmaxf(ge.y, l.G.y)};
+  const f2 a = mul2(dm, ex2x2(sub2(ge, g)));
+  const f2 b = ex2x2(sub2(l.G, g));
+  const f2 hp = fma2(fl, e.gp, e.hp), hq = fma2(fl, e.gq, e.hq);
+  e.gp = fma2(e.gp, a, mul2(l.gp, b));
+  e.gq = fma2(e.gq, a, mul2(l.gq, b));
+  e.hp = fma2(hp, a, mul2(l.hp, b));
+  e.hq = fma2(hq, a, mul2(l.hq, b));
+  e.G = g;
+  return e;
 }
 
 // Exact (per-step rescaling) adjoint summary of a staged tile from a zero

@@ -85,24 +85,25 @@ def drop_residual_grads() -> None:
 def _ln_shift_mix(x: Tensor, weight: Tensor, bias: Tensor, mix: Tensor, eps: float, token: int) -> list[Tensor]:
     b, t, c = x.shape
     n = mix.shape[0]
-    outs = [torch.empty((b, t, c), dtype=torch.bfloat16, device=x.device) for _ in range(n)]
+    # the n outputs as one [n, B, T, C] tensor: projections that share a shape
+    # can then run as one batched GEMM on it
+    stacked = torch.empty((n, b, t, c), dtype=torch.bfloat16, device=x.device)
     mean = torch.empty((b, t), dtype=torch.float32, device=x.device)
     rstd = torch.empty_like(mean)
-    ptrs = [o.data_ptr() for o in outs] + [None] * (MAX_MIX - n)
+    ptrs = [stacked[i].data_ptr() for i in range(n)] + [None] * (MAX_MIX - n)
     _capi.check(
         _capi.lib().ln_mix_forward(n, x.data_ptr(), weight.data_ptr(), bias.data_ptr(), mix.data_ptr(), *ptrs,
                                    mean.data_ptr(), rstd.data_ptr(), b, t, c, eps,
                                    torch.cuda.current_stream(x.device).cuda_stream),
         "ln_mix_forward",
     )
-    return outs + [mean, rstd]
+    return [stacked, mean, rstd]
 
 
 @_ln_shift_mix.register_fake
 def _(x, weight, bias, mix, eps, token):
     b, t, c = x.shape
-    return [x.new_empty((b, t, c), dtype=torch.bfloat16) for _ in range(mix.shape[0])] + [
-        x.new_empty((b, t)), x.new_empty((b, t))]
+    return [x.new_empty((mix.shape[0], b, t, c), dtype=torch.bfloat16), x.new_empty((b, t)), x.new_empty((b, t))]
 
 
 @torch.library.custom_op("spikegpt_b200::ln_shift_mix_backward", mutates_args=(), device_types="cuda")
@@ -137,17 +138,18 @@ def _(grads, x, weight, bias, mix, mean, rstd, grad_residual):
 
 def _setup(ctx, inputs, output):
     x, weight, bias, mix, _eps, token = inputs
-    n = mix.shape[0]
-    ctx.save_for_backward(x, weight, bias, mix, output[n], output[n + 1])
-    ctx.n = n
+    ctx.save_for_backward(x, weight, bias, mix, output[1], output[2])
+    ctx.n = mix.shape[0]
     ctx.token = token
-    ctx.mark_non_differentiable(output[n], output[n + 1])
+    ctx.mark_non_differentiable(output[1], output[2])
 
 
 def _backward(ctx, grads):
     x, weight, bias, mix, mean, rstd = ctx.saved_tensors
-    gouts = [g if g is not None else torch.zeros(x.shape, dtype=torch.bfloat16, device=x.device)
-             for g in grads[: ctx.n]]
+    g = grads[0]
+    if g is None:
+        g = torch.zeros((ctx.n,) + tuple(x.shape), dtype=torch.bfloat16, device=x.device)
+    gouts = list(g.unbind(0))
     gres = _RESIDUAL_GRADS.pop(ctx.token, None) if ctx.token else None
     if gres is not None:
         gres = _aligned(gres.float())
@@ -158,6 +160,21 @@ def _backward(ctx, grads):
 _ln_shift_mix.register_autograd(_backward, setup_context=_setup)
 
 
+def ln_shift_mix_stacked(x: Tensor, weight: Tensor, bias: Tensor, mixes: list[Tensor], eps: float = 1e-5,
+                         residual_token: int = 0) -> Tensor:
+    """``ln_shift_mix`` with the outputs stacked as one bf16 [len(mixes), B, T, C]
+    tensor."""
+    if not supported(x):
+        raise ValueError("ln_shift_mix needs a contiguous float32 CUDA [B, T, C] tensor with C % 128 == 0, C <= 1024")
+    if not 1 <= len(mixes) <= MAX_MIX:
+        raise ValueError(f"1..{MAX_MIX} mixing vectors")
+    c = x.shape[-1]
+    mix = torch.cat([m.reshape(1, c).float() for m in mixes], 0)
+    return torch.ops.spikegpt_b200.ln_shift_mix(x.contiguous(), weight.float().contiguous(),
+                                                bias.float().contiguous(), mix.contiguous(), float(eps),
+                                                int(residual_token))[0]
+
+
 def ln_shift_mix(x: Tensor, weight: Tensor, bias: Tensor, mixes: list[Tensor], eps: float = 1e-5,
                  residual_token: int = 0) -> list[Tensor]:
     """bf16 ``LayerNorm(x) * m + shift(LayerNorm(x)) * (1 - m)`` for each m in
@@ -165,16 +182,7 @@ def ln_shift_mix(x: Tensor, weight: Tensor, bias: Tensor, mixes: list[Tensor], e
     ``residual_token`` (from :func:`new_residual_token`) pairs it with the
     ``residual_add(x, ...)`` that closes the sublayer: the skip connection's
     gradient is then added to grad x in this op's backward kernel."""
-    if not supported(x):
-        raise ValueError("ln_shift_mix needs a contiguous float32 CUDA [B, T, C] tensor with C % 128 == 0, C <= 1024")
-    if not 1 <= len(mixes) <= MAX_MIX:
-        raise ValueError(f"1..{MAX_MIX} mixing vectors")
-    c = x.shape[-1]
-    mix = torch.cat([m.reshape(1, c).float() for m in mixes], 0)
-    outs = torch.ops.spikegpt_b200.ln_shift_mix(x.contiguous(), weight.float().contiguous(),
-                                                bias.float().contiguous(), mix.contiguous(), float(eps),
-                                                int(residual_token))
-    return list(outs[: len(mixes)])
+    return list(ln_shift_mix_stacked(x, weight, bias, mixes, eps, residual_token).unbind(0))
 
 
 # ------------------------------------------------------------------ gates

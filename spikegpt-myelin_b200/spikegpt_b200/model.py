@@ -20,6 +20,8 @@ building it on the CPU is fine.
 
 from __future__ import annotations
 
+import os
+
 import math
 from dataclasses import dataclass
 
@@ -93,6 +95,11 @@ def _mix_profile(n_embd: int, power: float, offset: float = 0.0) -> Tensor:
     return (torch.pow(position, power) + offset).view(1, 1, -1)
 
 
+# The time-mixing key, value and receptance projections as one batched GEMM
+# (SPIKEGPT_BATCHED_KVR=0: three GEMMs).
+_BATCHED_KVR = os.environ.get("SPIKEGPT_BATCHED_KVR", "1") != "0"
+
+
 class TimeMix(nn.Module):
     """RWKV-4 time mixing (reference SpikeTimeMix, language.py:920-1036)."""
 
@@ -118,9 +125,19 @@ class TimeMix(nn.Module):
 
     def from_mixed(self, xk: Tensor, xv: Tensor, xr: Tensor) -> Tensor:
         """The sublayer from its three token-shift-mixed inputs."""
-        k = self.key(xk)
-        v = self.value(xv)
-        rl = self.receptance(xr)
+        return self._from_projections(self.key(xk), self.value(xv), self.receptance(xr))
+
+    def from_stacked(self, x3: Tensor) -> Tensor:
+        """The sublayer from its three mixed inputs stacked as [3, B, T, C]: the
+        key, value and receptance projections (same shape) as one batched GEMM,
+        three times the tiles of each alone (the small-batch case fills the GPU)."""
+        n, b, t, c = x3.shape
+        w3 = torch.stack([self.key.weight, self.value.weight, self.receptance.weight])
+        kvr = torch.matmul(x3.reshape(n, b * t, c), w3.transpose(1, 2)).reshape(n, b, t, c)
+        k, v, rl = kvr.unbind(0)
+        return self._from_projections(k, v, rl)
+
+    def _from_projections(self, k: Tensor, v: Tensor, rl: Tensor) -> Tensor:
         if k.dtype in (torch.bfloat16, torch.float16):
             wkv = weighted_key_value_cuda_bf16io(k, v, self.time_decay, self.time_first)
         else:
@@ -204,9 +221,13 @@ class Block(nn.Module):
         if self._fused(x):
             att, ffn = self.att, self.ffn
             tok = fused.new_residual_token(x)
-            xk, xv, xr = fused.ln_shift_mix(x, self.ln1.weight, self.ln1.bias,
+            x3 = fused.ln_shift_mix_stacked(x, self.ln1.weight, self.ln1.bias,
                                             [att.time_mix_k, att.time_mix_v, att.time_mix_r], self.ln1.eps, tok)
-            x = self._residual(x, self._lif(att.from_mixed(xk, xv, xr)), tok)
+            if _BATCHED_KVR:
+                mixed = att.from_stacked(x3)
+            else:
+                mixed = att.from_mixed(*x3.unbind(0))
+            x = self._residual(x, self._lif(mixed), tok)
             tok = fused.new_residual_token(x)
             xk, xr = fused.ln_shift_mix(x, self.ln2.weight, self.ln2.bias, [ffn.time_mix_k, ffn.time_mix_r],
                                         self.ln2.eps, tok)
