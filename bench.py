@@ -114,8 +114,9 @@ def parse_args():
                     help="time the self-contained op pair (backward re-runs the forward sweep)")
     ap.add_argument("--eager", action="store_true",
                     help="train workloads: launch the step's kernels eagerly instead of replaying a CUDA graph")
-    ap.add_argument("--no-overlap", dest="overlap", action="store_false",
-                    help="train workloads: one gradient all-reduce after the backward instead of buckets during it")
+    ap.add_argument("--overlap", action="store_true",
+                    help="train workloads: all-reduce the gradients in buckets during the backward instead of once "
+                         "after it")
     ap.add_argument("--global-batch", type=int, default=None,
                     help="train workloads: override the global batch (e.g. the per-rank share of an N-GPU run on one GPU)")
     ap.add_argument("--no-train-leg", dest="train_leg", action="store_false",
@@ -1359,7 +1360,7 @@ def train_kernel_split(model, opt, x, y, dev, top: int) -> None:
 
 
 def measure_train(wl, *, steps: int, warmup: int, world: int, rank: int, dev, global_batch=None,
-                  eager: bool = False, clocks: bool = True, e2e_steps: int = 0, overlap: bool = True):
+                  eager: bool = False, clocks: bool = True, e2e_steps: int = 0, overlap: bool = False):
     """Time the data-parallel train step (the process group, if any, is already
     initialized). Returns (result dict, TrainStep, model, optimizer, x, y); the
     caller releases the step before destroying the process group."""
