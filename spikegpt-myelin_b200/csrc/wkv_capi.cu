@@ -442,12 +442,16 @@ int launch_forward(const void* k, const void* v, const float* decay, int decay_i
         wkv_fwd_kernel<IO, false, false><<<dim3(gx, p.nseg - 1), kThreads, sm, st>>>(s, mk, mv, my);
       });
     }
-    const int64_t lanes = (int64_t)B * C;
-    launch(K_CARRY_FWD, st, [&] {
-      wkv_carry_fwd_kernel<<<(unsigned)((lanes + 127) / 128), 128, 0, st>>>(
-          seg, decay, decay_is_w, B, T, C, p.nseg, p.seg_len);
-    });
-    a.seg_start = seg;
+    if (p.tma) {
+      a.seg_sums = seg;  // each CTA folds the summaries before its segment itself
+    } else {
+      const int64_t lanes = (int64_t)B * C;
+      launch(K_CARRY_FWD, st, [&] {
+        wkv_carry_fwd_kernel<<<(unsigned)((lanes + 127) / 128), 128, 0, st>>>(
+            seg, decay, decay_is_w, B, T, C, p.nseg, p.seg_len);
+      });
+      a.seg_start = seg;
+    }
   }
   // The main pass starts every segment from its true state, so the checkpoints
   // it writes are true states; it also zeroes the backward's arrival counters.
@@ -565,12 +569,17 @@ int launch_backward(const void* gy, const float* w, const float* u, const void* 
   if (p.nseg > 1) {
     // 2. segment start states (only when the checkpoints are segment-local);
     // 3. adjoint summaries of segments 1..nseg-1; 4. adjoint at every segment end
-    if (state == nullptr)
+    // (TMA kernels fold the summaries themselves; the generic ones take the
+    // carried states)
+    if (state == nullptr && !p.tma)
       launch(K_CARRY_FWD, st, [&] {
         wkv_carry_fwd_kernel<<<cgrid, 128, 0, st>>>(ws.seg, w, 1, B, T, C, p.nseg, p.seg_len);
       });
     BwdArgs s = a;
-    s.seg_start = state ? nullptr : ws.seg;
+    if (p.tma)
+      s.seg_sums = state ? nullptr : ws.seg;
+    else
+      s.seg_start = state ? nullptr : ws.seg;
     s.seg_base = 1;
     s.adj_out = ws.adj;
     if (p.tma) {
@@ -588,11 +597,16 @@ int launch_backward(const void* gy, const float* w, const float* u, const void* 
             <<<dim3(gx, p.nseg - 1), kThreads, ssm, st>>>(s, mk, mv, mgy, none, none);
       });
     }
-    launch(K_CARRY_ADJ, st, [&] {
-      wkv_carry_adj_kernel<<<cgrid, 128, 0, st>>>(ws.adj, w, B, T, C, p.nseg, p.seg_len);
-    });
-    a.seg_start = state ? nullptr : ws.seg;
-    a.adj_in = ws.adj;
+    if (p.tma) {
+      a.seg_sums = state ? nullptr : ws.seg;
+      a.adj_sums = ws.adj;
+    } else {
+      launch(K_CARRY_ADJ, st, [&] {
+        wkv_carry_adj_kernel<<<cgrid, 128, 0, st>>>(ws.adj, w, B, T, C, p.nseg, p.seg_len);
+      });
+      a.seg_start = state ? nullptr : ws.seg;
+      a.adj_in = ws.adj;
+    }
   }
   // 5. reverse sweep writing grad_key / grad_value and per-lane partials; the
   // last CTA of each column block reduces the partials into the time gradients

@@ -72,6 +72,7 @@ struct FwdArgs {
   float* seg_end;          // [B][nseg][3][C] segment end states, or null
   unsigned* zero_tickets;  // counters the first CTA resets for a later wkv_bwd_kernel, or null
   int nzero;
+  const float* seg_sums;   // [B][nseg][3][C] segment summaries (from zero) to fold into the start state, or null
   int force_slow;
   unsigned* err;
   // Debug (wkv_set_debug_pipeline): the consumers' copy-wait limit in cycles,
@@ -93,6 +94,8 @@ struct BwdArgs {
   const float* ckpt;       // [B][nsub][3][C]: true states, or states local to the segment
   const float* seg_start;  // [B][nseg][3][C] (ckpt is segment-local when non-null)
   const float* adj_in;     // [B][nseg][5][C] adjoint at segment ends, or null (zero)
+  const float* seg_sums;   // [B][nseg][3][C] state summaries to fold into the segment start, or null
+  const float* adj_sums;   // [B][nseg][5][C] adjoint summaries (s >= 1) to fold into the segment end, or null
   float* adj_out;          // [B][nseg][5][C] adjoint at segment starts, or null
   float* partial;          // [B][nseg][2][C] (gwacc, gu) per lane-segment, or null
   unsigned* tickets;       // [ncblk] arrival counters (zeroed beforehand), or null
@@ -155,6 +158,36 @@ __device__ __forceinline__ void store_adj(float* base, size_t row, int C, int c,
 }
 
 // Generic path: the warp fills rows [0, rows) of a [rows][kLanes] tile.
+// State at the start of segment `seg` of batch row b: the summaries of segments
+// 0 .. seg-1 (each the state the segment reaches from zero) folded in order,
+// every one decayed over a full segment. Loaded four at a time ahead of the
+// serial fold. (The carry kernel does the same for all segments at once.)
+__device__ __forceinline__ Fwd2 fold_state_summaries(const float* sums, int b, int nseg, int seg,
+                                                     int seg_len, int C, int c, bool v0, bool v1,
+                                                     const Lane2& lc) {
+  Fwd2 st = fwd_identity2();
+  constexpr int K = 4;
+  for (int s0 = 0; s0 < seg; s0 += K) {
+    Fwd2 l[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      l[k] = fwd_identity2();
+      if (s0 + k < seg) load3(sums, (size_t)b * nseg + s0 + k, C, c, v0, v1, l[k].S, l[k].p, l[k].q);
+    }
+#pragma unroll
+    for (int k = 0; k < K; ++k)
+      if (s0 + k < seg) st = fwd_combine2(st, seg_len, lc, l[k]);
+  }
+  return st;
+}
+
+// Adjoint at the end of segment `seg`: the adjoint summaries of segments
+// nseg-1 down to seg+1 (each accumulated from a zero adjoint at its own end)
+// folded from a zero adjoint at T; the last segment may be shorter.
+__device__ __forceinline__ Adj2 fold_adjoint_summaries(const float* sums, int b, int nseg, int seg,
+                                                       int seg_len, int T, int C, int c, bool v0,
+                                                       bool v1, const Lane2& lc);
+
 template <typename T>
 __device__ __forceinline__ void fill_tile(T* tile, const T* src, int b, int t0, int rows, int T_,
                                           int C, int c, bool v0, bool v1, int lane) {

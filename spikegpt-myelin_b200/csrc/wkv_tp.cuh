@@ -208,6 +208,8 @@ __global__ void __launch_bounds__(32 * W, 4)
   Fwd2 start = fwd_identity2();  // state at the segment start
   if (a.seg_start != nullptr)
     load3(a.seg_start, (size_t)b * a.nseg + seg, a.C, c, v0, v1, start.S, start.p, start.q);
+  else if (a.seg_sums != nullptr && seg > 0)
+    start = fold_state_summaries(a.seg_sums, b, a.nseg, seg, a.seg_len, a.C, c, v0, v1, lc);
 
   // (a.withhold_first: debug only, the first round's copies are never issued)
   auto withheld = [&](int r) { return a.withhold_first != 0 && r == 0; };
@@ -504,6 +506,26 @@ __device__ __forceinline__ Adj2 adj_combine2(const Adj2& l, Adj2 e, int len, con
   return e;
 }
 
+__device__ __forceinline__ Adj2 fold_adjoint_summaries(const float* sums, int b, int nseg, int seg,
+                                                       int seg_len, int T, int C, int c, bool v0,
+                                                       bool v1, const Lane2& lc) {
+  Adj2 e = adj_zero2();
+  const int last_len = T - (nseg - 1) * seg_len;
+  constexpr int K = 4;
+  for (int s0 = nseg - 1; s0 > seg; s0 -= K) {
+    Adj2 l[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      l[k] = adj_zero2();
+      if (s0 - k > seg) load_adj(sums, (size_t)b * nseg + s0 - k, C, c, v0, v1, l[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < K; ++k)
+      if (s0 - k > seg) e = adj_combine2(l[k], e, s0 - k == nseg - 1 ? last_len : seg_len, lc);
+  }
+  return e;
+}
+
 // Exact (per-step rescaling) adjoint summary of a staged tile from a zero
 // adjoint, both channels of the lane pair. Rare: only when the fast path's
 // range checks fail.
@@ -587,9 +609,16 @@ __global__ void __launch_bounds__(32 * W, 4)
   const size_t lseg = (size_t)b * a.nseg + seg;
 
   Adj2 adj = adj_zero2();  // adjoint entering the current round (at its last tile's end)
-  if (a.adj_in != nullptr) load_adj(a.adj_in, lseg, a.C, c, v0, v1, adj);
+  if (a.adj_in != nullptr)
+    load_adj(a.adj_in, lseg, a.C, c, v0, v1, adj);
+  else if (a.adj_sums != nullptr && seg + 1 < a.nseg)
+    adj = fold_adjoint_summaries(a.adj_sums, b, a.nseg, seg, a.seg_len, a.T, a.C, c, v0, v1, lc);
   Fwd2 segst = fwd_identity2();
-  if (a.seg_start != nullptr) load3(a.seg_start, lseg, a.C, c, v0, v1, segst.S, segst.p, segst.q);
+  if (a.seg_start != nullptr)
+    load3(a.seg_start, lseg, a.C, c, v0, v1, segst.S, segst.p, segst.q);
+  else if (a.seg_sums != nullptr && seg > 0)
+    segst = fold_state_summaries(a.seg_sums, b, a.nseg, seg, a.seg_len, a.C, c, v0, v1, lc);
+  const bool seg_local = a.seg_start != nullptr || a.seg_sums != nullptr;  // checkpoints from the segment start
   f2 gwacc = splat(0.f), gu = splat(0.f);
 
   auto issue = [&](bool on, int r) {  // by the threads with `on` (one per CTA)
@@ -647,7 +676,7 @@ __global__ void __launch_bounds__(32 * W, 4)
       const f2* ck = reinterpret_cast<const f2*>(base + 3 * G::kBoxBytes) + warp * 3 * (kLanes / 2) + lane;
       st0 = Fwd2{ck[0], ck[kLanes / 2], ck[kLanes]};
     }
-    if (a.seg_start != nullptr && n > 0)
+    if (seg_local && n > 0)
       st0 = (t0 == t_begin) ? segst : fwd_combine2(segst, t0 - t_begin, lc, st0);
     f2 kmax, kmin, gymax, s, p, q;
     if (n == R) {
