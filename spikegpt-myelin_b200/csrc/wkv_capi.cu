@@ -144,16 +144,17 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 // Segments (the chunked two-level scan across CTAs) against one sequential
 // sweep per lane set, chosen from a sweep of measured step times (forward +
-// backward, B200, C = 512, bf16, T in {1024, 3072}, B from 1 to 64, every
-// segment count from 1 to 24). A CTA covers one (batch row, 64-channel block,
-// segment); about 512 CTAs (3.46 per SM: the resident limit of the time-parallel
-// kernels is 4) fill the GPU. Segmenting adds a state sweep, an adjoint sweep
-// and two carries, which pays when the sweep alone leaves most SMs idle: at
-// T = 1024 up to 64 lane sets (B = 8: 99 us with 8 segments against 108 us with
-// one), not from 96 (B = 12: 109 us with one, 113-117 us with 4-6); at T = 3072
-// down to 192 lane sets (B = 24: 276 us with 3 against 295 us). The segment
-// count is then 512 / lane sets rounded up, with segments of at least 128 steps
-// (measured best within 3 % on every swept shape).
+// backward, B200, C = 512, bf16, T in {1024, 3072}, B from 1 to 24, segment
+// counts from 1 to 24). A CTA covers one (batch row, 64-channel block,
+// segment); about 512 CTAs (3.46 per SM: the resident limit of the
+// time-parallel kernels is 4) fill the GPU. Segmenting adds a state sweep and
+// an adjoint sweep (the TMA kernels fold the segment summaries themselves),
+// which pays when the sweep alone leaves most SMs idle: at T = 1024 up to 96
+// lane sets (B = 12: 98 us with 6 segments against 111 us with one), not at
+// 192 (B = 24: 116 us with one, 144 us with 3); at T = 3072 down to 192 lane
+// sets (B = 24: 262 us with 3 against 295 us). The segment count is then
+// 512 / lane sets rounded up, at most 16 and with segments of at least 128
+// steps (the measured best within 3 % on every swept shape).
 Plan make_plan(int dtype, int64_t B, int64_t T, int64_t C, bool ptrs_aligned) {
   Plan p;
   const size_t es = dtype_size(dtype);
@@ -161,8 +162,8 @@ Plan make_plan(int dtype, int64_t B, int64_t T, int64_t C, bool ptrs_aligned) {
   const int64_t sets = B * ((C + kLanes - 1) / kLanes);  // CTAs of one sweep
   const int64_t want = (int64_t)sm_count() * 346 / 100;     // 512 on 148 SMs
   int64_t nseg = 1;
-  if (sets > 0 && sets < want && (T >= 2048 || sets <= 64)) nseg = (want + sets - 1) / sets;
-  const int64_t max_seg = T / 128;
+  if (sets > 0 && sets < want && (T >= 2048 || sets <= 96)) nseg = (want + sets - 1) / sets;
+  const int64_t max_seg = std::min<int64_t>(16, T / 128);
   if (nseg > max_seg) nseg = max_seg;
   if (g_force_segments.load() > 0) nseg = g_force_segments.load();
   if (nseg < 1) nseg = 1;
