@@ -228,6 +228,27 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
 template <typename T>
 struct Pair;
 
+// Widens the two 16-bit floats of a packed word (element c in the low half) to
+// float32 with sm_100's mixed-precision add, d = a + (-0.0) with a 16-bit
+// source: one FP32-pipe instruction per value instead of a shift or a mask on
+// the integer pipe, and exact (adding -0.0 keeps every value, signed zeros,
+// subnormals and infinities included).
+template <bool kHalf>
+__device__ __forceinline__ f2 unpack16(uint32_t r) {
+  f2 d;
+  if constexpr (kHalf)
+    asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+        "add.rn.f32.f16 %0, l, 0f80000000;\n\tadd.rn.f32.f16 %1, h, 0f80000000;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "r"(r));
+  else
+    asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+        "add.rn.f32.bf16 %0, l, 0f80000000;\n\tadd.rn.f32.bf16 %1, h, 0f80000000;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "r"(r));
+  return d;
+}
+
 template <>
 struct Pair<float> {
   using raw = float2;
@@ -256,9 +277,7 @@ struct Pair<__nv_bfloat16> {
   static __device__ __forceinline__ void st(__nv_bfloat16* p, raw r) {
     *reinterpret_cast<uint32_t*>(p) = r;
   }
-  static __device__ __forceinline__ f2 unpack(raw r) {
-    return f2{__uint_as_float(r << 16), __uint_as_float(r & 0xffff0000u)};
-  }
+  static __device__ __forceinline__ f2 unpack(raw r) { return unpack16<false>(r); }
   static __device__ __forceinline__ raw pack(f2 v) {
     uint32_t d;
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(v.y), "f"(v.x));
@@ -279,11 +298,7 @@ struct Pair<__half> {
     return *reinterpret_cast<const uint32_t*>(p);
   }
   static __device__ __forceinline__ void st(__half* p, raw r) { *reinterpret_cast<uint32_t*>(p) = r; }
-  static __device__ __forceinline__ f2 unpack(raw r) {
-    __half2 h = *reinterpret_cast<__half2*>(&r);
-    const float2 f = __half22float2(h);
-    return f2{f.x, f.y};
-  }
+  static __device__ __forceinline__ f2 unpack(raw r) { return unpack16<true>(r); }
   static __device__ __forceinline__ raw pack(f2 v) {
     uint32_t d;
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(v.y), "f"(v.x));

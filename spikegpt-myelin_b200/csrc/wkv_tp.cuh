@@ -360,9 +360,10 @@ __global__ void __launch_bounds__(32 * W, 4)
 //   C. rerun the reverse recurrence from the incoming adjoint, writing
 //      grad_key / grad_value and accumulating dL/dw, dL/du.
 
-// Warps per backward CTA (the backward keeps y and gy/D of a tile in registers
-// across the round barrier, ~150 registers a thread; 4 CTAs of 2 warps fit an
-// SM, so B*C = 32768 runs in one wave).
+// Warps per backward CTA: a tile's records (e^{k-s}, gy/D, -gy y/D) stay in
+// registers across the round barrier (~235 registers a thread), so an SM runs
+// 4 CTAs of 2 warps and B*C = 32768 fits one wave; k, v and grad_y are read
+// from the staged boxes where they are used.
 template <typename T>
 constexpr int tp_bwd_warps() {
   return 2;
@@ -375,116 +376,142 @@ struct TpB {
   static constexpr uint32_t kBoxBytes = kBoxElems * sizeof(T);
   static constexpr uint32_t kCkBytes = W * 3 * kLanes * sizeof(float);  // W checkpoint rows
   static constexpr uint32_t kStageBytes = 3 * kBoxBytes + kCkBytes;     // k, v, gy, ckpt
+  // A stage's round r + NS - 1 copy is issued once every warp has passed round
+  // r's barrier (the stage was last read, and its staged outputs stored, in
+  // round r - 1). Three stages for 16-bit I/O (47 KB a CTA), two for float32.
   static constexpr int kStages = sizeof(T) == 4 ? 2 : 3;
   static constexpr int kSumFloats = 2 * W * 5 * kLanes;  // [2 rounds][W][G,gp,gq,hp,hq][lanes]
-  static constexpr uint32_t kOutTileBytes = kSub * kLanes * sizeof(T);  // one warp's gk (or gv) tile
-  static constexpr uint32_t kOutBytes = W * 2 * kOutTileBytes;          // [W][gk, gv] tiles
+  static_assert(kStages >= 2, "a stage is refilled one round after it was read");
   static_assert(kBoxBytes % 128 == 0 && kCkBytes % 128 == 0 && kStageBytes % 128 == 0 &&
                     (kSumFloats * 4) % 128 == 0 && (W * 2 * kLanes * 4) % 128 == 0 &&
-                    kOutTileBytes % 128 == 0,
+                    (kSub * kLanes * sizeof(T)) % 128 == 0,
                 "bulk-copy buffers start on 128-byte boundaries");
 };
 
-// Shared memory: stages | summaries | per-warp partial sums | output tiles | barriers.
+// Shared memory: stages | summaries | per-warp partial sums | barriers. A
+// warp's grad_key / grad_value tiles are staged over its own rows of the
+// round's k and grad_y boxes, which phase A was the last to read.
 template <typename T, int W>
 constexpr size_t bwd_tp_smem_bytes() {
   using G = TpB<T, W>;
   return (size_t)G::kStages * G::kStageBytes + G::kSumFloats * sizeof(float) +
-         W * 2 * kLanes * sizeof(float) + G::kOutBytes + 8 * G::kStages;
-}
-
-// Packed max |grad_y| over rows [0, n) of a register tile.
-template <typename T, bool kTail>
-__device__ __forceinline__ f2 tile_absmax(const typename Pair<T>::raw (&gr)[kSub], int n) {
-  using Sc = Scan<T>;
-  using raw = typename Pair<T>::raw;
-  raw g[kSub / 2];
-#pragma unroll
-  for (int i = 0; i < kSub / 2; ++i) {
-    const bool i0 = !kTail || i < n, i1 = !kTail || i + kSub / 2 < n;
-    g[i] = Sc::vmax(Sc::vabs(i0 ? gr[i] : scan_lo<T>()), Sc::vabs(i1 ? gr[i + kSub / 2] : scan_lo<T>()));
-  }
-#pragma unroll
-  for (int w = kSub / 4; w > 0; w /= 2) {
-#pragma unroll
-    for (int i = 0; i < w; ++i) g[i] = Sc::vmax(g[i], g[i + w]);
-  }
-  return Pair<T>::unpack(g[0]);
+         W * 2 * kLanes * sizeof(float) + 8 * G::kStages;
 }
 
 // Forward recompute of a tile from its start state rescaled to the tile scale
-// s: ry = y_t, rg = gy_t 2^s / D_t, re = e^{k_t - s} (kept for the reverse pass).
+// s, keeping for the reverse pass re = e^{k_t - s}, rg = gy_t 2^s / D_t and
+// rn = -rg_t y_t (the two adjoint increments of step t: dL/dP_t and dL/dQ_t
+// take rg_t and rn_t, and the output formulas need y_t only through rn_t).
 template <typename T, bool kTail>
-__device__ __forceinline__ void bwd_tp_recompute(const typename Pair<T>::raw (&kr)[kSub],
-                                                 const typename Pair<T>::raw (&vr)[kSub],
-                                                 const typename Pair<T>::raw (&gr)[kSub], int n,
+__device__ __forceinline__ void bwd_tp_recompute(const T* ks, const T* vs, const T* gys, int n,
                                                  const Lane2& lc, f2 s, f2 p, f2 q,
-                                                 f2 (&ry)[kSub], f2 (&rg)[kSub], f2 (&re)[kSub]) {
+                                                 f2 (&re)[kSub], f2 (&rg)[kSub], f2 (&rn)[kSub]) {
   using P = Pair<T>;
   const f2 l2e = splat(kL2E), ns = f2{-s.x, -s.y};
 #pragma unroll
   for (int i = 0; i < kSub; ++i) {
     if (kTail && i >= n) {
-      ry[i] = splat(0.f);
-      rg[i] = splat(0.f);
       re[i] = splat(0.f);
+      rg[i] = splat(0.f);
+      rn[i] = splat(0.f);
       continue;
     }
-    const f2 v = P::unpack(vr[i]);
-    const f2 ek = ex2x2(fma2(P::unpack(kr[i]), l2e, ns));
+    const f2 v = P::unpack(P::ld(vs + i * kLanes));
+    const f2 ek = ex2x2(fma2(P::unpack(P::ld(ks + i * kLanes)), l2e, ns));
     re[i] = ek;
     const f2 ekv = mul2(ek, v);
     const f2 rd = rcpx2(fma2(ek, lc.eu, q));  // 1 / D
-    ry[i] = mul2(fma2(lc.eu, ekv, p), rd);
-    rg[i] = mul2(P::unpack(gr[i]), rd);
+    const f2 y = mul2(fma2(lc.eu, ekv, p), rd);
+    const f2 g = mul2(P::unpack(P::ld(gys + i * kLanes)), rd);
+    rg[i] = g;
+    rn[i] = f2{-(g.x * y.x), -(g.y * y.y)};
     p = fma2(lc.ew, p, ekv);
     q = fma2(lc.ew, q, ek);
   }
 }
 
 // The tile's adjoint summary: the reverse recurrence over its rows from a zero
-// adjoint at the tile end (scaled by 2^s, like rg).
+// adjoint at the tile end (scaled by 2^s, like rg). The w-derivatives are
+// carried as K with H = e^w K (K_t = G_{t+1} + H_{t+1}, so K_t = G_{t+1} +
+// e^w K_{t+1}: one multiply-add per step instead of an add and a multiply).
 template <bool kTail>
-__device__ __forceinline__ void bwd_tp_summary(const f2 (&ry)[kSub], const f2 (&rg)[kSub], int n,
+__device__ __forceinline__ void bwd_tp_summary(const f2 (&rg)[kSub], const f2 (&rn)[kSub], int n,
                                                const Lane2& lc, f2& gp, f2& gq, f2& hp, f2& hq) {
-  gp = gq = hp = hq = splat(0.f);
+  f2 kp = splat(0.f), kq = splat(0.f);
+  gp = gq = splat(0.f);
 #pragma unroll
   for (int i = kSub - 1; i >= 0; --i) {
     if (kTail && i >= n) continue;
-    hp = mul2(lc.ew, add2(gp, hp));
-    hq = mul2(lc.ew, add2(gq, hq));
-    gq = sub2(mul2(lc.ew, gq), mul2(rg[i], ry[i]));
+    kp = fma2(lc.ew, kp, gp);
+    kq = fma2(lc.ew, kq, gq);
+    gq = fma2(lc.ew, gq, rn[i]);
     gp = fma2(lc.ew, gp, rg[i]);
   }
+  hp = mul2(lc.ew, kp);
+  hq = mul2(lc.ew, kq);
 }
 
 // Reverse pass of a tile from the adjoint at its end (scaled by 2^s): grad_key /
 // grad_value of its rows (kOut) and dL/dw, dL/du accumulated into gw, gu.
+// Per step, with X = dL/dP_{t+1} + e^u rg_t and Y = dL/dQ_{t+1} + e^u rn_t:
+//   grad_value = e^k X,  grad_key = grad_value v + e^k Y,
+//   dL/du += e^u e^k (rg v + rn),  dL/dw += e^k (v H^P_{t+1} + H^Q_{t+1}).
+// Full tiles take the top row with the incoming H and the rest with K
+// (H = e^w K, see bwd_tp_summary), the factors e^u and e^w applied once per
+// tile; partial tiles carry H itself.
 template <typename T, bool kTail, bool kOut>
-__device__ __forceinline__ void bwd_tp_outputs(const f2 (&re)[kSub],
-                                               const typename Pair<T>::raw (&vr)[kSub],
-                                               const f2 (&ry)[kSub], const f2 (&rg)[kSub], int n,
-                                               const Lane2& lc, f2 s, f2 gp, f2 gq, f2 hp, f2 hq,
+__device__ __forceinline__ void bwd_tp_outputs(const f2 (&re)[kSub], const T* vs,
+                                               const f2 (&rg)[kSub], const f2 (&rn)[kSub], int n,
+                                               const Lane2& lc, f2 gp, f2 gq, f2 hp, f2 hq,
                                                T* gks, T* gvs, f2& gw, f2& gu) {
   using P = Pair<T>;
-#pragma unroll
-  for (int i = kSub - 1; i >= 0; --i) {
-    if (kTail && i >= n) continue;
-    const f2 v = P::unpack(vr[i]);
-    const f2 ek = re[i];
-    const f2 a = mul2(mul2(rg[i], ek), lc.eu);  // gy e^{u+k} / D
-    const f2 av = mul2(a, sub2(v, ry[i]));
-    gu = add2(gu, av);
-    gw = fma2(ek, fma2(v, hp, hq), gw);
+  f2 tu = splat(0.f);
+  auto row = [&](int i, f2 v, f2 ek) {
+    const f2 gv = mul2(ek, fma2(lc.eu, rg[i], gp));
+    const f2 gk = fma2(gv, v, mul2(ek, fma2(lc.eu, rn[i], gq)));
+    tu = fma2(ek, fma2(rg[i], v, rn[i]), tu);
     if (kOut) {  // staged [kSub][kLanes] tiles
-      P::st(gvs + i * kLanes, P::pack(fma2(ek, gp, a)));
-      P::st(gks + i * kLanes, P::pack(fma2(ek, fma2(gp, v, gq), av)));
+      P::st(gvs + i * kLanes, P::pack(gv));
+      P::st(gks + i * kLanes, P::pack(gk));
     }
-    hp = mul2(lc.ew, add2(gp, hp));
-    hq = mul2(lc.ew, add2(gq, hq));
-    gq = sub2(mul2(lc.ew, gq), mul2(rg[i], ry[i]));
-    gp = fma2(lc.ew, gp, rg[i]);
+  };
+  if (kTail) {
+#pragma unroll
+    for (int i = kSub - 1; i >= 0; --i) {
+      if (i >= n) continue;
+      const f2 v = P::unpack(P::ld(vs + i * kLanes)), ek = re[i];
+      row(i, v, ek);
+      gw = fma2(ek, fma2(v, hp, hq), gw);
+      hp = mul2(lc.ew, add2(gp, hp));
+      hq = mul2(lc.ew, add2(gq, hq));
+      gq = fma2(lc.ew, gq, rn[i]);
+      gp = fma2(lc.ew, gp, rg[i]);
+    }
+  } else {
+    constexpr int top = kSub - 1;
+    f2 kp, kq, tw = splat(0.f);
+    {
+      const f2 v = P::unpack(P::ld(vs + top * kLanes)), ek = re[top];
+      row(top, v, ek);
+      gw = fma2(ek, fma2(v, hp, hq), gw);
+      kp = add2(gp, hp);
+      kq = add2(gq, hq);
+      gq = fma2(lc.ew, gq, rn[top]);
+      gp = fma2(lc.ew, gp, rg[top]);
+    }
+#pragma unroll
+    for (int i = top - 1; i >= 0; --i) {
+      const f2 v = P::unpack(P::ld(vs + i * kLanes)), ek = re[i];
+      row(i, v, ek);
+      tw = fma2(ek, fma2(v, kp, kq), tw);
+      kp = fma2(lc.ew, kp, gp);
+      kq = fma2(lc.ew, kq, gq);
+      gq = fma2(lc.ew, gq, rn[i]);
+      gp = fma2(lc.ew, gp, rg[i]);
+    }
+    gw = fma2(lc.ew, tw, gw);
   }
+  gu = fma2(lc.eu, tu, gu);
 }
 
 // adj_combine1 for both lanes of the pair with packed arithmetic (the same
@@ -563,10 +590,27 @@ __device__ __noinline__ void bwd_tp_exact(const BwdArgs& a, int b, int t0, int c
   }
 }
 
+// Adjoints (G, gp, gq, hp, hq) of the kLanes channels as [5][kLanes] floats.
+__device__ __forceinline__ Adj2 adj_ld(const float* slot, int lane) {
+  const f2* q = reinterpret_cast<const f2*>(slot) + lane;
+  return Adj2{q[0], q[kLanes / 2], q[kLanes], q[3 * kLanes / 2], q[2 * kLanes]};
+}
+__device__ __forceinline__ void adj_st(float* slot, int lane, const Adj2& x) {
+  f2* q = reinterpret_cast<f2*>(slot) + lane;
+  q[0] = x.G;
+  q[kLanes / 2] = x.gp;
+  q[kLanes] = x.gq;
+  q[3 * kLanes / 2] = x.hp;
+  q[2 * kLanes] = x.hq;
+}
+
 // Backward. kOut: grad_key/grad_value, per-lane partial sums and (last CTA per
 // column block) the time gradients; !kOut: only the adjoint at the segment
 // start (a.adj_out), for the segmented plan. Grid (B * ncblk, nseg), W warps
 // per CTA; reference wkv_triton.py:60-142.
+//
+// Shared memory: NS stages | summaries [2][W][5][kLanes] | per-warp partial
+// sums [W][2][kLanes] | barriers.
 template <typename T, int W, bool kOut>
 __global__ void __launch_bounds__(32 * W, 4)
     wkv_bwd_tp_kernel(const BwdArgs a, const __grid_constant__ CUtensorMap tk,
@@ -574,23 +618,27 @@ __global__ void __launch_bounds__(32 * W, 4)
                       const __grid_constant__ CUtensorMap tck, const __grid_constant__ CUtensorMap tgk,
                       const __grid_constant__ CUtensorMap tgv) {
   using G = TpB<T, W>;
-  using P = Pair<T>;
-  using raw = typename P::raw;
   constexpr int NS = G::kStages;
   constexpr int R = kSub;
   extern __shared__ __align__(128) unsigned char smem[];
   float* sum = reinterpret_cast<float*>(smem + NS * G::kStageBytes);
   float* red = sum + G::kSumFloats;  // [W][2][kLanes]
-  T* gks = reinterpret_cast<T*>(red + W * 2 * kLanes) + (threadIdx.x >> 5) * 2 * kSub * kLanes;
-  T* gvs = gks + kSub * kLanes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(red + W * 2 * kLanes) +
-                                               G::kOutBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(red + W * 2 * kLanes);
+  auto slot = [&](int parity, int m) { return sum + (parity * W + m) * 5 * kLanes; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cb = blockIdx.x % a.ncblk, b = blockIdx.x / a.ncblk;
   const int c = cb * kLanes + 2 * lane;
   const int seg = blockIdx.y + a.seg_base;
   const bool v0 = c < a.C, v1 = c + 1 < a.C;
+  const int t_begin = seg * a.seg_len;
+  const int t_end = min(a.T, t_begin + a.seg_len);
+  const int ntiles = (t_end - t_begin + R - 1) / R;
+  const int nrounds = (ntiles + W - 1) / W;
+  const bool force_slow = a.force_slow != 0;
+  const size_t lseg = (size_t)b * a.nseg + seg;
+  const bool seg_local = a.seg_start != nullptr || a.seg_sums != nullptr;  // checkpoints from the segment start
+
   f2 ww = splat(0.f), uu = splat(0.f);
   if (v0) {
     ww.x = a.w[c];
@@ -601,13 +649,6 @@ __global__ void __launch_bounds__(32 * W, 4)
     uu.y = a.u[c + 1];
   }
   const Lane2 lc = make_lane2(ww, uu);
-  const int t_begin = seg * a.seg_len;
-  const int t_end = min(a.T, t_begin + a.seg_len);
-  const int ntiles = (t_end - t_begin + R - 1) / R;
-  const int nrounds = (ntiles + W - 1) / W;
-  const bool force_slow = a.force_slow != 0;
-  const size_t lseg = (size_t)b * a.nseg + seg;
-
   Adj2 adj = adj_zero2();  // adjoint entering the current round (at its last tile's end)
   if (a.adj_in != nullptr)
     load_adj(a.adj_in, lseg, a.C, c, v0, v1, adj);
@@ -618,7 +659,6 @@ __global__ void __launch_bounds__(32 * W, 4)
     load3(a.seg_start, lseg, a.C, c, v0, v1, segst.S, segst.p, segst.q);
   else if (a.seg_sums != nullptr && seg > 0)
     segst = fold_state_summaries(a.seg_sums, b, a.nseg, seg, a.seg_len, a.C, c, v0, v1, lc);
-  const bool seg_local = a.seg_start != nullptr || a.seg_sums != nullptr;  // checkpoints from the segment start
   f2 gwacc = splat(0.f), gu = splat(0.f);
 
   auto issue = [&](bool on, int r) {  // by the threads with `on` (one per CTA)
@@ -646,31 +686,26 @@ __global__ void __launch_bounds__(32 * W, 4)
     }
   }
   __syncthreads();
-  for (int r = 0; r < min(NS, nrounds); ++r) issue(threadIdx.x == 0, r);
+  for (int r = 0; r < min(NS - 1, nrounds); ++r) issue(threadIdx.x == 0, r);
 
 #pragma unroll 1
   for (int r = 0; r < nrounds; ++r) {
     const int st = r % NS;
-    const unsigned char* base = smem + st * G::kStageBytes;
+    unsigned char* base = smem + st * G::kStageBytes;
     const int jb = ntiles - (r + 1) * W;
     const int j = jb + warp;
     const int t0 = t_begin + j * R;
     const int n = j < 0 ? 0 : min(R, t_end - t0);
     const bool arrived = mbar_wait_bounded(&bars[st], (r / NS) & 1);
 
-    // A. recompute and local adjoint summary
-    raw kr[R], vr[R], gr[R];
-    {
-      const T* kt = reinterpret_cast<const T*>(base) + warp * R * kLanes + 2 * lane;
-      const T* vt = reinterpret_cast<const T*>(base + G::kBoxBytes) + warp * R * kLanes + 2 * lane;
-      const T* gt = reinterpret_cast<const T*>(base + 2 * G::kBoxBytes) + warp * R * kLanes + 2 * lane;
-#pragma unroll
-      for (int i = 0; i < R; ++i) {
-        kr[i] = P::ld(kt + i * kLanes);
-        vr[i] = P::ld(vt + i * kLanes);
-        gr[i] = P::ld(gt + i * kLanes);
-      }
-    }
+    // A. recompute and local adjoint summary, reading this warp's rows of the
+    // staged boxes; grad_key / grad_value are later staged over its k and
+    // grad_y rows
+    T* ktw = reinterpret_cast<T*>(base) + warp * R * kLanes;
+    T* gtw = reinterpret_cast<T*>(base + 2 * G::kBoxBytes) + warp * R * kLanes;
+    const T* kt = ktw + 2 * lane;
+    const T* vt = reinterpret_cast<const T*>(base + G::kBoxBytes) + warp * R * kLanes + 2 * lane;
+    const T* gt = gtw + 2 * lane;
     Fwd2 st0;  // forward state at the tile start
     {
       const f2* ck = reinterpret_cast<const f2*>(base + 3 * G::kBoxBytes) + warp * 3 * (kLanes / 2) + lane;
@@ -678,84 +713,68 @@ __global__ void __launch_bounds__(32 * W, 4)
     }
     if (seg_local && n > 0)
       st0 = (t0 == t_begin) ? segst : fwd_combine2(segst, t0 - t_begin, lc, st0);
-    f2 kmax, kmin, gymax, s, p, q;
-    if (n == R) {
-      tile_kminmax<T, false>(kr, n, kmax, kmin);
-      gymax = tile_absmax<T, false>(gr, n);
-    } else {
-      tile_kminmax<T, true>(kr, n, kmax, kmin);
-      gymax = tile_absmax<T, true>(gr, n);
-    }
-    bool ok = n == 0 || (fast_ok1(st0.S.x, st0.p.x, st0.q.x, kmax.x, kmin.x, n, lc.w2.x, lc.u2.x,
-                                  s.x, p.x, q.x) &&
-                         fast_ok1(st0.S.y, st0.p.y, st0.q.y, kmax.y, kmin.y, n, lc.w2.y, lc.u2.y,
-                                  s.y, p.y, q.y) &&
-                         fmaxf(gymax.x, gymax.y) <= 0x1p40f && !force_slow);
+    const Pre pre = n == R ? prescan<T, false, true>(kt, gt, n) : prescan<T, true, true>(kt, gt, n);
+    f2 s, p, q;
+    bool ok = n == 0 || (fast_ok1(st0.S.x, st0.p.x, st0.q.x, pre.kmax.x, pre.kmin.x, n, lc.w2.x,
+                                  lc.u2.x, s.x, p.x, q.x) &&
+                         fast_ok1(st0.S.y, st0.p.y, st0.q.y, pre.kmax.y, pre.kmin.y, n, lc.w2.y,
+                                  lc.u2.y, s.y, p.y, q.y) &&
+                         fmaxf(pre.gymax.x, pre.gymax.y) <= 0x1p40f && !force_slow);
     if (n == 0) s = p = q = splat(0.f);
-    f2 ry[R], rg[R], re[R];
+    f2 re[R], rg[R], rn[R];
     Adj2 loc;
     if (n == R) {
-      bwd_tp_recompute<T, false>(kr, vr, gr, n, lc, s, p, q, ry, rg, re);
-      bwd_tp_summary<false>(ry, rg, n, lc, loc.gp, loc.gq, loc.hp, loc.hq);
+      bwd_tp_recompute<T, false>(kt, vt, gt, n, lc, s, p, q, re, rg, rn);
+      bwd_tp_summary<false>(rg, rn, n, lc, loc.gp, loc.gq, loc.hp, loc.hq);
     } else {
-      bwd_tp_recompute<T, true>(kr, vr, gr, n, lc, s, p, q, ry, rg, re);
-      bwd_tp_summary<true>(ry, rg, n, lc, loc.gp, loc.gq, loc.hp, loc.hq);
+      bwd_tp_recompute<T, true>(kt, vt, gt, n, lc, s, p, q, re, rg, rn);
+      bwd_tp_summary<true>(rg, rn, n, lc, loc.gp, loc.gq, loc.hp, loc.hq);
     }
     loc.G = f2{-s.x, -s.y};
     const bool fast = __all_sync(kFull, ok);
-    if (!fast && n > 0)
-      loc = bwd_tp_exact_summary<T>(
-          reinterpret_cast<const T*>(base) + warp * R * kLanes + 2 * lane,
-          reinterpret_cast<const T*>(base + G::kBoxBytes) + warp * R * kLanes + 2 * lane,
-          reinterpret_cast<const T*>(base + 2 * G::kBoxBytes) + warp * R * kLanes + 2 * lane, n, st0,
-          lc);
-    {
-      f2* sw = reinterpret_cast<f2*>(sum + ((r & 1) * W + warp) * 5 * kLanes) + lane;
-      sw[0] = loc.G;
-      sw[kLanes / 2] = loc.gp;
-      sw[kLanes] = loc.gq;
-      sw[3 * kLanes / 2] = loc.hp;
-      sw[2 * kLanes] = loc.hq;
-    }
+    if (!fast && n > 0) loc = bwd_tp_exact_summary<T>(kt, vt, gt, n, st0, lc);
+    // the previous round's staged outputs (lane 0's bulk group) have been read
+    // out of the stage the next copy refills
+    if (kOut) bulk_wait_read<0>();
+    adj_st(slot(r & 1, warp), lane, loc);
     if (!__syncthreads_and(arrived)) {
       if (threadIdx.x == 0) {
         report_timeout(a.err);
-        for (int q2 = r; q2 < min(r + NS, nrounds); ++q2)
+        for (int q2 = r; q2 < min(r + NS - 1, nrounds); ++q2)
           mbar_wait_bounded(&bars[q2 % NS], (q2 / NS) & 1);
       }
       if (kOut) bulk_wait_all();
       return;
     }
-    if (r + NS < nrounds) issue(threadIdx.x == 0, r + NS);
+    // every warp is past its last read of stage (r - 1) % NS
+    if (r + NS - 1 < nrounds) issue(threadIdx.x == 0, r + NS - 1);
 
-    // B. adjoint at this warp's tile end; adj becomes the adjoint at the round start
+    // B. the adjoint at this warp's tile end; adj becomes the adjoint entering
+    // the next round (every warp folds all of the round's summaries, in the
+    // same order)
     Adj2 ein = adj;
 #pragma unroll
     for (int m = W - 1; m >= 0; --m) {
       const int nm = (jb + m) < 0 ? 0 : min(R, t_end - (t_begin + (jb + m) * R));
       if (m == warp) ein = adj;
-      if (nm > 0) {
-        const f2* sm = reinterpret_cast<const f2*>(sum + ((r & 1) * W + m) * 5 * kLanes) + lane;
-        const Adj2 l{sm[0], sm[kLanes / 2], sm[kLanes], sm[3 * kLanes / 2], sm[2 * kLanes]};
-        adj = adj_combine2(l, adj, nm, lc);
-      }
+      if (nm > 0) adj = adj_combine2(adj_ld(slot(r & 1, m), lane), adj, nm, lc);
     }
 
-    // C. outputs from the incoming adjoint, staged in this warp's tiles and
-    // written with one bulk tensor store per tensor
+    // C. outputs from the incoming adjoint, staged over this warp's k and
+    // grad_y rows and written with one bulk tensor store per tensor
     if (kOut && n > 0) {
-      bulk_wait_read<0>();  // the previous tile's stores (lane 0's group) have read gks/gvs
-      __syncwarp();
+      T* gks = ktw;
+      T* gvs = gtw;
       const f2 f = ex2x2(add2(ein.G, s));  // integer exponents: exact
       const f2 gp = mul2(ein.gp, f), gq = mul2(ein.gq, f), hp = mul2(ein.hp, f), hq = mul2(ein.hq, f);
       const float amax = fmaxf(fmaxf(fmaxf(fabsf(gp.x), fabsf(gp.y)), fmaxf(fabsf(gq.x), fabsf(gq.y))),
                                fmaxf(fmaxf(fabsf(hp.x), fabsf(hp.y)), fmaxf(fabsf(hq.x), fabsf(hq.y))));
       if (fast && __all_sync(kFull, amax <= 0x1p80f)) {
         if (n == R)
-          bwd_tp_outputs<T, false, kOut>(re, vr, ry, rg, n, lc, s, gp, gq, hp, hq, gks + 2 * lane,
+          bwd_tp_outputs<T, false, kOut>(re, vt, rg, rn, n, lc, gp, gq, hp, hq, gks + 2 * lane,
                                          gvs + 2 * lane, gwacc, gu);
         else
-          bwd_tp_outputs<T, true, kOut>(re, vr, ry, rg, n, lc, s, gp, gq, hp, hq, gks + 2 * lane,
+          bwd_tp_outputs<T, true, kOut>(re, vt, rg, rn, n, lc, gp, gq, hp, hq, gks + 2 * lane,
                                         gvs + 2 * lane, gwacc, gu);
       } else {
         bwd_tp_exact<T>(a, b, t0, c, v0, v1, n, st0, ein, lc, gks + 2 * lane, gvs + 2 * lane,
