@@ -422,6 +422,20 @@ __device__ __forceinline__ Fwd2 fwd_combine2(const Fwd2& g, int delta, const Lan
   return l;
 }
 
+// fwd_combine2 over exactly kSub steps (the decay ew^kSub precomputed in lc):
+// branch-free, so a run of them schedules as one short chain of scales, ex2s
+// that do not wait on each other, and multiply-add chains. Same roundings.
+__device__ __forceinline__ Fwd2 fwd_combine16(const Fwd2& g, const Lane2& lc, Fwd2 l) {
+  const f2 ge = add2(g.S, lc.de16);
+  const f2 s = f2{fmaxf(ge.x, l.S.x), fmaxf(ge.y, l.S.y)};
+  const f2 a = mul2(lc.dm16, ex2x2(sub2(ge, s)));
+  const f2 b = ex2x2(sub2(l.S, s));
+  l.p = fma2(g.p, a, mul2(l.p, b));
+  l.q = fma2(g.q, a, mul2(l.q, b));
+  l.S = s;
+  return l;
+}
+
 // Adjoint at the start of a segment of `len` steps: its own contribution
 // `local` (accumulated from a zero adjoint) plus the adjoint at the segment end
 // decayed through the segment, e^{w len} dL/dP_end; the w-derivatives pick up

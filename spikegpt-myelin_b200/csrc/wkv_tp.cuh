@@ -39,8 +39,8 @@ struct Tp {
   // Two stages: a stage is read only in phase A, so the box of round r+2 is
   // requested a whole round before it is needed.
   static constexpr int kFwdStages = 2;
-  // [2 rounds][W tile summaries + the state after the round][S, p, q][lanes]
-  static constexpr int kSumFloats = 2 * (W + 1) * 3 * kLanes;
+  // [2 rounds][W tile summaries][S, p, q][lanes]
+  static constexpr int kSumFloats = 2 * W * 3 * kLanes;
   static constexpr uint32_t kYTileBytes = kSub * kLanes * sizeof(T);  // one warp's staged y tile
   static_assert(kSegAlign % kSub == 0, "segments start on tile boundaries");
   static_assert(kBoxBytes % 128 == 0 && (kSumFloats * 4) % 128 == 0 && kYTileBytes % 128 == 0,
@@ -231,14 +231,14 @@ __global__ void __launch_bounds__(32 * W, 4)
   __syncthreads();
   for (int r = 0; r < min(NS, nrounds); ++r) issue(threadIdx.x == 0, r);
 
-  Fwd2 cur = start;  // warp W-1: the state after the latest round
+  Fwd2 cur = start;  // the state at the start of the current round (every warp)
 #pragma unroll 1
   for (int r = 0; r < nrounds; ++r) {
     const int s = r % NS;
     const int rt0 = t_begin + r * G::kRoundRows;
     const int t0 = rt0 + warp * R;  // this warp's tile
     const int n = max(0, min(R, t_end - t0));
-    float* sr = sum + (r & 1) * (W + 1) * 3 * kLanes;  // this round's summaries
+    float* sr = sum + (r & 1) * W * 3 * kLanes;  // this round's summaries
     const bool arrived = mbar_wait_bounded(&bars[s], (r / NS) & 1, a.wait_limit);
 
     // A. summary of the tile from a zero state, scaled by 2^-sj, sj = ceil(max k log2 e)
@@ -277,30 +277,33 @@ __global__ void __launch_bounds__(32 * W, 4)
     }
     if (r + NS < nrounds) issue(threadIdx.x == 0, r + NS);
 
-    // B. carry-in of this warp's tile: the round's start state (left in shared
-    // memory by warp W-1 during the previous round) folded with the summaries
-    // of the earlier tiles of the round; warp W-1 also folds its own tile and
-    // leaves the result for the next round.
-    Fwd2 sin = start;
-    if (r > 0) {
-      const f2* ps = reinterpret_cast<const f2*>(sum + ((r - 1) & 1) * (W + 1) * 3 * kLanes +
-                                                 W * 3 * kLanes) + lane;
-      sin = Fwd2{ps[0], ps[kLanes / 2], ps[kLanes]};
-    }
+    // B. carry-in of this warp's tile: the round's start state folded with the
+    // summaries of the earlier tiles of the round. Every warp folds all W
+    // summaries (so every warp holds the next round's start state), and a
+    // round of full tiles takes the branch-free 16-step combine: the fold's
+    // latency is then one short chain, not W dependent combines.
+    Fwd2 sin = cur;
+    {
+      Fwd2 sm[W];
 #pragma unroll
-    for (int m = 0; m < W - 1; ++m) {
-      if (m < warp) {
-        const f2* sm = reinterpret_cast<const f2*>(sr + m * 3 * kLanes) + lane;
-        sin = fwd_combine2(sin, min(R, max(0, t_end - (rt0 + m * R))), lc,
-                           Fwd2{sm[0], sm[kLanes / 2], sm[kLanes]});
+      for (int m = 0; m < W; ++m) {
+        const f2* q = reinterpret_cast<const f2*>(sr + m * 3 * kLanes) + lane;
+        sm[m] = Fwd2{q[0], q[kLanes / 2], q[kLanes]};
       }
-    }
-    if (warp == W - 1) {
-      cur = fwd_combine2(sin, n, lc, Fwd2{sj, lp, lq});
-      f2* pw = reinterpret_cast<f2*>(sr + W * 3 * kLanes) + lane;
-      pw[0] = cur.S;
-      pw[kLanes / 2] = cur.p;
-      pw[kLanes] = cur.q;
+      if (rt0 + W * R <= t_end) {
+#pragma unroll
+        for (int m = 0; m < W; ++m) {
+          cur = fwd_combine16(cur, lc, sm[m]);
+          if (m + 1 == warp) sin = cur;
+        }
+      } else {
+#pragma unroll
+        for (int m = 0; m < W; ++m) {
+          const int nm = min(R, max(0, t_end - (rt0 + m * R)));
+          if (nm > 0) cur = fwd_combine2(cur, nm, lc, sm[m]);
+          if (m + 1 == warp) sin = cur;
+        }
+      }
     }
 
     // C. outputs of the tile from its carry-in
@@ -533,6 +536,22 @@ __device__ __forceinline__ Adj2 adj_combine2(const Adj2& l, Adj2 e, int len, con
   return e;
 }
 
+// adj_combine2 over exactly kSub steps: branch-free (see fwd_combine16).
+__device__ __forceinline__ Adj2 adj_combine16(const Adj2& l, Adj2 e, const Lane2& lc) {
+  const f2 fl = splat(static_cast<float>(kSub));
+  const f2 ge = add2(e.G, lc.de16);
+  const f2 g = f2{fmaxf(ge.x, l.G.x), fmaxf(ge.y, l.G.y)};
+  const f2 a = mul2(lc.dm16, ex2x2(sub2(ge, g)));
+  const f2 b = ex2x2(sub2(l.G, g));
+  const f2 hp = fma2(fl, e.gp, e.hp), hq = fma2(fl, e.gq, e.hq);
+  e.gp = fma2(e.gp, a, mul2(l.gp, b));
+  e.gq = fma2(e.gq, a, mul2(l.gq, b));
+  e.hp = fma2(hp, a, mul2(l.hp, b));
+  e.hq = fma2(hq, a, mul2(l.hq, b));
+  e.G = g;
+  return e;
+}
+
 __device__ __forceinline__ Adj2 fold_adjoint_summaries(const float* sums, int b, int nseg, int seg,
                                                        int seg_len, int T, int C, int c, bool v0,
                                                        bool v1, const Lane2& lc) {
@@ -751,13 +770,26 @@ __global__ void __launch_bounds__(32 * W, 4)
 
     // B. the adjoint at this warp's tile end; adj becomes the adjoint entering
     // the next round (every warp folds all of the round's summaries, in the
-    // same order)
+    // same order; a round of full tiles takes the branch-free 16-step combine)
     Adj2 ein = adj;
+    {
+      Adj2 sm[W];
 #pragma unroll
-    for (int m = W - 1; m >= 0; --m) {
-      const int nm = (jb + m) < 0 ? 0 : min(R, t_end - (t_begin + (jb + m) * R));
-      if (m == warp) ein = adj;
-      if (nm > 0) adj = adj_combine2(adj_ld(slot(r & 1, m), lane), adj, nm, lc);
+      for (int m = 0; m < W; ++m) sm[m] = adj_ld(slot(r & 1, m), lane);
+      if (jb >= 0 && t_begin + (jb + W) * R <= t_end) {
+#pragma unroll
+        for (int m = W - 1; m >= 0; --m) {
+          if (m == warp) ein = adj;
+          adj = adj_combine16(sm[m], adj, lc);
+        }
+      } else {
+#pragma unroll
+        for (int m = W - 1; m >= 0; --m) {
+          const int nm = (jb + m) < 0 ? 0 : min(R, t_end - (t_begin + (jb + m) * R));
+          if (m == warp) ein = adj;
+          if (nm > 0) adj = adj_combine2(sm[m], adj, nm, lc);
+        }
+      }
     }
 
     // C. outputs from the incoming adjoint, staged over this warp's k and
