@@ -20,6 +20,7 @@ building it on the CPU is fine.
 
 from __future__ import annotations
 
+import contextlib
 import os
 
 import math
@@ -97,6 +98,83 @@ def _mix_profile(n_embd: int, power: float, offset: float = 0.0) -> Tensor:
 
 # The time-mixing key, value and receptance projections as one batched GEMM
 # (SPIKEGPT_BATCHED_KVR=0: three GEMMs).
+# ------------------------------------------------------------- weight cache
+#
+# Under bf16 autocast every projection casts its float32 weight to bf16 in the
+# forward and widens its bf16 weight gradient back to float32 in the backward:
+# two small kernels per weight and step, about 200 in SpikeGPT-41M, which at a
+# few sequences per GPU cost as much as the LIF recurrences. A train step can
+# instead cast all matmul weights with one kernel and hand the projections
+# their bf16 copies: inside ``weight_cache(entries)`` a projection whose weight
+# has an entry (bf16 copy, bf16 gradient buffer) multiplies by the copy, and its
+# backward writes the bf16 weight gradient into the buffer instead of handing
+# the parameter a gradient through autograd; the caller widens the buffers
+# into the float32 gradients with one kernel. The values are autocast's: the
+# copy is the round-to-nearest cast, and the weight gradient is the same bf16
+# product, widened exactly. The key, value and receptance weights of a time
+# mixing have one more entry under the tuple of their ids: the [3, C, C] copy
+# and gradient buffer of the three, for the batched projection.
+
+_CACHE: dict = {}
+
+
+@contextlib.contextmanager
+def weight_cache(entries: dict):
+    """Projections read their weights' bf16 copies from ``entries`` (id of the
+    parameter -> (bf16 copy, bf16 gradient buffer)) inside the block."""
+    _CACHE.update(entries)
+    try:
+        yield
+    finally:
+        _CACHE.clear()
+
+
+class _CachedLinear(torch.autograd.Function):
+    """``x @ wb.T`` with a cached bf16 weight; the backward returns grad x and
+    writes grad W = gy^T x into the weight's bf16 gradient buffer."""
+
+    @staticmethod
+    def forward(ctx, x: Tensor, wb: Tensor, gb: Tensor) -> Tensor:
+        x = x.to(wb.dtype)
+        ctx.save_for_backward(x)
+        ctx.wb, ctx.gb = wb, gb
+        return F.linear(x, wb)
+
+    @staticmethod
+    def backward(ctx, gy: Tensor):
+        (x,) = ctx.saved_tensors
+        gy = gy.to(ctx.wb.dtype)
+        torch.mm(gy.reshape(-1, gy.shape[-1]).t(), x.reshape(-1, x.shape[-1]), out=ctx.gb)
+        return gy.matmul(ctx.wb), None, None
+
+
+class _CachedStacked(torch.autograd.Function):
+    """``x3 @ w3b^T`` per slice for a [3, M, C] input and cached [3, N, C] bf16
+    weights; the backward writes the three weight gradients into their buffer."""
+
+    @staticmethod
+    def forward(ctx, x3: Tensor, w3b: Tensor, g3b: Tensor) -> Tensor:
+        x3 = x3.to(w3b.dtype)
+        ctx.save_for_backward(x3)
+        ctx.w3b, ctx.g3b = w3b, g3b
+        return torch.matmul(x3, w3b.transpose(1, 2))
+
+    @staticmethod
+    def backward(ctx, gy3: Tensor):
+        (x3,) = ctx.saved_tensors
+        gy3 = gy3.to(ctx.w3b.dtype)
+        torch.bmm(gy3.transpose(1, 2), x3, out=ctx.g3b)
+        return torch.matmul(gy3, ctx.w3b), None, None
+
+
+def _linear(x: Tensor, weight: Tensor) -> Tensor:
+    """``F.linear(x, weight)``, on the weight's cached bf16 copy when it has one."""
+    c = _CACHE.get(id(weight)) if _CACHE else None
+    if c is None:
+        return F.linear(x, weight)
+    return _CachedLinear.apply(x, c[0], c[1])
+
+
 _BATCHED_KVR = os.environ.get("SPIKEGPT_BATCHED_KVR", "1") != "0"
 
 
@@ -125,15 +203,20 @@ class TimeMix(nn.Module):
 
     def from_mixed(self, xk: Tensor, xv: Tensor, xr: Tensor) -> Tensor:
         """The sublayer from its three token-shift-mixed inputs."""
-        return self._from_projections(self.key(xk), self.value(xv), self.receptance(xr))
+        return self._from_projections(_linear(xk, self.key.weight), _linear(xv, self.value.weight),
+                                      _linear(xr, self.receptance.weight))
 
     def from_stacked(self, x3: Tensor) -> Tensor:
         """The sublayer from its three mixed inputs stacked as [3, B, T, C]: the
         key, value and receptance projections (same shape) as one batched GEMM,
         three times the tiles of each alone (the small-batch case fills the GPU)."""
         n, b, t, c = x3.shape
-        w3 = torch.stack([self.key.weight, self.value.weight, self.receptance.weight])
-        kvr = torch.matmul(x3.reshape(n, b * t, c), w3.transpose(1, 2)).reshape(n, b, t, c)
+        cached = _CACHE.get((id(self.key.weight), id(self.value.weight), id(self.receptance.weight))) if _CACHE else None
+        if cached is not None:
+            kvr = _CachedStacked.apply(x3.reshape(n, b * t, c), cached[0], cached[1]).reshape(n, b, t, c)
+        else:
+            w3 = torch.stack([self.key.weight, self.value.weight, self.receptance.weight])
+            kvr = torch.matmul(x3.reshape(n, b * t, c), w3.transpose(1, 2)).reshape(n, b, t, c)
         k, v, rl = kvr.unbind(0)
         return self._from_projections(k, v, rl)
 
@@ -143,8 +226,8 @@ class TimeMix(nn.Module):
         else:
             wkv = weighted_key_value_cuda(k, v, self.time_decay, self.time_first)
         if fused.gates_supported(rl, wkv):  # bf16 autocast: one kernel each way
-            return self.output(fused.gate(rl, wkv))
-        return self.output(torch.sigmoid(rl) * wkv)
+            return _linear(fused.gate(rl, wkv), self.output.weight)
+        return _linear(torch.sigmoid(rl) * wkv, self.output.weight)
 
 
 class ChannelMix(nn.Module):
@@ -168,15 +251,15 @@ class ChannelMix(nn.Module):
         computed in float32 and cast back for the value projection, which
         rounds the same exact square to bf16 once either way. With bf16
         projections the activation and the gate are the fused kernels."""
-        k = self.key(xk)
+        k = _linear(xk, self.key.weight)
         if fused.gates_supported(k):  # bf16 autocast: one kernel each way
-            v = self.value(fused.relu_square(k))
-            return fused.gate(self.receptance(xr), v)
+            v = _linear(fused.relu_square(k), self.value.weight)
+            return fused.gate(_linear(xr, self.receptance.weight), v)
         k = torch.relu(k)
         with torch.autocast("cuda", enabled=False):
             k = torch.square(k)
-        r = torch.sigmoid(self.receptance(xr))
-        return r * self.value(k)
+        r = torch.sigmoid(_linear(xr, self.receptance.weight))
+        return r * _linear(k, self.value.weight)
 
 
 class Block(nn.Module):
@@ -257,6 +340,14 @@ class SpikeGPT(nn.Module):
             elif isinstance(m, nn.Linear):
                 nn.init.normal_(m.weight, mean=0.0, std=0.01)
 
+    def matmul_weights(self) -> tuple[list[list[nn.Parameter]], nn.Parameter]:
+        """The weights of the matrix products: per block, in this order, the
+        time mixing's key, value, receptance (the batched projection), output,
+        and the channel mixing's key, receptance, value; then the head."""
+        groups = [[b.att.key.weight, b.att.value.weight, b.att.receptance.weight, b.att.output.weight,
+                   b.ffn.key.weight, b.ffn.receptance.weight, b.ffn.value.weight] for b in self.blocks]
+        return groups, self.head.weight
+
     def forward(self, input_ids: Tensor, targets: Tensor | None = None) -> Tensor:
         if input_ids.ndim != 2:
             raise ValueError(f"input_ids must have shape [B, T]; got {tuple(input_ids.shape)}")
@@ -285,10 +376,18 @@ def _head(h: Tensor, weight: Tensor, multiple: int = 64) -> tuple[Tensor, int]:
     216M-class step). The padded columns are never read as classes, so values
     and gradients are those of the plain projection."""
     v = weight.shape[0]
+    c = _CACHE.get(id(weight)) if _CACHE else None
+    if c is not None:  # the cached copy is stored padded (zero rows past V)
+        return _CachedLinear.apply(h, c[0], c[1]), v
     pad = (-v) % multiple
     if pad == 0 or not h.is_cuda:
         return F.linear(h, weight), v
     return F.linear(h, F.pad(weight, (0, 0, 0, pad))), v
+
+
+def head_rows(v: int, multiple: int = 64) -> int:
+    """Rows of the head weight as ``_head`` multiplies by it on CUDA."""
+    return v + (-v) % multiple
 
 
 def parameter_count(model: nn.Module) -> int:

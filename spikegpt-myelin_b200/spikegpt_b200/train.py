@@ -30,9 +30,21 @@ sequences per GPU: 21.07 against 20.64 ms per step; 8 per GPU: 8.57 against
 
 ``graph=False`` runs the same step eagerly (any device, any process group:
 the CPU tests use it over gloo).
+
+Weight cache (bf16 autocast on CUDA, a model with ``matmul_weights()``, no
+bucketed overlap): the matmul weights live in one flat float32 buffer (the
+parameters become views of it); each step casts it to a flat bf16 copy with
+one kernel, the projections multiply by the copies (``model.weight_cache``)
+and write their bf16 weight gradients into a flat bf16 buffer, which one more
+kernel widens into the flat float32 gradient buffer: [matmul weights | head |
+the other parameters in backward order], of which every parameter's ``.grad``
+is a view. This replaces autocast's per-weight casts (about 200 kernels a step
+in SpikeGPT-41M) with four, and computes the same values.
 """
 
 from __future__ import annotations
+
+import contextlib
 
 import torch
 import torch.distributed as dist
@@ -53,7 +65,7 @@ class TrainStep:
     def __init__(self, model: nn.Module, optimizer: torch.optim.Optimizer, batch_shape: tuple[int, int], *,
                  device: torch.device | str, autocast_dtype: torch.dtype | None = torch.bfloat16,
                  graph: bool = True, group=None, warmup: int = 3, overlap: bool = False,
-                 bucket_mb: float = 25.0) -> None:
+                 bucket_mb: float = 25.0, weight_cache: bool = True) -> None:
         self.model = model
         self.optimizer = optimizer
         self.device = torch.device(device)
@@ -72,7 +84,12 @@ class TrainStep:
         self.grad_views = None
         self.overlap = overlap and self.world > 1
         self.buckets: list[tuple[list[nn.Parameter], Tensor]] = []
-        if self.world > 1:
+        self.cache = None  # weight cache entries (see the module docstring)
+        self.cached_ids: set[int] = set()
+        if (weight_cache and autocast_dtype == torch.bfloat16 and self.device.type == "cuda"
+                and not self.overlap and hasattr(model, "matmul_weights")):
+            self._build_cache()
+        elif self.world > 1:
             self._layout(bucket_mb)
         self.ids = torch.zeros(batch_shape, dtype=torch.long, device=self.device)
         self.targets = torch.zeros(batch_shape, dtype=torch.long, device=self.device)
@@ -108,6 +125,56 @@ class TrainStep:
             for p in self.params:
                 p.register_post_accumulate_grad_hook(self._grad_ready)
 
+    def _build_cache(self) -> None:
+        from .model import head_rows
+
+        groups, head = self.model.matmul_weights()
+        mm = [p for g in groups for p in g]
+        ids = {id(p) for p in mm} | {id(head)}
+        owned = {id(p) for p in self.params}
+        if len(ids) != len(mm) + 1 or not ids <= owned:
+            raise ValueError("matmul_weights() must list distinct trainable parameters")
+        dev = self.device
+        n = sum(p.numel() for p in mm)
+        self.w32 = torch.empty(n, dtype=torch.float32, device=dev)
+        self.w16 = torch.empty(n, dtype=torch.bfloat16, device=dev)
+        self.g16 = torch.empty(n, dtype=torch.bfloat16, device=dev)
+        entries: dict = {}
+        off = 0
+        for g in groups:
+            start = off
+            for p in g:
+                k = p.numel()
+                self.w32[off:off + k].copy_(p.detach().reshape(-1))
+                p.data = self.w32[off:off + k].view_as(p)
+                entries[id(p)] = (self.w16[off:off + k].view_as(p), self.g16[off:off + k].view_as(p))
+                off += k
+            kk, vv, rr = g[0], g[1], g[2]  # the batched key / value / receptance projection
+            if kk.shape == vv.shape == rr.shape:
+                m = 3 * kk.numel()
+                entries[(id(kk), id(vv), id(rr))] = (self.w16[start:start + m].view(3, *kk.shape),
+                                                     self.g16[start:start + m].view(3, *kk.shape))
+        v, c = head.shape
+        # the head's copy is stored with the zero rows _head pads to
+        self.h16 = torch.zeros(head_rows(v), c, dtype=torch.bfloat16, device=dev)
+        self.hg16 = torch.zeros(head_rows(v), c, dtype=torch.bfloat16, device=dev)
+        entries[id(head)] = (self.h16, self.hg16)
+        self.head = head
+        self.cache = entries
+        self.cached_ids = ids
+        self.others = [p for p in reversed(self.params) if id(p) not in ids]
+        self.n_mm, self.n_head_end = n, n + head.numel()
+        self.grads = torch.zeros(self.n_head_end + sum(p.numel() for p in self.others),
+                                 dtype=torch.float32, device=dev)
+        view_of: dict[int, Tensor] = {}
+        off = 0
+        for p in mm + [head] + self.others:
+            view_of[id(p)] = self.grads[off:off + p.numel()].view_as(p)
+            off += p.numel()
+        self.grad_views = [view_of[id(p)] for p in self.params]
+        for p in mm + [head]:
+            p.grad = view_of[id(p)]
+
     def _grad_ready(self, p: Tensor) -> None:
         # autograd hook: p.grad is final for this backward
         if not self._collecting:
@@ -140,13 +207,21 @@ class TrainStep:
         self._ready = [0] * len(self.buckets)
 
     def _forward_backward(self) -> Tensor:
+        from .model import weight_cache
+
         for p in self.params:
-            p.grad = None
+            if id(p) not in self.cached_ids:
+                p.grad = None
+        cache = contextlib.nullcontext()
+        if self.cache is not None:  # this step's bf16 copies of the matmul weights
+            self.w16.copy_(self.w32)
+            self.h16[:self.head.shape[0]].copy_(self.head.detach())
+            cache = weight_cache(self.cache)
         # the full backward below consumes every skip gradient handed over
         # between a residual_add and its LayerNorm-mix (fused.residual_handoff)
         self._collecting = self.overlap
         try:
-            with fused.residual_handoff():
+            with fused.residual_handoff(), cache:
                 if self.autocast_dtype is None:
                     loss = self.model(self.ids, self.targets)
                 else:
@@ -158,7 +233,11 @@ class TrainStep:
         if fused.pending_residual_grads():
             fused.drop_residual_grads()
             raise RuntimeError("TrainStep: a residual gradient was handed over but never consumed")
-        if self.overlap:
+        if self.cache is not None:
+            self.grads[:self.n_mm].copy_(self.g16)
+            self.grads[self.n_mm:self.n_head_end].view_as(self.head).copy_(self.hg16[:self.head.shape[0]])
+            torch.cat([p.grad.reshape(-1) for p in self.others], out=self.grads[self.n_head_end:])
+        elif self.overlap:
             self._finish_buckets()
         elif self.grads is not None:
             torch.cat([p.grad.reshape(-1) for p in reversed(self.params)], out=self.grads)
@@ -197,7 +276,7 @@ class TrainStep:
             loss = self.loss
         else:
             loss = self._forward_backward()
-        if self.grads is not None and not self.overlap:
+        if self.grads is not None and self.world > 1 and not self.overlap:
             ev = None
             if self._ar_events is not None:
                 ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))

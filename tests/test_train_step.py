@@ -186,3 +186,24 @@ def test_graph_gradients_match_autograd(cuda):
         scale = max(float(pr.grad.abs().max()), 1e-12)
         assert float((pr.grad - pg.grad).abs().max()) <= 1e-3 * scale, name
     step.release()
+
+
+@pytest.mark.gpu
+def test_weight_cache_matches_autocast_casts(cuda):
+    """The step's one-kernel bf16 weight copies and widened bf16 weight
+    gradients give autocast's per-weight casts' gradients."""
+    plain, cached = _spikegpt(cuda, 11), _spikegpt(cuda, 11)
+    ids = torch.randint(0, 256, (2, 257), generator=torch.Generator(device="cpu").manual_seed(2)).to(cuda)
+    steps = [TrainStep(m, torch.optim.SGD(m.parameters(), lr=0.0), (2, 256), device=cuda, graph=False,
+                       weight_cache=wc) for m, wc in ((plain, False), (cached, True))]
+    assert steps[0].cache is None and steps[1].cache is not None
+    losses = [float(s(ids[:, :-1], ids[:, 1:])) for s in steps]
+    assert abs(losses[0] - losses[1]) <= 1e-6 * max(1.0, abs(losses[0])), losses
+    for (name, pp), pc in zip(plain.named_parameters(), cached.parameters()):
+        scale = max(float(pp.grad.abs().max()), 1e-12)
+        assert float((pp.grad - pc.grad).abs().max()) <= 1e-3 * scale, name
+    # the matmul weights are views of the flat buffer, their gradients too
+    groups, head = cached.matmul_weights()
+    for p in [q for g in groups for q in g]:
+        assert p.data_ptr() >= steps[1].w32.data_ptr()
+        assert p.grad.data_ptr() >= steps[1].grads.data_ptr()
