@@ -114,19 +114,50 @@ def _mix_profile(n_embd: int, power: float, offset: float = 0.0) -> Tensor:
 # product, widened exactly. The key, value and receptance weights of a time
 # mixing have one more entry under the tuple of their ids: the [3, C, C] copy
 # and gradient buffer of the three, for the batched projection.
+#
+# With a side stream, each weight-gradient product runs there (forked from the
+# backward's stream when its operands are ready): nothing in the backward reads
+# it, so it overlaps the rest of the backward, whose kernels leave most SMs idle
+# at a few sequences per GPU. The caller joins the side stream before reading
+# the gradient buffers, and until then ``side_operands()`` holds the products'
+# operands, so the caching allocator (and a graph capture's memory pool) cannot
+# hand their memory out while a product still reads it.
 
 _CACHE: dict = {}
+_SIDE: list = [None]  # the weight-gradient stream while a cache is active
+_SIDE_KEEP: list = []  # operands of the products issued on it since the last join
 
 
 @contextlib.contextmanager
-def weight_cache(entries: dict):
+def weight_cache(entries: dict, side_stream=None):
     """Projections read their weights' bf16 copies from ``entries`` (id of the
-    parameter -> (bf16 copy, bf16 gradient buffer)) inside the block."""
+    parameter -> (bf16 copy, bf16 gradient buffer)) inside the block; weight
+    gradients go to ``side_stream`` when one is given."""
     _CACHE.update(entries)
+    _SIDE[0] = side_stream
     try:
         yield
     finally:
         _CACHE.clear()
+        _SIDE[0] = None
+
+
+def side_operands() -> list:
+    """The operands of the weight-gradient products issued on the side stream
+    since the caller last cleared this list (after joining the stream)."""
+    return _SIDE_KEEP
+
+
+def _weight_grad(side, product, *operands: Tensor) -> None:
+    """Run ``product()`` (which writes a weight gradient buffer) on the side
+    stream after the current stream's work so far, or inline without one."""
+    if side is None:
+        product()
+        return
+    side.wait_stream(torch.cuda.current_stream(operands[0].device))
+    with torch.cuda.stream(side):
+        product()
+    _SIDE_KEEP.extend(operands)
 
 
 class _CachedLinear(torch.autograd.Function):
@@ -137,14 +168,17 @@ class _CachedLinear(torch.autograd.Function):
     def forward(ctx, x: Tensor, wb: Tensor, gb: Tensor) -> Tensor:
         x = x.to(wb.dtype)
         ctx.save_for_backward(x)
-        ctx.wb, ctx.gb = wb, gb
+        ctx.wb, ctx.gb, ctx.side = wb, gb, _SIDE[0]
         return F.linear(x, wb)
 
     @staticmethod
     def backward(ctx, gy: Tensor):
         (x,) = ctx.saved_tensors
         gy = gy.to(ctx.wb.dtype)
-        torch.mm(gy.reshape(-1, gy.shape[-1]).t(), x.reshape(-1, x.shape[-1]), out=ctx.gb)
+        gb = ctx.gb
+        _weight_grad(ctx.side,
+                     lambda: torch.mm(gy.reshape(-1, gy.shape[-1]).t(), x.reshape(-1, x.shape[-1]), out=gb),
+                     gy, x)
         return gy.matmul(ctx.wb), None, None
 
 
@@ -156,14 +190,15 @@ class _CachedStacked(torch.autograd.Function):
     def forward(ctx, x3: Tensor, w3b: Tensor, g3b: Tensor) -> Tensor:
         x3 = x3.to(w3b.dtype)
         ctx.save_for_backward(x3)
-        ctx.w3b, ctx.g3b = w3b, g3b
+        ctx.w3b, ctx.g3b, ctx.side = w3b, g3b, _SIDE[0]
         return torch.matmul(x3, w3b.transpose(1, 2))
 
     @staticmethod
     def backward(ctx, gy3: Tensor):
         (x3,) = ctx.saved_tensors
         gy3 = gy3.to(ctx.w3b.dtype)
-        torch.bmm(gy3.transpose(1, 2), x3, out=ctx.g3b)
+        g3b = ctx.g3b
+        _weight_grad(ctx.side, lambda: torch.bmm(gy3.transpose(1, 2), x3, out=g3b), gy3, x3)
         return torch.matmul(gy3, ctx.w3b), None, None
 
 

@@ -39,7 +39,9 @@ and write their bf16 weight gradients into a flat bf16 buffer, which one more
 kernel widens into the flat float32 gradient buffer: [matmul weights | head |
 the other parameters in backward order], of which every parameter's ``.grad``
 is a view. This replaces autocast's per-weight casts (about 200 kernels a step
-in SpikeGPT-41M) with four, and computes the same values.
+in SpikeGPT-41M) with four, and computes the same values. The weight-gradient
+products run on a side stream (``side_wgrad``), joined before the widening:
+they overlap the rest of the backward.
 """
 
 from __future__ import annotations
@@ -65,7 +67,7 @@ class TrainStep:
     def __init__(self, model: nn.Module, optimizer: torch.optim.Optimizer, batch_shape: tuple[int, int], *,
                  device: torch.device | str, autocast_dtype: torch.dtype | None = torch.bfloat16,
                  graph: bool = True, group=None, warmup: int = 3, overlap: bool = False,
-                 bucket_mb: float = 25.0, weight_cache: bool = True) -> None:
+                 bucket_mb: float = 25.0, weight_cache: bool = True, side_wgrad: bool = True) -> None:
         self.model = model
         self.optimizer = optimizer
         self.device = torch.device(device)
@@ -86,9 +88,12 @@ class TrainStep:
         self.buckets: list[tuple[list[nn.Parameter], Tensor]] = []
         self.cache = None  # weight cache entries (see the module docstring)
         self.cached_ids: set[int] = set()
+        self.side = None  # the stream of the cached projections' weight gradients
         if (weight_cache and autocast_dtype == torch.bfloat16 and self.device.type == "cuda"
                 and not self.overlap and hasattr(model, "matmul_weights")):
             self._build_cache()
+            if side_wgrad:
+                self.side = torch.cuda.Stream(self.device)
         elif self.world > 1:
             self._layout(bucket_mb)
         self.ids = torch.zeros(batch_shape, dtype=torch.long, device=self.device)
@@ -207,7 +212,7 @@ class TrainStep:
         self._ready = [0] * len(self.buckets)
 
     def _forward_backward(self) -> Tensor:
-        from .model import weight_cache
+        from .model import side_operands, weight_cache
 
         for p in self.params:
             if id(p) not in self.cached_ids:
@@ -216,7 +221,7 @@ class TrainStep:
         if self.cache is not None:  # this step's bf16 copies of the matmul weights
             self.w16.copy_(self.w32)
             self.h16[:self.head.shape[0]].copy_(self.head.detach())
-            cache = weight_cache(self.cache)
+            cache = weight_cache(self.cache, self.side)
         # the full backward below consumes every skip gradient handed over
         # between a residual_add and its LayerNorm-mix (fused.residual_handoff)
         self._collecting = self.overlap
@@ -234,6 +239,9 @@ class TrainStep:
             fused.drop_residual_grads()
             raise RuntimeError("TrainStep: a residual gradient was handed over but never consumed")
         if self.cache is not None:
+            if self.side is not None:  # the weight gradients written on the side stream
+                torch.cuda.current_stream(self.device).wait_stream(self.side)
+                side_operands().clear()
             self.grads[:self.n_mm].copy_(self.g16)
             self.grads[self.n_mm:self.n_head_end].view_as(self.head).copy_(self.hg16[:self.head.shape[0]])
             torch.cat([p.grad.reshape(-1) for p in self.others], out=self.grads[self.n_head_end:])
