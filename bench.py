@@ -1434,9 +1434,12 @@ def measure_train(wl, *, steps: int, warmup: int, world: int, rank: int, dev, gl
         "data": f"synthetic Zipf({wl['zipf']}) token ids, seeded numpy PCG64 per rank",
         "config": {"workload": wl["desc"], "model": name, "global_batch": gb, "seq_len": t, "B_per_gpu": b,
                    "params": sum(p.numel() for p in model.parameters()),
-                   "parallelism": f"dp{world}" + (" (bucketed NCCL all-reduce, AVG)" if world > 1 else ""),
+                   "parallelism": f"dp{world}" + ((" (bucketed NCCL all-reduce, AVG)" if step.overlap else
+                                                   " (one NCCL all-reduce, AVG)") if world > 1 else ""),
                    "launch": "eager" if eager else "CUDA graph (forward + backward), eager all-reduce "
                                                    "and fused AdamW",
+                   "weights": ("bf16 copies cast once a step, weight gradients on a side stream"
+                               if step.cache is not None else "autocast casts"),
                    "l2": "model state and activations far above L2; no flush"},
         "allreduce_ms_per_step": ar if world > 1 and not step.overlap else None,
         "allreduce": (f"{len(step.buckets)} buckets of about 25 MB, all-reduced asynchronously during the backward "
