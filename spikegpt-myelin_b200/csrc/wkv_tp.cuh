@@ -433,6 +433,47 @@ __device__ __forceinline__ void bwd_tp_recompute(const T* ks, const T* vs, const
   }
 }
 
+// bwd_tp_recompute for a full tile whose k and grad_y rows are already in
+// registers (loaded once for the range scan), v read from the staged box.
+template <typename T>
+__device__ __forceinline__ void bwd_tp_recompute_regs(const typename Pair<T>::raw (&kr)[kSub],
+                                                      const typename Pair<T>::raw (&gr)[kSub], const T* vs,
+                                                      const Lane2& lc, f2 s, f2 p, f2 q, f2 (&re)[kSub],
+                                                      f2 (&rg)[kSub], f2 (&rn)[kSub]) {
+  using P = Pair<T>;
+  const f2 l2e = splat(kL2E), ns = f2{-s.x, -s.y};
+#pragma unroll
+  for (int i = 0; i < kSub; ++i) {
+    const f2 v = P::unpack(P::ld(vs + i * kLanes));
+    const f2 ek = ex2x2(fma2(P::unpack(kr[i]), l2e, ns));
+    re[i] = ek;
+    const f2 ekv = mul2(ek, v);
+    const f2 rd = rcpx2(fma2(ek, lc.eu, q));  // 1 / D
+    const f2 y = mul2(fma2(lc.eu, ekv, p), rd);
+    const f2 g = mul2(P::unpack(gr[i]), rd);
+    rg[i] = g;
+    rn[i] = f2{-(g.x * y.x), -(g.y * y.y)};
+    p = fma2(lc.ew, p, ekv);
+    q = fma2(lc.ew, q, ek);
+  }
+}
+
+// Packed max |grad_y| over the rows of a full register tile.
+template <typename T>
+__device__ __forceinline__ f2 tile_absmax(const typename Pair<T>::raw (&gr)[kSub]) {
+  using Sc = Scan<T>;
+  using raw = typename Pair<T>::raw;
+  raw g[kSub / 2];
+#pragma unroll
+  for (int i = 0; i < kSub / 2; ++i) g[i] = Sc::vmax(Sc::vabs(gr[i]), Sc::vabs(gr[i + kSub / 2]));
+#pragma unroll
+  for (int w = kSub / 4; w > 0; w /= 2) {
+#pragma unroll
+    for (int i = 0; i < w; ++i) g[i] = Sc::vmax(g[i], g[i + w]);
+  }
+  return Pair<T>::unpack(g[0]);
+}
+
 // The tile's adjoint summary: the reverse recurrence over its rows from a zero
 // adjoint at the tile end (scaled by 2^s, like rg). The w-derivatives are
 // carried as K with H = e^w K (K_t = G_{t+1} + H_{t+1}, so K_t = G_{t+1} +
@@ -732,20 +773,31 @@ __global__ void __launch_bounds__(32 * W, 4)
     }
     if (seg_local && n > 0)
       st0 = (t0 == t_begin) ? segst : fwd_combine2(segst, t0 - t_begin, lc, st0);
-    const Pre pre = n == R ? prescan<T, false, true>(kt, gt, n) : prescan<T, true, true>(kt, gt, n);
     f2 s, p, q;
-    bool ok = n == 0 || (fast_ok1(st0.S.x, st0.p.x, st0.q.x, pre.kmax.x, pre.kmin.x, n, lc.w2.x,
-                                  lc.u2.x, s.x, p.x, q.x) &&
-                         fast_ok1(st0.S.y, st0.p.y, st0.q.y, pre.kmax.y, pre.kmin.y, n, lc.w2.y,
-                                  lc.u2.y, s.y, p.y, q.y) &&
-                         fmaxf(pre.gymax.x, pre.gymax.y) <= 0x1p40f && !force_slow);
-    if (n == 0) s = p = q = splat(0.f);
+    bool ok;
     f2 re[R], rg[R], rn[R];
     Adj2 loc;
-    if (n == R) {
-      bwd_tp_recompute<T, false>(kt, vt, gt, n, lc, s, p, q, re, rg, rn);
+    auto check = [&](f2 kmax, f2 kmin, f2 gymax) {
+      return fast_ok1(st0.S.x, st0.p.x, st0.q.x, kmax.x, kmin.x, n, lc.w2.x, lc.u2.x, s.x, p.x, q.x) &&
+             fast_ok1(st0.S.y, st0.p.y, st0.q.y, kmax.y, kmin.y, n, lc.w2.y, lc.u2.y, s.y, p.y, q.y) &&
+             fmaxf(gymax.x, gymax.y) <= 0x1p40f && !force_slow;
+    };
+    if (n == R) {  // k and grad_y rows read once, into registers, for the range scan and the recompute
+      typename Pair<T>::raw kr[R], gr[R];
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        kr[i] = Pair<T>::ld(kt + i * kLanes);
+        gr[i] = Pair<T>::ld(gt + i * kLanes);
+      }
+      f2 kmax, kmin;
+      tile_kminmax<T, false>(kr, n, kmax, kmin);
+      ok = check(kmax, kmin, tile_absmax<T>(gr));
+      bwd_tp_recompute_regs<T>(kr, gr, vt, lc, s, p, q, re, rg, rn);
       bwd_tp_summary<false>(rg, rn, n, lc, loc.gp, loc.gq, loc.hp, loc.hq);
     } else {
+      const Pre pre = prescan<T, true, true>(kt, gt, n);
+      ok = n == 0 || check(pre.kmax, pre.kmin, pre.gymax);
+      if (n == 0) s = p = q = splat(0.f);
       bwd_tp_recompute<T, true>(kt, vt, gt, n, lc, s, p, q, re, rg, rn);
       bwd_tp_summary<true>(rg, rn, n, lc, loc.gp, loc.gq, loc.hp, loc.hq);
     }
