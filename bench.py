@@ -117,6 +117,9 @@ def parse_args():
     ap.add_argument("--overlap", action="store_true",
                     help="train workloads: all-reduce the gradients in buckets during the backward instead of once "
                          "after it")
+    ap.add_argument("--micro-batches", type=int, default=None,
+                    help="train workloads: run each rank's batch as this many micro-batches on their own streams "
+                         "(default: 2 for 8 to 16 sequences per rank, else 1, as measured on one B200)")
     ap.add_argument("--global-batch", type=int, default=None,
                     help="train workloads: override the global batch (e.g. the per-rank share of an N-GPU run on one GPU)")
     ap.add_argument("--no-train-leg", dest="train_leg", action="store_false",
@@ -1360,7 +1363,8 @@ def train_kernel_split(model, opt, x, y, dev, top: int) -> None:
 
 
 def measure_train(wl, *, steps: int, warmup: int, world: int, rank: int, dev, global_batch=None,
-                  eager: bool = False, clocks: bool = True, e2e_steps: int = 0, overlap: bool = False):
+                  eager: bool = False, clocks: bool = True, e2e_steps: int = 0, overlap: bool = False,
+                  micro_batches: int | None = None):
     """Time the data-parallel train step (the process group, if any, is already
     initialized). Returns (result dict, TrainStep, model, optimizer, x, y); the
     caller releases the step before destroying the process group."""
@@ -1386,7 +1390,9 @@ def measure_train(wl, *, steps: int, warmup: int, world: int, rank: int, dev, gl
     ids = torch.as_tensor(ids_np).to(dev)
     x, y = ids[:, :-1].contiguous(), ids[:, 1:].contiguous()
     launches_before = sum(_capi.launch_counts().values())
-    step = TrainStep(model, opt, (b, t), device=dev, graph=not eager, overlap=overlap)
+    if micro_batches is None:  # measured (SpikeGPT-41M, one B200): two micro-batches pay at 8 and 16 sequences
+        micro_batches = 2 if 8 <= b <= 16 and not overlap else 1
+    step = TrainStep(model, opt, (b, t), device=dev, graph=not eager, overlap=overlap, micro_batches=micro_batches)
     capture_launches = sum(_capi.launch_counts().values()) - launches_before
 
     for _ in range(warmup):
@@ -1440,6 +1446,7 @@ def measure_train(wl, *, steps: int, warmup: int, world: int, rank: int, dev, gl
                                                    "and fused AdamW",
                    "weights": ("bf16 copies cast once a step, weight gradients on a side stream"
                                if step.cache is not None else "autocast casts"),
+                   "micro_batches": step.micro,
                    "l2": "model state and activations far above L2; no flush"},
         "allreduce_ms_per_step": ar if world > 1 and not step.overlap else None,
         "allreduce": (f"{len(step.buckets)} buckets of about 25 MB, all-reduced asynchronously during the backward "
@@ -1501,7 +1508,7 @@ def run_train(args, wl):
     result, step, model, opt, x, y = measure_train(
         wl, steps=args.steps, warmup=args.warmup, world=world, rank=rank, dev=dev,
         global_batch=args.global_batch, eager=args.eager, clocks=not args.profile,
-        e2e_steps=0 if args.profile else args.e2e_steps, overlap=args.overlap)
+        e2e_steps=0 if args.profile else args.e2e_steps, overlap=args.overlap, micro_batches=args.micro_batches)
     result["cpu_baseline"] = None
     result["cpu_baseline_note"] = ("no CPU leg: the model step runs only on this package's CUDA ops, and the "
                                    "reference's own CPU step needs myelin@68b8ebb, absent")

@@ -67,7 +67,8 @@ class TrainStep:
     def __init__(self, model: nn.Module, optimizer: torch.optim.Optimizer, batch_shape: tuple[int, int], *,
                  device: torch.device | str, autocast_dtype: torch.dtype | None = torch.bfloat16,
                  graph: bool = True, group=None, warmup: int = 3, overlap: bool = False,
-                 bucket_mb: float = 25.0, weight_cache: bool = True, side_wgrad: bool = True) -> None:
+                 bucket_mb: float = 25.0, weight_cache: bool = True, side_wgrad: bool = True,
+                 micro_batches: int = 1) -> None:
         self.model = model
         self.optimizer = optimizer
         self.device = torch.device(device)
@@ -89,11 +90,17 @@ class TrainStep:
         self.cache = None  # weight cache entries (see the module docstring)
         self.cached_ids: set[int] = set()
         self.side = None  # the stream of the cached projections' weight gradients
+        self.micro = int(micro_batches)
+        if self.micro < 1 or batch_shape[0] % self.micro:
+            raise ValueError(f"micro_batches={micro_batches} must divide the {batch_shape[0]} rows")
         if (weight_cache and autocast_dtype == torch.bfloat16 and self.device.type == "cuda"
                 and not self.overlap and hasattr(model, "matmul_weights")):
             self._build_cache()
             if side_wgrad:
                 self.side = torch.cuda.Stream(self.device)
+            self.mb_streams = [torch.cuda.Stream(self.device) for _ in range(self.micro)] if self.micro > 1 else []
+        elif self.micro > 1:
+            raise ValueError("micro_batches > 1 needs the weight cache (bf16 autocast on CUDA, no overlap)")
         elif self.world > 1:
             self._layout(bucket_mb)
         self.ids = torch.zeros(batch_shape, dtype=torch.long, device=self.device)
@@ -141,10 +148,15 @@ class TrainStep:
             raise ValueError("matmul_weights() must list distinct trainable parameters")
         dev = self.device
         n = sum(p.numel() for p in mm)
+        v, c = head.shape
         self.w32 = torch.empty(n, dtype=torch.float32, device=dev)
         self.w16 = torch.empty(n, dtype=torch.bfloat16, device=dev)
-        self.g16 = torch.empty(n, dtype=torch.bfloat16, device=dev)
-        entries: dict = {}
+        # the head's copy is stored with the zero rows _head pads to
+        self.h16 = torch.zeros(head_rows(v), c, dtype=torch.bfloat16, device=dev)
+        # bf16 weight-gradient buffers, one set per micro-batch
+        self.g16s = [torch.empty(n, dtype=torch.bfloat16, device=dev) for _ in range(self.micro)]
+        self.hg16s = [torch.zeros(head_rows(v), c, dtype=torch.bfloat16, device=dev) for _ in range(self.micro)]
+        self.caches = [{} for _ in range(self.micro)]
         off = 0
         for g in groups:
             start = off
@@ -152,20 +164,19 @@ class TrainStep:
                 k = p.numel()
                 self.w32[off:off + k].copy_(p.detach().reshape(-1))
                 p.data = self.w32[off:off + k].view_as(p)
-                entries[id(p)] = (self.w16[off:off + k].view_as(p), self.g16[off:off + k].view_as(p))
+                for e, g16 in zip(self.caches, self.g16s):
+                    e[id(p)] = (self.w16[off:off + k].view_as(p), g16[off:off + k].view_as(p))
                 off += k
             kk, vv, rr = g[0], g[1], g[2]  # the batched key / value / receptance projection
             if kk.shape == vv.shape == rr.shape:
                 m = 3 * kk.numel()
-                entries[(id(kk), id(vv), id(rr))] = (self.w16[start:start + m].view(3, *kk.shape),
-                                                     self.g16[start:start + m].view(3, *kk.shape))
-        v, c = head.shape
-        # the head's copy is stored with the zero rows _head pads to
-        self.h16 = torch.zeros(head_rows(v), c, dtype=torch.bfloat16, device=dev)
-        self.hg16 = torch.zeros(head_rows(v), c, dtype=torch.bfloat16, device=dev)
-        entries[id(head)] = (self.h16, self.hg16)
+                for e, g16 in zip(self.caches, self.g16s):
+                    e[(id(kk), id(vv), id(rr))] = (self.w16[start:start + m].view(3, *kk.shape),
+                                                   g16[start:start + m].view(3, *kk.shape))
+        for e, hg16 in zip(self.caches, self.hg16s):
+            e[id(head)] = (self.h16, hg16)
         self.head = head
-        self.cache = entries
+        self.cache = self.caches[0]
         self.cached_ids = ids
         self.others = [p for p in reversed(self.params) if id(p) not in ids]
         self.n_mm, self.n_head_end = n, n + head.numel()
@@ -226,13 +237,16 @@ class TrainStep:
         # between a residual_add and its LayerNorm-mix (fused.residual_handoff)
         self._collecting = self.overlap
         try:
-            with fused.residual_handoff(), cache:
-                if self.autocast_dtype is None:
-                    loss = self.model(self.ids, self.targets)
-                else:
-                    with torch.autocast(self.device.type, dtype=self.autocast_dtype):
+            if self.micro > 1:
+                loss = self._micro_forward_backward()
+            else:
+                with fused.residual_handoff(), cache:
+                    if self.autocast_dtype is None:
                         loss = self.model(self.ids, self.targets)
-                loss.backward()
+                    else:
+                        with torch.autocast(self.device.type, dtype=self.autocast_dtype):
+                            loss = self.model(self.ids, self.targets)
+                    loss.backward()
         finally:
             self._collecting = False
         if fused.pending_residual_grads():
@@ -242,14 +256,46 @@ class TrainStep:
             if self.side is not None:  # the weight gradients written on the side stream
                 torch.cuda.current_stream(self.device).wait_stream(self.side)
                 side_operands().clear()
-            self.grads[:self.n_mm].copy_(self.g16)
-            self.grads[self.n_mm:self.n_head_end].view_as(self.head).copy_(self.hg16[:self.head.shape[0]])
+            gmm, ghead = self.grads[:self.n_mm], self.grads[self.n_mm:self.n_head_end].view_as(self.head)
+            v = self.head.shape[0]
+            gmm.copy_(self.g16s[0])
+            ghead.copy_(self.hg16s[0][:v])
+            for g16, hg16 in zip(self.g16s[1:], self.hg16s[1:]):  # the other micro-batches' shares
+                gmm.add_(g16)
+                ghead.add_(hg16[:v])
             torch.cat([p.grad.reshape(-1) for p in self.others], out=self.grads[self.n_head_end:])
         elif self.overlap:
             self._finish_buckets()
         elif self.grads is not None:
             torch.cat([p.grad.reshape(-1) for p in reversed(self.params)], out=self.grads)
         return loss.detach()
+
+    def _micro_forward_backward(self) -> Tensor:
+        """Forward and backward of the rank's batch as ``micro`` micro-batches,
+        each on its own stream: autograd runs each backward op on the stream of
+        its forward op, so the micro-batches' kernels overlap (at a few
+        sequences per GPU most kernels leave SMs idle). Each micro-batch writes
+        its own bf16 weight gradients; the loss is the mean of the micro-batch
+        means (equal sizes: the batch mean)."""
+        from .model import weight_cache
+
+        cur = torch.cuda.current_stream(self.device)
+        rows = self.ids.shape[0] // self.micro
+        losses = []
+        with fused.residual_handoff():
+            for i, s in enumerate(self.mb_streams):
+                s.wait_stream(cur)
+                sl = slice(i * rows, (i + 1) * rows)
+                with torch.cuda.stream(s), weight_cache(self.caches[i], self.side), \
+                        torch.autocast(self.device.type, dtype=self.autocast_dtype):
+                    losses.append(self.model(self.ids[sl], self.targets[sl]))
+            for s in self.mb_streams:
+                cur.wait_stream(s)
+            loss = torch.stack(losses).mean()
+            loss.backward()
+        for s in self.mb_streams:
+            cur.wait_stream(s)
+        return loss
 
     def _capture(self, warmup: int) -> None:
         # Warm-up on a side stream (as graph capture requires), then capture.

@@ -207,3 +207,26 @@ def test_weight_cache_matches_autocast_casts(cuda):
     for p in [q for g in groups for q in g]:
         assert p.data_ptr() >= steps[1].w32.data_ptr()
         assert p.grad.data_ptr() >= steps[1].grads.data_ptr()
+
+
+@pytest.mark.gpu
+def test_micro_batches_match_one_batch(cuda):
+    """Two micro-batches on their own streams (replayed from the graph) give
+    the one-batch step's loss and, up to the bf16 rounding of each micro-batch's
+    weight gradients, its gradients."""
+    one, two = _spikegpt(cuda, 13), _spikegpt(cuda, 13)
+    ids = torch.randint(0, 256, (4, 257), generator=torch.Generator(device="cpu").manual_seed(5)).to(cuda)
+    s1 = TrainStep(one, torch.optim.SGD(one.parameters(), lr=0.0), (4, 256), device=cuda, graph=True)
+    s2 = TrainStep(two, torch.optim.SGD(two.parameters(), lr=0.0), (4, 256), device=cuda, graph=True,
+                   micro_batches=2)
+    for _ in range(2):  # the second replay rewrites every gradient the first wrote
+        l1, l2 = float(s1(ids[:, :-1], ids[:, 1:])), float(s2(ids[:, :-1], ids[:, 1:]))
+    assert abs(l1 - l2) <= 1e-4 * max(1.0, abs(l1)), (l1, l2)
+    for (name, p1), p2 in zip(one.named_parameters(), two.parameters()):
+        scale = max(float(p1.grad.abs().max()), 1e-12)
+        assert float((p1.grad - p2.grad).abs().max()) <= 1e-2 * scale, name
+    s1.release()
+    s2.release()
+    with pytest.raises(ValueError):
+        TrainStep(_spikegpt(cuda), torch.optim.SGD(one.parameters(), lr=0.0), (3, 256), device=cuda,
+                  graph=False, micro_batches=2)
