@@ -24,7 +24,7 @@
 
 namespace wkv {
 
-// Warps per CTA: 4 for 16-bit I/O (4 CTAs of 54 KB shared memory fit an SM, so
+// Warps per CTA: 4 for 16-bit I/O (4 CTAs of 47 KB shared memory fit an SM, so
 // B*C = 32768 runs in one wave), 2 for float32 (twice the bytes per box).
 template <typename T>
 constexpr int tp_warps() {
@@ -364,9 +364,10 @@ __global__ void __launch_bounds__(32 * W, 4)
 //      grad_key / grad_value and accumulating dL/dw, dL/du.
 
 // Warps per backward CTA: a tile's records (e^{k-s}, gy/D, -gy y/D) stay in
-// registers across the round barrier (~235 registers a thread), so an SM runs
-// 4 CTAs of 2 warps and B*C = 32768 fits one wave; k, v and grad_y are read
-// from the staged boxes where they are used.
+// registers across the round barrier (~237 registers a thread), so an SM runs
+// 4 CTAs of 2 warps and B*C = 32768 fits one wave. A full tile's k and grad_y
+// rows are loaded into registers once, for the range scan and the recompute;
+// v is read from the staged box where it is used (recompute and outputs).
 template <typename T>
 constexpr int tp_bwd_warps() {
   return 2;
