@@ -132,7 +132,9 @@ _SIDE_KEEP: list = []  # operands of the products issued on it since the last jo
 def weight_cache(entries: dict, side_stream=None):
     """Projections read their weights' bf16 copies from ``entries`` (id of the
     parameter -> (bf16 copy, bf16 gradient buffer)) inside the block; weight
-    gradients go to ``side_stream`` when one is given."""
+    gradients go to ``side_stream`` when one is given. The cache is state of
+    this module: one block at a time per process (not nested, not from two
+    threads at once); TrainStep enters it around each forward it issues."""
     _CACHE.update(entries)
     _SIDE[0] = side_stream
     try:
