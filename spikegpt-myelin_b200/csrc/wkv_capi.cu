@@ -1205,8 +1205,12 @@ int64_t mix_ctas_per_seq(int64_t B, int64_t T) {
 }
 
 template <int N>
-void mix_bwd_go(const MixArgs& a, unsigned grid, cudaStream_t st) {
-  ln_mix_bwd_kernel<N><<<grid, a.C / 4, 0, st>>>(a);
+cudaError_t mix_bwd_go(const MixArgs& a, unsigned grid, cudaStream_t st) {
+  const cudaError_t e = allow_smem(ln_mix_bwd_kernel<N>, kMixStages * mix_bwd_stage_bytes(N, kMixMaxC, true));
+  if (e != cudaSuccess) return e;
+  const size_t smem = kMixStages * mix_bwd_stage_bytes(N, a.C, a.gres != nullptr);
+  launch(K_MIX_BWD, st, [&] { ln_mix_bwd_kernel<N><<<grid, a.C / 4, smem, st>>>(a); });
+  return cudaSuccess;
 }
 
 }  // namespace
@@ -1303,11 +1307,9 @@ int ln_mix_backward(int n, const void* g0, const void* g1, const void* g2, const
   a.nct = (int)mix_ctas_per_seq(B, T);
   const int chunks = (int)(B * a.nct);  // CTAs, each leaving one partial row set
   const unsigned grid = (unsigned)chunks;
-  launch(K_MIX_BWD, st, [&] {
-    if (n == 1) mix_bwd_go<1>(a, grid, st);
-    else if (n == 2) mix_bwd_go<2>(a, grid, st);
-    else mix_bwd_go<3>(a, grid, st);
-  });
+  const cudaError_t ae = n == 1 ? mix_bwd_go<1>(a, grid, st) : n == 2 ? mix_bwd_go<2>(a, grid, st)
+                                                                    : mix_bwd_go<3>(a, grid, st);
+  if (ae != cudaSuccess) return cuda_fail(ae, "setting the ln_mix backward kernel's shared memory size");
   const int rows = 2 + n;
   launch(K_MIX_RED, st, [&] {
     ln_mix_reduce_kernel<<<dim3((unsigned)((C + 31) / 32), (unsigned)rows), dim3(32, 32), 0, st>>>(
