@@ -156,14 +156,17 @@ def forward(
 
 
 def backward(
-    grad_y: Tensor, w: Tensor, u: Tensor, k: Tensor, v: Tensor, state: Tensor | None = None
+    grad_y: Tensor, w: Tensor, u: Tensor, k: Tensor, v: Tensor, state: Tensor | None = None, *,
+    out: tuple[Tensor, Tensor] | None = None,
 ) -> list[Tensor]:
     """[grad_key, grad_value, grad_time_decay (already x w), grad_time_first].
 
     Mirrors the output contract of the reference op (wkv_triton.py:164-198):
     grad_key/grad_value like ``k``, the per-channel grads like ``w``/``u``.
     With ``state`` (from forward(save_state=True) on the same inputs) the
-    forward sweep is skipped.
+    forward sweep is skipped. ``out`` = (grad_key, grad_value) tensors to
+    write into (contiguous, k's shape, k's dtype, which must be a kernel I/O
+    dtype); they are the ones returned.
     """
     if k.ndim != 3 or grad_y.shape != k.shape or v.shape != k.shape:
         raise ValueError(
@@ -180,8 +183,14 @@ def backward(
     w32 = w.to(torch.float32).contiguous()
     u32 = u.to(torch.float32).contiguous()
     b, t, c = kk.shape
-    gk = torch.empty_like(kk, memory_format=torch.contiguous_format)
-    gv = torch.empty_like(kk, memory_format=torch.contiguous_format)
+    if out is None:
+        gk = torch.empty_like(kk, memory_format=torch.contiguous_format)
+        gv = torch.empty_like(kk, memory_format=torch.contiguous_format)
+    else:
+        gk, gv = out
+        for g in (gk, gv):
+            if g.shape != kk.shape or g.dtype != io or k.dtype != io or not g.is_contiguous() or g.device != kk.device:
+                raise ValueError("out tensors must be contiguous, of k's shape and device, in k's (kernel) dtype")
     gtd = torch.empty(c, dtype=torch.float32, device=kk.device)
     gtf = torch.empty(c, dtype=torch.float32, device=kk.device)
     code = _CODES[io]

@@ -229,6 +229,18 @@ def _(grad, r, x):
     return [torch.empty_like(r), torch.empty_like(x)]
 
 
+def gate_backward_into(grad: Tensor, r: Tensor, x: Tensor, gr: Tensor, gx: Tensor) -> None:
+    """The gate's backward written into ``gr`` and ``gx`` (contiguous bf16 CUDA
+    tensors of r's shape): what ``gate``'s autograd computes, for a caller
+    that keeps the gradients in buffers of its own (eager use only)."""
+    if not gates_supported(r, x, gr, gx) or not (gr.is_contiguous() and gx.is_contiguous()):
+        raise ValueError("gate_backward_into needs contiguous bf16 CUDA tensors of one shape")
+    grad = _aligned(grad.to(torch.bfloat16))
+    r, x = _aligned(r), _aligned(x)
+    _capi.check(_capi.lib().gate_backward(grad.data_ptr(), r.data_ptr(), x.data_ptr(), gr.data_ptr(), gx.data_ptr(),
+                                          x.numel(), _stream(x)), "gate_backward")
+
+
 def _gate_setup(ctx, inputs, output):
     ctx.save_for_backward(*inputs)
 

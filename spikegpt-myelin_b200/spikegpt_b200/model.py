@@ -30,7 +30,7 @@ import torch
 import torch.nn.functional as F
 from torch import Tensor, nn
 
-from . import fused
+from . import _ops, fused
 from .lif import surrogate_lif
 from .wkv import weighted_key_value_cuda
 from .wkv_bf16 import weighted_key_value_cuda_bf16io
@@ -204,6 +204,71 @@ class _CachedStacked(torch.autograd.Function):
         return torch.matmul(gy3, ctx.w3b), None, None
 
 
+class _CachedPair(torch.autograd.Function):
+    """``x2[0] @ wa^T`` and ``x2[1] @ wb^T`` for a stacked [2, B, T, C] input
+    (channel mixing's key and receptance inputs) and cached bf16 weights. The
+    backward writes both input gradients into one [2, B, T, C] tensor, the
+    stacked gradient the LayerNorm-mix backward reads, where two projections
+    of unbound slices would leave autograd to stack them (one copy of both);
+    the weight gradients go to their bf16 buffers as in ``_CachedLinear``."""
+
+    @staticmethod
+    def forward(ctx, x2: Tensor, wa: Tensor, ga: Tensor, wb: Tensor, gb: Tensor):
+        x2 = x2.to(wa.dtype)
+        ctx.save_for_backward(x2)
+        ctx.ws, ctx.side = ((wa, ga), (wb, gb)), _SIDE[0]
+        return F.linear(x2[0], wa), F.linear(x2[1], wb)
+
+    @staticmethod
+    def backward(ctx, gya: Tensor, gyb: Tensor):
+        (x2,) = ctx.saved_tensors
+        c = x2.shape[-1]
+        gx2 = torch.empty_like(x2)
+        for i, (gy, (w, g)) in enumerate(zip((gya, gyb), ctx.ws)):
+            x = x2[i].reshape(-1, c)
+            if gy is None:
+                gy = x.new_zeros(x.shape[0], w.shape[0])
+            gy = gy.to(w.dtype).reshape(-1, w.shape[0])
+            _weight_grad(ctx.side, lambda gy=gy, x=x, g=g: torch.mm(gy.t(), x, out=g), gy, x)
+            torch.mm(gy, w, out=gx2[i].view(-1, c))
+        return gx2, None, None, None, None
+
+
+class _TimeCore(torch.autograd.Function):
+    """``sigmoid(r) * WKV(k, v)`` (the time-mixing core, bf16) from the stacked
+    [3, B, T, C] key / value / receptance projections. The same kernels as
+    the WKV op and ``fused.gate``, but the backward writes the three
+    projection gradients into one [3, B, T, C] tensor, the stacked input of
+    the projections' batched weight and input gradients, where separate ops
+    on unbound slices would leave autograd to stack them (one copy of all
+    three). The saved-state hand-off of the WKV op is kept."""
+
+    @staticmethod
+    def forward(ctx, kvr: Tensor, time_decay: Tensor, time_first: Tensor) -> Tensor:
+        k, v, rl = kvr.unbind(0)
+        state = None
+        if _ops.state_saving_enabled():
+            y, state = _ops.forward(k, v, time_decay, time_first, save_state=True)
+        else:
+            y = _ops.forward(k, v, time_decay, time_first)
+        ctx.save_for_backward(kvr, time_decay, time_first)
+        ctx.y, ctx.state = y, state  # made here, not inputs or outputs
+        return fused.gate(rl, y)
+
+    @staticmethod
+    def backward(ctx, g: Tensor):
+        kvr, time_decay, time_first = ctx.saved_tensors
+        y, state = ctx.y, ctx.state
+        k, v, rl = kvr.unbind(0)
+        gkvr = torch.empty_like(kvr)
+        gy = torch.empty_like(y)
+        fused.gate_backward_into(g, rl, y, gkvr[2], gy)
+        w = -torch.exp(time_decay.float())
+        u = time_first.float()
+        _gk, _gv, gtd, gtf = _ops.backward(gy, w, u, k, v, state, out=(gkvr[0], gkvr[1]))
+        return gkvr, gtd.to(time_decay.dtype), gtf.to(time_first.dtype)
+
+
 def _linear(x: Tensor, weight: Tensor) -> Tensor:
     """``F.linear(x, weight)``, on the weight's cached bf16 copy when it has one."""
     c = _CACHE.get(id(weight)) if _CACHE else None
@@ -213,6 +278,10 @@ def _linear(x: Tensor, weight: Tensor) -> Tensor:
 
 
 _BATCHED_KVR = os.environ.get("SPIKEGPT_BATCHED_KVR", "1") != "0"
+# With cached weights, the sublayers' projection gradients are produced
+# stacked (_TimeCore, _CachedPair); SPIKEGPT_STACKED_GRADS=0: separate ops
+# on unbound slices, whose gradients autograd stacks.
+_STACKED_GRADS = os.environ.get("SPIKEGPT_STACKED_GRADS", "1") != "0"
 
 
 class TimeMix(nn.Module):
@@ -251,6 +320,8 @@ class TimeMix(nn.Module):
         cached = _CACHE.get((id(self.key.weight), id(self.value.weight), id(self.receptance.weight))) if _CACHE else None
         if cached is not None:
             kvr = _CachedStacked.apply(x3.reshape(n, b * t, c), cached[0], cached[1]).reshape(n, b, t, c)
+            if _STACKED_GRADS and fused.gates_supported(kvr[0]):
+                return _linear(_TimeCore.apply(kvr, self.time_decay, self.time_first), self.output.weight)
         else:
             w3 = torch.stack([self.key.weight, self.value.weight, self.receptance.weight])
             kvr = torch.matmul(x3.reshape(n, b * t, c), w3.transpose(1, 2)).reshape(n, b, t, c)
@@ -281,6 +352,17 @@ class ChannelMix(nn.Module):
 
     def forward(self, x: Tensor) -> Tensor:
         return self.from_mixed(_shift_mix(x, self.time_mix_k), _shift_mix(x, self.time_mix_r))
+
+    def from_stacked(self, x2: Tensor) -> Tensor:
+        """The sublayer from its two mixed inputs stacked as [2, B, T, C]; with
+        cached bf16 weights (and bf16 inputs) the two projections are one
+        autograd node whose input gradient is that stacked shape."""
+        ca = _CACHE.get(id(self.key.weight)) if _CACHE else None
+        cb = _CACHE.get(id(self.receptance.weight)) if _CACHE else None
+        if not _STACKED_GRADS or ca is None or cb is None or not fused.gates_supported(x2[0]):
+            return self.from_mixed(*x2.unbind(0))
+        k, r = _CachedPair.apply(x2, ca[0], ca[1], cb[0], cb[1])
+        return fused.gate(r, _linear(fused.relu_square(k), self.value.weight))
 
     def from_mixed(self, xk: Tensor, xr: Tensor) -> Tensor:
         """The sublayer from its two token-shift-mixed inputs. The square is
@@ -349,9 +431,9 @@ class Block(nn.Module):
                 mixed = att.from_mixed(*x3.unbind(0))
             x = self._residual(x, self._lif(mixed), tok)
             tok = fused.new_residual_token(x)
-            xk, xr = fused.ln_shift_mix(x, self.ln2.weight, self.ln2.bias, [ffn.time_mix_k, ffn.time_mix_r],
-                                        self.ln2.eps, tok)
-            x = self._residual(x, self._lif(ffn.from_mixed(xk, xr)), tok)
+            x2 = fused.ln_shift_mix_stacked(x, self.ln2.weight, self.ln2.bias, [ffn.time_mix_k, ffn.time_mix_r],
+                                            self.ln2.eps, tok)
+            x = self._residual(x, self._lif(ffn.from_stacked(x2)), tok)
         else:
             x = x + self._lif(self.att(self.ln1(x)))
             x = x + self._lif(self.ffn(self.ln2(x)))

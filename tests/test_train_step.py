@@ -210,6 +210,28 @@ def test_weight_cache_matches_autocast_casts(cuda):
 
 
 @pytest.mark.gpu
+def test_stacked_gradients_match_unbound_slices(cuda, monkeypatch):
+    """With cached weights, the time-mixing core (_TimeCore) and the channel
+    mixing's paired projections (_CachedPair) write their input gradients
+    stacked; the loss and every gradient equal, bit for bit, those of the
+    separate ops on unbound slices whose gradients autograd stacks."""
+    import spikegpt_b200.model as model_mod
+
+    ids = torch.randint(0, 256, (2, 257), generator=torch.Generator(device="cpu").manual_seed(4)).to(cuda)
+    results = []
+    for stacked in (False, True):
+        monkeypatch.setattr(model_mod, "_STACKED_GRADS", stacked)
+        m = _spikegpt(cuda, 17)
+        step = TrainStep(m, torch.optim.SGD(m.parameters(), lr=0.0), (2, 256), device=cuda, graph=False)
+        assert step.cache is not None
+        loss = float(step(ids[:, :-1], ids[:, 1:]))
+        results.append((loss, [p.grad.clone() for p in m.parameters()]))
+    assert results[0][0] == results[1][0]
+    for (name, _), g0, g1 in zip(m.named_parameters(), results[0][1], results[1][1]):
+        assert torch.equal(g0, g1), name
+
+
+@pytest.mark.gpu
 def test_micro_batches_match_one_batch(cuda):
     """Two micro-batches on their own streams (replayed from the graph) give
     the one-batch step's loss and, up to the bf16 rounding of each micro-batch's
