@@ -417,8 +417,9 @@ class Block(nn.Module):
         return (torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16
                 and fused.supported(x))
 
-    def forward(self, x: Tensor) -> Tensor:
-        if self.ln0 is not None:
+    def forward(self, x: Tensor, normalized: bool = False) -> Tensor:
+        """``normalized``: x already went through this block's ln0."""
+        if self.ln0 is not None and not normalized:
             x = self.ln0(x)
         if self._fused(x):
             att, ffn = self.att, self.ffn
@@ -472,12 +473,36 @@ class SpikeGPT(nn.Module):
             raise ValueError(f"input_ids must have shape [B, T]; got {tuple(input_ids.shape)}")
         if input_ids.shape[1] > self.config.context_length:
             raise ValueError("input sequence length exceeds context_length")
-        x = self.embedding(input_ids)
-        if self.config.spike_embedding:
-            x = _HardSpike.apply(self.config.surrogate_slope * x)
-        for block in self.blocks:
+        blocks = list(self.blocks)
+        ln0 = blocks[0].ln0 if blocks else None
+        if ln0 is not None and self.config.vocab_size <= input_ids.numel():
+            # The spike and the first block's LayerNorm act row by row, so they
+            # commute with the lookup: applied to the table's V rows instead of
+            # the batch's B*T tokens (the same forward values; the backward sums
+            # the tokens' gradients per row before the LayerNorm's backward
+            # instead of after it, which also skips PyTorch's LayerNorm
+            # weight-gradient reduction over B*T rows, slow at this shape).
+            table = self.embedding.weight
+            if self.config.spike_embedding:
+                table = _HardSpike.apply(self.config.surrogate_slope * table)
+            x = blocks[0](F.embedding(input_ids, ln0(table)), normalized=True)
+            blocks = blocks[1:]
+        else:
+            x = self.embedding(input_ids)
+            if self.config.spike_embedding:
+                x = _HardSpike.apply(self.config.surrogate_slope * x)
+        for block in blocks:
             x = block(x)
-        full, v = _head(self.ln_out(x), self.head.weight)
+        if Block._fused(x):
+            # the LayerNorm-mix kernel with a mixing vector of ones is the
+            # LayerNorm, rounded to the bf16 the head's product reads (its
+            # backward also replaces PyTorch's LayerNorm weight-gradient
+            # reduction, slow at this shape)
+            ln = self.ln_out
+            h = fused.ln_shift_mix_stacked(x, ln.weight, ln.bias, [x.new_ones(x.shape[-1])], ln.eps).squeeze(0)
+        else:
+            h = self.ln_out(x)
+        full, v = _head(h, self.head.weight)
         if targets is None:
             return full[..., :v]
         if full.dtype == torch.bfloat16 and full.is_cuda:  # bf16 autocast: the fused loss, logits read in place

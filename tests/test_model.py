@@ -153,3 +153,36 @@ def test_padded_head_matches_plain_projection(cuda):
     ref.backward(go)
     assert scaled_err(out.detach().cpu().numpy(), ref.detach().cpu().numpy()) <= 1e-5
     assert scaled_err(w.grad.cpu().numpy(), w2.grad.cpu().numpy()) <= 1e-5
+
+
+def test_embedding_table_normalization_matches_per_token():
+    """The spike and the first block's LayerNorm act row by row, so with V <=
+    B*T the model applies them to the embedding table's rows before the lookup
+    (the model's forward needs CUDA; this checks the front it changes, on
+    CPU): the values equal the per-token order's bit for bit, and the
+    gradients of the table and the LayerNorm agree to float32 rounding. The
+    whole model stays pinned to the reference's by the GPU parity test."""
+    import torch.nn.functional as F
+
+    from spikegpt_b200.model import _HardSpike
+
+    model = _golden_model("cpu")
+    emb, ln0, slope = model.embedding, model.blocks[0].ln0, model.config.surrogate_slope
+    ids = torch.as_tensor(GOLDEN["ids"])[:, :-1]
+    assert model.config.vocab_size <= ids.numel()  # the model takes the table order here
+    up = torch.randn(*ids.shape, emb.weight.shape[1], generator=torch.Generator().manual_seed(3))
+
+    def run(table_order):
+        model.zero_grad(set_to_none=True)
+        if table_order:
+            x = F.embedding(ids, ln0(_HardSpike.apply(slope * emb.weight)))
+        else:
+            x = ln0(_HardSpike.apply(slope * emb(ids)))
+        (x * up).sum().backward()
+        return x.detach(), [p.grad.clone() for p in (emb.weight, ln0.weight, ln0.bias)]
+
+    (xt, gt), (xp, gp) = run(True), run(False)
+    assert torch.equal(xt, xp)
+    for a_, b_ in zip(gt, gp):
+        scale = max(float(b_.abs().max()), 1e-30)
+        assert float((a_ - b_).abs().max()) <= 1e-5 * scale
