@@ -198,7 +198,11 @@ WKV_API int lif_backward(int dtype, const void* grad_spikes, const void* x, floa
  * reduced in a fixed order through `workspace`, ln_mix_workspace_size
  * bytes). grad_residual, when non-null ([B,T,C] float32), is added to
  * grad_x (the gradient the sublayer's residual connection passes to x,
- * language.py:1353-1358), one rounded add as autograd's sum of the two. n in 1..3, C a multiple of 128 up to 1024; x, w, b, mix, grad_x
+ * language.py:1353-1358), one rounded add as autograd's sum of the two.
+ * grad_x_bf16, when non-null ([B,T,C] bf16), also receives grad_x rounded to
+ * bf16 (to nearest even): when x is the residual stream after bf16 spikes
+ * were added to it, that is the spikes' gradient, without a cast pass of its
+ * own. n in 1..3, C a multiple of 128 up to 1024; x, w, b, mix, grad_x
  * 16-byte aligned, bf16 tensors 8-byte aligned; unused output pointers null.
  */
 WKV_API size_t ln_mix_workspace_size(int n, int64_t B, int64_t T, int64_t C);
@@ -208,7 +212,7 @@ WKV_API int ln_mix_forward(int n, const float* x, const float* w, const float* b
 WKV_API int ln_mix_backward(int n, const void* grad_out0, const void* grad_out1,
                             const void* grad_out2, const float* x, const float* w, const float* b,
                             const float* mix, const float* mean, const float* rstd,
-                            const float* grad_residual, float* grad_x,
+                            const float* grad_residual, float* grad_x, void* grad_x_bf16,
                             float* grad_w, float* grad_b, float* grad_mix, void* workspace,
                             size_t workspace_bytes, int64_t B, int64_t T, int64_t C, void* stream);
 

@@ -33,7 +33,9 @@
 // (8..64) is chosen per launch so that a launch has about 8 CTAs per SM
 // whatever the batch. C is a multiple of 128, at most kMixMaxC.
 // Memory-bound: forward reads x (4 B) and writes n bf16 outputs (2n B) per
-// element; backward reads x and n gradients, writes dx.
+// element; backward reads x and n gradients, writes dx (and, on request, its
+// bf16 copy: the gradient of the bf16 spikes added to the residual stream
+// that x is, which would otherwise take a separate cast pass over dx).
 #pragma once
 
 #include "wkv_device.cuh"
@@ -56,6 +58,7 @@ struct MixArgs {
   float* mean;     // [B*T]
   float* rstd;     // [B*T]
   float* gx;       // [B*T][C]
+  __nv_bfloat16* gx16;  // [B*T][C] or null: bf16(gx) as well
   const float* gres;  // [B*T][C] or null: the residual connection's gradient, added to gx
   float* partial;  // [B*nct][2 + n][C]: dw, db, dm_0 .. dm_{n-1} per CTA
   int n, B, T, C;
@@ -309,6 +312,13 @@ __global__ void __launch_bounds__(kMixMaxC / 4, 3) ln_mix_bwd_kernel(const MixAr
     if (res)  // the skip connection's gradient, one rounded add as autograd's sum
       o = make_float4(__fadd_rn(o.x, gr.x), __fadd_rn(o.y, gr.y), __fadd_rn(o.z, gr.z), __fadd_rn(o.w, gr.w));
     *reinterpret_cast<float4*>(a.gx + r * a.C + c) = o;
+    if (a.gx16 != nullptr) {  // round to nearest, as a cast of gx would
+      __nv_bfloat162 lo = __floats2bfloat162_rn(o.x, o.y), hi = __floats2bfloat162_rn(o.z, o.w);
+      uint2 pk;
+      pk.x = *reinterpret_cast<uint32_t*>(&lo);
+      pk.y = *reinterpret_cast<uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(a.gx16 + r * a.C + c) = pk;
+    }
     hp = h;
   }
   mix_wait<0>();

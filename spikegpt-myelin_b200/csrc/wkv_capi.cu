@@ -1261,7 +1261,8 @@ int ln_mix_forward(int n, const float* x, const float* w, const float* b, const 
 
 int ln_mix_backward(int n, const void* g0, const void* g1, const void* g2, const float* x, const float* w,
                     const float* b, const float* mix, const float* mean, const float* rstd,
-                    const float* grad_residual, float* gx, float* gw, float* gb, float* gmix, void* workspace,
+                    const float* grad_residual, float* gx, void* gx_bf16, float* gw, float* gb, float* gmix,
+                    void* workspace,
                     size_t workspace_bytes, int64_t B, int64_t T, int64_t C, void* stream) {
   g_last_error[0] = '\0';
   int rc = mix_check(n, B, T, C);
@@ -1280,6 +1281,8 @@ int ln_mix_backward(int n, const void* g0, const void* g1, const void* g2, const
   if (!aligned16(x) || !aligned16(w) || !aligned16(b) || !aligned16(mix) || !aligned16(gx) ||
       !aligned16(grad_residual))
     return fail(WKV_ERR_INVALID_ARGUMENT, "x, w, b, mix, grad_residual and grad_x must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(gx_bf16) & 7u)
+    return fail(WKV_ERR_INVALID_ARGUMENT, "grad_x_bf16 must be 8-byte aligned");
   const size_t need = ln_mix_workspace_size(n, B, T, C);
   if (workspace_bytes < need || !workspace)
     return fail(WKV_ERR_WORKSPACE_TOO_SMALL, "ln_mix backward needs %zu workspace bytes, got %zu", need,
@@ -1297,6 +1300,7 @@ int ln_mix_backward(int n, const void* g0, const void* g1, const void* g2, const
   a.mean = const_cast<float*>(mean);
   a.rstd = const_cast<float*>(rstd);
   a.gx = gx;
+  a.gx16 = static_cast<__nv_bfloat16*>(gx_bf16);
   a.gres = grad_residual;
   a.partial = static_cast<float*>(workspace);
   a.n = n;

@@ -87,7 +87,7 @@ def lib() -> ctypes.CDLL:
         handle.ln_mix_workspace_size.restype = sz
         handle.ln_mix_forward.argtypes = [ci, vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, f32, vp]
         handle.ln_mix_forward.restype = ci
-        handle.ln_mix_backward.argtypes = [ci, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
+        handle.ln_mix_backward.argtypes = [ci, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                            sz, i64, i64, i64, vp]
         handle.ln_mix_backward.restype = ci
         handle.gate_forward.argtypes = [vp, vp, vp, i64, vp]

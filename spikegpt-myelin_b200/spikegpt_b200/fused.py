@@ -44,6 +44,12 @@ def supported(x: Tensor) -> bool:
 # outside torch.compile, and for an x that requires grad; everywhere else the
 # token is 0 and residual_add returns x's gradient itself.
 _RESIDUAL_GRADS: dict[int, Tensor] = {}
+# ln_shift_mix backwards run inside residual_handoff() also write bf16(grad x),
+# keyed by id(grad x), for the residual_add backward that receives grad x as its
+# output gradient (the bf16 spikes' gradient; no separate cast pass). Entries
+# nothing takes (an x that is not a residual_add's output) are dropped with
+# the handed-over skip gradients.
+_BF16_GRADS: dict[int, tuple[Tensor, Tensor]] = {}
 _TOKENS = itertools.count(1)
 _HANDOFF = threading.local()
 
@@ -79,6 +85,7 @@ def pending_residual_grads() -> int:
 
 def drop_residual_grads() -> None:
     _RESIDUAL_GRADS.clear()
+    _BF16_GRADS.clear()
 
 
 @torch.library.custom_op("spikegpt_b200::ln_shift_mix", mutates_args=(), device_types="cuda")
@@ -108,11 +115,15 @@ def _(x, weight, bias, mix, eps, token):
 
 @torch.library.custom_op("spikegpt_b200::ln_shift_mix_backward", mutates_args=(), device_types="cuda")
 def _ln_shift_mix_backward(grads: list[Tensor], x: Tensor, weight: Tensor, bias: Tensor, mix: Tensor,
-                           mean: Tensor, rstd: Tensor, grad_residual: Tensor | None) -> list[Tensor]:
+                           mean: Tensor, rstd: Tensor, grad_residual: Tensor | None,
+                           bf16_copy: bool = False) -> list[Tensor]:
+    """[grad x, grad weight, grad bias, grad mix, bf16(grad x) when ``bf16_copy``
+    (else an empty tensor)]."""
     b, t, c = x.shape
     n = mix.shape[0]
     gs = [g.to(torch.bfloat16).contiguous() for g in grads]
     gx = torch.empty_like(x)
+    gx16 = torch.empty(x.shape if bf16_copy else (0,), dtype=torch.bfloat16, device=x.device)
     gw = torch.empty_like(weight)
     gb = torch.empty_like(bias)
     gm = torch.empty_like(mix)
@@ -123,17 +134,19 @@ def _ln_shift_mix_backward(grads: list[Tensor], x: Tensor, weight: Tensor, bias:
     _capi.check(
         lib.ln_mix_backward(n, *ptrs, x.data_ptr(), weight.data_ptr(), bias.data_ptr(), mix.data_ptr(),
                             mean.data_ptr(), rstd.data_ptr(),
-                            None if grad_residual is None else grad_residual.data_ptr(), gx.data_ptr(), gw.data_ptr(), gb.data_ptr(),
+                            None if grad_residual is None else grad_residual.data_ptr(), gx.data_ptr(),
+                            gx16.data_ptr() if bf16_copy else None, gw.data_ptr(), gb.data_ptr(),
                             gm.data_ptr(), ws.data_ptr(), nws, b, t, c,
                             torch.cuda.current_stream(x.device).cuda_stream),
         "ln_mix_backward",
     )
-    return [gx, gw, gb, gm]
+    return [gx, gw, gb, gm, gx16]
 
 
 @_ln_shift_mix_backward.register_fake
-def _(grads, x, weight, bias, mix, mean, rstd, grad_residual):
-    return [torch.empty_like(x), torch.empty_like(weight), torch.empty_like(bias), torch.empty_like(mix)]
+def _(grads, x, weight, bias, mix, mean, rstd, grad_residual, bf16_copy=False):
+    return [torch.empty_like(x), torch.empty_like(weight), torch.empty_like(bias), torch.empty_like(mix),
+            x.new_empty(x.shape if bf16_copy else (0,), dtype=torch.bfloat16)]
 
 
 def _setup(ctx, inputs, output):
@@ -141,6 +154,9 @@ def _setup(ctx, inputs, output):
     ctx.save_for_backward(x, weight, bias, mix, output[1], output[2])
     ctx.n = mix.shape[0]
     ctx.token = token
+    # inside residual_handoff(): x is normally the residual stream right after
+    # a residual_add, whose backward then takes the bf16 copy of grad x
+    ctx.bf16_copy = bool(getattr(_HANDOFF, "on", False)) and not torch.compiler.is_compiling()
     ctx.mark_non_differentiable(output[1], output[2])
 
 
@@ -153,7 +169,10 @@ def _backward(ctx, grads):
     gres = _RESIDUAL_GRADS.pop(ctx.token, None) if ctx.token else None
     if gres is not None:
         gres = _aligned(gres.float())
-    gx, gw, gb, gm = torch.ops.spikegpt_b200.ln_shift_mix_backward(gouts, x, weight, bias, mix, mean, rstd, gres)
+    gx, gw, gb, gm, gx16 = torch.ops.spikegpt_b200.ln_shift_mix_backward(gouts, x, weight, bias, mix, mean, rstd,
+                                                                         gres, ctx.bf16_copy)
+    if ctx.bf16_copy:
+        _BF16_GRADS[id(gx)] = (gx, gx16)
     return gx, gw, gb, gm, None, None
 
 
@@ -340,10 +359,14 @@ def _resid_setup(ctx, inputs, output):
 
 
 def _resid_grad(ctx, grad):
+    # the spikes' gradient: bf16(grad), already made by the ln_shift_mix
+    # backward that produced grad when there is one
+    made = _BF16_GRADS.pop(id(grad), None)
+    g16 = made[1] if made is not None and made[0] is grad else grad.to(torch.bfloat16)
     if ctx.token:  # the paired ln_shift_mix adds it to grad x in its kernel
         _RESIDUAL_GRADS[ctx.token] = grad
-        return None, grad.to(torch.bfloat16), None
-    return grad, grad.to(torch.bfloat16), None
+        return None, g16, None
+    return grad, g16, None
 
 
 _residual_add.register_autograd(_resid_grad, setup_context=_resid_setup)

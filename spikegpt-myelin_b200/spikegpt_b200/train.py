@@ -252,6 +252,7 @@ class TrainStep:
         if fused.pending_residual_grads():
             fused.drop_residual_grads()
             raise RuntimeError("TrainStep: a residual gradient was handed over but never consumed")
+        fused.drop_residual_grads()  # bf16 grad-x copies no residual_add took (the first sublayer's)
         if self.cache is not None:
             if self.side is not None:  # the weight gradients written on the side stream
                 torch.cuda.current_stream(self.device).wait_stream(self.side)

@@ -121,6 +121,47 @@ def test_residual_gradient_summed_in_kernel(cuda):
     assert fused.pending_residual_grads() == 0  # every handed-over gradient was consumed
 
 
+def test_bf16_grad_copy_is_the_cast(cuda):
+    """Asked for it, the LayerNorm-mix backward also writes grad x rounded to
+    bf16, bit for bit grad_x.to(bfloat16); inside residual_handoff() the
+    residual_add whose output is x takes it as the spikes' gradient, which then
+    equals the eager cast of that add's output gradient."""
+    from spikegpt_b200 import fused
+
+    g = torch.Generator(device="cpu").manual_seed(23)
+    shape = (2, 130, 512)
+    x = torch.randn(shape, generator=g).to(cuda)
+    w = (1 + 0.3 * torch.randn(512, generator=g)).to(cuda)
+    b = (0.2 * torch.randn(512, generator=g)).to(cuda)
+    mix = torch.rand(3, 512, generator=g).to(cuda)
+    stacked, mean, rstd = torch.ops.spikegpt_b200.ln_shift_mix(x, w, b, mix, 1e-5, 0)
+    gouts = [torch.randn(shape, generator=g).to(cuda).to(torch.bfloat16) for _ in range(3)]
+    gres = torch.randn(shape, generator=g).to(cuda)
+    for res in (None, gres):
+        gx, _, _, _, gx16 = torch.ops.spikegpt_b200.ln_shift_mix_backward(gouts, x, w, b, mix, mean, rstd, res, True)
+        assert torch.equal(gx16, gx.to(torch.bfloat16))
+        gx_plain, *_, empty = torch.ops.spikegpt_b200.ln_shift_mix_backward(gouts, x, w, b, mix, mean, rstd, res)
+        assert torch.equal(gx_plain, gx) and empty.numel() == 0
+
+    # through autograd: spikes -> residual_add -> ln_shift_mix
+    x0 = torch.randn(shape, generator=g).to(cuda)
+    s0 = (torch.rand(shape, generator=g) < 0.3).to(torch.bfloat16).to(cuda)
+    m = [torch.rand(1, 1, 512, generator=g).to(cuda) for _ in range(2)]
+    go = [torch.randn(shape, generator=g).to(cuda).to(torch.bfloat16) for _ in range(2)]
+
+    def run(handoff):
+        spikes = s0.clone().requires_grad_()
+        with fused.residual_handoff() if handoff else contextlib.nullcontext():
+            out = fused.residual_add(x0, spikes, 0)
+            xk, xr = fused.ln_shift_mix(out, w, b, m, 1e-5, 0)
+            torch.autograd.backward([xk, xr], go)
+        fused.drop_residual_grads()
+        return spikes.grad
+
+    ga, gb = run(True), run(False)
+    assert ga.dtype == torch.bfloat16 and torch.equal(ga, gb)
+
+
 def test_residual_token_only_inside_the_handoff_context(cuda):
     """Outside residual_handoff(), for inputs without grad, and under
     torch.compile no token is handed out, so a partial backward
