@@ -29,6 +29,8 @@
 // bytes per element, backward 3 *.
 #pragma once
 
+#include <type_traits>
+
 #include "wkv_kernels.cuh"
 
 namespace wkv {
@@ -356,6 +358,176 @@ __global__ void __launch_bounds__(32 * kLifWarps, 1) lif_fwd_kernel(const LifArg
     }
   }
   if (kTma) bulk_wait_all();
+}
+
+// ------------------------------------------------ time-segmented forward
+//
+// With few sequences the forward above leaves most SMs idle: one warp per
+// (64-channel block, batch row) and a serial chain of T steps, so the launch
+// takes T steps of one warp's arithmetic whatever the batch. The segmented
+// forward gives a CTA of nseg warps one (block, row); warp j takes the
+// sub-tiles [j ls, (j+1) ls) (ls sub-tiles of kSub steps, the last segment
+// shorter) and the result is the sequential forward's, bit for bit, whatever
+// the input:
+//  A. every warp runs its segment from the membrane 0 (warp 0 from the true
+//     start, which is 0), writing spikes and checkpoints, and leaves its end
+//     membrane in shared memory;
+//  B. warp j >= 1 reruns its segment from the end membrane of segment j-1,
+//     writing nothing, until each channel's membrane at a sub-tile boundary
+//     equals, bit for bit, the checkpoint pass A left there. From that
+//     boundary on the two runs are the same computation: a spike sets the
+//     membrane to the constant reset * decay, and with decay < 1 a difference
+//     that no spike removes shrinks below the rounding within a few dozen
+//     steps;
+//  V. warp 0 walks the segments in order, per channel: where the start pass
+//     B used is the true end of the previous segment, pass B's convergence
+//     point and end hold; where it is not (the previous segment never
+//     converged), it reruns the segment from the true start itself;
+//  C. warp j >= 1 reruns its segment from the true start up to the last
+//     boundary at which a channel of its block had not converged, rewriting
+//     those sub-tiles' spikes and checkpoints (converged channels write the
+//     values pass A wrote).
+// Needs the checkpoints (state != null), whole sub-tiles (T % kSub == 0) and
+// whole 64-channel blocks (C % 64 == 0, 4-byte aligned pairs).
+constexpr int kLifSegMax = 8;
+
+template <typename T>
+__device__ __forceinline__ void lif_seg_load(typename Pair<T>::raw (&xin)[kSub], const T* xg, size_t ld) {
+#pragma unroll
+  for (int i = 0; i < kSub; ++i) xin[i] = Pair<T>::ld(xg + i * ld);
+}
+
+// kSub steps from m (the membrane entering them times decay); spikes to sg
+// (row stride ld) when kWrite. Returns m after the sub-tile.
+template <bool kWrite, bool kPlain, typename T>
+__device__ __forceinline__ f2 lif_seg_run(f2 m, const typename Pair<T>::raw (&xin)[kSub], T* sg, size_t ld,
+                                          const LifK& k) {
+#pragma unroll
+  for (int i = 0; i < kSub; ++i) {
+    uint32_t w0, w1;
+    f2 vn;
+    lif_step<T, kPlain>(m, Pair<T>::unpack(xin[i]), k, vn, w0, w1);
+    if constexpr (kWrite) {
+      if constexpr (sizeof(T) == 2) *reinterpret_cast<uint32_t*>(sg + i * ld) = w0;
+      else *reinterpret_cast<uint2*>(sg + i * ld) = make_uint2(w0, w1);
+    }
+  }
+  return m;
+}
+
+__device__ __forceinline__ bool lif_same(float a, float b) { return __float_as_uint(a) == __float_as_uint(b); }
+
+template <typename T, bool kPlain>
+__global__ void __launch_bounds__(32 * kLifSegMax) lif_fwd_seg_kernel(const LifArgs a, int nseg, int ls) {
+  using raw = typename Pair<T>::raw;
+  __shared__ f2 s_end[kLifSegMax][32];     // pass A: end membrane (times decay) per segment and lane
+  __shared__ f2 s_endb[kLifSegMax][32];    // pass B: end membrane
+  __shared__ int2 s_conv[kLifSegMax][32];  // pass B, then V: sub-tiles to recompute per channel
+  __shared__ f2 s_start[kLifSegMax][32];   // V: true start membrane
+  const int w = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int cb = blockIdx.x % a.ncblk, b = blockIdx.x / a.ncblk;
+  const int c = cb * kLanes + 2 * lane;
+  const LifK k = lif_constants(a);
+  const size_t ld = (size_t)a.C;
+  const int ntiles = a.T / kSub;
+  const T* xrow = static_cast<const T*>(a.x) + (size_t)b * a.T * ld + c;
+  T* srow = static_cast<T*>(a.s) + (size_t)b * a.T * ld + c;
+  float* state = a.state + (size_t)b * a.ntiles * ld + c;
+  auto seg_begin = [&](int j) { return min(ntiles, j * ls); };
+  auto ckpt = [&](int q) { return reinterpret_cast<f2*>(state + (size_t)q * ld); };
+
+  // Runs sub-tiles [q0, q1) from m with the next sub-tile's loads in flight;
+  // kWrite: checkpoints and spikes written.
+  auto sweep = [&](auto write_tag, f2 m, int q0, int q1) {
+    constexpr bool kWrite = decltype(write_tag)::value;
+    raw cur[kSub], nxt[kSub];
+    if (q0 < q1) lif_seg_load<T>(cur, xrow + (size_t)q0 * kSub * ld, ld);
+#pragma unroll 1
+    for (int q = q0; q < q1; ++q) {
+      if (q + 1 < q1) lif_seg_load<T>(nxt, xrow + (size_t)(q + 1) * kSub * ld, ld);
+      if constexpr (kWrite) *ckpt(q) = m;
+      m = lif_seg_run<kWrite, kPlain, T>(m, cur, srow + (size_t)q * kSub * ld, ld, k);
+#pragma unroll
+      for (int i = 0; i < kSub; ++i) cur[i] = nxt[i];
+    }
+    return m;
+  };
+  using WriteOn = std::integral_constant<bool, true>;
+  using WriteOff = std::integral_constant<bool, false>;
+
+  // Reruns segment j from m0 without writing, comparing each boundary with
+  // pass A's membrane there; returns the end membrane and, per channel, the
+  // sub-tiles before the first agreeing boundary (the segment's length when
+  // none agrees). Every lane runs until its own channels agree.
+  auto converge = [&](int j, f2 m0, int2& conv) {
+    const int q0 = seg_begin(j), q1 = seg_begin(j + 1), n = q1 - q0;
+    const f2 g = *ckpt(q0);  // pass A's start (the guess)
+    conv = make_int2(lif_same(m0.x, g.x) ? 0 : n, lif_same(m0.y, g.y) ? 0 : n);
+    f2 m = m0;
+    raw cur[kSub], nxt[kSub];
+    if (n > 0) lif_seg_load<T>(cur, xrow + (size_t)q0 * kSub * ld, ld);
+#pragma unroll 1
+    for (int i = 0; i < n && (conv.x == n || conv.y == n); ++i) {
+      const int q = q0 + i;
+      if (i + 1 < n) lif_seg_load<T>(nxt, xrow + (size_t)(q + 1) * kSub * ld, ld);
+      const f2 ref = i + 1 < n ? *ckpt(q + 1) : s_end[j][lane];
+      m = lif_seg_run<false, kPlain, T>(m, cur, nullptr, ld, k);
+      if (conv.x == n && lif_same(m.x, ref.x)) conv.x = i + 1;
+      if (conv.y == n && lif_same(m.y, ref.y)) conv.y = i + 1;
+#pragma unroll
+      for (int r = 0; r < kSub; ++r) cur[r] = nxt[r];
+    }
+    // a converged channel ends where pass A ended
+    const f2 ea = s_end[j][lane];
+    return f2{conv.x < n ? ea.x : m.x, conv.y < n ? ea.y : m.y};
+  };
+
+  // A
+  if (w < nseg) {
+    const f2 m = sweep(WriteOn{}, k.zero, seg_begin(w), seg_begin(w + 1));
+    s_end[w][lane] = m;
+  }
+  __syncthreads();
+  // B
+  if (w >= 1 && w < nseg) {
+    int2 conv;
+    s_endb[w][lane] = converge(w, s_end[w - 1][lane], conv);
+    s_conv[w][lane] = conv;
+  }
+  __syncthreads();
+  // V
+  if (w == 0) {
+    f2 te = s_end[0][lane];  // the true end of segment 0
+#pragma unroll 1
+    for (int j = 1; j < nseg; ++j) {
+      const f2 used = s_end[j - 1][lane];
+      s_start[j][lane] = te;
+      int2 conv = s_conv[j][lane];
+      f2 e = s_endb[j][lane];
+      if (!lif_same(used.x, te.x) || !lif_same(used.y, te.y)) {  // rerun from the true start
+        int2 c2;
+        const f2 e2 = converge(j, te, c2);
+        if (!lif_same(used.x, te.x)) {
+          conv.x = c2.x;
+          e.x = e2.x;
+        }
+        if (!lif_same(used.y, te.y)) {
+          conv.y = c2.y;
+          e.y = e2.y;
+        }
+        s_conv[j][lane] = conv;
+      }
+      te = e;
+    }
+  }
+  __syncthreads();
+  // C
+  if (w >= 1 && w < nseg) {
+    const int2 conv = s_conv[w][lane];
+    const int n = __reduce_max_sync(kFull, max(conv.x, conv.y));
+    const int q0 = seg_begin(w);
+    sweep(WriteOn{}, s_start[w][lane], q0, q0 + n);
+  }
 }
 
 // Backward on the generic path (unaligned tensors), last sub-tile first,

@@ -1025,6 +1025,40 @@ void lif_fwd_go(const LifArgs& a, const CUtensorMap& mx, const CUtensorMap& ms, 
   lif_fwd_kernel<IO, kTma, kPlain><<<grid, 32 * kLifWarps, sm, st>>>(a, mx, ms);
 }
 
+// Segments of the time-segmented LIF forward (lif_fwd_seg_kernel), 1 for the
+// sequential one: with the checkpoints requested, whole 16-step sub-tiles and
+// whole 64-channel blocks on the aligned path, and decay <= 0.75 (tau <= 4:
+// a membrane difference no spike removes falls below the rounding within
+// about four sub-tiles, so the repair passes stay short; with a decay near 1
+// segments often fail to converge and their repair runs in sequence), and
+// at most 256 (block, row) units (the sequential forward then runs fewer
+// than half a warp per scheduler; above that it is left as measured), as
+// many segments (up to kLifSegMax, each at least 4 sub-tiles) as keep a
+// launch within 2048 warps (about 3.5 a scheduler). force_segments of
+// wkv_set_debug_overrides fixes the count whatever the decay (1: the
+// sequential forward). `ls` = sub-tiles a segment (the last one shorter); no
+// segment is empty.
+int lif_fwd_segments(const LifArgs& a, bool tma, int& ls) {
+  ls = 0;
+  if (!tma || a.state == nullptr || a.C % kLanes != 0 || a.T % kSub != 0) return 1;
+  if (g_force_segments.load() <= 0 && !(a.decay <= 0.75f)) return 1;
+  const int ntiles = a.T / kSub;
+  const int forced = g_force_segments.load();
+  int n = kLifSegMax;
+  if (forced > 0) {
+    n = std::min(forced, kLifSegMax);
+  } else {
+    const int64_t units = (int64_t)a.ncblk * a.B;
+    if (units > 256) return 1;
+    while (n > 1 && units * n > 2048) n /= 2;
+    n = std::min(n, ntiles / 4);
+  }
+  n = std::min(n, ntiles);
+  if (n < 2) return 1;
+  ls = (ntiles + n - 1) / n;
+  return (ntiles + ls - 1) / ls;
+}
+
 template <typename IO>
 int lif_launch_forward(LifArgs& a, bool tma, cudaStream_t st) {
   const int dt = sizeof(IO) == 4 ? WKV_DTYPE_F32
@@ -1038,6 +1072,17 @@ int lif_launch_forward(LifArgs& a, bool tma, cudaStream_t st) {
               (rc = make_map(&ms, dt, a.s, a.B, a.T, a.C, lif_rows<IO>()))))
     return rc;
   const bool plain = lif_plain_test(a);
+  int ls = 0;
+  const int fseg = lif_fwd_segments(a, tma, ls);
+  if (fseg > 1) {
+    const unsigned grid = (unsigned)((int64_t)a.ncblk * a.B);
+    launch(K_LIF_FWD, st, [&] {
+      if (plain) lif_fwd_seg_kernel<IO, true><<<grid, 32 * fseg, 0, st>>>(a, fseg, ls);
+      else lif_fwd_seg_kernel<IO, false><<<grid, 32 * fseg, 0, st>>>(a, fseg, ls);
+    });
+    const cudaError_t le = cudaGetLastError();
+    return le == cudaSuccess ? WKV_OK : cuda_fail(le, "LIF forward launch");
+  }
   const size_t sm = kLifWarps * lif_fwd_smem_bytes();
   cudaError_t e = tma ? (plain ? allow_smem(lif_fwd_kernel<IO, true, true>, sm)
                                : allow_smem(lif_fwd_kernel<IO, true, false>, sm))

@@ -232,3 +232,59 @@ def test_segmented_non_finite_inputs(cuda):
     np.testing.assert_array_equal(np.isnan(gx), np.isnan(gx_ref))
     ok = ~np.isnan(gx_ref)
     assert scaled_err(gx[ok], gx_ref[ok]) <= TOL_FP32
+
+
+def _lif_forward_capi(x, segments, tau, threshold=1.0, reset=0.0, slope=2.0):
+    """Spikes and checkpoints ([B, ceil(T/16), C] float32, the part of the
+    state buffer the forward writes) of lif_forward with the segment count
+    forced (1: the sequential forward)."""
+    code = {torch.float32: _capi.DTYPE_F32, torch.bfloat16: _capi.DTYPE_BF16}[x.dtype]
+    b, t, c = x.shape
+    lib = _capi.lib()
+    spikes = torch.empty_like(x)
+    _capi.set_debug_overrides(force_segments=segments)
+    try:
+        nbytes = int(lib.lif_state_size(code, b, t, c))  # under the override, as lif_forward checks it
+        state = torch.empty(nbytes // 4, dtype=torch.float32, device=x.device)
+        _capi.check(lib.lif_forward(code, x.data_ptr(), spikes.data_ptr(), state.data_ptr(), nbytes, b, t, c, tau,
+                                    threshold, reset, slope, torch.cuda.current_stream(x.device).cuda_stream),
+                    "lif_forward")
+        torch.cuda.synchronize()
+    finally:
+        _capi.set_debug_overrides()
+    return spikes, state[:b * (-(-t // 16)) * c].clone()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("case", ["tau2", "tau100", "no_spikes_tau100", "non_finite"])
+def test_time_segmented_forward_matches_sequential(cuda, dtype, case):
+    """The time-segmented forward (speculated segments, repaired up to the
+    first sub-tile boundary where the membranes agree) gives the sequential
+    forward's spikes and checkpoints bit for bit: with fast decay (segments
+    converge in a sub-tile or two), slow decay and no spikes (segments never
+    converge, so the repair runs through every segment in order), and with
+    non-finite currents."""
+    rng = np.random.default_rng(31)
+    shape = (3, 1024, 128)
+    x = (rng.standard_normal(shape) * 1.5).astype(np.float32)
+    tau = 2.0
+    if case in ("tau100", "no_spikes_tau100"):
+        tau = 100.0
+    if case == "no_spikes_tau100":
+        x[:] = 0.0
+        x[:, 0] = 0.9  # below threshold: a membrane that decays and never spikes
+    if case == "non_finite":
+        x[0, 100, 3] = np.inf
+        x[1, 300, 5] = np.nan
+        x[2, 700, 7] = -np.inf
+    xt = torch.as_tensor(x).to(device=cuda, dtype=dtype)
+    bits = torch.int16 if dtype == torch.bfloat16 else torch.int32
+    s_seq, st_seq = _lif_forward_capi(xt, 1, tau)
+    for segments in (0, 3, 8):  # 0: the automatic choice (segmented at tau 2, sequential at tau 100)
+        s_seg, st_seg = _lif_forward_capi(xt, segments, tau)
+        assert torch.equal(s_seg.view(bits), s_seq.view(bits)), segments
+        assert torch.equal(st_seg.view(torch.int32), st_seq.view(torch.int32)), segments
+    if tau == 2.0:
+        s_ref = oracle.lif_forward(xt.double().cpu().numpy(), dtype=np.float32, tau=tau, threshold=1.0, reset=0.0,
+                                   slope=2.0)
+        np.testing.assert_array_equal(s_seq.double().cpu().numpy(), s_ref)
