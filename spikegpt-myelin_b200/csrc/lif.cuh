@@ -25,7 +25,10 @@
 // are the unit of computation and of the checkpoints the forward stores (the
 // membrane entering each sub-tile times decay, [B][ceil(T/kSub)][C] float32)
 // and the backward recomputes from, last sub-tile first. The generic path (unaligned tensors) stages kSub-row tiles
-// with plain loads and stores. Memory-bound target: forward 2 * sizeof(T)
+// with plain loads and stores. With few sequences the forward instead splits
+// T into segments run at once and repaired where their speculated starts were
+// wrong (lif_fwd_seg_kernel, below), and the backward splits T into segments
+// joined by affine adjoint maps. Memory-bound target: forward 2 * sizeof(T)
 // bytes per element, backward 3 *.
 #pragma once
 
