@@ -316,7 +316,8 @@ WKV_API int wkv_plan(int dtype, int64_t B, int64_t T, int64_t C, int* tma, int* 
 
 /*
  * Test and benchmark hooks (process-wide; no reference counterpart).
- * force_segments > 0 fixes the segment count; force_generic != 0 disables the
+ * force_segments > 0 fixes the segment count (of the WKV plan, the LIF
+ * backward and the LIF forward; 1 = the sequential forms); force_generic != 0 disables the
  * TMA path; force_slow != 0 makes every sub-chunk take the exact per-step
  * rescaling path. Pass zeros to restore the defaults.
  */
