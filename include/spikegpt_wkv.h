@@ -177,6 +177,17 @@ WKV_API int wkv_step(int dtype, int state_dtype, const void* key, const void* va
  * float32 rounding.
  */
 WKV_API size_t lif_state_size(int dtype, int64_t B, int64_t T, int64_t C);
+/*
+ * The segment counts lif_forward and lif_backward pick for a shape (no
+ * reference counterpart; like wkv_plan, it exposes a choice the reference
+ * never makes), for 16-byte aligned tensors. forward_segments: 1 = the
+ * sequential forward; > 1 = the time-segmented forward (few sequences, T a
+ * multiple of 16, C a multiple of 64, with_state != 0 (the checkpoints
+ * requested, as autograd does), tau <= 4), whose results equal the
+ * sequential forward's bit for bit. backward_segments as described above.
+ */
+WKV_API int lif_plan(int dtype, int64_t B, int64_t T, int64_t C, float tau, int with_state,
+                     int* forward_segments, int* backward_segments);
 WKV_API int lif_forward(int dtype, const void* x, void* spikes, float* state, size_t state_bytes,
                         int64_t B, int64_t T, int64_t C, float tau, float threshold, float reset,
                         float slope, void* stream);

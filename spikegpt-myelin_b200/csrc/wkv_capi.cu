@@ -993,8 +993,9 @@ size_t lif_state_size(int dtype, int64_t B, int64_t T, int64_t C) {
 
 namespace {
 
+// with_device = false: the shape and constants only (no CUDA call; for plans)
 int lif_prepare(int dtype, int64_t B, int64_t T, int64_t C, float tau, float threshold,
-                float reset, float slope, LifArgs& a) {
+                float reset, float slope, LifArgs& a, bool with_device = true) {
   int rc = check_dims(dtype, B, T, C);
   if (rc) return rc;
   if (!(tau > 0.f)) return fail(WKV_ERR_INVALID_ARGUMENT, "tau must be positive");
@@ -1008,7 +1009,7 @@ int lif_prepare(int dtype, int64_t B, int64_t T, int64_t C, float tau, float thr
   a.C = (int)C;
   a.ncblk = (int)((C + kLanes - 1) / kLanes);
   a.ntiles = (int)((T + kSub - 1) / kSub);
-  a.err = device_err_ptr();
+  a.err = with_device ? device_err_ptr() : nullptr;
   return WKV_OK;
 }
 
@@ -1038,9 +1039,9 @@ void lif_fwd_go(const LifArgs& a, const CUtensorMap& mx, const CUtensorMap& ms, 
 // wkv_set_debug_overrides fixes the count whatever the decay (1: the
 // sequential forward). `ls` = sub-tiles a segment (the last one shorter); no
 // segment is empty.
-int lif_fwd_segments(const LifArgs& a, bool tma, int& ls) {
+int lif_fwd_segments(const LifArgs& a, bool tma, bool with_state, int& ls) {
   ls = 0;
-  if (!tma || a.state == nullptr || a.C % kLanes != 0 || a.T % kSub != 0) return 1;
+  if (!tma || !with_state || a.C % kLanes != 0 || a.T % kSub != 0) return 1;
   if (g_force_segments.load() <= 0 && !(a.decay <= 0.75f)) return 1;
   const int ntiles = a.T / kSub;
   const int forced = g_force_segments.load();
@@ -1073,7 +1074,7 @@ int lif_launch_forward(LifArgs& a, bool tma, cudaStream_t st) {
     return rc;
   const bool plain = lif_plain_test(a);
   int ls = 0;
-  const int fseg = lif_fwd_segments(a, tma, ls);
+  const int fseg = lif_fwd_segments(a, tma, a.state != nullptr, ls);
   if (fseg > 1) {
     const unsigned grid = (unsigned)((int64_t)a.ncblk * a.B);
     launch(K_LIF_FWD, st, [&] {
@@ -1190,6 +1191,20 @@ int lif_forward(int dtype, const void* x, void* spikes, float* state, size_t sta
     case WKV_DTYPE_BF16: return lif_launch_forward<__nv_bfloat16>(a, tma, st);
     default: return lif_launch_forward<__half>(a, tma, st);
   }
+}
+
+int lif_plan(int dtype, int64_t B, int64_t T, int64_t C, float tau, int with_state, int* forward_segments,
+             int* backward_segments) {
+  g_last_error[0] = '\0';
+  LifArgs a;
+  const int rc = lif_prepare(dtype, B, T, C, tau, 1.f, 0.f, 1.f, a, false);
+  if (rc) return rc;
+  const bool tma = (C * (int64_t)dtype_size(dtype)) % 16 == 0;  // aligned tensors assumed
+  int ls = 0, per = 0;
+  if (forward_segments)
+    *forward_segments = (B == 0 || T == 0 || C == 0) ? 1 : lif_fwd_segments(a, tma, with_state != 0, ls);
+  if (backward_segments) *backward_segments = lif_bwd_segments(dtype, B, T, C, &per);
+  return WKV_OK;
 }
 
 int lif_backward(int dtype, const void* grad_spikes, const void* x, float* state,

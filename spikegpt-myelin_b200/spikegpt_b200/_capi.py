@@ -79,6 +79,8 @@ def lib() -> ctypes.CDLL:
         f32 = ctypes.c_float
         handle.lif_state_size.argtypes = [ci, i64, i64, i64]
         handle.lif_state_size.restype = sz
+        handle.lif_plan.argtypes = [ci, i64, i64, i64, f32, ci, ctypes.POINTER(ci), ctypes.POINTER(ci)]
+        handle.lif_plan.restype = ci
         handle.lif_forward.argtypes = [ci, vp, vp, vp, sz, i64, i64, i64, f32, f32, f32, f32, vp]
         handle.lif_forward.restype = ci
         handle.lif_backward.argtypes = [ci, vp, vp, vp, sz, vp, i64, i64, i64, f32, f32, f32, f32, vp]
@@ -157,6 +159,15 @@ def plan(dtype_code: int, b: int, t: int, c: int) -> tuple[bool, int]:
     tma, seg = ctypes.c_int(0), ctypes.c_int(0)
     check(lib().wkv_plan(dtype_code, b, t, c, ctypes.byref(tma), ctypes.byref(seg)), "wkv_plan")
     return bool(tma.value), int(seg.value)
+
+
+def lif_plan(dtype_code: int, b: int, t: int, c: int, tau: float = 2.0, with_state: bool = True) -> tuple[int, int]:
+    """(forward segments, backward segments) the LIF op picks for a shape
+    (aligned tensors; 1 = the sequential form)."""
+    fwd, bwd = ctypes.c_int(0), ctypes.c_int(0)
+    check(lib().lif_plan(dtype_code, b, t, c, float(tau), int(with_state), ctypes.byref(fwd), ctypes.byref(bwd)),
+          "lif_plan")
+    return int(fwd.value), int(bwd.value)
 
 
 def set_debug_overrides(force_segments: int = 0, force_generic: bool = False, force_slow: bool = False) -> None:

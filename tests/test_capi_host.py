@@ -105,3 +105,29 @@ def test_plan_follows_the_measured_segment_choice(b, t, nseg):
     """The segment counts the plan picks on a 148-SM device (the host fallback
     here) at the swept shapes (C = 512, bf16)."""
     assert _capi.plan(1, b, t, 512) == (True, nseg)
+
+
+def test_lif_plan_segments_the_forward_for_few_sequences():
+    """The LIF forward runs time-segmented only with few (64-channel block,
+    row) units, T a multiple of 16, C a multiple of 64, the checkpoints
+    requested and tau <= 4; it stays sequential at 64 sequences of 512
+    channels (the one-GPU SpikeGPT-41M step)."""
+    bf16, f32 = _capi.DTYPE_BF16, _capi.DTYPE_F32
+    assert _capi.lif_plan(bf16, 64, 1024, 512)[0] == 1
+    assert _capi.lif_plan(bf16, 8, 1024, 512)[0] == 8  # the 8-GPU share of global batch 64
+    assert _capi.lif_plan(bf16, 32, 1024, 512)[0] == 8  # 256 units: the largest segmented case
+    assert _capi.lif_plan(bf16, 33, 1024, 512)[0] == 1
+    assert _capi.lif_plan(f32, 4, 512, 256)[0] == 8
+    assert _capi.lif_plan(bf16, 8, 1000, 512)[0] == 1  # T not a multiple of 16
+    assert _capi.lif_plan(bf16, 8, 1024, 72)[0] == 1  # a partial channel block
+    assert _capi.lif_plan(bf16, 8, 1024, 512, tau=100.0)[0] == 1  # slow decay
+    assert _capi.lif_plan(bf16, 8, 1024, 512, with_state=False)[0] == 1  # no checkpoints (no grad)
+    assert _capi.lif_plan(bf16, 8, 48, 512)[0] == 1  # under 4 sub-tiles a segment
+    _capi.set_debug_overrides(force_segments=3)
+    try:
+        assert _capi.lif_plan(bf16, 64, 1024, 512)[0] == 3
+        assert _capi.lif_plan(bf16, 8, 1024, 512, tau=100.0)[0] == 3
+    finally:
+        _capi.set_debug_overrides()
+    with pytest.raises(_capi.WKVError):
+        _capi.lif_plan(bf16, 8, 1024, 512, tau=0.0)
