@@ -106,3 +106,27 @@ def test_dropin_install_aliases_reference_module_names(monkeypatch):
     assert sys.modules["spikegpt.wkv_bf16"] is wkv_bf16
     assert wkv.weighted_key_value_triton is wkv.weighted_key_value_cuda
     assert wkv_bf16.weighted_key_value_triton_bf16io is wkv_bf16.weighted_key_value_cuda_bf16io
+
+
+def test_residual_add_backward_takes_the_handed_bf16_gradient():
+    """residual_add's backward (host logic, CPU tensors): the bf16 copy of its
+    output gradient that an ln_shift_mix backward left under that gradient's
+    identity is used as the spikes' gradient and consumed; any other gradient
+    is cast. The skip gradient goes to the paired op only with a token."""
+    from types import SimpleNamespace
+
+    from spikegpt_b200 import fused
+
+    g = torch.randn(2, 3, 4)
+    made = (g * 0 + 1).to(torch.bfloat16)  # a stand-in that differs from the cast
+    fused._BF16_GRADS[id(g)] = (g, made)
+    gx, gs, _ = fused._resid_grad(SimpleNamespace(token=0), g)
+    assert gx is g and gs is made and id(g) not in fused._BF16_GRADS
+    other = torch.randn(2, 3, 4)
+    gx, gs, _ = fused._resid_grad(SimpleNamespace(token=0), other)
+    assert torch.equal(gs, other.to(torch.bfloat16))
+    gx, gs, _ = fused._resid_grad(SimpleNamespace(token=7), other)
+    assert gx is None and fused._RESIDUAL_GRADS.pop(7) is other
+    fused._BF16_GRADS[id(g)] = (g, made)
+    fused.drop_residual_grads()  # what TrainStep does after each backward
+    assert not fused._BF16_GRADS and not fused._RESIDUAL_GRADS
