@@ -456,7 +456,6 @@ __global__ void __launch_bounds__(32 * kLifSegMax) lif_fwd_seg_kernel(const LifA
     return m;
   };
   using WriteOn = std::integral_constant<bool, true>;
-  using WriteOff = std::integral_constant<bool, false>;
 
   // Reruns segment j from m0 without writing, comparing each boundary with
   // pass A's membrane there; returns the end membrane and, per channel, the
